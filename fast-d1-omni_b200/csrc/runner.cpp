@@ -1,0 +1,681 @@
+// Host runner of the d1rs text forward pass: a C++ restatement of src/model.rs (TextModel, PrefixCache, Workspace,
+// MetaWriter, work_items, Runner::trunk / launch_prefix / launch_text / finish) and of Blas::gemm
+// (src/cuda.rs:433-490), driving any library that exports the d1kernels.h ABI through a function table.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "d1h.h"
+
+namespace {
+
+constexpr int D = 1024;         // src/model.rs:12
+constexpr int HEADS = 16;       // :13
+constexpr int KV_HEADS = 8;     // :14
+constexpr int HD = 64;          // :15
+constexpr int KV_DIM = KV_HEADS * HD;
+constexpr int MAX_POS = 16384 + 64;  // :17
+constexpr size_t META_BYTES = 8 << 20;  // :250
+constexpr int SLOTS = 2;        // :251
+
+thread_local std::string g_err;
+
+int fail(const std::string& msg, int code = -1) {
+    g_err = msg;
+    return code;
+}
+
+// ------------------------------------------------------------------------------------------------ kernel table
+
+struct Kt {
+    void* dl = nullptr;
+    int (*rmsnorm)(const float*, const float*, d1_half*, int, int, float, cudaStream_t) = nullptr;
+    int (*layernorm)(float*, const float*, float, const float*, const float*, d1_half*, float*, int, int, float,
+                     cudaStream_t) = nullptr;
+    int (*head_init)(const float*, const float*, const float*, const int*, const SeqInfo*, float*, int, float,
+                     cudaStream_t) = nullptr;
+    int (*embed)(const d1_half*, const int*, float*, int, int, cudaStream_t) = nullptr;
+    int (*swiglu)(const d1_half*, d1_half*, int, int, cudaStream_t) = nullptr;
+    int (*bias_act_h)(d1_half*, const float*, int, int, int, cudaStream_t) = nullptr;
+    int (*gather_rows)(const void*, void*, const int*, int, int, cudaStream_t) = nullptr;
+    int (*shortconv)(const d1_half*, const float*, const int*, const SeqInfo*, d1_half*, int, int, int,
+                     cudaStream_t) = nullptr;
+    int (*qk_norm_rope)(d1_half*, int, int, int, const float*, const float*, const float*, const int*,
+                        const SeqInfo*, int, int, float, cudaStream_t) = nullptr;
+    int (*flash_attn)(const d1_half*, int, const d1_half*, const d1_half*, int, int, const float*, const float*,
+                      const float*, d1_half*, int, const AttnSeq*, const int*, int, int, int, float,
+                      cudaStream_t) = nullptr;
+    int (*scorer_out)(const d1_half*, const float*, const d1_half*, float, float*, int, int, cudaStream_t) = nullptr;
+    void* (*lt_init)(size_t) = nullptr;
+    int (*lt_gemm)(void*, int, int, int, const void*, int, const void*, int, int, void*, int, int, int, float, float,
+                   cudaStream_t) = nullptr;
+    float (*lt_tune)(void*, int, int, int, int, int, int, int, int, int, int, cudaStream_t) = nullptr;
+    int (*lt_bucket)(int) = nullptr;
+    void (*lt_free_scratch)(void*) = nullptr;
+    // optional (this library's fused epilogues)
+    int (*gemm_swiglu)(void*, int, int, int, const d1_half*, int, const d1_half*, int, d1_half*, int,
+                       cudaStream_t) = nullptr;
+    int (*gemm_bias_act)(void*, int, int, int, const d1_half*, int, const d1_half*, int, const float*, int, d1_half*,
+                         int, cudaStream_t) = nullptr;
+    void (*lt_destroy)(void*) = nullptr;
+
+    bool load_builtin() {
+        rmsnorm = d1_rmsnorm;
+        layernorm = d1_layernorm;
+        head_init = d1_head_init;
+        embed = d1_embed;
+        swiglu = d1_swiglu;
+        bias_act_h = d1_bias_act_h;
+        gather_rows = d1_gather_rows;
+        shortconv = d1_shortconv;
+        qk_norm_rope = d1_qk_norm_rope;
+        flash_attn = d1_flash_attn;
+        scorer_out = d1_scorer_out;
+        lt_init = d1_lt_init;
+        lt_gemm = d1_lt_gemm;
+        lt_tune = d1_lt_tune;
+        lt_bucket = d1_lt_bucket;
+        lt_free_scratch = d1_lt_free_scratch;
+        gemm_swiglu = d1_gemm_swiglu;
+        gemm_bias_act = d1_gemm_bias_act;
+        lt_destroy = d1_lt_destroy;
+        return true;
+    }
+
+    template <class F>
+    bool sym(F& f, const char* name, bool required = true) {
+        f = reinterpret_cast<F>(dlsym(dl, name));
+        if (!f && required) {
+            g_err = std::string("kernel library lacks ") + name;
+            return false;
+        }
+        return true;
+    }
+
+    bool load_lib(const char* path) {
+        dl = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+        if (!dl) {
+            g_err = std::string("dlopen failed: ") + dlerror();
+            return false;
+        }
+        return sym(rmsnorm, "d1_rmsnorm") && sym(layernorm, "d1_layernorm") && sym(head_init, "d1_head_init") &&
+               sym(embed, "d1_embed") && sym(swiglu, "d1_swiglu") && sym(bias_act_h, "d1_bias_act_h") &&
+               sym(gather_rows, "d1_gather_rows") && sym(shortconv, "d1_shortconv") &&
+               sym(qk_norm_rope, "d1_qk_norm_rope") && sym(flash_attn, "d1_flash_attn") &&
+               sym(scorer_out, "d1_scorer_out") && sym(lt_init, "d1_lt_init") && sym(lt_gemm, "d1_lt_gemm") &&
+               sym(lt_tune, "d1_lt_tune") && sym(lt_bucket, "d1_lt_bucket") &&
+               sym(lt_free_scratch, "d1_lt_free_scratch") && sym(gemm_swiglu, "d1_gemm_swiglu", false) &&
+               sym(gemm_bias_act, "d1_gemm_bias_act", false) && sym(lt_destroy, "d1_lt_destroy", false);
+    }
+};
+
+// RoPE table [pos][32] of (cos, sin), computed as src/model.rs:121-136 does: fp32 inverse frequency, fp32 angle
+// p * f, then cos/sin in double precision rounded to float.
+std::vector<float> rope_table(float theta) {
+    float inv[32];
+    for (int i = 0; i < 32; i++) {
+        const float e = (float)(2 * i) / (float)HD;
+        inv[i] = 1.0f / powf(theta, e);
+    }
+    std::vector<float> t;
+    t.reserve((size_t)MAX_POS * 64);
+    for (int p = 0; p < MAX_POS; p++)
+        for (int i = 0; i < 32; i++) {
+            const double a = (double)((float)p * inv[i]);
+            t.push_back((float)cos(a));
+            t.push_back((float)sin(a));
+        }
+    return t;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ model
+
+struct D1Model {
+    Kt k;
+    void* lt = nullptr;       // GEMM context (d1_lt_init)
+    D1TextWeights w{};
+    std::vector<D1TrunkLayer> layers;
+    std::vector<D1HeadLayer> head;
+    std::vector<int> mixer_idx;  // per trunk layer: index among its kind (conv_idx / attn_idx)
+    int n_attn = 0, n_conv = 0, max_ffn = 0;
+    float* rope = nullptr;
+    bool fused = false;
+    long long launches = 0;
+    int dev = 0;
+
+    // Blas::gemm (src/cuda.rs:433-490): Y = alpha X W^T + beta Y. A library without a plan for the shape
+    // (d1_lt_gemm == -2) gets a heuristic plan tuned on the spot instead of a cuBLAS fallback.
+    int gemm(int m, int n, int kk, const d1_half* x, int ldx, const d1_half* wt, int ldw, void* y, int ldy, int y_f32,
+             float alpha, float beta, cudaStream_t st) {
+        if (m == 0 || n == 0) return 0;
+        launches++;
+        int e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
+        if (e == -2) {
+            if (k.lt_tune(lt, m, n, kk, ldx, ldw, 0, ldy, y_f32, 0, 0, st) < 0.f)
+                return fail("GEMM tuning failed for m=" + std::to_string(m) + " n=" + std::to_string(n));
+            e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
+        }
+        if (e) return fail("d1_lt_gemm failed (" + std::to_string(e) + ") m=" + std::to_string(m) + " n=" +
+                           std::to_string(n) + " k=" + std::to_string(kk), e);
+        return 0;
+    }
+};
+
+struct D1Workspace {
+    int cap_tokens = 0, cap_markers = 0;
+    float* h = nullptr;
+    d1_half* xn = nullptr;
+    d1_half* big = nullptr;
+    d1_half* act = nullptr;
+    d1_half* mq = nullptr;
+    d1_half* mo = nullptr;
+    float* mh = nullptr;
+    d1_half* mx = nullptr;
+    d1_half* mbig = nullptr;
+    float* logits = nullptr;
+    uint8_t* meta = nullptr;
+    uint8_t* host_meta[SLOTS] = {};
+    float* host_logits[SLOTS] = {};
+    cudaEvent_t events[SLOTS] = {};
+    bool busy[SLOTS] = {};
+    int n_logits[SLOTS] = {};
+};
+
+namespace {
+
+// Bump writer over a pinned host buffer returning the device address of each section (src/model.rs:309-326).
+struct MetaWriter {
+    uint8_t* host;
+    uint8_t* dev;
+    size_t off = 0;
+    bool overflow = false;
+    template <class T>
+    const T* put(const T* items, size_t n) {
+        off = (off + 15) / 16 * 16;
+        const size_t bytes = n * sizeof(T);
+        if (off + bytes > META_BYTES) {
+            overflow = true;
+            return nullptr;
+        }
+        if (bytes) memcpy(host + off, items, bytes);
+        const T* d = reinterpret_cast<const T*>(dev + off);
+        off += bytes;
+        return d;
+    }
+    template <class T>
+    const T* put(const std::vector<T>& v) {
+        return put(v.data(), v.size());
+    }
+};
+
+// (seq index, query-tile start) for every 64-row query tile (src/model.rs:328-339), longest sequences first so
+// the long tiles start in the first wave.
+std::vector<int> work_items(const std::vector<std::pair<int, int>>& spans) {
+    std::vector<int> order(spans.size());
+    for (size_t i = 0; i < order.size(); i++) order[i] = (int)i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return spans[a].second > spans[b].second; });
+    std::vector<int> w;
+    for (int i : order)
+        for (int q = 0; q < spans[i].second; q += 64) {
+            w.push_back(i);
+            w.push_back(q);
+        }
+    return w;
+}
+
+#define CK(expr)                                                                               \
+    do {                                                                                       \
+        int _e = (expr);                                                                       \
+        if (_e) return fail(std::string("kernel failed (") + std::to_string(_e) + "): " #expr, _e); \
+    } while (0)
+
+template <class T>
+int dmalloc(T** p, size_t bytes) {
+    if (cudaMalloc((void**)p, bytes < 16 ? 16 : bytes) != cudaSuccess) return fail("cudaMalloc failed");
+    return 0;
+}
+
+int wait_slot(D1Workspace* ws, int slot) {
+    if (ws->busy[slot]) {
+        if (cudaEventSynchronize(ws->events[slot]) != cudaSuccess) return fail("event sync failed");
+        ws->busy[slot] = false;
+    }
+    return 0;
+}
+
+// Runner::trunk (src/model.rs:355-399).
+int trunk(D1Model* m, D1Workspace* ws, int t, const int* tok_seq, const SeqInfo* seqs,
+          const std::vector<const AttnSeq*>& attn, const int* work, int n_work, bool prefix_pass, cudaStream_t st) {
+    Kt& k = m->k;
+    float* h = ws->h;
+    d1_half *xn = ws->xn, *big = ws->big, *act = ws->act;
+    const int nl = (int)m->layers.size();
+    for (int li = 0; li < nl; li++) {
+        const D1TrunkLayer& l = m->layers[li];
+        const bool last = li + 1 == nl;
+        const int idx = m->mixer_idx[li];
+        m->launches++;
+        CK(k.rmsnorm(h, l.op_norm, xn, t, D, m->w.eps, st));
+        if (!l.is_attn) {
+            CK(m->gemm(t, 3 * D, D, xn, D, l.in_proj, D, big, 3 * D, 0, 1.f, 0.f, st));
+            m->launches++;
+            CK(k.shortconv(big, l.convw, tok_seq, seqs, act, t, D, idx, st));
+            if (prefix_pass && last) return 0;  // only the conv state of the last layer is needed
+            CK(m->gemm(t, D, D, act, D, l.out_proj, D, h, D, 1, 1.f, 1.f, st));
+        } else {
+            const int ld = D + 2 * KV_DIM;
+            CK(m->gemm(t, ld, D, xn, D, l.qkv, D, big, ld, 0, 1.f, 0.f, st));
+            m->launches += 2;
+            CK(k.qk_norm_rope(big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq, seqs, idx, t, m->w.eps, st));
+            CK(k.flash_attn(big, ld, big + D, big + D + KV_DIM, ld, KV_DIM, nullptr, nullptr, nullptr, act, D, attn[idx],
+                            work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, st));
+            if (prefix_pass && last) return 0;
+            CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
+        }
+        m->launches++;
+        CK(k.rmsnorm(h, l.ffn_norm, xn, t, D, m->w.eps, st));
+        if (m->fused && k.gemm_swiglu) {
+            m->launches++;
+            CK(k.gemm_swiglu(m->lt, t, l.ffn, D, xn, D, l.gate_up, D, act, l.ffn, st));
+        } else {
+            CK(m->gemm(t, 2 * l.ffn, D, xn, D, l.gate_up, D, big, 2 * l.ffn, 0, 1.f, 0.f, st));
+            m->launches++;
+            CK(k.swiglu(big, act, t, l.ffn, st));
+        }
+        CK(m->gemm(t, D, l.ffn, act, l.ffn, l.down, l.ffn, h, D, 1, 1.f, 1.f, st));
+    }
+    return 0;
+}
+
+// up GEMM + ReLU(+b) of a head FFN: fused epilogue when available, else GEMM then d1_bias_act_h (src/model.rs:568-569).
+int head_up(D1Model* m, int rows, int F, const d1_half* x, const d1_half* w, const float* b, d1_half* y,
+            cudaStream_t st) {
+    if (m->fused && m->k.gemm_bias_act) {
+        m->launches++;
+        CK(m->k.gemm_bias_act(m->lt, rows, F, D, x, D, w, D, b, 1, y, F, st));
+        return 0;
+    }
+    CK(m->gemm(rows, F, D, x, D, w, D, y, F, 0, 1.f, 0.f, st));
+    m->launches++;
+    CK(m->k.bias_act_h(y, b, rows, F, 1, st));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* d1h_last_error(void) { return g_err.c_str(); }
+
+D1Model* d1h_model_create(const D1TextWeights* w, const char* kernel_lib, int fused) {
+    if (!w || w->n_layers <= 0 || !w->layers) {
+        fail("invalid weights");
+        return nullptr;
+    }
+    D1Model* m = new D1Model();
+    bool ok = kernel_lib ? m->k.load_lib(kernel_lib) : m->k.load_builtin();
+    if (!ok) {
+        delete m;
+        return nullptr;
+    }
+    cudaGetDevice(&m->dev);
+    m->w = *w;
+    m->layers.assign(w->layers, w->layers + w->n_layers);
+    if (w->n_head > 0) m->head.assign(w->head, w->head + w->n_head);
+    m->w.layers = nullptr;
+    m->w.head = nullptr;
+    for (const auto& l : m->layers) {
+        m->mixer_idx.push_back(l.is_attn ? m->n_attn++ : m->n_conv++);
+        m->max_ffn = std::max(m->max_ffn, l.ffn);
+    }
+    for (const auto& l : m->head) m->max_ffn = std::max(m->max_ffn, l.ffn);
+    m->fused = fused != 0;
+    m->lt = m->k.lt_init(32 << 20);  // src/cuda.rs:406
+    if (!m->lt) {
+        fail("d1_lt_init failed (needs an sm_100 GPU)");
+        delete m;
+        return nullptr;
+    }
+    std::vector<float> rt = rope_table(w->rope_theta);
+    if (cudaMalloc(&m->rope, rt.size() * sizeof(float)) != cudaSuccess ||
+        cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        fail("rope table upload failed");
+        d1h_model_destroy(m);
+        return nullptr;
+    }
+    return m;
+}
+
+void d1h_model_destroy(D1Model* m) {
+    if (!m) return;
+    if (m->rope) cudaFree(m->rope);
+    if (m->lt && m->k.lt_destroy) m->k.lt_destroy(m->lt);
+    if (m->k.dl) dlclose(m->k.dl);
+    delete m;
+}
+
+long long d1h_launch_count(const D1Model* m) { return m ? m->launches : 0; }
+
+D1Workspace* d1h_workspace_create(D1Model* m, int cap_tokens) {
+    if (!m || cap_tokens <= 0) return nullptr;
+    D1Workspace* ws = new D1Workspace();
+    ws->cap_tokens = cap_tokens;
+    ws->cap_markers = cap_tokens / 2 + 64;
+    const size_t ct = cap_tokens, cm = ws->cap_markers;
+    const size_t big_w = std::max<size_t>(2 * (size_t)m->max_ffn, 3 * D);
+    int e = 0;
+    e |= dmalloc(&ws->h, ct * D * 4);
+    e |= dmalloc(&ws->xn, ct * D * 2);
+    e |= dmalloc(&ws->big, ct * big_w * 2);
+    e |= dmalloc(&ws->act, ct * std::max(m->max_ffn, D) * 2);
+    e |= dmalloc(&ws->mq, cm * 3 * D * 2);
+    e |= dmalloc(&ws->mo, cm * D * 2);
+    e |= dmalloc(&ws->mh, cm * D * 4);
+    e |= dmalloc(&ws->mx, cm * D * 2);
+    e |= dmalloc(&ws->mbig, cm * std::max(m->max_ffn, 1) * 2);
+    e |= dmalloc(&ws->logits, cm * 4);
+    e |= dmalloc(&ws->meta, META_BYTES);
+    for (int s = 0; s < SLOTS && !e; s++) {
+        if (cudaMallocHost((void**)&ws->host_meta[s], META_BYTES) != cudaSuccess ||
+            cudaMallocHost((void**)&ws->host_logits[s], cm * 4) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ws->events[s], cudaEventDisableTiming) != cudaSuccess)
+            e = fail("workspace host allocation failed");
+    }
+    if (e) {
+        d1h_workspace_destroy(ws);
+        return nullptr;
+    }
+    return ws;
+}
+
+void d1h_workspace_destroy(D1Workspace* ws) {
+    if (!ws) return;
+    for (void* p : {(void*)ws->h, (void*)ws->xn, (void*)ws->big, (void*)ws->act, (void*)ws->mq, (void*)ws->mo,
+                    (void*)ws->mh, (void*)ws->mx, (void*)ws->mbig, (void*)ws->logits, (void*)ws->meta})
+        if (p) cudaFree(p);
+    for (int s = 0; s < SLOTS; s++) {
+        if (ws->busy[s]) cudaEventSynchronize(ws->events[s]);
+        if (ws->host_meta[s]) cudaFreeHost(ws->host_meta[s]);
+        if (ws->host_logits[s]) cudaFreeHost(ws->host_logits[s]);
+        if (ws->events[s]) cudaEventDestroy(ws->events[s]);
+    }
+    delete ws;
+}
+
+int d1h_prefix_alloc(D1Model* m, int len, D1PrefixCache* out, cudaStream_t st) {
+    if (!m || !out || len <= 0) return fail("bad prefix size");
+    const size_t kv = (size_t)m->n_attn * len * KV_DIM * 2;
+    out->len = len;
+    out->k = out->v = out->bx = nullptr;
+    if (cudaMallocAsync((void**)&out->k, std::max<size_t>(kv, 256), st) != cudaSuccess ||
+        cudaMallocAsync((void**)&out->v, std::max<size_t>(kv, 256), st) != cudaSuccess ||
+        cudaMallocAsync((void**)&out->bx, std::max<size_t>((size_t)m->n_conv * D * 2, 256), st) != cudaSuccess)
+        return fail("cudaMallocAsync failed for a prefix cache");
+    return 0;
+}
+
+void d1h_prefix_free(D1PrefixCache* c, cudaStream_t st) {
+    if (!c) return;
+    for (d1_half** p : {&c->k, &c->v, &c->bx})
+        if (*p) {
+            cudaFreeAsync(*p, st);
+            *p = nullptr;
+        }
+}
+
+// Runner::launch_prefix (src/model.rs:402-459).
+int d1h_launch_prefix(D1Model* m, D1Workspace* ws, int slot, const D1PrefixSeq* items, int n_items, cudaStream_t st) {
+    if (!m || !ws || slot < 0 || slot >= SLOTS || n_items <= 0) return fail("bad arguments");
+    int t = 0;
+    for (int i = 0; i < n_items; i++) t += items[i].cache->len;
+    if (t > ws->cap_tokens) return fail("prefix batch exceeds workspace capacity");
+    if (wait_slot(ws, slot)) return -1;
+    MetaWriter w{ws->host_meta[slot], ws->meta};
+    std::vector<int> tok_seq;
+    tok_seq.reserve(t);
+    std::vector<SeqInfo> seqs;
+    std::vector<std::pair<int, int>> spans;
+    int start = 0;
+    for (int i = 0; i < n_items; i++) {
+        const int n = items[i].cache->len;
+        tok_seq.insert(tok_seq.end(), n, i);
+        SeqInfo s{};
+        s.start = start;
+        s.len = n;
+        s.save_bx = items[i].cache->bx;
+        s.save_k = items[i].cache->k;
+        s.save_v = items[i].cache->v;
+        seqs.push_back(s);
+        spans.push_back({start, n});
+        start += n;
+    }
+    const int* d_tok = w.put(tok_seq);
+    const SeqInfo* d_seqs = w.put(seqs);
+    std::vector<const AttnSeq*> attn;
+    for (int l = 0; l < m->n_attn; l++) {
+        std::vector<AttnSeq> a;
+        for (auto& sp : spans) a.push_back(AttnSeq{sp.first, sp.second, sp.first, sp.second, 0, 0, nullptr, nullptr});
+        attn.push_back(w.put(a));
+    }
+    std::vector<int> work = work_items(spans);
+    const int* d_work = w.put(work);
+    if (w.overflow) return fail("batch metadata exceeds 8 MB");
+    if (cudaMemcpyAsync(ws->meta, ws->host_meta[slot], w.off, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail("metadata upload failed");
+    for (int i = 0; i < n_items; i++)
+        if (cudaMemcpyAsync(ws->h + (size_t)spans[i].first * D, items[i].emb, (size_t)spans[i].second * D * 4,
+                            cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return fail("prefix embedding copy failed");
+    int e = trunk(m, ws, t, d_tok, d_seqs, attn, d_work, (int)work.size() / 2, true, st);
+    if (e) return e;
+    cudaEventRecord(ws->events[slot], st);
+    ws->busy[slot] = true;
+    ws->n_logits[slot] = 0;
+    return 0;
+}
+
+// Runner::launch_text (src/model.rs:470-599).
+int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs_in, int n_seqs, cudaStream_t st) {
+    if (!m || !ws || slot < 0 || slot >= SLOTS || n_seqs <= 0) return fail("bad arguments");
+    if (m->head.empty()) return fail("the model has no decision head");
+    Kt& k = m->k;
+    int t = 0, n_mark = 0;
+    for (int i = 0; i < n_seqs; i++) {
+        if (seqs_in[i].n_ids <= 0) return fail("empty sequence");
+        t += seqs_in[i].n_ids;
+        n_mark += seqs_in[i].n_markers;
+        for (int j = 0; j < seqs_in[i].n_markers; j++)
+            if (seqs_in[i].markers[j] < 0 || seqs_in[i].markers[j] >= seqs_in[i].n_ids) return fail("marker out of range");
+    }
+    if (t > ws->cap_tokens) return fail("text batch exceeds workspace capacity");
+    if (n_mark > ws->cap_markers) return fail("too many markers for the workspace");
+    if (wait_slot(ws, slot)) return -1;
+    MetaWriter w{ws->host_meta[slot], ws->meta};
+
+    std::vector<int> ids, tok_seq, marker_rows;
+    ids.reserve(t);
+    tok_seq.reserve(t);
+    std::vector<SeqInfo> seqs;
+    std::vector<std::pair<int, int>> spans, mspans;
+    int start = 0;
+    for (int i = 0; i < n_seqs; i++) {
+        const D1TextSeq& s = seqs_in[i];
+        ids.insert(ids.end(), s.ids, s.ids + s.n_ids);
+        tok_seq.insert(tok_seq.end(), s.n_ids, i);
+        SeqInfo si{};
+        si.start = start;
+        si.len = s.n_ids;
+        si.pos_off = s.prefix ? s.prefix->len : 0;
+        si.qtype = s.qtype;
+        si.ext_bx = s.prefix ? s.prefix->bx : nullptr;
+        seqs.push_back(si);
+        mspans.push_back({(int)marker_rows.size(), s.n_markers});
+        for (int j = 0; j < s.n_markers; j++) marker_rows.push_back(start + s.markers[j]);
+        spans.push_back({start, s.n_ids});
+        start += s.n_ids;
+    }
+    const int* d_ids = w.put(ids);
+    const int* d_tok = w.put(tok_seq);
+    const SeqInfo* d_seqs = w.put(seqs);
+    std::vector<const AttnSeq*> attn;
+    for (int l = 0; l < m->n_attn; l++) {
+        std::vector<AttnSeq> a;
+        for (int i = 0; i < n_seqs; i++) {
+            const D1PrefixCache* p = seqs_in[i].prefix;
+            AttnSeq as{spans[i].first, spans[i].second, spans[i].first, spans[i].second, 0, 0, nullptr, nullptr};
+            if (p) {
+                as.ext_len = p->len;
+                as.ext_k = p->k + (size_t)l * p->len * KV_DIM;
+                as.ext_v = p->v + (size_t)l * p->len * KV_DIM;
+            }
+            a.push_back(as);
+        }
+        attn.push_back(w.put(a));
+    }
+    std::vector<AttnSeq> head_attn, last_attn;
+    for (int i = 0; i < n_seqs; i++) {
+        head_attn.push_back(AttnSeq{spans[i].first, spans[i].second, spans[i].first, spans[i].second, 0, 0, nullptr, nullptr});
+        last_attn.push_back(AttnSeq{mspans[i].first, mspans[i].second, spans[i].first, spans[i].second, 0, 0, nullptr, nullptr});
+    }
+    const AttnSeq* d_head_attn = w.put(head_attn);
+    const AttnSeq* d_last_attn = w.put(last_attn);
+    std::vector<int> work = work_items(spans), mwork = work_items(mspans);
+    const int* d_work = w.put(work);
+    const int* d_mwork = w.put(mwork);
+    const int* d_mrows = w.put(marker_rows);
+    if (w.overflow) return fail("batch metadata exceeds 8 MB");
+    const int n_work = (int)work.size() / 2, n_mwork = (int)mwork.size() / 2;
+
+    float* h = ws->h;
+    d1_half *xn = ws->xn, *big = ws->big, *act = ws->act;
+    if (cudaMemcpyAsync(ws->meta, ws->host_meta[slot], w.off, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail("metadata upload failed");
+    m->launches++;
+    CK(k.embed(m->w.embed, d_ids, h, t, D, st));
+    int e = trunk(m, ws, t, d_tok, d_seqs, attn, d_work, n_work, false, st);
+    if (e) return e;
+
+    m->launches++;
+    CK(k.head_init(h, m->w.final_norm, m->w.type_emb, d_tok, d_seqs, h, t, m->w.eps, st));
+    const float* pend = nullptr;
+    const int nh = (int)m->head.size();
+    const int qkv_ld = 3 * D;
+    for (int li = 0; li < nh; li++) {
+        const D1HeadLayer& l = m->head[li];
+        m->launches++;
+        CK(k.layernorm(h, pend, 1.f, l.n1_w, l.n1_b, xn, nullptr, t, D, 1e-5f, st));
+        CK(m->gemm(t, qkv_ld, D, xn, D, l.qkv, D, big, qkv_ld, 0, 1.f, 0.f, st));
+        const float* qb = l.qkv_b;
+        if (li + 1 < nh) {
+            m->launches++;
+            CK(k.flash_attn(big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, qb, qb + D, qb + 2 * D, act, D, d_head_attn,
+                            d_work, n_work, HEADS, 1, 0.125f, st));
+            CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
+            m->launches++;
+            CK(k.layernorm(h, l.out_b, 1.f, l.n2_w, l.n2_b, xn, nullptr, t, D, 1e-5f, st));
+            if (head_up(m, t, l.ffn, xn, l.up, l.up_b, big, st)) return -1;
+            CK(m->gemm(t, D, l.ffn, big, l.ffn, l.down, l.ffn, h, D, 1, 1.f, 1.f, st));
+            pend = l.down_b;
+        } else {
+            // Last head layer: queries, the output projection and the FFN run on marker rows only; keys/values
+            // still cover every text position (src/model.rs:572-592).
+            const int nm = n_mark;
+            if (nm > 0) {
+                m->launches += 3;
+                CK(k.gather_rows(big, ws->mq, d_mrows, nm, qkv_ld * 2, st));
+                CK(k.gather_rows(h, ws->mh, d_mrows, nm, D * 4, st));
+                CK(k.flash_attn(ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, qb, qb + D, qb + 2 * D, ws->mo, D,
+                                d_last_attn, d_mwork, n_mwork, HEADS, 1, 0.125f, st));
+                CK(m->gemm(nm, D, D, ws->mo, D, l.out, D, ws->mh, D, 1, 1.f, 1.f, st));
+                m->launches++;
+                CK(k.layernorm(ws->mh, l.out_b, 1.f, l.n2_w, l.n2_b, ws->mx, nullptr, nm, D, 1e-5f, st));
+                if (head_up(m, nm, l.ffn, ws->mx, l.up, l.up_b, ws->mbig, st)) return -1;
+                CK(m->gemm(nm, D, l.ffn, ws->mbig, l.ffn, l.down, l.ffn, ws->mh, D, 1, 1.f, 1.f, st));
+                // scorer: LN -> Linear -> GELU -> Linear(1)
+                m->launches++;
+                CK(k.layernorm(ws->mh, l.down_b, 1.f, m->w.cls_norm_w, m->w.cls_norm_b, ws->mx, nullptr, nm, D, 1e-5f,
+                               st));
+                CK(m->gemm(nm, D, D, ws->mx, D, m->w.cls_w, D, ws->mo, D, 0, 1.f, 0.f, st));
+                m->launches++;
+                CK(k.scorer_out(ws->mo, m->w.cls_b, m->w.out_w, m->w.out_b, ws->logits, nm, D, st));
+            }
+        }
+    }
+    if (n_mark > 0 &&
+        cudaMemcpyAsync(ws->host_logits[slot], ws->logits, (size_t)n_mark * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return fail("logits download failed");
+    cudaEventRecord(ws->events[slot], st);
+    ws->busy[slot] = true;
+    ws->n_logits[slot] = n_mark;
+    return 0;
+}
+
+// Runner::finish (src/model.rs:602-607).
+int d1h_finish(D1Model* m, D1Workspace* ws, int slot, float* out, int cap) {
+    if (!m || !ws || slot < 0 || slot >= SLOTS) return fail("bad arguments");
+    if (!ws->busy[slot]) return fail("slot not launched");
+    if (cudaEventSynchronize(ws->events[slot]) != cudaSuccess) return fail("event sync failed");
+    ws->busy[slot] = false;
+    const int n = ws->n_logits[slot];
+    if (out) memcpy(out, ws->host_logits[slot], (size_t)std::min(n, cap) * 4);
+    return n;
+}
+
+// GEMM tuning over every trunk/head shape and M bucket (src/engine.rs:528-616, text shapes only).
+int d1h_tune(D1Model* m, D1Workspace* ws, int max_tokens, cudaStream_t st) {
+    if (!m || !ws) return fail("bad arguments");
+    struct Shape {
+        int n, k, ldx, ldw, ldy, y_f32, cap;
+    };
+    std::vector<Shape> shapes;
+    auto add = [&](Shape s) {
+        for (auto& x : shapes)
+            if (x.n == s.n && x.k == s.k && x.ldx == s.ldx && x.ldw == s.ldw && x.ldy == s.ldy && x.y_f32 == s.y_f32) {
+                x.cap = std::max(x.cap, s.cap);
+                return;
+            }
+        shapes.push_back(s);
+    };
+    const int mk = std::min(max_tokens, ws->cap_tokens), mm = std::min(max_tokens / 2 + 64, ws->cap_markers);
+    for (const auto& l : m->layers) {
+        if (l.is_attn) {
+            add({D + 2 * KV_DIM, D, D, D, D + 2 * KV_DIM, 0, mk});
+        } else {
+            add({3 * D, D, D, D, 3 * D, 0, mk});
+        }
+        add({D, D, D, D, D, 1, mk});
+        if (!(m->fused && m->k.gemm_swiglu)) add({2 * l.ffn, D, D, D, 2 * l.ffn, 0, mk});
+        add({D, l.ffn, l.ffn, l.ffn, D, 1, mk});
+    }
+    for (const auto& l : m->head) {
+        add({3 * D, D, D, D, 3 * D, 0, mk});
+        if (!(m->fused && m->k.gemm_bias_act)) add({l.ffn, D, D, D, l.ffn, 0, mk});
+        add({D, l.ffn, l.ffn, l.ffn, D, 1, mk});
+        add({D, D, D, D, D, 0, mm});
+    }
+    int n = 0;
+    for (const auto& s : shapes) {
+        int b = 1;
+        while (true) {
+            const int nb = m->k.lt_bucket(b);
+            if (m->k.lt_tune(m->lt, nb, s.n, s.k, s.ldx, s.ldw, 0, s.ldy, s.y_f32, 0, 1, st) < 0.f)
+                return fail("tuning failed for n=" + std::to_string(s.n) + " k=" + std::to_string(s.k));
+            n++;
+            if (nb >= s.cap || nb >= 16384) break;
+            b = nb + 1;
+        }
+    }
+    cudaStreamSynchronize(st);
+    m->k.lt_free_scratch(m->lt);
+    return n;
+}
+
+}  // extern "C"

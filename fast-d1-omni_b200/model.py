@@ -1,0 +1,169 @@
+"""The text model on one GPU: uploads weights, owns a d1h runner (include/d1h.h) and its workspace, and runs
+packed batches (src/model.rs Runner::launch_text / launch_prefix / finish).
+
+torch is used only for device memory and streams; every kernel is libd1kernels'.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import abi, check, lib
+
+
+def _ptr(t: torch.Tensor):
+    return C.c_void_p(t.data_ptr())
+
+
+class TextModel:
+    """Device copy of `weights.text_weights(...)` plus a runner.
+
+    kernel_lib: None runs this library's kernels; a path runs another library with the d1kernels.h ABI through the
+    same host runner (the tests use it for the reference's own kernels). fused: use the fused GEMM epilogues.
+    """
+
+    def __init__(self, w: dict, device: int = 0, kernel_lib: str | None = None, fused: bool = True,
+                 cap_tokens: int = 8192):
+        self.device = torch.device("cuda", device)
+        self.L = lib()
+        self._keep = []
+
+        def h16(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16)).to(self.device)
+            self._keep.append(t)
+            return _ptr(t)
+
+        def f32(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.device)
+            self._keep.append(t)
+            return _ptr(t)
+
+        with torch.cuda.device(self.device):
+            layers = (abi.TrunkLayer * len(w["layers"]))()
+            for i, l in enumerate(w["layers"]):
+                x = layers[i]
+                x.is_attn = int(l["is_attn"])
+                x.ffn = l["ffn"]
+                x.op_norm = f32(l["op_norm"])
+                x.ffn_norm = f32(l["ffn_norm"])
+                x.gate_up = h16(l["gate_up"])
+                x.down = h16(l["down"])
+                if l["is_attn"]:
+                    x.qkv, x.out, x.qn, x.kn = h16(l["qkv"]), h16(l["out"]), f32(l["qn"]), f32(l["kn"])
+                else:
+                    x.in_proj, x.out_proj, x.convw = h16(l["in_proj"]), h16(l["out_proj"]), f32(l["convw"])
+            head = (abi.HeadLayer * max(1, len(w["head"])))()
+            for i, l in enumerate(w["head"]):
+                x = head[i]
+                x.n1_w, x.n1_b, x.qkv, x.qkv_b = f32(l["n1_w"]), f32(l["n1_b"]), h16(l["qkv"]), f32(l["qkv_b"])
+                x.out, x.out_b, x.n2_w, x.n2_b = h16(l["out"]), f32(l["out_b"]), f32(l["n2_w"]), f32(l["n2_b"])
+                x.up, x.up_b, x.down, x.down_b = h16(l["up"]), f32(l["up_b"]), h16(l["down"]), f32(l["down_b"])
+                x.ffn = l["ffn"]
+            tw = abi.TextWeights()
+            tw.n_layers = len(w["layers"])
+            tw.layers = layers
+            tw.n_head = len(w["head"])
+            tw.head = head
+            tw.vocab = w["vocab"]
+            tw.embed = h16(w["embed"])
+            tw.final_norm = f32(w["final_norm"])
+            tw.type_emb = f32(w["type_emb"])
+            tw.cls_norm_w, tw.cls_norm_b = f32(w["cls_norm_w"]), f32(w["cls_norm_b"])
+            tw.cls_w, tw.cls_b, tw.out_w = h16(w["cls_w"]), f32(w["cls_b"]), h16(w["out_w"])
+            tw.out_b = float(w["out_b"])
+            tw.eps = float(w["eps"])
+            tw.rope_theta = float(w["rope_theta"])
+            torch.cuda.synchronize(self.device)
+            self.m = self.L.d1h_model_create(C.byref(tw), kernel_lib.encode() if kernel_lib else None, int(fused))
+            if not self.m:
+                raise RuntimeError(f"d1h_model_create failed: {self.L.d1h_last_error().decode()}")
+            self.ws = self.L.d1h_workspace_create(self.m, cap_tokens)
+            if not self.ws:
+                raise RuntimeError(f"d1h_workspace_create failed: {self.L.d1h_last_error().decode()}")
+        self.cap_tokens = cap_tokens
+        self._pending = {}
+
+    # ---------------------------------------------------------------------------------------------------- runs
+    def _stream(self, stream):
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return C.c_void_p(s.cuda_stream)
+
+    def launch(self, batch, slot: int = 0, stream=None) -> None:
+        """Enqueue a batch (list of dict(ids, markers, qtype[, prefix])) on `stream` (default: current)."""
+        seqs = (abi.TextSeq * len(batch))()
+        keep = []
+        for i, s in enumerate(batch):
+            ids = np.ascontiguousarray(s["ids"], dtype=np.int32)
+            mk = np.ascontiguousarray(s["markers"], dtype=np.int32)
+            keep += [ids, mk]
+            seqs[i].ids = ids.ctypes.data_as(C.POINTER(C.c_int))
+            seqs[i].n_ids = len(ids)
+            seqs[i].markers = mk.ctypes.data_as(C.POINTER(C.c_int))
+            seqs[i].n_markers = len(mk)
+            seqs[i].qtype = int(s["qtype"])
+            pc = s.get("prefix")
+            seqs[i].prefix = C.pointer(pc) if pc is not None else None
+        with torch.cuda.device(self.device):
+            check(self.L.d1h_launch_text(self.m, self.ws, slot, seqs, len(batch), self._stream(stream)), "launch_text")
+        self._pending[slot] = sum(len(s["markers"]) for s in batch)
+
+    def finish(self, slot: int = 0) -> np.ndarray:
+        n = self._pending.pop(slot)
+        out = np.zeros(max(n, 1), np.float32)
+        r = self.L.d1h_finish(self.m, self.ws, slot, out.ctypes.data_as(C.POINTER(C.c_float)), len(out))
+        if r < 0:
+            raise RuntimeError(f"d1h_finish failed: {self.L.d1h_last_error().decode()}")
+        return out[:n]
+
+    def __call__(self, batch, stream=None) -> np.ndarray:
+        self.launch(batch, 0, stream)
+        return self.finish(0)
+
+    # ---------------------------------------------------------------------------------------------------- prefixes
+    def prefix_alloc(self, n: int, stream=None) -> abi.PrefixCache:
+        pc = abi.PrefixCache()
+        with torch.cuda.device(self.device):
+            check(self.L.d1h_prefix_alloc(self.m, n, C.byref(pc), self._stream(stream)), "prefix_alloc")
+        return pc
+
+    def prefix_free(self, pc: abi.PrefixCache, stream=None) -> None:
+        with torch.cuda.device(self.device):
+            self.L.d1h_prefix_free(C.byref(pc), self._stream(stream))
+
+    def launch_prefix(self, items, slot: int = 0, stream=None) -> None:
+        """items: list of (emb fp32 [len, 1024] CUDA tensor, PrefixCache)."""
+        arr = (abi.PrefixSeq * len(items))()
+        for i, (emb, pc) in enumerate(items):
+            assert emb.is_cuda and emb.dtype == torch.float32 and emb.is_contiguous()
+            arr[i].emb = _ptr(emb)
+            arr[i].cache = C.pointer(pc)
+        with torch.cuda.device(self.device):
+            check(self.L.d1h_launch_prefix(self.m, self.ws, slot, arr, len(items), self._stream(stream)), "prefix")
+
+    def tune(self, max_tokens: int | None = None, stream=None) -> int:
+        with torch.cuda.device(self.device):
+            n = self.L.d1h_tune(self.m, self.ws, max_tokens or self.cap_tokens, self._stream(stream))
+        if n < 0:
+            raise RuntimeError(f"d1h_tune failed: {self.L.d1h_last_error().decode()}")
+        return n
+
+    @property
+    def launches(self) -> int:
+        return int(self.L.d1h_launch_count(self.m))
+
+    def close(self) -> None:
+        if getattr(self, "ws", None):
+            self.L.d1h_workspace_destroy(self.ws)
+            self.ws = None
+        if getattr(self, "m", None):
+            self.L.d1h_model_destroy(self.m)
+            self.m = None
+        self._keep.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,164 @@
+"""Seeded synthetic weights and batches of the shapes the reference loads (numpy only, no GPU).
+
+There is no network and no GGUF file here, so every benchmark and parity check runs on random-init weights of the
+d1-omni-600M architecture (the reference's BASELINE configs): weights N(0, 0.02) rounded to fp16 (the F16 GGUF
+stores fp16, src/model.rs:106-118), norm weights set to 1, biases N(0, 0.02).
+
+The text trunk follows src/model.rs:139-231 (hidden 1024, 16 layers, attention at {2,5,8,10,12,14}, SwiGLU 4608,
+vocab 65536). The decision head's sizes come from GGUF metadata in the reference (src/model.rs:145,193) and are not
+given by the configs; this build fixes 2 head layers with a ReLU FFN of width 2048 and 4 question types.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+D = 1024
+KV_DIM = 512
+ATTN_LAYERS = (2, 5, 8, 10, 12, 14)
+
+
+class _Gen:
+    """Each tensor draws from its own stream seeded by (seed, tensor index), so tensors can be generated in
+    parallel threads and still come out the same on every machine."""
+
+    def __init__(self, seed: int):
+        self.seed = seed
+        self.n = 0
+        self.jobs = []
+
+    def _rng(self):
+        self.n += 1
+        return np.random.default_rng([self.seed, self.n])
+
+    def mat(self, *shape, std=0.02):
+        rng = self._rng()
+        out = np.empty(shape, np.float32)
+        self.jobs.append((rng, out, std, True))
+        return out
+
+    def vec(self, n, std=0.02):
+        rng = self._rng()
+        out = np.empty(n, np.float32)
+        self.jobs.append((rng, out, std, False))
+        return out
+
+    def run(self):
+        from concurrent.futures import ThreadPoolExecutor
+
+        def fill(job):
+            rng, out, std, round16 = job
+            v = rng.standard_normal(out.shape, dtype=np.float32)
+            v *= np.float32(std)
+            if round16:  # fp16-representable values, as the F16 GGUF stores them
+                try:
+                    import torch
+                    v = torch.from_numpy(v).half().float().numpy()
+                except Exception:  # pragma: no cover
+                    v = v.astype(np.float16).astype(np.float32)
+            out[...] = v
+
+        with ThreadPoolExecutor(8) as ex:
+            list(ex.map(fill, self.jobs))
+        self.jobs.clear()
+
+
+def _rope(theta):
+    # same table as src/model.rs:121-136 (the runner builds its own on the device)
+    e = (2.0 * np.arange(32, dtype=np.float32) / np.float32(64)).astype(np.float32)
+    inv = (np.float32(1.0) / np.power(np.float32(theta), e, dtype=np.float32)).astype(np.float32)
+    pos = np.arange(16384 + 64, dtype=np.float32)[:, None]
+    ang = (pos * inv[None, :]).astype(np.float32).astype(np.float64)
+    t = np.empty((16384 + 64, 32, 2), np.float32)
+    t[..., 0] = np.cos(ang)
+    t[..., 1] = np.sin(ang)
+    return t
+
+
+def text_weights(seed=0, n_layers=16, attn_layers=ATTN_LAYERS, ffn=4608, vocab=65536, n_head=2, head_ffn=2048,
+                 n_types=4, eps=1e-5, rope_theta=1e6):
+    """Weights in the layout the runner and the oracle take (matrices as fp16-valued float32 arrays)."""
+    g = _Gen(seed)
+    w = {"eps": np.float32(eps), "rope_theta": np.float32(rope_theta), "vocab": vocab}
+    w["embed"] = g.mat(vocab, D)
+    layers = []
+    for i in range(n_layers):
+        l = {"is_attn": i in attn_layers, "ffn": ffn,
+             "op_norm": np.ones(D, np.float32), "ffn_norm": np.ones(D, np.float32)}
+        if l["is_attn"]:
+            l["qkv"] = g.mat(D + 2 * KV_DIM, D)   # [q; k; v] rows (src/model.rs:160)
+            l["out"] = g.mat(D, D)
+            l["qn"] = np.ones(64, np.float32)
+            l["kn"] = np.ones(64, np.float32)
+        else:
+            l["in_proj"] = g.mat(3 * D, D)
+            l["out_proj"] = g.mat(D, D)
+            l["convw"] = g.vec(D * 3).reshape(D, 3)
+        l["gate_up"] = g.mat(2 * ffn, D)           # [gate; up] rows (src/model.rs:184)
+        l["down"] = g.mat(D, ffn)
+        layers.append(l)
+    w["layers"] = layers
+    w["final_norm"] = np.ones(D, np.float32)
+    w["type_emb"] = g.vec(n_types * D).reshape(n_types, D)
+    head = []
+    for _ in range(n_head):
+        head.append({
+            "n1_w": np.ones(D, np.float32), "n1_b": g.vec(D),
+            "qkv": g.mat(3 * D, D), "qkv_b": g.vec(3 * D),
+            "out": g.mat(D, D), "out_b": g.vec(D),
+            "n2_w": np.ones(D, np.float32), "n2_b": g.vec(D),
+            "up": g.mat(head_ffn, D), "up_b": g.vec(head_ffn),
+            "down": g.mat(D, head_ffn), "down_b": g.vec(D), "ffn": head_ffn})
+    w["head"] = head
+    w["cls_norm_w"] = np.ones(D, np.float32)
+    w["cls_norm_b"] = g.vec(D)
+    w["cls_w"] = g.mat(D, D)
+    w["cls_b"] = g.vec(D)
+    w["out_w"] = g.mat(D, std=0.02)
+    out_b = g.vec(1)
+    g.run()
+    w["out_b"] = np.float32(out_b[0])
+    w["rope"] = _rope(rope_theta)
+    return w
+
+
+def text_batch(seed, n_seqs, seq_len=None, lengths=None, vocab=65536, n_markers=3, n_types=4):
+    """A packed batch of question sequences: uniform token ids, n_markers distinct marker rows per sequence
+    (option rows), a random question type. lengths overrides seq_len per sequence."""
+    rng = np.random.default_rng(seed)
+    if lengths is None:
+        lengths = [seq_len] * n_seqs
+    batch = []
+    for n in lengths:
+        ids = rng.integers(0, vocab, size=n, dtype=np.int32)
+        k = min(n_markers, n)
+        markers = np.sort(rng.choice(n, size=k, replace=False)).astype(np.int32)
+        batch.append({"ids": ids, "markers": markers, "qtype": int(rng.integers(0, n_types))})
+    return batch
+
+
+def lognormal_lengths(seed, total, median=384, sigma=1.0, lo=32, hi=16384):
+    """Per-sequence lengths drawn log-normal (median, sigma), clipped to [lo, hi], until they fill `total`
+    tokens; the last one is cut to fit (sigma is not given there and is fixed to 1.0)."""
+    rng = np.random.default_rng(seed)
+    out, used = [], 0
+    while used < total:
+        n = int(np.clip(round(median * np.exp(sigma * rng.standard_normal())), lo, hi))
+        n = min(n, total - used)
+        out.append(n)
+        used += n
+    return out
+
+
+def loguniform_lengths(seed, total, lo=128, hi=2048):
+    """Text rows of 128-2048 tokens, log-uniform, packed up to `total` tokens."""
+    rng = np.random.default_rng(seed)
+    out, used = [], 0
+    while True:
+        n = int(round(np.exp(rng.uniform(np.log(lo), np.log(hi)))))
+        if used + n > total:
+            if total - used >= lo:
+                out.append(total - used)
+            break
+        out.append(n)
+        used += n
+    return out

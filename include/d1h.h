@@ -1,0 +1,146 @@
+/*
+ * d1h.h — host runner of the d1rs text forward pass over a d1kernels library.
+ *
+ * A C++ restatement of the reference's Rust host for this path, kept call-for-call:
+ *   - TextModel / TrunkLayer / HeadLayer weights            src/model.rs:19-68
+ *   - PrefixCache (media prefix K/V + conv state)            src/model.rs:70-104
+ *   - Workspace, MetaWriter, work_items                      src/model.rs:250-339
+ *   - Runner::trunk, launch_prefix, launch_text, finish      src/model.rs:355-607
+ *   - Blas::gemm over d1_lt_gemm                             src/cuda.rs:433-490
+ * There is no Rust toolchain on this machine, so the Rust host cannot be linked here; this runner is what the
+ * tests and the benchmark drive, and the Rust crate links libd1kernels unchanged (the d1_* ABI in d1kernels.h).
+ *
+ * The runner reaches every kernel through a function table. By default the table holds this library's own
+ * sm_100a kernels; d1h_model_create can instead load any library that exports the d1kernels.h ABI (used by the
+ * tests to run the reference's own kernels through the same host code).
+ *
+ * Weights are device pointers owned by the caller (they must outlive the model). All launches are asynchronous
+ * on the stream given to each call. Functions return 0 on success, a nonzero kernel/CUDA status otherwise.
+ */
+#ifndef D1H_H
+#define D1H_H
+
+#include "d1kernels.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One trunk layer (src/model.rs:19-31). is_attn selects the mixer; fields of the other mixer are ignored. */
+typedef struct D1TrunkLayer {
+    int is_attn;
+    const d1_half* in_proj;   /* conv: shortconv.in_proj [3D, D] */
+    const d1_half* out_proj;  /* conv: shortconv.out_proj [D, D] */
+    const float* convw;       /* conv: shortconv.conv [D][3] */
+    const d1_half* qkv;       /* attn: [q; k; v] rows [D + 2*512, D] (src/model.rs:160) */
+    const d1_half* out;       /* attn: attn_output [D, D] */
+    const float* qn;          /* attn: attn_q_norm [64] */
+    const float* kn;          /* attn: attn_k_norm [64] */
+    const float* op_norm;     /* attn_norm [D] */
+    const float* ffn_norm;    /* ffn_norm [D] */
+    const d1_half* gate_up;   /* [gate; up] rows [2F, D] (src/model.rs:184) */
+    const d1_half* down;      /* ffn_down [D, F] */
+    int ffn;                  /* F */
+} D1TrunkLayer;
+
+/* One decision-head layer (src/model.rs:33-47). */
+typedef struct D1HeadLayer {
+    const float* n1_w;
+    const float* n1_b;
+    const d1_half* qkv;       /* [3D, D] */
+    const float* qkv_b;       /* [3D] */
+    const d1_half* out;       /* [D, D] */
+    const float* out_b;
+    const float* n2_w;
+    const float* n2_b;
+    const d1_half* up;        /* [F, D] */
+    const float* up_b;
+    const d1_half* down;      /* [D, F] */
+    const float* down_b;
+    int ffn;
+} D1HeadLayer;
+
+/* The text model (src/model.rs:49-68). D = 1024, 16 heads, 8 kv heads, head dim 64 (src/model.rs:12-17). */
+typedef struct D1TextWeights {
+    int n_layers;
+    const D1TrunkLayer* layers;
+    int n_head;
+    const D1HeadLayer* head;
+    int vocab;
+    const d1_half* embed;     /* token_embd [vocab, D] */
+    const float* final_norm;  /* token_embd_norm [D] */
+    const float* type_emb;    /* token_types [n_types, D] */
+    const float* cls_norm_w;
+    const float* cls_norm_b;
+    const d1_half* cls_w;     /* [D, D] */
+    const float* cls_b;
+    const d1_half* out_w;     /* [D] */
+    float out_b;
+    float eps;                /* RMSNorm eps (1e-5) */
+    float rope_theta;         /* 1e6 */
+} D1TextWeights;
+
+typedef struct D1Model D1Model;
+typedef struct D1Workspace D1Workspace;
+
+/* A media prefix that went through the trunk (src/model.rs:70-104): per attention layer K/V and the last
+ * position's conv state, allocated in stream order. */
+typedef struct D1PrefixCache {
+    int len;
+    d1_half* k;   /* [n_attn][len][512] */
+    d1_half* v;   /* [n_attn][len][512] */
+    d1_half* bx;  /* [n_conv][D] */
+} D1PrefixCache;
+
+/* One question sequence of a text batch (src/model.rs:236-242). markers are row offsets within the sequence. */
+typedef struct D1TextSeq {
+    const int* ids;
+    int n_ids;
+    const int* markers;
+    int n_markers;
+    int qtype;
+    const D1PrefixCache* prefix; /* NULL for text without media */
+} D1TextSeq;
+
+/* One prefix to run through the trunk: fp32 embeddings [len, D] on the device -> cache (src/model.rs:244-248). */
+typedef struct D1PrefixSeq {
+    const float* emb;
+    const D1PrefixCache* cache;
+} D1PrefixSeq;
+
+/* Creates a model over caller-owned device weights on the current device. kernel_lib: NULL for this library's
+ * kernels, else the path of a library exporting the d1kernels.h ABI. fused: 1 uses the fused GEMM epilogues
+ * (d1_gemm_swiglu, d1_gemm_bias_act) when the library exports them. Returns NULL on failure. */
+D1Model* d1h_model_create(const D1TextWeights* w, const char* kernel_lib, int fused);
+void d1h_model_destroy(D1Model* m);
+/* Last error text of the calling thread (static storage). */
+const char* d1h_last_error(void);
+
+/* Scratch for batches of up to cap_tokens tokens (src/model.rs:277-299); 2 in-flight slots. */
+D1Workspace* d1h_workspace_create(D1Model* m, int cap_tokens);
+void d1h_workspace_destroy(D1Workspace* ws);
+
+/* Enqueue a text batch (src/model.rs:470-599). The slot's logits (one per option marker, in sequence then
+ * marker order) are ready after d1h_finish. Returns 0 or an error status. */
+int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs, int n_seqs, cudaStream_t stream);
+/* Blocks until the slot's batch is done; copies its logits to out (up to cap floats). Returns the number of
+ * logits, or a negative status. */
+int d1h_finish(D1Model* m, D1Workspace* ws, int slot, float* out, int cap);
+
+/* Prefix caches (src/model.rs:85-103) and prefix passes (src/model.rs:402-459). */
+int d1h_prefix_alloc(D1Model* m, int len, D1PrefixCache* out, cudaStream_t stream);
+void d1h_prefix_free(D1PrefixCache* c, cudaStream_t stream);
+int d1h_launch_prefix(D1Model* m, D1Workspace* ws, int slot, const D1PrefixSeq* items, int n_items, cudaStream_t stream);
+
+/* Tunes the GEMM plans of every trunk/head shape for every M bucket up to max_tokens (src/engine.rs:528-616).
+ * Returns the number of shapes tuned or a negative status. */
+int d1h_tune(D1Model* m, D1Workspace* ws, int max_tokens, cudaStream_t stream);
+
+/* Number of kernel launches the runner made since the model was created (a counter for benchmarks). */
+long long d1h_launch_count(const D1Model* m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* D1H_H */

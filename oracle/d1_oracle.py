@@ -1,0 +1,391 @@
+"""CPU oracle for the d1rs forward pass — TEST INFRASTRUCTURE, not product code.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs may import this module; the
+product path (libd1kernels + its runner) never calls it.
+
+A numpy restatement of the reference's arithmetic for the hot path, function by function, each citing the
+reference file:line it follows (paths within cnmoro/fast-d1-omni). Two precisions:
+  * prec="f16": activations are rounded to fp16 exactly where the reference's F16 engine stores fp16
+    (GEMM outputs, normed inputs, attention outputs ...), math in fp32 — the model of the F16 engine;
+  * prec="f32": everything in fp32 with the same (fp16-valued) weights — the stand-in for the fp32 PyTorch
+    reference of tools/ref_model.py, whose remote modeling code and weights are not available here.
+Sequences are packed without padding: `spans` is a list of (start, len) row ranges.
+
+Pinning: the reference ships no numeric golden vectors (its only KATs are host-side: SHA-256, JSON, sniffing).
+tests/golden/*.npz are outputs of the reference's own CUDA kernels (cuda/kernels.cu, built unchanged into
+oracle/_ref by oracle/Makefile) run on a B200 by tests/golden/make_golden.py; tests/test_oracle_golden.py checks
+this module against them.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+D = 1024          # src/model.rs:12
+HEADS = 16        # :13
+KV_HEADS = 8      # :14
+HD = 64           # :15
+KV_DIM = KV_HEADS * HD
+MAX_POS = 16384 + 64  # :17
+
+
+def r16(x, prec="f16"):
+    """Round to fp16 and back when modelling the F16 engine."""
+    if prec != "f16":
+        return np.asarray(x, dtype=np.float32)
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------------ activations
+# cuda/kernels.cu:40-54: 0 none, 1 ReLU, 2 GELU (erf), 3 GELU (tanh), 4 SiLU.
+
+def _erf(x):
+    try:
+        from scipy.special import erf
+        return erf(x).astype(np.float32)
+    except Exception:  # pragma: no cover
+        return np.vectorize(math.erf)(x).astype(np.float32)
+
+
+def gelu_erf(x):
+    x = np.asarray(x, np.float32)
+    return (0.5 * x * (1.0 + _erf(x * np.float32(0.70710678118654752)))).astype(np.float32)
+
+
+def gelu_tanh(x):
+    x = np.asarray(x, np.float32)
+    k0, k1 = np.float32(0.7978845608028654), np.float32(0.044715)
+    return (0.5 * x * (1.0 + np.tanh(k0 * (x + k1 * x * x * x)))).astype(np.float32)
+
+
+def silu(x):
+    x = np.asarray(x, np.float32)
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def apply_act(x, act):
+    if act == 1:
+        return np.maximum(x, 0).astype(np.float32)
+    if act == 2:
+        return gelu_erf(x)
+    if act == 3:
+        return gelu_tanh(x)
+    if act == 4:
+        return silu(x)
+    return np.asarray(x, np.float32)
+
+
+# ------------------------------------------------------------------------------------------------ kernels
+
+def rmsnorm(x, w, eps):
+    """cuda/kernels.cu:59-79: y = x * rsqrt(sum(x^2)/D + eps) * w (fp32 math)."""
+    x = np.asarray(x, np.float32)
+    r = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True, dtype=np.float32) / x.shape[-1] + np.float32(eps))
+    return (x * r.astype(np.float32) * w).astype(np.float32)
+
+
+def layernorm(x, w, b, eps, pend=None, pend_scale=1.0):
+    """cuda/kernels.cu:82-117: x += s*pend (returned as the new x), then LayerNorm(x)*w + b."""
+    x = np.asarray(x, np.float32)
+    if pend is not None:
+        x = (x + np.float32(pend_scale) * pend).astype(np.float32)
+    mean = x.mean(-1, keepdims=True, dtype=np.float32)
+    d = x - mean
+    r = 1.0 / np.sqrt((d * d).sum(-1, keepdims=True, dtype=np.float32) / x.shape[-1] + np.float32(eps))
+    return x, (d * r.astype(np.float32) * w + b).astype(np.float32)
+
+
+def head_init(h, w, type_emb, row_qtype, eps):
+    """cuda/kernels.cu:120-142: RMSNorm(h)*w + type_emb[qtype of the row's sequence]."""
+    return (rmsnorm(h, w, eps) + type_emb[row_qtype]).astype(np.float32)
+
+
+def embed(table, ids):
+    """cuda/kernels.cu:146-156."""
+    return np.asarray(table, np.float32)[np.asarray(ids)]
+
+
+def swiglu(gu, F):
+    """cuda/kernels.cu:159-168: silu(gu[:, :F]) * gu[:, F:]."""
+    gu = np.asarray(gu, np.float32)
+    return silu(gu[:, :F]) * gu[:, F:2 * F]
+
+
+def bias_act(x, bias, act):
+    """cuda/kernels.cu:171-194."""
+    x = np.asarray(x, np.float32)
+    if bias is not None:
+        x = x + bias
+    return apply_act(x, act)
+
+
+def gemm(x, w, y=None, alpha=1.0, beta=0.0):
+    """cuda/gemm.cu:8 semantics: Y = alpha * X . W^T + beta * Y (fp32 accumulation)."""
+    out = np.float32(alpha) * (np.asarray(x, np.float32) @ np.asarray(w, np.float32).T)
+    if y is not None and beta != 0.0:
+        out = out + np.float32(beta) * y
+    return out.astype(np.float32)
+
+
+def shortconv(bcu, convw, spans, conv_idx=0, ext_bx=None, prec="f16"):
+    """cuda/kernels.cu:224-259: bcu [T,3D] = [b|c|u]; bx = b*u; out[t] = c[t]*(w0*bx[t-1] + w1*bx[t] + w2*bx[t+1]),
+    zero outside each sequence (centred 3-tap). ext_bx[i] (optional, [D] fp16 values) is sequence i's left state.
+    Returns (out, saved) where saved[i] is half(bx of the sequence's last row) (the save_bx store)."""
+    bcu = np.asarray(bcu, np.float32)
+    Dm = bcu.shape[1] // 3
+    b, c, u = bcu[:, :Dm], bcu[:, Dm:2 * Dm], bcu[:, 2 * Dm:]
+    bx = (b * u).astype(np.float32)
+    w = np.asarray(convw, np.float32).reshape(Dm, 3)
+    out = np.zeros_like(c)
+    saved = []
+    for i, (s, n) in enumerate(spans):
+        seg = bx[s:s + n]
+        left = np.zeros_like(seg)
+        left[1:] = seg[:-1]
+        if ext_bx is not None and ext_bx[i] is not None:
+            left[0] = ext_bx[i]
+        right = np.zeros_like(seg)
+        right[:-1] = seg[1:]
+        y = w[:, 0] * left + w[:, 1] * seg + w[:, 2] * right
+        out[s:s + n] = c[s:s + n] * y
+        saved.append(r16(seg[-1], prec))
+    return out.astype(np.float32), saved
+
+
+def rope_table(theta=1e6):
+    """src/model.rs:121-136: [MAX_POS][32] (cos, sin), fp32 inverse frequency and fp32 angle, cos/sin in f64."""
+    e = (2.0 * np.arange(32, dtype=np.float32) / np.float32(HD)).astype(np.float32)
+    inv = (np.float32(1.0) / np.power(np.float32(theta), e, dtype=np.float32)).astype(np.float32)
+    pos = np.arange(MAX_POS, dtype=np.float32)[:, None]
+    ang = (pos * inv[None, :]).astype(np.float32).astype(np.float64)
+    t = np.empty((MAX_POS, 32, 2), np.float32)
+    t[..., 0] = np.cos(ang)
+    t[..., 1] = np.sin(ang)
+    return t
+
+
+def qk_norm_rope(qkv, H, KVH, qn, kn, rope, pos, eps, prec="f16"):
+    """cuda/kernels.cu:263-303: per-head RMSNorm (dim 64, per-dim weights) of the q and k heads, then RoPE
+    rotate-half on pairs (l, l+32) at position pos[row]. Returns the updated qkv (v untouched)."""
+    qkv = np.array(qkv, np.float32, copy=True)
+    T = qkv.shape[0]
+    cs = rope[np.asarray(pos)]  # [T, 32, 2]
+    cos, sin = cs[:, None, :, 0], cs[:, None, :, 1]
+    for lo, nh, wt in ((0, H, qn), (H * 64, KVH, kn)):
+        x = qkv[:, lo:lo + nh * 64].reshape(T, nh, 64)
+        r = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True, dtype=np.float32) / 64.0 + np.float32(eps))
+        x = x * r.astype(np.float32) * wt
+        a, b = x[..., :32], x[..., 32:]
+        oa = a * cos - b * sin
+        ob = b * cos + a * sin
+        qkv[:, lo:lo + nh * 64] = r16(np.concatenate([oa, ob], -1), prec).reshape(T, nh * 64)
+    return qkv
+
+
+def attention(Q, K, V, seqs, heads, group, scale, bq=None, bk=None, bv=None, ext=None, prec="f16"):
+    """cuda/kernels.cu:351-500: bidirectional softmax(scale * q . k^T) . v within each sequence, kv head
+    g = h // group, keys = [ext prefix | local]; optional fp32 biases added on load (rounded to fp16 as the
+    kernel's load8 does). seqs: list of (q_start, q_len, kv_start, kv_len); ext: per seq (k, v) [ext_len, 512]
+    or None. Q/K/V are [rows, heads*64] (K/V [rows, kv_heads*64]). Returns O [Q rows, heads*64]."""
+    Q = np.asarray(Q, np.float32)
+    K = np.asarray(K, np.float32)
+    V = np.asarray(V, np.float32)
+    if bq is not None:
+        Q = r16(Q + bq, prec)
+    if bk is not None:
+        K = r16(K + bk, prec)
+    if bv is not None:
+        V = r16(V + bv, prec)
+    O = np.zeros((Q.shape[0], heads * 64), np.float32)
+    for i, (qs, ql, ks, kl) in enumerate(seqs):
+        if ql == 0:
+            continue
+        k_all, v_all = K[ks:ks + kl], V[ks:ks + kl]
+        if ext is not None and ext[i] is not None:
+            k_all = np.concatenate([np.asarray(ext[i][0], np.float32), k_all])
+            v_all = np.concatenate([np.asarray(ext[i][1], np.float32), v_all])
+        q = Q[qs:qs + ql].reshape(ql, heads, 64).transpose(1, 0, 2)  # [h, q, 64]
+        kvh = k_all.shape[1] // 64
+        k = k_all.reshape(-1, kvh, 64).transpose(1, 0, 2)
+        v = v_all.reshape(-1, kvh, 64).transpose(1, 0, 2)
+        g = np.arange(heads) // group
+        s = np.einsum("hqd,hkd->hqk", q, k[g], dtype=np.float32) * np.float32(scale)
+        s = s - s.max(-1, keepdims=True)
+        pexp = np.exp(s).astype(np.float32)
+        l = pexp.sum(-1, keepdims=True, dtype=np.float32)
+        pr = r16(pexp, prec)  # the kernel feeds fp16 P to the PV product and divides by the fp32 row sum
+        o = np.einsum("hqk,hkd->hqd", pr, v[g], dtype=np.float32) / l
+        O[qs:qs + ql] = o.transpose(1, 0, 2).reshape(ql, heads * 64)
+    return O
+
+
+def scorer_out(x, b1, w2, b2):
+    """cuda/kernels.cu:504-513: sum_i gelu_erf(x + b1) * w2 + b2."""
+    return (gelu_erf(np.asarray(x, np.float32) + b1) @ np.asarray(w2, np.float32) + np.float32(b2)).astype(np.float32)
+
+
+def unshuffle(x, ph, pw, C):
+    """cuda/kernels.cu:517-525: [ph*pw, C] -> [(ph/2)*(pw/2), 4C], quadrant order (0,0),(0,1),(1,0),(1,1)."""
+    x = np.asarray(x).reshape(ph // 2, 2, pw // 2, 2, C)
+    return x.transpose(0, 2, 1, 3, 4).reshape((ph // 2) * (pw // 2), 4 * C)
+
+
+# ------------------------------------------------------------------------------------------------ text model
+
+def work_spans(seqs):
+    return [(s, n) for s, n in seqs]
+
+
+def trunk(w, h, spans, pos, prec="f16", fused_swiglu=True, prefix=None, prefix_pass=False):
+    """src/model.rs:355-399. h: fp32 [T, D] residual (modified copy returned). spans: [(start, len)].
+    prefix: per sequence None or dict(k=[n_attn][len][512], v=..., bx=[n_conv][D]) of a cached media prefix.
+    prefix_pass: stop after the last layer's mixer and return the saved per-sequence K/V/bx (src/model.rs:370-372).
+    fused_swiglu: model the fused GEMM epilogue (g and u rounded to fp16, the product rounded once), which is
+    also exactly what the reference's GEMM + k_swiglu compute."""
+    h = np.array(h, np.float32, copy=True)
+    T = h.shape[0]
+    eps = w["eps"]
+    rope = w["rope"]
+    n_attn = sum(1 for l in w["layers"] if l["is_attn"])
+    n_conv = len(w["layers"]) - n_attn
+    saves = {"k": [[None] * n_attn for _ in spans], "v": [[None] * n_attn for _ in spans],
+             "bx": [[None] * n_conv for _ in spans]}
+    ai = ci = 0
+    nl = len(w["layers"])
+    for li, l in enumerate(w["layers"]):
+        last = li + 1 == nl
+        xn = r16(rmsnorm(h, l["op_norm"], eps), prec)
+        if not l["is_attn"]:
+            big = r16(gemm(xn, l["in_proj"]), prec)
+            ext = [p["bx"][ci] if p is not None else None for p in prefix] if prefix is not None else None
+            act, saved = shortconv(big, l["convw"], spans, ci, ext, prec)
+            act = r16(act, prec)
+            if prefix_pass:
+                for i in range(len(spans)):
+                    saves["bx"][i][ci] = saved[i]
+            if prefix_pass and last:
+                return h, saves
+            h = gemm(act, l["out_proj"], h, 1.0, 1.0)
+            ci += 1
+        else:
+            big = r16(gemm(xn, l["qkv"]), prec)
+            big = qk_norm_rope(big, HEADS, KV_HEADS, l["qn"], l["kn"], rope, pos, eps, prec)
+            q, k, v = big[:, :D], big[:, D:D + KV_DIM], big[:, D + KV_DIM:]
+            if prefix_pass:
+                for i, (s, n) in enumerate(spans):
+                    saves["k"][i][ai] = k[s:s + n].copy()
+                    saves["v"][i][ai] = v[s:s + n].copy()
+            ext = None
+            if prefix is not None:
+                ext = [(p["k"][ai], p["v"][ai]) if p is not None else None for p in prefix]
+            seqs = [(s, n, s, n) for s, n in spans]
+            act = r16(attention(q, k, v, seqs, HEADS, HEADS // KV_HEADS, 0.125, ext=ext, prec=prec), prec)
+            if prefix_pass and last:
+                return h, saves
+            h = gemm(act, l["out"], h, 1.0, 1.0)
+            ai += 1
+        xn = r16(rmsnorm(h, l["ffn_norm"], eps), prec)
+        F = l["ffn"]
+        gu = r16(gemm(xn, l["gate_up"]), prec)
+        act = r16(swiglu(gu, F), prec)
+        h = gemm(act, l["down"], h, 1.0, 1.0)
+    return h, saves
+
+
+def launch_text(w, batch, prec="f16"):
+    """src/model.rs:470-599 for a list of sequences dict(ids, markers, qtype[, prefix]) -> logits per marker
+    (sequence order, then marker order)."""
+    spans, ids, pos, row_qtype, mrows, mspans = [], [], [], [], [], []
+    prefix = []
+    start = 0
+    for s in batch:
+        n = len(s["ids"])
+        spans.append((start, n))
+        ids.extend(s["ids"])
+        off = s["prefix"]["len"] if s.get("prefix") is not None else 0
+        pos.extend(range(off, off + n))
+        row_qtype.extend([s["qtype"]] * n)
+        mspans.append((len(mrows), len(s["markers"])))
+        mrows.extend(start + m for m in s["markers"])
+        prefix.append(s.get("prefix"))
+        start += n
+    T = start
+    h = embed(w["embed"], ids)
+    h, _ = trunk(w, h, spans, np.asarray(pos), prec, prefix=prefix if any(p is not None for p in prefix) else None)
+    h = head_init(h, w["final_norm"], w["type_emb"], np.asarray(row_qtype), w["eps"])
+    pend = None
+    nh = len(w["head"])
+    mrows = np.asarray(mrows, dtype=np.int64)
+    logits = np.zeros(len(mrows), np.float32)
+    for li, l in enumerate(w["head"]):
+        h, xn = layernorm(h, l["n1_w"], l["n1_b"], 1e-5, pend)
+        xn = r16(xn, prec)
+        big = r16(gemm(xn, l["qkv"]), prec)
+        qb = l["qkv_b"]
+        if li + 1 < nh:
+            seqs = [(s, n, s, n) for s, n in spans]
+            act = r16(attention(big[:, :D], big[:, D:2 * D], big[:, 2 * D:], seqs, HEADS, 1, 0.125,
+                                qb[:D], qb[D:2 * D], qb[2 * D:], prec=prec), prec)
+            h = gemm(act, l["out"], h, 1.0, 1.0)
+            h, xn = layernorm(h, l["n2_w"], l["n2_b"], 1e-5, l["out_b"])
+            xn = r16(xn, prec)
+            up = r16(bias_act(r16(gemm(xn, l["up"]), prec), l["up_b"], 1), prec)
+            h = gemm(up, l["down"], h, 1.0, 1.0)
+            pend = l["down_b"]
+        else:
+            if len(mrows) == 0:
+                break
+            mq = big[mrows]
+            mh = h[mrows]
+            seqs = [(ms, mn, s, n) for (ms, mn), (s, n) in zip(mspans, spans)]
+            mo = r16(attention(mq[:, :D], big[:, D:2 * D], big[:, 2 * D:], seqs, HEADS, 1, 0.125,
+                               qb[:D], qb[D:2 * D], qb[2 * D:], prec=prec), prec)
+            mh = gemm(mo, l["out"], mh, 1.0, 1.0)
+            mh, mx = layernorm(mh, l["n2_w"], l["n2_b"], 1e-5, l["out_b"])
+            mx = r16(mx, prec)
+            mbig = r16(bias_act(r16(gemm(mx, l["up"]), prec), l["up_b"], 1), prec)
+            mh = gemm(mbig, l["down"], mh, 1.0, 1.0)
+            mh, mx = layernorm(mh, w["cls_norm_w"], w["cls_norm_b"], 1e-5, l["down_b"])
+            mx = r16(mx, prec)
+            mo = r16(gemm(mx, w["cls_w"]), prec)
+            logits = scorer_out(mo, w["cls_b"], w["out_w"], w["out_b"])
+    return logits
+
+
+def launch_prefix(w, embs, prec="f16"):
+    """src/model.rs:402-459: run media embeddings [len, D] (fp32) through the trunk, saving per attention layer
+    K/V and the last conv state. Returns one cache dict(len, k, v, bx) per item."""
+    spans, start, pos = [], 0, []
+    for e in embs:
+        spans.append((start, e.shape[0]))
+        pos.extend(range(e.shape[0]))
+        start += e.shape[0]
+    h = np.concatenate([np.asarray(e, np.float32) for e in embs])
+    _, saves = trunk(w, h, spans, np.asarray(pos), prec, prefix_pass=True)
+    return [{"len": n, "k": saves["k"][i], "v": saves["v"][i], "bx": saves["bx"][i]}
+            for i, (s, n) in enumerate(spans)]
+
+
+# ------------------------------------------------------------------------------------------------ metrics
+
+def centred_logit_err(ref_logits, logits, group_sizes):
+    """tools/logit_err.py:6-14: per question (a group of option logits), max over options of the difference of
+    centred log-probs; log-softmax is the logits minus a constant, so centring the logits is equivalent."""
+    errs, o = [], 0
+    for n in group_sizes:
+        a = np.asarray(ref_logits[o:o + n], np.float64)
+        b = np.asarray(logits[o:o + n], np.float64)
+        errs.append(float(np.max(np.abs((a - a.mean()) - (b - b.mean())))) if n else 0.0)
+        o += n
+    return np.asarray(errs)
+
+
+def top_flips(ref_logits, logits, group_sizes):
+    """tools/compare.py:10-15: questions whose top answer differs."""
+    flips, o = 0, 0
+    for n in group_sizes:
+        if n and int(np.argmax(ref_logits[o:o + n])) != int(np.argmax(logits[o:o + n])):
+            flips += 1
+        o += n
+    return flips

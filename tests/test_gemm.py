@@ -1,0 +1,200 @@
+"""tcgen05 GEMM parity through the C ABI (d1_lt_gemm, d1_gemm_swiglu, d1_gemm_bias_act) against an fp32
+reference GEMM of the same fp16 inputs ("each GEMM is checked against an fp32 host GEMM").
+
+Tolerances: fp16 outputs within 1 fp16 ulp of the fp32 result plus accumulation-order noise
+(|err| <= 2^-10 |ref| + 2e-3 * rms(ref)); fp32 outputs within 1e-4 * max|ref| (fp32 accumulation in a
+different order than the reference GEMM).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+CONFIG1_NK = [(3072, 1024), (2048, 1024), (1024, 1024), (9216, 1024), (1024, 4608)]
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def ref_gemm(x, w):
+    return x.double() @ w.double().T
+
+
+def check_f16(y, ref):
+    ref = ref.float()
+    err = (y.float() - ref).abs()
+    tol = ref.abs() * 2.0 ** -10 + 2e-3 * ref.pow(2).mean().sqrt()
+    bad = (err > tol).sum().item()
+    assert bad == 0, f"{bad} elements off, max err {err.max().item():.3e}"
+
+
+@pytest.fixture(scope="module")
+def ctx(gpu_lib):
+    c = gpu_lib.d1_lt_init(32 << 20)
+    assert c, "d1_lt_init failed"
+    yield c
+    assert gpu_lib.d1_lt_error(c) == 0
+    gpu_lib.d1_lt_destroy(c)
+
+
+def run_gemm(lib, ctx, x, w, y, alpha=1.0, beta=0.0):
+    M, K = x.shape
+    N = w.shape[0]
+    y_f32 = int(y.dtype == torch.float32)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    r = lib.d1_lt_gemm(ctx, M, N, K, _p(x), x.stride(0), _p(w), w.stride(0), 0, _p(y), y.stride(0), y_f32, 0,
+                       alpha, beta, st)
+    assert r == 0
+    torch.cuda.synchronize()
+    assert lib.d1_lt_error(ctx) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,K", CONFIG1_NK)
+@pytest.mark.parametrize("M", [256, 1024, 8192])
+def test_config1_f16_out(gpu_lib, ctx, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    run_gemm(gpu_lib, ctx, x, w, y)
+    check_f16(y, ref_gemm(x, w))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,K", [(1024, 1024), (1024, 4608)])
+@pytest.mark.parametrize("M", [1, 3, 127, 129, 4096])
+def test_residual_f32(gpu_lib, ctx, M, N, K):
+    """The trunk's residual projections: Y32 = X.W^T + Y32 (beta = 1, src/model.rs:373,390,396)."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y0 = torch.randn(M, N, device="cuda", generator=g)
+    y = y0.clone()
+    run_gemm(gpu_lib, ctx, x, w, y, 1.0, 1.0)
+    ref = ref_gemm(x, w) + y0.double()
+    err = (y.double() - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item(), err
+
+
+@pytest.mark.gpu
+def test_alpha_beta_general(gpu_lib, ctx):
+    """alpha/beta as the audio half-step FFN uses them (alpha 0.5, beta 1, src/audio.rs:553) and fp16 beta."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    M, N, K = 300, 512, 2048
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y0 = torch.randn(M, N, device="cuda", generator=g)
+    y = y0.clone()
+    run_gemm(gpu_lib, ctx, x, w, y, 0.5, 1.0)
+    ref = 0.5 * ref_gemm(x, w) + y0.double()
+    assert (y.double() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
+    yh0 = torch.randn(M, N, device="cuda", generator=g).half()
+    yh = yh0.clone()
+    run_gemm(gpu_lib, ctx, x, w, yh, 1.0, 0.5)
+    check_f16(yh, ref_gemm(x, w) + 0.5 * yh0.double())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(77, 200, 136), (130, 1000, 1000), (5, 40, 72)])
+def test_ragged_shapes(gpu_lib, ctx, M, N, K):
+    """N and K that are not tile multiples (TMA zero fill on loads, masked epilogue stores)."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    y = torch.full((M, N), 7.0, device="cuda", dtype=torch.float16)
+    run_gemm(gpu_lib, ctx, x, w, y)
+    check_f16(y, ref_gemm(x, w))
+
+
+@pytest.mark.gpu
+def test_strided_views(gpu_lib, ctx):
+    """Column-offset views into a wider buffer, as the runner passes big.add(D) etc. (src/model.rs:383)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    M, N, K = 512, 1024, 1024
+    xb = torch.randn(M, 3 * K, device="cuda", generator=g).half()
+    x = xb[:, K:2 * K]
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    yb = torch.zeros(M, 2 * N, device="cuda", dtype=torch.float16)
+    y = yb[:, N:]
+    run_gemm(gpu_lib, ctx, x, w, y)
+    check_f16(y, ref_gemm(x, w))
+    assert yb[:, :N].abs().max().item() == 0
+
+
+@pytest.mark.gpu
+def test_wkn_layout(gpu_lib, ctx):
+    """W given as [K, N] (w_kn = 1, cuda/gemm.cu:63-71)."""
+    g = torch.Generator(device="cuda").manual_seed(6)
+    M, N, K = 100, 64, 96
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    wkn = (torch.randn(K, N, device="cuda", generator=g) * 0.05).half()
+    y = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert gpu_lib.d1_lt_gemm(ctx, M, N, K, _p(x), K, _p(wkn), N, 1, _p(y), N, 1, 0, 1.0, 0.0, st) == 0
+    torch.cuda.synchronize()
+    ref = x.double() @ wkn.double()
+    assert (y.double() - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 200, 8192])
+def test_swiglu_fused(gpu_lib, ctx, M):
+    """d1_gemm_swiglu == d1_lt_gemm(N = 2F) + d1_swiglu (src/model.rs:394-395)."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    F, K = 4608, 1024
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(2 * F, K, device="cuda", generator=g) * 0.02).half()
+    out = torch.empty(M, F, device="cuda", dtype=torch.float16)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert gpu_lib.d1_gemm_swiglu(ctx, M, F, K, _p(x), K, _p(w), K, _p(out), F, st) == 0
+    # unfused path of the same library
+    gu = torch.empty(M, 2 * F, device="cuda", dtype=torch.float16)
+    run_gemm(gpu_lib, ctx, x, w, gu)
+    out2 = torch.empty(M, F, device="cuda", dtype=torch.float16)
+    assert gpu_lib.d1_swiglu(_p(gu), _p(out2), M, F, st) == 0
+    torch.cuda.synchronize()
+    assert gpu_lib.d1_lt_error(ctx) == 0
+    ref = ref_gemm(x, w)
+    g16, u16 = ref[:, :F].half().double(), ref[:, F:].half().double()
+    exact = g16 / (1 + torch.exp(-g16)) * u16
+    check_f16(out, exact)
+    # fused vs unfused: identical up to the rounding of g and u (1 fp16 ulp on either side)
+    d = (out.float() - out2.float()).abs()
+    assert (d <= out2.float().abs() * 2.0 ** -9 + 1e-3).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("act", [0, 1, 2, 3, 4])
+def test_bias_act_fused(gpu_lib, ctx, act):
+    """d1_gemm_bias_act == d1_lt_gemm(fp16) + d1_bias_act_h (src/model.rs:568-569)."""
+    g = torch.Generator(device="cuda").manual_seed(8 + act)
+    M, N, K = 333, 2048, 1024
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert gpu_lib.d1_gemm_bias_act(ctx, M, N, K, _p(x), K, _p(w), K, _p(b), act, _p(y), N, st) == 0
+    y2 = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    run_gemm(gpu_lib, ctx, x, w, y2)
+    assert gpu_lib.d1_bias_act_h(_p(y2), _p(b), M, N, act, st) == 0
+    torch.cuda.synchronize()
+    d = (y.float() - y2.float()).abs()
+    assert (d <= y2.float().abs() * 2.0 ** -9 + 2e-3).all(), d.max().item()
+
+
+@pytest.mark.gpu
+def test_tune_save_load(gpu_lib, ctx, tmp_path):
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    us = gpu_lib.d1_lt_tune(ctx, 1000, 1024, 1024, 1024, 1024, 0, 1024, 1, 0, 1, st)
+    assert us > 0
+    assert gpu_lib.d1_lt_bucket(1000) == 1024
+    path = str(tmp_path / "plans.txt").encode()
+    assert gpu_lib.d1_lt_save(ctx, path) == 0
+    c2 = gpu_lib.d1_lt_init(0)
+    assert gpu_lib.d1_lt_load(c2, path) >= 1
+    gpu_lib.d1_lt_destroy(c2)
