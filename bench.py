@@ -1,0 +1,316 @@
+"""Benchmark of the d1rs text prefill forward on B200 (one JSON line on rank 0).
+
+Metric: prefill tokens/s per B200 at 8192-token batches, plus the GEMM share of the tensor-core
+peak. One step = one Runner::launch_text (src/model.rs:470-599) of an 8192-token batch: the config-0 architecture
+(hidden 1024, 16 layers, attention at {2,5,8,10,12,14}, SwiGLU 4608, 2-layer decision head), random-init weights
+(seed 0; no checkpoint is available offline), 32 packed sequences x 256 uniform token ids, 3 option markers each.
+
+  value   tokens/s over all ranks, device-timed (CUDA events on the launch stream) over K back-to-back steps; the
+          weights and activations (>700 MB) exceed the 126 MB L2, so no flush is needed between steps.
+  e2e     the same steps through the public API with host buffers: host token ids -> d1h_launch_text (metadata
+          built on the host, one pinned H2D copy) -> d1h_finish (logits D2H + sync), wall clock.
+  roofline the dominant kernel (the fused SwiGLU projection GEMM, 302.0 MFLOP/token, 52.5% of the trunk FLOPs)
+          timed alone with CUDA events: algorithmic FLOPs per launch / average launch time, against the measured
+          cuBLAS bf16 peak (MEASURED_PEAKS.json, burst figure: the kernel is timed alone).
+  cpu_baseline the oracle port (numpy fp32, oracle/d1_oracle.py) on a bounded sample of the same workload.
+
+--impl reference: the reference's CPU implementation of the path. The reference has none (its forward is CUDA
+only; its fp32 PyTorch path needs remote code and weights that are not available offline), so this arm times the
+oracle port (fp32 numpy restatement of the reference's arithmetic) on all host threads, on bounded samples.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own replica on its own batches (the model is
+replicated and requests are sharded; no collective on the data path); value = all ranks' tokens / max time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SEQ_LEN = 256
+N_SEQS = 32
+TOKENS = SEQ_LEN * N_SEQS
+GEMM_FLOP_PER_TOKEN = 574_619_648          # trunk projection GEMMs (2 x 287,309,824 linear params)
+SWIGLU_FLOP_PER_TOKEN = 2 * 9216 * 1024    # w1|w3, fused SwiGLU epilogue
+SWIGLU_TRAFFIC_PER_LAUNCH = None           # ncu dram bytes, profiles/gemm_swiglu_m8192.md (scaled), filled below
+
+
+def load_package():
+    import importlib.util
+    name = "fast_d1_omni_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    d = ROOT / "fast-d1-omni_b200"
+    spec = importlib.util.spec_from_file_location(name, d / "__init__.py", submodule_search_locations=[str(d)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(n_seqs: int, seed: int = 3):
+    """Time the oracle port (fp32 numpy) on a bounded sample: n_seqs x 256-token sequences of the workload."""
+    from oracle import d1_oracle as O
+    pkg = load_package()
+    from fast_d1_omni_b200.weights import text_batch, text_weights
+    w = text_weights(0)
+    b = text_batch(seed, n_seqs, SEQ_LEN)
+    O.launch_text(w, b[:1], "f32")  # warm the BLAS pool
+    t0 = time.perf_counter()
+    O.launch_text(w, b, "f32")
+    dt = time.perf_counter() - t0
+    return n_seqs * SEQ_LEN / dt, dt
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max(i.get("num_threads", 1) for i in threadpool_info()) or os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the oracle port on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import d1_oracle as O
+    load_package()
+    from fast_d1_omni_b200.weights import text_batch, text_weights
+    w = text_weights(0)
+    n_sample = 2  # 512 tokens per step: a bounded sample of the 8192-token batch
+    for i in range(args.warmup):
+        O.launch_text(w, text_batch(100 + i, n_sample, SEQ_LEN), "f32")
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        O.launch_text(w, text_batch(200 + i, n_sample, SEQ_LEN), "f32")
+    dt = time.perf_counter() - t0
+    v = n_sample * SEQ_LEN * args.steps / dt
+    cores = cpu_threads()
+    line = {"impl": "reference", "metric": "prefill tokens/s per B200 at 8192-token batches", "value": v,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and token ids)",
+            "config": {"workload": f"text trunk+head forward, {TOKENS}-token batches of {N_SEQS}x{SEQ_LEN}",
+                       "sample_per_step": f"{n_sample}x{SEQ_LEN} tokens"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"{n_sample} sequences x {SEQ_LEN} tokens per step, oracle/d1_oracle.py fp32"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="d1", choices=["d1", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    pkg = load_package()
+    from fast_d1_omni_b200.model import TextModel
+    from fast_d1_omni_b200.weights import text_batch, text_weights
+    import ctypes as C
+
+    w = text_weights(0)
+    model = TextModel(w, device=local, cap_tokens=TOKENS)
+    batches = [text_batch(1000 * rank + i, N_SEQS, SEQ_LEN) for i in range(4)]
+    stream = torch.cuda.Stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---------------------------------------------------------------- device-timed steps (value)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            model.launch(batches[i % 4], i % 2, stream)
+        for s in (0, 1):
+            model.finish(s) if s in model._pending else None
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        l0 = model.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            e0.record(stream)
+            for i in range(args.steps):
+                model.launch(batches[i % 4], i % 2, stream)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        for s in (0, 1):
+            model._pending.pop(s, None)
+        launches = model.launches - l0
+        dev_ms = e0.elapsed_time(e1)
+        barrier()
+
+        # ---------------------------------------------------------------- end to end through the API (e2e)
+        torch.cuda.synchronize(dev)
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            model.launch(batches[i % 4], i % 2, stream)
+            if i >= 1:
+                model.finish((i - 1) % 2)
+        model.finish((args.steps - 1) % 2)
+        torch.cuda.synchronize(dev)
+        e2e_s = time.perf_counter() - t0
+        h2d = int(model.L.d1h_h2d_bytes(model.ws, 0))
+        d2h = int(model.L.d1h_d2h_bytes(model.ws, 0))
+        barrier()
+
+    # ---------------------------------------------------------------- roofline: the fused SwiGLU GEMM alone
+    lib = pkg.lib()
+    ctx = lib.d1_lt_init(0)
+    M, F, K = TOKENS, 4608, 1024
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, K, device=dev, generator=g).half()
+    wt = (torch.randn(2 * F, K, device=dev, generator=g) * 0.02).half()
+    out = torch.empty(M, F, device=dev, dtype=torch.float16)
+    st = C.c_void_p(stream.cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    for _ in range(3):
+        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
+    reps = 20
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(reps):
+        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    gemm_ms = g0.elapsed_time(g1) / reps
+    err = lib.d1_lt_error(ctx)
+    lib.d1_lt_destroy(ctx)
+    if err:
+        raise RuntimeError(f"GEMM kernel reported error {err}")
+
+    # ---------------------------------------------------------------- aggregate over ranks
+    t = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms_max, e2e_max = float(t[0]), float(t[1])
+    total_tokens = TOKENS * args.steps * world
+    value = total_tokens / (dev_ms_max / 1e3)
+    e2e_value = total_tokens / e2e_max
+
+    if rank == 0:
+        hbm, tflops, kind = peaks()
+        achieved = SWIGLU_FLOP_PER_TOKEN * M / (gemm_ms / 1e3) / 1e12
+        line = {
+            "metric": "prefill tokens/s per B200 at 8192-token batches", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random weights and token ids)",
+            "config": {"workload": f"text trunk+head forward (config-0 architecture), {TOKENS}-token batches of "
+                                   f"{N_SEQS}x{SEQ_LEN} tokens, 3 markers per sequence",
+                       "global_batch_tokens": TOKENS * world, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (weights + activations > 700 MB)"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gemm_tflops_trunk_equiv": GEMM_FLOP_PER_TOKEN * value / world / 1e12,
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc<256,4,EPI_SWIGLU> (w1|w3 + SwiGLU), M=8192",
+                         "achieved": achieved, "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
+                         "peak_kind": f"{kind} (bf16 cuBLAS burst)", "traffic": SWIGLU_TRAFFIC_PER_LAUNCH,
+                         "gemm_ms": gemm_ms},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            v, dt = cpu_sample(2)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                                    "sample": f"2 sequences x {SEQ_LEN} tokens of the workload, oracle fp32 "
+                                              f"({dt:.1f} s)"}
+        print(json.dumps(line), flush=True)
+
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

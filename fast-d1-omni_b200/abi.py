@@ -108,6 +108,8 @@ RUNNER = {
     "d1h_launch_prefix": (i32, [p, p, i32, C.POINTER(PrefixSeq), i32, p]),
     "d1h_tune": (i32, [p, p, i32, p]),
     "d1h_launch_count": (C.c_longlong, [p]),
+    "d1h_h2d_bytes": (C.c_longlong, [p, i32]),
+    "d1h_d2h_bytes": (C.c_longlong, [p, i32]),
 }
 
 

@@ -187,6 +187,7 @@ struct D1Workspace {
     cudaEvent_t events[SLOTS] = {};
     bool busy[SLOTS] = {};
     int n_logits[SLOTS] = {};
+    long long h2d[SLOTS] = {};
 };
 
 namespace {
@@ -364,6 +365,14 @@ void d1h_model_destroy(D1Model* m) {
 
 long long d1h_launch_count(const D1Model* m) { return m ? m->launches : 0; }
 
+long long d1h_h2d_bytes(const D1Workspace* ws, int slot) {
+    return ws && slot >= 0 && slot < SLOTS ? ws->h2d[slot] : -1;
+}
+
+long long d1h_d2h_bytes(const D1Workspace* ws, int slot) {
+    return ws && slot >= 0 && slot < SLOTS ? 4LL * ws->n_logits[slot] : -1;
+}
+
 D1Workspace* d1h_workspace_create(D1Model* m, int cap_tokens) {
     if (!m || cap_tokens <= 0) return nullptr;
     D1Workspace* ws = new D1Workspace();
@@ -476,6 +485,7 @@ int d1h_launch_prefix(D1Model* m, D1Workspace* ws, int slot, const D1PrefixSeq* 
             return fail("prefix embedding copy failed");
     int e = trunk(m, ws, t, d_tok, d_seqs, attn, d_work, (int)work.size() / 2, true, st);
     if (e) return e;
+    ws->h2d[slot] = (long long)w.off;
     cudaEventRecord(ws->events[slot], st);
     ws->busy[slot] = true;
     ws->n_logits[slot] = 0;
@@ -612,6 +622,7 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
     if (n_mark > 0 &&
         cudaMemcpyAsync(ws->host_logits[slot], ws->logits, (size_t)n_mark * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
         return fail("logits download failed");
+    ws->h2d[slot] = (long long)w.off;
     cudaEventRecord(ws->events[slot], st);
     ws->busy[slot] = true;
     ws->n_logits[slot] = n_mark;

@@ -138,6 +138,10 @@ int d1h_tune(D1Model* m, D1Workspace* ws, int max_tokens, cudaStream_t stream);
 
 /* Number of kernel launches the runner made since the model was created (a counter for benchmarks). */
 long long d1h_launch_count(const D1Model* m);
+/* Bytes the last launch on `slot` copied host->device (its batch metadata, token ids included) and
+ * device->host (its logits). */
+long long d1h_h2d_bytes(const D1Workspace* ws, int slot);
+long long d1h_d2h_bytes(const D1Workspace* ws, int slot);
 
 #ifdef __cplusplus
 }

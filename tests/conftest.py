@@ -42,3 +42,28 @@ def gpu_lib(pkg):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return pkg.lib()
+
+
+REF_LIB = ROOT / "oracle" / "_ref" / "libd1ref.so"
+
+
+@pytest.fixture(scope="session")
+def ref_lib(pkg, gpu_lib):
+    """The reference's own kernels (cuda/kernels.cu + cuda/gemm.cu built unchanged by oracle/Makefile)."""
+    import ctypes
+    if not REF_LIB.exists():
+        pytest.skip("oracle/_ref/libd1ref.so not built (make -C oracle)")
+    lib = ctypes.CDLL(str(REF_LIB))
+    pkg.abi.bind(lib, (pkg.abi.KERNELS,))
+    return lib
+
+
+def half_ulp_close(a, b, rel=2.0 ** -10, abs_tol=1e-6):
+    """|a - b| <= rel*|b| + abs_tol elementwise (one fp16 rounding step)."""
+    import numpy as np
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b) <= rel * np.abs(b) + abs_tol
+
+
+load_package()  # make `fast_d1_omni_b200` importable for module-level imports in the tests

@@ -1,0 +1,141 @@
+"""Flash attention parity through the C ABI (d1_flash_attn) against the oracle and the reference's own kernel.
+
+packed varlen bidirectional attention, 16 query heads, 8 KV heads, head dim 64, Q/K/V N(0,1)
+fp16 (seed 2), lengths log-normal (median 384, sigma 1.0) clipped to [32, 16384]. Plus the decision-head forms
+(MHA with q/k/v bias, marker-row queries) and the media-prefix form (external keys before the local ones).
+Tolerance: |O - O_ref| <= 4e-3 (fp16 output of a convex combination of N(0,1) values; fp16 P as the reference)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import d1_oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def P(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def attn_meta(pkg, seqs, ext=None):
+    """seqs: [(q_start, q_len, kv_start, kv_len)]; ext: per seq None or (k tensor, v tensor) [ext_len, ext_ld]."""
+    arr = (pkg.abi.AttnSeq * len(seqs))()
+    for i, (qs, ql, ks, kl) in enumerate(seqs):
+        arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = qs, ql, ks, kl
+        if ext is not None and ext[i] is not None:
+            arr[i].ext_len = ext[i][0].shape[0]
+            arr[i].ext_k, arr[i].ext_v = ext[i][0].data_ptr(), ext[i][1].data_ptr()
+    meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    work = []
+    for i, (qs, ql, ks, kl) in enumerate(seqs):
+        work += [(i, q) for q in range(0, ql, 64)]
+    w = torch.tensor(np.asarray(work, np.int32).reshape(-1), device="cuda")
+    return meta, w, len(work)
+
+
+def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, ext_ld=0, q_rows=None):
+    meta, work, n_work = attn_meta(pkg, seqs, ext)
+    rows = q_rows if q_rows is not None else Q.shape[0]
+    O_ = torch.zeros(rows, heads * 64, dtype=torch.float16, device="cuda")
+    bq, bk, bv = bias if bias is not None else (None, None, None)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    r = lib.d1_flash_attn(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(bq), P(bk), P(bv), P(O_), heads * 64, P(meta),
+                          P(work), n_work, heads, group, 0.125, st)
+    assert r == 0
+    torch.cuda.synchronize()
+    return O_.float().cpu().numpy()
+
+
+def lognormal(total, seed=2):
+    from fast_d1_omni_b200.weights import lognormal_lengths
+    return lognormal_lengths(seed, total)
+
+
+@pytest.mark.parametrize("total", [2048, 8192])
+def test_config2_gqa(pkg, gpu_lib, ref_lib, total):
+    lens = lognormal(total)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    qkv = torch.randn(total, 2048, device="cuda", generator=g).half()
+    spans, s = [], 0
+    for n in lens:
+        spans.append((s, n, s, n))
+        s += n
+    Q, K, V = qkv, qkv[:, 1024:], qkv[:, 1536:]
+    got = run(gpu_lib, pkg, Q, 2048, K, V, 2048, spans, 16, 2)
+    ref_k = run(ref_lib, pkg, Q, 2048, K, V, 2048, spans, 16, 2)
+    q = qkv.float().cpu().numpy()
+    want = O.attention(q[:, :1024], q[:, 1024:1536], q[:, 1536:], spans, 16, 2, 0.125)
+    assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(ref_k - want).max() <= 4e-3
+    assert np.abs(got - ref_k).max() <= 4e-3
+
+
+@pytest.mark.parametrize("lens", [[1], [63, 64, 65], [1, 2, 3, 130, 7]])
+def test_edge_lengths_mha_bias(pkg, gpu_lib, ref_lib, lens):
+    """Decision-head / SigLIP2 form: MHA (group 1) with fp32 q/k/v biases added on load, ld = 3D."""
+    rng = np.random.default_rng(len(lens))
+    T = sum(lens)
+    qkv = rng.standard_normal((T, 3072)).astype(np.float16)
+    b = (rng.standard_normal(3072) * 0.5).astype(np.float32)
+    spans, s = [], 0
+    for n in lens:
+        spans.append((s, n, s, n))
+        s += n
+    d = torch.from_numpy(qkv).cuda()
+    bd = torch.from_numpy(b).cuda()
+    bias = (bd[:1024], bd[1024:2048], bd[2048:])
+    got = run(gpu_lib, pkg, d, 3072, d[:, 1024:], d[:, 2048:], 3072, spans, 16, 1, bias)
+    ref_k = run(ref_lib, pkg, d, 3072, d[:, 1024:], d[:, 2048:], 3072, spans, 16, 1, bias)
+    q = qkv.astype(np.float32)
+    want = O.attention(q[:, :1024], q[:, 1024:2048], q[:, 2048:], spans, 16, 1, 0.125, b[:1024], b[1024:2048], b[2048:])
+    assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(got - ref_k).max() <= 4e-3
+
+
+def test_marker_queries(pkg, gpu_lib, ref_lib):
+    """Last head layer: queries are gathered marker rows (q_start indexes the gathered buffer), keys cover every
+    row of the sequence (src/model.rs:534-539)."""
+    rng = np.random.default_rng(11)
+    lens, marks = [100, 40, 300], [[3, 50, 99], [0, 39], [1, 2, 150, 299]]
+    T = sum(lens)
+    qkv = rng.standard_normal((T, 3072)).astype(np.float16)
+    rows, seqs, s, ms = [], [], 0, 0
+    for n, mk in zip(lens, marks):
+        rows += [s + m for m in mk]
+        seqs.append((ms, len(mk), s, n))
+        s += n
+        ms += len(mk)
+    mq = qkv[rows]
+    d = torch.from_numpy(qkv).cuda()
+    dq = torch.from_numpy(np.ascontiguousarray(mq)).cuda()
+    got = run(gpu_lib, pkg, dq, 3072, d[:, 1024:], d[:, 2048:], 3072, seqs, 16, 1)
+    ref_k = run(ref_lib, pkg, dq, 3072, d[:, 1024:], d[:, 2048:], 3072, seqs, 16, 1)
+    q = qkv.astype(np.float32)
+    want = O.attention(mq.astype(np.float32)[:, :1024], q[:, 1024:2048], q[:, 2048:], seqs, 16, 1, 0.125)
+    assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(got - ref_k).max() <= 4e-3
+
+
+def test_prefix_keys(pkg, gpu_lib, ref_lib):
+    """Text after a media prefix: the prefix's cached K/V ([ext_len][512]) come before the local keys."""
+    rng = np.random.default_rng(12)
+    lens, ext_lens = [70, 5], [129, 64]
+    T = sum(lens)
+    qkv = rng.standard_normal((T, 2048)).astype(np.float16)
+    ext_np = [(rng.standard_normal((e, 512)).astype(np.float16), rng.standard_normal((e, 512)).astype(np.float16))
+              for e in ext_lens]
+    ext = [(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda()) for k, v in ext_np]
+    spans, s = [], 0
+    for n in lens:
+        spans.append((s, n, s, n))
+        s += n
+    d = torch.from_numpy(qkv).cuda()
+    got = run(gpu_lib, pkg, d, 2048, d[:, 1024:], d[:, 1536:], 2048, spans, 16, 2, ext=ext, ext_ld=512)
+    ref_k = run(ref_lib, pkg, d, 2048, d[:, 1024:], d[:, 1536:], 2048, spans, 16, 2, ext=ext, ext_ld=512)
+    q = qkv.astype(np.float32)
+    want = O.attention(q[:, :1024], q[:, 1024:1536], q[:, 1536:], spans, 16, 2, 0.125,
+                       ext=[(k.astype(np.float32), v.astype(np.float32)) for k, v in ext_np])
+    assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(got - ref_k).max() <= 4e-3

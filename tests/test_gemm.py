@@ -159,9 +159,14 @@ def test_swiglu_fused(gpu_lib, ctx, M):
     torch.cuda.synchronize()
     assert gpu_lib.d1_lt_error(ctx) == 0
     ref = ref_gemm(x, w)
-    g16, u16 = ref[:, :F].half().double(), ref[:, F:].half().double()
-    exact = g16 / (1 + torch.exp(-g16)) * u16
-    check_f16(out, exact)
+    gg, uu = ref[:, :F], ref[:, F:]
+    sig = torch.sigmoid(gg)
+    exact = gg * sig * uu
+    # g and u are rounded to fp16 before the gate (as the reference stores them): allow one fp16 ulp on each,
+    # propagated through silu(g) * u, plus the final rounding of the product.
+    slack = 2.0 ** -10 * ((sig * (1 + gg * (1 - sig)) * gg * uu).abs() + (gg * sig * uu).abs())
+    err = (out.double() - exact).abs()
+    assert (err <= 2 * slack + 2.0 ** -10 * exact.abs() + 1e-6).all(), err.max().item()
     # fused vs unfused: identical up to the rounding of g and u (1 fp16 ulp on either side)
     d = (out.float() - out2.float()).abs()
     assert (d <= out2.float().abs() * 2.0 ** -9 + 1e-3).all()
