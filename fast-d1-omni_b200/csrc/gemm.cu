@@ -12,8 +12,10 @@
 //   warp 1      allocates TMEM (2 x BN fp32 columns: a double-buffered 128 x BN accumulator); one thread
 //               issues tcgen05.mma (M=128, N=BN, K=16) and releases ring slots with tcgen05.commit.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp owns the 32 TMEM lanes = rows it may
-//               access), the fused epilogue in registers, and stores to global memory. The double-buffered
-//               accumulator lets the epilogue of one tile overlap the main loop of the next.
+//               access), the fused epilogue in registers, then each 32x32 output block goes through a swizzled
+//               shared-memory staging tile to one TMA bulk store (or TMA reduce-add for the fp32 residual
+//               Y += X.W^T). The double-buffered accumulator lets the epilogue of one tile overlap the main loop
+//               of the next; the accumulator is handed back as soon as its last column is read.
 // Every mbarrier wait is bounded in time: on expiry the kernel records an error code in the context's device
 // error word and returns instead of hanging.
 #include <stdio.h>
@@ -35,8 +37,18 @@ constexpr int BM = 128;           // rows of A per tile (tcgen05 M)
 constexpr int BK = 64;            // K per ring stage: 64 fp16 = one 128-byte swizzle row
 constexpr int kThreads = 192;     // 6 warps
 constexpr int A_BYTES = BM * BK * 2;
+constexpr int EPI_BUF = 4096;     // one staging tile: 32 rows x 128 bytes
+constexpr int EPI_SMEM = 4 * 2 * EPI_BUF;  // 4 epilogue warps, double-buffered
 
-enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_BIAS_ACT = 2 };
+// Epilogue forms. The TMA forms stage each 32x32 output block through swizzled shared memory and write it with
+// one bulk tensor store (or reduce-add) per warp; rows/columns past M/N are clipped by the tensor map.
+enum Epi : int {
+    EPI_STORE = 0,     // Y = alpha * acc (fp16 or fp32 Y), beta == 0
+    EPI_ADD = 1,       // Y += alpha * acc (fp32 Y, beta == 1): TMA reduce-add, Y is never read by the SM
+    EPI_SWIGLU = 2,    // out = silu(half(g)) * half(u), fp16
+    EPI_BIAS_ACT = 3,  // Y = act(half(acc) + bias), fp16
+    EPI_DIRECT = 4,    // any alpha/beta, direct stores (strides or alignment the tensor maps cannot take)
+};
 
 struct GemmArgs {
     int M, N, K;          // N: accumulator columns in total (2F for SwiGLU)
@@ -45,7 +57,6 @@ struct GemmArgs {
     void* Y;
     int ldy;
     int y_f32;
-    int vec;              // 16-byte aligned rows of Y: vector stores allowed
     float alpha, beta;
     const float* bias;
     int act;
@@ -59,7 +70,7 @@ struct Smem {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int RING = STAGES * STAGE_BYTES;
     static constexpr int NBARS = 2 * STAGES + 5;
-    static constexpr size_t BYTES = 1024 /* alignment slack */ + RING + NBARS * 8 + 16;
+    static constexpr size_t BYTES = 1024 /* alignment slack */ + RING + EPI_SMEM + NBARS * 8 + 16;
 };
 
 __device__ __forceinline__ void record_error(int* err, volatile int* abort_flag, int code) {
@@ -80,149 +91,78 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// ---------------------------------------------------------------------------------------------- epilogues
+// ---------------------------------------------------------------------------------------------- bulk stores
 
-// Y = alpha * acc + beta * Y (beta == 0: Y is not read), fp16 or fp32 Y.
-template <int BN>
-__device__ __forceinline__ void epi_store(const GemmArgs& a, uint32_t tbase, int row, int n0) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c0, r);
-        tc_wait_ld();
-        const int col = n0 + c0;
-        if (row >= a.M || col >= a.N) continue;
-        float v[32];
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)map),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_add_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     (uint64_t)map),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Thread t of the warp owns row t of a 32-row staging tile. fp16: 64-byte rows in the 64-byte swizzle pattern
+// (16-byte chunk j of row t at chunk j ^ ((t >> 1) & 3)); fp32: 128-byte rows in the 128-byte pattern (chunk
+// j ^ (t & 7)). These are the layouts the tensor maps' SWIZZLE_64B / SWIZZLE_128B expect, and each quarter-warp
+// of 16-byte stores hits 8 distinct bank groups.
+__device__ __forceinline__ void stage_h(uint8_t* buf, int t, const float* v) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
-        const bool full = a.vec && col + 32 <= a.N;
-        if (a.y_f32) {
-            float* y = reinterpret_cast<float*>(a.Y) + (size_t)row * a.ldy + col;
-            if (full) {
-                float4* y4 = reinterpret_cast<float4*>(y);
-                if (a.beta != 0.f) {
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float4 o = y4[i];
-                        v[4 * i] += a.beta * o.x;
-                        v[4 * i + 1] += a.beta * o.y;
-                        v[4 * i + 2] += a.beta * o.z;
-                        v[4 * i + 3] += a.beta * o.w;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) y4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-            } else {
-                for (int i = 0; i < 32 && col + i < a.N; i++) y[i] = v[i] + (a.beta != 0.f ? a.beta * y[i] : 0.f);
-            }
-        } else {
-            __half* y = reinterpret_cast<__half*>(a.Y) + (size_t)row * a.ldy + col;
-            if (full) {
-                uint4* y4 = reinterpret_cast<uint4*>(y);
-                if (a.beta != 0.f) {
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        uint4 o = y4[i];
-                        const __half2* h = reinterpret_cast<const __half2*>(&o);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            float2 f = __half22float2(h[j]);
-                            v[8 * i + 2 * j] += a.beta * f.x;
-                            v[8 * i + 2 * j + 1] += a.beta * f.y;
-                        }
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    y4[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                       pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
-            } else {
-                for (int i = 0; i < 32 && col + i < a.N; i++)
-                    y[i] = __float2half_rn(v[i] + (a.beta != 0.f ? a.beta * __half2float(y[i]) : 0.f));
-            }
-        }
+    for (int j = 0; j < 4; j++) {
+        const uint4 q = make_uint4(pack_h2(v[8 * j], v[8 * j + 1]), pack_h2(v[8 * j + 2], v[8 * j + 3]),
+                                   pack_h2(v[8 * j + 4], v[8 * j + 5]), pack_h2(v[8 * j + 6], v[8 * j + 7]));
+        *reinterpret_cast<uint4*>(buf + t * 64 + ((j ^ ((t >> 1) & 3)) << 4)) = q;
     }
 }
-
-// out[row][c] = silu(g) * u with g, u the fp16-rounded gate and up accumulators (as the reference's GEMM writes
-// fp16 and k_swiglu, cuda/kernels.cu:159-168, reads it back). Accumulator columns [0, BN/2) hold gate rows
-// [n0, n0+BN/2) of W and [BN/2, BN) the matching up rows [F+n0, ...).
-template <int BN>
-__device__ __forceinline__ void epi_swiglu(const GemmArgs& a, uint32_t tbase, int row, int n0) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-        uint32_t g[32], u[32];
-        tmem_ld32(tbase + c0, g);
-        tmem_ld32(tbase + BN / 2 + c0, u);
-        tc_wait_ld();
-        const int col = n0 + c0;
-        if (row >= a.M || col >= a.F) continue;
-        float v[32];
+__device__ __forceinline__ void stage_f(uint8_t* buf, int t, const float* v) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = silu(round_h(__uint_as_float(g[i]))) * round_h(__uint_as_float(u[i]));
+    for (int j = 0; j < 8; j++)
+        *reinterpret_cast<float4*>(buf + t * 128 + ((j ^ (t & 7)) << 4)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// Direct stores for EPI_DIRECT (fully unrolled so v[] stays in registers).
+__device__ __forceinline__ void direct_store(const GemmArgs& a, int row, int col, float* v) {
+    if (row >= a.M) return;
+    if (a.y_f32) {
+        float* y = reinterpret_cast<float*>(a.Y) + (size_t)row * a.ldy + col;
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (col + i < a.N) y[i] = v[i] + (a.beta != 0.f ? a.beta * y[i] : 0.f);
+    } else {
         __half* y = reinterpret_cast<__half*>(a.Y) + (size_t)row * a.ldy + col;
-        if (a.vec && col + 32 <= a.F) {
-            uint4* y4 = reinterpret_cast<uint4*>(y);
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                y4[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                   pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
-        } else {
-            for (int i = 0; i < 32 && col + i < a.F; i++) y[i] = __float2half_rn(v[i]);
-        }
-    }
-}
-
-// Y = act(half(acc) + bias), fp16 (the reference's fp16 GEMM output followed by k_bias_act_h,
-// cuda/kernels.cu:171-184).
-template <int BN>
-__device__ __forceinline__ void epi_bias_act(const GemmArgs& a, uint32_t tbase, int row, int n0) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c0, r);
-        tc_wait_ld();
-        const int col = n0 + c0;
-        if (row >= a.M || col >= a.N) continue;
-        float v[32];
-        const bool full = a.vec && col + 32 <= a.N;
-        if (full) {
-            const float4* b4 = reinterpret_cast<const float4*>(a.bias + col);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                float4 b = a.bias ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                v[4 * i] = apply_act(round_h(__uint_as_float(r[4 * i])) + b.x, a.act);
-                v[4 * i + 1] = apply_act(round_h(__uint_as_float(r[4 * i + 1])) + b.y, a.act);
-                v[4 * i + 2] = apply_act(round_h(__uint_as_float(r[4 * i + 2])) + b.z, a.act);
-                v[4 * i + 3] = apply_act(round_h(__uint_as_float(r[4 * i + 3])) + b.w, a.act);
-            }
-            uint4* y4 = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.Y) + (size_t)row * a.ldy + col);
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-                y4[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                   pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
-        } else {
-            __half* y = reinterpret_cast<__half*>(a.Y) + (size_t)row * a.ldy + col;
-            for (int i = 0; i < 32 && col + i < a.N; i++)
-                y[i] = __float2half_rn(apply_act(round_h(__uint_as_float(r[i])) + (a.bias ? a.bias[col + i] : 0.f), a.act));
-        }
+        for (int i = 0; i < 32; i++)
+            if (col + i < a.N) y[i] = __float2half_rn(v[i] + (a.beta != 0.f ? a.beta * __half2float(y[i]) : 0.f));
     }
 }
 
 // ---------------------------------------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool OUT32>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmY, const GemmArgs a) {
     using S = Smem<BN, STAGES>;
     constexpr uint32_t TMEM_COLS = 2 * BN;
     constexpr uint32_t IDESC = idesc_f16_f32(BM, BN);
+    constexpr int OUT_COLS = EPI == EPI_SWIGLU ? BN / 2 : BN;  // output columns per tile
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "tcgen05 M=128 needs N % 16 == 0, 16..256");
     static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocations are powers of 2");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::RING);
+    uint8_t* epi_smem = smem + S::RING;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::RING + EPI_SMEM);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -252,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (EPI != EPI_DIRECT) prefetch_tmap(&tmY);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -341,8 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------------ epilogue (warps 2..5)
-        const int sub = warp & 3;  // TMEM lane quarter this warp may access
-        int it = 0;
+        const int sub = warp & 3;  // TMEM lane quarter (rows sub*32 .. +31) this warp may access
+        uint8_t* stage0 = epi_smem + sub * 2 * EPI_BUF;
+        int buf = 0, it = 0;
         for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, it++) {
             const int acc = it & 1;
             const uint32_t acc_par = (it >> 1) & 1;
@@ -353,18 +295,67 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
-            const int row = m_blk * BM + sub * 32 + lane;
+            const int row0 = m_blk * BM + sub * 32;
+            const int col_base = n_blk * OUT_COLS;
             const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
-            if (EPI == EPI_SWIGLU)
-                epi_swiglu<BN>(a, tbase, row, n_blk * (BN / 2));
-            else if (EPI == EPI_BIAS_ACT)
-                epi_bias_act<BN>(a, tbase, row, n_blk * BN);
-            else
-                epi_store<BN>(a, tbase, row, n_blk * BN);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acce_bar(acc));
+#pragma unroll 1
+            for (int c0 = 0; c0 < OUT_COLS; c0 += 32) {
+                float v[32];
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c0, r);
+                    if (EPI == EPI_SWIGLU) {
+                        uint32_t u[32];
+                        tmem_ld32(tbase + BN / 2 + c0, u);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            v[i] = silu(round_h(__uint_as_float(r[i]))) * round_h(__uint_as_float(u[i]));
+                    } else {
+                        tc_wait_ld();
+                        if (EPI == EPI_BIAS_ACT) {
+                            const int col = col_base + c0;
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                const float b = (a.bias && col + i < a.N) ? __ldg(a.bias + col + i) : 0.f;
+                                v[i] = apply_act(round_h(__uint_as_float(r[i])) + b, a.act);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
+                        }
+                    }
+                }
+                if (c0 + 32 >= OUT_COLS) {  // last TMEM read of this tile: hand the accumulator back to the MMA
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acce_bar(acc));
+                }
+                if (EPI == EPI_DIRECT) {
+                    direct_store(a, row0 + lane, col_base + c0, v);
+                    continue;
+                }
+                uint8_t* sbuf = stage0 + buf * EPI_BUF;
+                if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
+                __syncwarp();
+                if (OUT32)
+                    stage_f(sbuf, lane, v);
+                else
+                    stage_h(sbuf, lane, v);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (EPI == EPI_ADD)
+                        tma_add_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                    else
+                        tma_store_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                    bulk_commit();
+                }
+                buf ^= 1;
+            }
         }
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -372,6 +363,254 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- CTA-pair kernel
+// The same pipeline on a cluster of 2 CTAs (2 SMs) sharing one tcgen05 cta_group::2 MMA of 256 x BN x 16:
+// each CTA holds 128 rows of A and BN/2 rows of B per stage (its own TMA loads, both completing on the pair
+// leader's `full` barrier), and 128 rows x BN columns of the accumulator in its own TMEM. Per SM this halves the
+// shared-memory operand bytes the tensor core reads per MMA and the L2->SM operand traffic per FLOP drops by
+// a third, relative to the single-SM 128 x BN tile. The leader's thread issues the MMAs; its commits arrive on both CTAs'
+// `empty` and `accf` barriers. 8 epilogue warps per CTA (2 per TMEM lane quarter, alternating 32-column chunks)
+// arrive on the leader's `acce` barrier when their part of an accumulator has been read.
+constexpr int kPairEpiWarps = 8;
+constexpr int kPairThreads = 64 + 32 * kPairEpiWarps;
+constexpr int PAIR_EPI_SMEM = kPairEpiWarps * EPI_BUF;
+
+template <int BN, int STAGES>
+struct PairSmem {
+    static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the B tile
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RING = STAGES * STAGE_BYTES;
+    static constexpr int NBARS = 2 * STAGES + 5;
+    static constexpr size_t BYTES = 1024 + RING + PAIR_EPI_SMEM + NBARS * 8 + 16;
+};
+
+template <int BN, int STAGES, int EPI, bool OUT32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmY, const GemmArgs a) {
+    using S = PairSmem<BN, STAGES>;
+    constexpr uint32_t TMEM_COLS = BN <= 128 ? 256 : 512;  // 2 accumulators of BN fp32 columns
+    constexpr uint32_t IDESC = idesc_f16_f32(2 * BM, BN);
+    constexpr int OUT_COLS = EPI == EPI_SWIGLU ? BN / 2 : BN;
+    constexpr int SUBTILES = OUT32 ? 1 : 2;  // 32x32 output blocks per 4 KB staging buffer
+    constexpr int SUB_BYTES = EPI_BUF / SUBTILES;
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair MMA: M=256 needs N % 16 == 0, 16..256");
+    static_assert(EPI != EPI_DIRECT, "the pair kernel only takes the TMA epilogues");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* epi_smem = smem + S::RING;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::RING + PAIR_EPI_SMEM);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + S::NBARS);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    auto sA = [&](int s) { return smem_u32(smem + s * S::STAGE_BYTES); };
+    auto sB = [&](int s) { return smem_u32(smem + s * S::STAGE_BYTES + A_BYTES); };
+    auto full_bar = [&](int s) { return smem_u32(bars + s); };
+    auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+    auto accf_bar = [&](int i) { return smem_u32(bars + 2 * STAGES + i); };
+    auto acce_bar = [&](int i) { return smem_u32(bars + 2 * STAGES + 2 + i); };
+    const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(accf_bar(0), 1);
+        mbar_init(accf_bar(1), 1);
+        mbar_init(acce_bar(0), 2 * kPairEpiWarps);
+        mbar_init(acce_bar(1), 2 * kPairEpiWarps);
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        prefetch_tmap(&tmY);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers are initialised before either signals the other
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, issued_par = 0;
+            bool aborted = false;
+            for (int tile = pair; tile < a.num_tiles && !aborted; tile += npairs) {
+                const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+                const int arow = m_blk * 2 * BM + (int)rank * BM;
+                const int brow = EPI == EPI_SWIGLU ? (int)rank * a.F + n_blk * (BN / 2) : n_blk * BN + (int)rank * (BN / 2);
+                for (int kb = 0; kb < a.num_kb; kb++) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
+                        record_error(a.err, abort_flag, kErrWaitEmpty);
+                        aborted = true;
+                        break;
+                    }
+                    const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * S::STAGE_BYTES);
+                    tma_load_2d_pair(sA(stage), &tmA, kb * BK, arow, fb);
+                    tma_load_2d_pair(sB(stage), &tmB, kb * BK, brow, fb);
+                    issued |= 1u << stage;
+                    issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // The leader's full barriers see both CTAs' bytes; wait there for every stage last issued.
+            if (leader)
+                for (int s = 0; s < STAGES; s++)
+                    if ((issued >> s) & 1)
+                        if (!mbar_wait_timed(full_bar(s), (issued_par >> s) & 1))
+                            record_error(a.err, abort_flag, kErrDrain);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer (leader CTA)
+        if (leader && lane == 0) {
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            bool aborted = false;
+            for (int tile = pair; tile < a.num_tiles && !aborted; tile += npairs, it++) {
+                const int acc = it & 1;
+                const uint32_t acc_par = (it >> 1) & 1;
+                if (!mbar_wait_cluster(acce_bar(acc), acc_par ^ 1, abort_flag)) {
+                    record_error(a.err, abort_flag, kErrWaitAccEmpty);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * (TMEM_COLS / 2);
+                for (int kb = 0; kb < a.num_kb; kb++) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+                        record_error(a.err, abort_flag, kErrWaitFull);
+                        aborted = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = sA(stage), b0 = sB(stage);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        tc_mma_f16_pair(d_tmem, smem_desc_k128(a0 + k * 32), smem_desc_k128(b0 + k * 32), IDESC,
+                                        (kb | k) != 0);
+                    tc_commit_pair_both(empty_bar(stage));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (aborted) break;
+                tc_commit_pair_both(accf_bar(acc));
+            }
+            tc_commit_pair(drain_bar);
+            if (!mbar_wait_timed(drain_bar, 0)) record_error(a.err, abort_flag, kErrDrain);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
+        const int ew = warp - 2;
+        const int sub = warp & 3;          // TMEM lane quarter this warp may access
+        const int half = ew >> 2;          // which alternating 32-column chunks
+        uint8_t* sbuf0 = epi_smem + ew * EPI_BUF;
+        const uint32_t acce_leader0 = mapa_shared(acce_bar(0), 0), acce_leader1 = mapa_shared(acce_bar(1), 0);
+        int sb = 0, it = 0;
+        for (int tile = pair; tile < a.num_tiles; tile += npairs, it++) {
+            const int acc = it & 1;
+            const uint32_t acc_par = (it >> 1) & 1;
+            const bool ok = __all_sync(D1_FULL_MASK, mbar_wait(accf_bar(acc), acc_par, abort_flag));
+            if (!ok) {
+                if (lane == 0) record_error(a.err, abort_flag, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+            const int row0 = m_blk * 2 * BM + (int)rank * BM + sub * 32;
+            const int col_base = n_blk * OUT_COLS;
+            const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * (TMEM_COLS / 2));
+#pragma unroll 1
+            for (int c0 = half * 32; c0 < OUT_COLS; c0 += 64) {
+                float v[32];
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c0, r);
+                    if (EPI == EPI_SWIGLU) {
+                        uint32_t u[32];
+                        tmem_ld32(tbase + BN / 2 + c0, u);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            const float g = round_h(__uint_as_float(r[i]));
+                            v[i] = __fdividef(g, 1.0f + __expf(-g)) * round_h(__uint_as_float(u[i]));
+                        }
+                    } else {
+                        tc_wait_ld();
+                        if (EPI == EPI_BIAS_ACT) {
+                            const int col = col_base + c0;
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                const float b = (a.bias && col + i < a.N) ? __ldg(a.bias + col + i) : 0.f;
+                                v[i] = apply_act(round_h(__uint_as_float(r[i])) + b, a.act);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
+                        }
+                    }
+                }
+                if (c0 + 64 >= OUT_COLS) {  // this warp's last read of the accumulator
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? acce_leader1 : acce_leader0);
+                }
+                uint8_t* sbuf = sbuf0 + sb * SUB_BYTES;
+                if (lane == 0) {
+                    if (SUBTILES == 2)
+                        bulk_wait_read<1>();
+                    else
+                        bulk_wait_read<0>();
+                }
+                __syncwarp();
+                if (OUT32)
+                    stage_f(sbuf, lane, v);
+                else
+                    stage_h(sbuf, lane, v);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (EPI == EPI_ADD)
+                        tma_add_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                    else
+                        tma_store_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                    bulk_commit();
+                }
+                sb = (sb + 1) % SUBTILES;
+            }
+        }
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers or read its shared memory
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -451,10 +690,10 @@ EncodeTiledFn encode_fn() {
 struct TmapKey {
     uintptr_t ptr;
     uint64_t inner, outer, stride;
-    uint32_t box_inner, box_outer;
+    uint32_t box_inner, box_outer, kind;
     bool operator==(const TmapKey& o) const {
         return ptr == o.ptr && inner == o.inner && outer == o.outer && stride == o.stride &&
-               box_inner == o.box_inner && box_outer == o.box_outer;
+               box_inner == o.box_inner && box_outer == o.box_outer && kind == o.kind;
     }
 };
 struct TmapHash {
@@ -463,7 +702,7 @@ struct TmapHash {
         h ^= k.inner + 0x9E3779B9 + (h << 6) + (h >> 2);
         h ^= k.outer + 0x9E3779B9 + (h << 6) + (h >> 2);
         h ^= k.stride + 0x9E3779B9 + (h << 6) + (h >> 2);
-        h ^= ((uint64_t)k.box_inner << 32 | k.box_outer) + 0x9E3779B9 + (h << 6) + (h >> 2);
+        h ^= ((uint64_t)k.box_inner << 40 | (uint64_t)k.box_outer << 8 | k.kind) + 0x9E3779B9 + (h << 6) + (h >> 2);
         return h;
     }
 };
@@ -471,7 +710,7 @@ struct TmapHash {
 // Tile plan: which kernel configuration runs a shape (the analogue of the reference's cuBLASLt algo choice).
 typedef std::tuple<int, int, int, int, int, int, int, int, int> PlanKey;  // N K ldx ldw ldy w_kn y_f32 epi bucket
 struct Plan {
-    int bn;
+    int cfg;  // Cfg
     float us;
 };
 
@@ -481,7 +720,8 @@ struct Ctx {
     int* d_err = nullptr;
     std::unordered_map<TmapKey, CUtensorMap, TmapHash> tmaps;
     std::map<PlanKey, Plan> plans;
-    uint32_t attr_done = 0;  // per kernel instance: max dynamic smem attribute set
+    uint64_t attr_done = 0;  // per kernel instance: max dynamic smem attribute set
+    int pair_slots = 74;     // co-resident CTA pairs (clusters of 2) for the pair kernels
     void* sx = nullptr;
     void* sw = nullptr;
     void* sy = nullptr;
@@ -498,51 +738,111 @@ int bucket_of(int m) {
     return BUCKETS[NBUCKETS - 1];
 }
 
-const CUtensorMap* get_tmap(Ctx* c, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
-                            uint32_t box_inner, uint32_t box_outer) {
-    TmapKey key{(uintptr_t)base, inner, outer, ld_elems * 2, box_inner, box_outer};
+// Tensor map kinds: operand loads (fp16, 128B swizzle) and output stores (fp16 64B / fp32 128B swizzle).
+enum TmapKind : uint32_t { TM_LOAD16 = 0, TM_STORE16 = 1, TM_STORE32 = 2 };
+
+bool get_tmap(Ctx* c, CUtensorMap* out, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+              uint32_t box_inner, uint32_t box_outer, TmapKind kind) {
+    const uint64_t esize = kind == TM_STORE32 ? 4 : 2;
+    TmapKey key{(uintptr_t)base, inner, outer, ld_elems * esize, box_inner, box_outer, (uint32_t)kind};
     auto it = c->tmaps.find(key);
-    if (it != c->tmaps.end()) return &it->second;
+    if (it != c->tmaps.end()) {
+        *out = it->second;
+        return true;
+    }
     EncodeTiledFn enc = encode_fn();
-    if (!enc) return nullptr;
+    if (!enc) return false;
     CUtensorMap m;
     cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {ld_elems * 2};
+    cuuint64_t strides[1] = {ld_elems * esize};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return nullptr;
+    const CUtensorMapDataType dt = kind == TM_STORE32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUtensorMapSwizzle sw = kind == TM_STORE16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUresult r = enc(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
     if (c->tmaps.size() > 4096) c->tmaps.clear();
-    return &c->tmaps.emplace(key, m).first->second;
+    c->tmaps.emplace(key, m);
+    *out = m;
+    return true;
 }
 
 bool tc_ok(const void* X, int ldx, const void* W, int ldw, int w_kn, int K) {
     return !w_kn && K >= 1 && ldx % 8 == 0 && ldw % 8 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
 }
 
-template <int BN, int STAGES, int EPI>
+// Output through a TMA tensor map: base 16-byte aligned and a row pitch that is a multiple of 16 bytes.
+bool tma_out_ok(const void* Y, int ldy, int y_f32) {
+    return ((uintptr_t)Y & 15) == 0 && ((size_t)ldy * (y_f32 ? 4 : 2)) % 16 == 0;
+}
+
+template <int BN, int STAGES, int EPI, bool OUT32>
 int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, int w_rows, GemmArgs& a,
               cudaStream_t st) {
     using S = Smem<BN, STAGES>;
-    auto kern = k_gemm_tc<BN, STAGES, EPI>;
-    if (!(c->attr_done & (1u << bit))) {
+    auto kern = k_gemm_tc<BN, STAGES, EPI, OUT32>;
+    if (!(c->attr_done & (1ull << bit))) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::BYTES) != cudaSuccess)
             return -1;
-        c->attr_done |= 1u << bit;
+        c->attr_done |= 1ull << bit;
     }
     const uint32_t b_rows = EPI == EPI_SWIGLU ? BN / 2 : BN;
-    const CUtensorMap* ta = get_tmap(c, X, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)ldx, BK, BM);
-    const CUtensorMap* tb = get_tmap(c, W, (uint64_t)a.K, (uint64_t)w_rows, (uint64_t)ldw, BK, b_rows);
-    if (!ta || !tb) return -1;
+    CUtensorMap ta, tb, ty;
+    if (!get_tmap(c, &ta, X, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)ldx, BK, BM, TM_LOAD16) ||
+        !get_tmap(c, &tb, W, (uint64_t)a.K, (uint64_t)w_rows, (uint64_t)ldw, BK, b_rows, TM_LOAD16))
+        return -1;
+    const int out_cols = EPI == EPI_SWIGLU ? a.F : a.N;
+    if (EPI == EPI_DIRECT)
+        ty = ta;  // unused
+    else if (!get_tmap(c, &ty, a.Y, (uint64_t)out_cols, (uint64_t)a.M, (uint64_t)a.ldy, 32, 32,
+                       OUT32 ? TM_STORE32 : TM_STORE16))
+        return -1;
     a.num_m = (a.M + BM - 1) / BM;
     a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
     a.num_tiles = a.num_m * a.num_n;
     a.num_kb = (a.K + BK - 1) / BK;
     a.err = c->d_err;
     const int grid = a.num_tiles < c->num_sms ? a.num_tiles : c->num_sms;
-    kern<<<grid, kThreads, S::BYTES, st>>>(*ta, *tb, a);
+    kern<<<grid, kThreads, S::BYTES, st>>>(ta, tb, ty, a);
+    return (int)cudaGetLastError();
+}
+
+template <int BN, int STAGES, int EPI, bool OUT32>
+int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, int w_rows, GemmArgs& a,
+               cudaStream_t st) {
+    using S = PairSmem<BN, STAGES>;
+    auto kern = k_gemm_tc2<BN, STAGES, EPI, OUT32>;
+    if (!(c->attr_done & (1ull << bit))) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::BYTES) != cudaSuccess)
+            return -1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (c->num_sms / 2));
+        cfg.blockDim = dim3(kPairThreads);
+        cfg.dynamicSmemBytes = S::BYTES;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = c->num_sms / 2;
+        }
+        c->pair_slots = n;
+        c->attr_done |= 1ull << bit;
+    }
+    const uint32_t b_rows = BN / 2;
+    CUtensorMap ta, tb, ty;
+    const int out_cols = EPI == EPI_SWIGLU ? a.F : a.N;
+    if (!get_tmap(c, &ta, X, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)ldx, BK, BM, TM_LOAD16) ||
+        !get_tmap(c, &tb, W, (uint64_t)a.K, (uint64_t)w_rows, (uint64_t)ldw, BK, b_rows, TM_LOAD16) ||
+        !get_tmap(c, &ty, a.Y, (uint64_t)out_cols, (uint64_t)a.M, (uint64_t)a.ldy, 32, 32,
+                  OUT32 ? TM_STORE32 : TM_STORE16))
+        return -1;
+    a.num_m = (a.M + 2 * BM - 1) / (2 * BM);
+    a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
+    a.num_tiles = a.num_m * a.num_n;
+    a.num_kb = (a.K + BK - 1) / BK;
+    a.err = c->d_err;
+    const int pairs = a.num_tiles < c->pair_slots ? a.num_tiles : c->pair_slots;
+    kern<<<2 * pairs, kPairThreads, S::BYTES, st>>>(ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
 
@@ -552,14 +852,34 @@ double wave_eff(long tiles, int sms) {
     return (double)tiles / (double)(waves * sms);
 }
 
-int default_bn(Ctx* c, int M, int N) {
-    const long mt = (M + BM - 1) / BM;
-    const double e256 = wave_eff(mt * ((N + 255) / 256), c->num_sms) * (double)N / (double)(((N + 255) / 256) * 256);
-    const double e128 = wave_eff(mt * ((N + 127) / 128), c->num_sms) * (double)N / (double)(((N + 127) / 128) * 128);
-    return e128 > e256 + 0.08 ? 128 : 256;
+// Kernel configurations a plan can name: the single-SM kernel with 128- or 256-column tiles, or the CTA-pair
+// kernel with 256 x 256 or 256 x 128 tiles.
+enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3 };
+
+// Fraction of the SM-time the tiles keep busy (wave quantisation x column padding), per configuration.
+double cfg_eff(Ctx* c, int cfg, int M, int N) {
+    const bool pair = cfg >= CFG_PAIR_256;
+    const int bm = pair ? 2 * BM : BM;
+    const int bn = (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
+    const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+    const int slots = pair ? c->pair_slots : c->num_sms;
+    const double pad = (double)M * N / ((double)((M + bm - 1) / bm) * bm * ((N + bn - 1) / bn) * bn);
+    return wave_eff(tiles, slots) * pad;
 }
 
-int run_store(Ctx* c, int bn, int M, int N, int K, const void* X, int ldx, const void* W, int ldw, void* Y, int ldy,
+// Heuristic plan when none was tuned: the pair kernel for large problems (it needs half the shared-memory and
+// L2 operand bandwidth per FLOP), preferring the tile width that quantises better.
+int default_cfg(Ctx* c, int M, int N) {
+    if (M >= 512) {
+        const double e256 = cfg_eff(c, CFG_PAIR_256, M, N), e128 = cfg_eff(c, CFG_PAIR_128, M, N);
+        return e128 > e256 + 0.05 ? CFG_PAIR_128 : CFG_PAIR_256;
+    }
+    const double e256 = cfg_eff(c, CFG_1SM_256, M, N), e128 = cfg_eff(c, CFG_1SM_128, M, N);
+    return e128 > e256 + 0.08 ? CFG_1SM_128 : CFG_1SM_256;
+}
+
+// Y = alpha X W^T + beta Y: TMA store (beta 0), TMA reduce-add (fp32 Y, beta 1), else direct stores.
+int run_store(Ctx* c, int cfg, int M, int N, int K, const void* X, int ldx, const void* W, int ldw, void* Y, int ldy,
               int y_f32, float alpha, float beta, cudaStream_t st) {
     GemmArgs a{};
     a.M = M;
@@ -568,11 +888,33 @@ int run_store(Ctx* c, int bn, int M, int N, int K, const void* X, int ldx, const
     a.Y = Y;
     a.ldy = ldy;
     a.y_f32 = y_f32;
-    a.vec = ((uintptr_t)Y % 16 == 0) && ((size_t)ldy * (y_f32 ? 4 : 2)) % 16 == 0;
     a.alpha = alpha;
     a.beta = beta;
-    if (bn == 128) return launch_tc<128, 6, EPI_STORE>(c, 0, X, ldx, W, ldw, N, a, st);
-    return launch_tc<256, 4, EPI_STORE>(c, 1, X, ldx, W, ldw, N, a, st);
+    const bool tma = tma_out_ok(Y, ldy, y_f32);
+    const bool store = tma && beta == 0.f, add = tma && beta == 1.f && y_f32;
+    if (cfg == CFG_PAIR_256 && (store || add)) {
+        if (add) return launch_tc2<256, 6, EPI_ADD, true>(c, 11, X, ldx, W, ldw, N, a, st);
+        if (y_f32) return launch_tc2<256, 6, EPI_STORE, true>(c, 12, X, ldx, W, ldw, N, a, st);
+        return launch_tc2<256, 6, EPI_STORE, false>(c, 13, X, ldx, W, ldw, N, a, st);
+    }
+    if (cfg == CFG_PAIR_128 && (store || add)) {
+        if (add) return launch_tc2<128, 8, EPI_ADD, true>(c, 14, X, ldx, W, ldw, N, a, st);
+        if (y_f32) return launch_tc2<128, 8, EPI_STORE, true>(c, 15, X, ldx, W, ldw, N, a, st);
+        return launch_tc2<128, 8, EPI_STORE, false>(c, 16, X, ldx, W, ldw, N, a, st);
+    }
+    const bool b128 = cfg == CFG_1SM_128;
+    if (store) {
+        if (y_f32)
+            return b128 ? launch_tc<128, 6, EPI_STORE, true>(c, 0, X, ldx, W, ldw, N, a, st)
+                        : launch_tc<256, 4, EPI_STORE, true>(c, 1, X, ldx, W, ldw, N, a, st);
+        return b128 ? launch_tc<128, 6, EPI_STORE, false>(c, 2, X, ldx, W, ldw, N, a, st)
+                    : launch_tc<256, 4, EPI_STORE, false>(c, 3, X, ldx, W, ldw, N, a, st);
+    }
+    if (add)
+        return b128 ? launch_tc<128, 6, EPI_ADD, true>(c, 4, X, ldx, W, ldw, N, a, st)
+                    : launch_tc<256, 4, EPI_ADD, true>(c, 5, X, ldx, W, ldw, N, a, st);
+    return b128 ? launch_tc<128, 6, EPI_DIRECT, false>(c, 6, X, ldx, W, ldw, N, a, st)
+                : launch_tc<256, 4, EPI_DIRECT, false>(c, 7, X, ldx, W, ldw, N, a, st);
 }
 
 int run_simt(int M, int N, int K, const void* X, int ldx, const void* W, int ldw, int w_kn, void* Y, int ldy,
@@ -602,7 +944,7 @@ void ensure(void** p, size_t* have, size_t need, uint32_t seed) {
 // ================================================================================================ C ABI
 extern "C" {
 
-const char* d1_build_id(void) { return "d1b200-tc-gemm-v1"; }
+const char* d1_build_id(void) { return "d1b200-tc-gemm-v3"; }
 
 void* d1_lt_init(size_t ws_bytes) {
     (void)ws_bytes;
@@ -650,10 +992,9 @@ int d1_lt_gemm(void* ctx, int M, int N, int K, const void* X, int ldx, const voi
     if (M == 0 || N == 0) return 0;
     if (!tc_ok(X, ldx, W, ldw, w_kn, K))
         return run_simt(M, N, K, X, ldx, W, ldw, w_kn, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
-    int bn;
     auto it = c->plans.find(PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, EPI_STORE, bucket_of(M)));
-    bn = it != c->plans.end() ? it->second.bn : default_bn(c, M, N);
-    return run_store(c, bn, M, N, K, X, ldx, W, ldw, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
+    const int cfg = it != c->plans.end() ? it->second.cfg : default_cfg(c, M, N);
+    return run_store(c, cfg, M, N, K, X, ldx, W, ldw, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
 }
 
 int d1_gemm_swiglu(void* ctx, int M, int F, int K, const d1_half* X, int ldx, const d1_half* W, int ldw,
@@ -669,9 +1010,10 @@ int d1_gemm_swiglu(void* ctx, int M, int F, int K, const d1_half* X, int ldx, co
     a.F = F;
     a.Y = out;
     a.ldy = ldo;
-    a.vec = ((uintptr_t)out % 16 == 0) && (ldo % 8 == 0);
     a.alpha = 1.f;
-    return launch_tc<256, 4, EPI_SWIGLU>(c, 2, X, ldx, W, ldw, 2 * F, a, st) ? -1 : 0;
+    if (!tma_out_ok(out, ldo, 0)) return -1;
+    if (M >= 512) return launch_tc2<256, 6, EPI_SWIGLU, false>(c, 17, X, ldx, W, ldw, 2 * F, a, st) ? -1 : 0;
+    return launch_tc<256, 4, EPI_SWIGLU, false>(c, 8, X, ldx, W, ldw, 2 * F, a, st) ? -1 : 0;
 }
 
 int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, const d1_half* W, int ldw,
@@ -686,12 +1028,16 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
     a.K = K;
     a.Y = Y;
     a.ldy = ldy;
-    a.vec = ((uintptr_t)Y % 16 == 0) && (ldy % 8 == 0) && ((uintptr_t)bias % 16 == 0);
     a.alpha = 1.f;
     a.bias = bias;
     a.act = act;
-    if (default_bn(c, M, N) == 128) return launch_tc<128, 6, EPI_BIAS_ACT>(c, 3, X, ldx, W, ldw, N, a, st) ? -1 : 0;
-    return launch_tc<256, 4, EPI_BIAS_ACT>(c, 4, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+    if (!tma_out_ok(Y, ldy, 0)) return -1;
+    switch (default_cfg(c, M, N)) {
+        case CFG_PAIR_256: return launch_tc2<256, 6, EPI_BIAS_ACT, false>(c, 18, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        case CFG_PAIR_128: return launch_tc2<128, 8, EPI_BIAS_ACT, false>(c, 19, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        case CFG_1SM_128: return launch_tc<128, 6, EPI_BIAS_ACT, false>(c, 9, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        default: return launch_tc<256, 4, EPI_BIAS_ACT, false>(c, 10, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+    }
 }
 
 float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int ldy, int y_f32, int f16acc,
@@ -714,11 +1060,11 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
     cudaEventCreate(&e1);
     const int reps = M >= 4096 ? 5 : M >= 1024 ? 10 : 20;
     float best = 1e30f;
-    int best_bn = 256;
+    int best_cfg = CFG_1SM_256;
     const bool tc = tc_ok(c->sx, ldx, c->sw, ldw, w_kn, K);
-    for (int bn : {128, 256}) {
+    for (int cfg : {CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128}) {
         auto run = [&]() {
-            return tc ? run_store(c, bn, M, N, K, c->sx, ldx, c->sw, ldw, c->sy, ldy, y_f32, 1.f, 0.f, st)
+            return tc ? run_store(c, cfg, M, N, K, c->sx, ldx, c->sw, ldw, c->sy, ldy, y_f32, 1.f, y_f32 ? 1.f : 0.f, st)
                       : run_simt(M, N, K, c->sx, ldx, c->sw, ldw, w_kn, c->sy, ldy, y_f32, 1.f, 0.f, st);
         };
         if (run() || run()) continue;
@@ -731,14 +1077,14 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
         const float us = ms * 1000.f / reps;
         if (cudaGetLastError() == cudaSuccess && us < best) {
             best = us;
-            best_bn = bn;
+            best_cfg = cfg;
         }
         if (!tc) break;
     }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     if (best >= 1e29f) return -1.f;
-    c->plans[key] = Plan{best_bn, best};
+    c->plans[key] = Plan{best_cfg, best};
     return best;
 }
 
@@ -750,7 +1096,7 @@ int d1_lt_save(void* ctx, const char* path) {
     for (auto& kv : c->plans) {
         int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b;
         std::tie(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b) = kv.first;
-        fprintf(f, "%d %d %d %d %d %d %d %d %d %d %.2f\n", N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, kv.second.bn,
+        fprintf(f, "%d %d %d %d %d %d %d %d %d %d %.2f\n", N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, kv.second.cfg,
                 kv.second.us);
     }
     fclose(f);
@@ -768,13 +1114,13 @@ int d1_lt_load(void* ctx, const char* path) {
     }
     int n = 0;
     while (true) {
-        int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, bn;
+        int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, cfg;
         float us;
-        if (fscanf(f, "%d %d %d %d %d %d %d %d %d %d %f", &N, &K, &ldx, &ldw, &ldy, &w_kn, &y_f32, &epi, &b, &bn,
+        if (fscanf(f, "%d %d %d %d %d %d %d %d %d %d %f", &N, &K, &ldx, &ldw, &ldy, &w_kn, &y_f32, &epi, &b, &cfg,
                    &us) != 11)
             break;
-        if (bn != 128 && bn != 256) continue;
-        c->plans[PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b)] = Plan{bn, us};
+        if (cfg < CFG_1SM_128 || cfg > CFG_PAIR_128) continue;
+        c->plans[PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b)] = Plan{cfg, us};
         n++;
     }
     fclose(f);

@@ -99,7 +99,7 @@ def test_alpha_beta_general(gpu_lib, ctx):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K", [(77, 200, 136), (130, 1000, 1000), (5, 40, 72)])
+@pytest.mark.parametrize("M,N,K", [(77, 200, 136), (130, 1000, 1000), (5, 40, 72), (777, 1000, 1000), (600, 96, 4608)])
 def test_ragged_shapes(gpu_lib, ctx, M, N, K):
     """N and K that are not tile multiples (TMA zero fill on loads, masked epilogue stores)."""
     g = torch.Generator(device="cuda").manual_seed(4)
@@ -166,7 +166,8 @@ def test_swiglu_fused(gpu_lib, ctx, M):
     # propagated through silu(g) * u, plus the final rounding of the product.
     slack = 2.0 ** -10 * ((sig * (1 + gg * (1 - sig)) * gg * uu).abs() + (gg * sig * uu).abs())
     err = (out.double() - exact).abs()
-    assert (err <= 2 * slack + 2.0 ** -10 * exact.abs() + 1e-6).all(), err.max().item()
+    # plus fp32 accumulation noise over K (~1e-6 absolute near zero)
+    assert (err <= 2 * slack + 2.0 ** -10 * exact.abs() + 2e-5).all(), err.max().item()
     # fused vs unfused: identical up to the rounding of g and u (1 fp16 ulp on either side)
     d = (out.float() - out2.float()).abs()
     assert (d <= out2.float().abs() * 2.0 ** -9 + 1e-3).all()
@@ -174,10 +175,12 @@ def test_swiglu_fused(gpu_lib, ctx, M):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("act", [0, 1, 2, 3, 4])
-def test_bias_act_fused(gpu_lib, ctx, act):
-    """d1_gemm_bias_act == d1_lt_gemm(fp16) + d1_bias_act_h (src/model.rs:568-569)."""
+@pytest.mark.parametrize("M", [333, 1000])
+def test_bias_act_fused(gpu_lib, ctx, act, M):
+    """d1_gemm_bias_act == d1_lt_gemm(fp16) + d1_bias_act_h (src/model.rs:568-569); M 333 runs the single-SM
+    kernel, M 1000 the CTA-pair kernel."""
     g = torch.Generator(device="cuda").manual_seed(8 + act)
-    M, N, K = 333, 2048, 1024
+    N, K = 2048, 1024
     x = torch.randn(M, K, device="cuda", generator=g).half()
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
     b = torch.randn(N, device="cuda", generator=g) * 0.1
