@@ -167,6 +167,34 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def swiglu_gemm_ms(pkg, dev, stream, reps=20):
+    """Average CUDA-event time of one d1_gemm_swiglu launch at M=8192 (the trunk's w1|w3 projection)."""
+    import ctypes as C
+    import torch
+    lib = pkg.lib()
+    ctx = lib.d1_lt_init(0)
+    M, F, K = TOKENS, 4608, 1024
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, K, device=dev, generator=g).half()
+    wt = (torch.randn(2 * F, K, device=dev, generator=g) * 0.02).half()
+    out = torch.empty(M, F, device=dev, dtype=torch.float16)
+    st = C.c_void_p(stream.cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    for _ in range(3):
+        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(reps):
+        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    err = lib.d1_lt_error(ctx)
+    lib.d1_lt_destroy(ctx)
+    if err:
+        raise RuntimeError(f"GEMM kernel reported error {err}")
+    return g0.elapsed_time(g1) / reps
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -174,6 +202,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="d1", choices=["d1", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-roofline", action="store_true",
+                    help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -193,6 +223,11 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     pkg = load_package()
+    if args.only_roofline:
+        ms = swiglu_gemm_ms(pkg, dev, torch.cuda.Stream(dev))
+        if rank == 0:
+            print(json.dumps({"kernel": "fused SwiGLU GEMM", "M": TOKENS, "gemm_ms": ms}), flush=True)
+        return
     from fast_d1_omni_b200.model import TextModel
     from fast_d1_omni_b200.weights import text_batch, text_weights
     import ctypes as C
@@ -245,29 +280,7 @@ def main():
         barrier()
 
     # ---------------------------------------------------------------- roofline: the fused SwiGLU GEMM alone
-    lib = pkg.lib()
-    ctx = lib.d1_lt_init(0)
-    M, F, K = TOKENS, 4608, 1024
-    g = torch.Generator(device=dev).manual_seed(7)
-    x = torch.randn(M, K, device=dev, generator=g).half()
-    wt = (torch.randn(2 * F, K, device=dev, generator=g) * 0.02).half()
-    out = torch.empty(M, F, device=dev, dtype=torch.float16)
-    st = C.c_void_p(stream.cuda_stream)
-    P = lambda t: C.c_void_p(t.data_ptr())
-    for _ in range(3):
-        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
-    reps = 20
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record(stream)
-    for _ in range(reps):
-        lib.d1_gemm_swiglu(ctx, M, F, K, P(x), K, P(wt), K, P(out), F, st)
-    g1.record(stream)
-    torch.cuda.synchronize(dev)
-    gemm_ms = g0.elapsed_time(g1) / reps
-    err = lib.d1_lt_error(ctx)
-    lib.d1_lt_destroy(ctx)
-    if err:
-        raise RuntimeError(f"GEMM kernel reported error {err}")
+    gemm_ms = swiglu_gemm_ms(pkg, dev, stream)
 
     # ---------------------------------------------------------------- aggregate over ranks
     t = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device=dev)
@@ -292,7 +305,7 @@ def main():
                        "l2": "inputs larger than L2 (weights + activations > 700 MB)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gemm_tflops_trunk_equiv": GEMM_FLOP_PER_TOKEN * value / world / 1e12,
-            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc<256,4,EPI_SWIGLU> (w1|w3 + SwiGLU), M=8192",
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc2<256,6,EPI_SWIGLU> (w1|w3 + SwiGLU, CTA pair), M=8192",
                          "achieved": achieved, "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
                          "peak_kind": f"{kind} (bf16 cuBLAS burst)", "traffic": SWIGLU_TRAFFIC_PER_LAUNCH,
                          "gemm_ms": gemm_ms},

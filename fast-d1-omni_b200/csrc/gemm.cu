@@ -61,8 +61,21 @@ struct GemmArgs {
     const float* bias;
     int act;
     int F;                // SwiGLU: output columns (rows [0,F) of W are gate, [F,2F) up)
+    int n_fast;           // tile order: 1 walks N fastest (A, the larger operand, is read from DRAM once)
     int* err;
 };
+
+// Tile index -> (row block, column block). The CTAs running at the same time share the operand that the order
+// repeats, so the larger operand is walked slowest: it streams from DRAM once while the smaller stays in L2.
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& m_blk, int& n_blk) {
+    if (a.n_fast) {
+        n_blk = tile % a.num_n;
+        m_blk = tile / a.num_n;
+    } else {
+        m_blk = tile % a.num_m;
+        n_blk = tile / a.num_m;
+    }
+}
 
 template <int BN, int STAGES>
 struct Smem {
@@ -210,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
             for (int tile = blockIdx.x; tile < a.num_tiles && !aborted; tile += gridDim.x) {
-                const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+                int m_blk, n_blk;
+                tile_coords(a, tile, m_blk, n_blk);
                 for (int kb = 0; kb < a.num_kb; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
                         record_error(a.err, abort_flag, kErrWaitEmpty);
@@ -294,7 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+            int m_blk, n_blk;
+                tile_coords(a, tile, m_blk, n_blk);
             const int row0 = m_blk * BM + sub * 32;
             const int col_base = n_blk * OUT_COLS;
             const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
@@ -454,7 +469,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
             for (int tile = pair; tile < a.num_tiles && !aborted; tile += npairs) {
-                const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+                int m_blk, n_blk;
+                tile_coords(a, tile, m_blk, n_blk);
                 const int arow = m_blk * 2 * BM + (int)rank * BM;
                 const int brow = EPI == EPI_SWIGLU ? (int)rank * a.F + n_blk * (BN / 2) : n_blk * BN + (int)rank * (BN / 2);
                 for (int kb = 0; kb < a.num_kb; kb++) {
@@ -539,7 +555,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int m_blk = tile % a.num_m, n_blk = tile / a.num_m;
+            int m_blk, n_blk;
+                tile_coords(a, tile, m_blk, n_blk);
             const int row0 = m_blk * 2 * BM + (int)rank * BM + sub * 32;
             const int col_base = n_blk * OUT_COLS;
             const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * (TMEM_COLS / 2));
@@ -802,6 +819,7 @@ int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, i
     a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
     a.num_tiles = a.num_m * a.num_n;
     a.num_kb = (a.K + BK - 1) / BK;
+    a.n_fast = a.M > w_rows;
     a.err = c->d_err;
     const int grid = a.num_tiles < c->num_sms ? a.num_tiles : c->num_sms;
     kern<<<grid, kThreads, S::BYTES, st>>>(ta, tb, ty, a);
@@ -840,6 +858,7 @@ int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, 
     a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
     a.num_tiles = a.num_m * a.num_n;
     a.num_kb = (a.K + BK - 1) / BK;
+    a.n_fast = a.M > w_rows;
     a.err = c->d_err;
     const int pairs = a.num_tiles < c->pair_slots ? a.num_tiles : c->pair_slots;
     kern<<<2 * pairs, kPairThreads, S::BYTES, st>>>(ta, tb, ty, a);

@@ -24,11 +24,23 @@ def ST():
     return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+_KEEP = []  # device copies stay alive until the test ends (a freed temporary's block is reused at once)
+
+
+@pytest.fixture(autouse=True)
+def _release_inputs():
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 def cu(a, dtype=None):
     t = torch.from_numpy(np.ascontiguousarray(a))
     if dtype is not None:
         t = t.to(dtype)
-    return t.cuda()
+    t = t.cuda()
+    _KEEP.append(t)
+    return t
 
 
 def np_(t):
