@@ -41,7 +41,7 @@ N_SEQS = 32
 TOKENS = SEQ_LEN * N_SEQS
 GEMM_FLOP_PER_TOKEN = 574_619_648          # trunk projection GEMMs (2 x 287,309,824 linear params)
 SWIGLU_FLOP_PER_TOKEN = 2 * 9216 * 1024    # w1|w3, fused SwiGLU epilogue
-SWIGLU_TRAFFIC_PER_LAUNCH = None           # ncu dram bytes, profiles/gemm_swiglu_m8192.md (scaled), filled below
+SWIGLU_TRAFFIC_PER_LAUNCH = 69.6e6          # ncu dram read+write per launch at this shape (profiles/gemm_swiglu_pair_m8192.md)
 
 
 def load_package():
@@ -293,7 +293,7 @@ def main():
 
     if rank == 0:
         hbm, tflops, kind = peaks()
-        achieved = SWIGLU_FLOP_PER_TOKEN * M / (gemm_ms / 1e3) / 1e12
+        achieved = SWIGLU_FLOP_PER_TOKEN * TOKENS / (gemm_ms / 1e3) / 1e12
         line = {
             "metric": "prefill tokens/s per B200 at 8192-token batches", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
