@@ -54,6 +54,7 @@ struct GemmArgs {
     int M, N, K;          // N: accumulator columns in total (2F for SwiGLU)
     int num_m, num_n;     // tile grid
     int num_tiles, num_kb;
+    int num_units, kb_per; // split-K: work unit u = (tile u % num_tiles, K blocks [(u / num_tiles) * kb_per, +kb_per))
     void* Y;
     int ldy;
     int y_f32;
@@ -143,6 +144,47 @@ __device__ __forceinline__ void stage_f(uint8_t* buf, int t, const float* v) {
             make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
+// v = act(half(acc) + bias) for one 32-column chunk: bias read as float4 when aligned, the activation chosen once
+// per chunk (cuda/kernels.cu:171-184 applied to the fp16-rounded GEMM output).
+__device__ __forceinline__ void bias_act32(const GemmArgs& a, int col, const uint32_t (&r)[32], float (&v)[32]) {
+    float bb[32];
+    if (a.bias && col + 32 <= a.N && ((reinterpret_cast<uintptr_t>(a.bias + col) & 15) == 0)) {
+        const float4* b4 = reinterpret_cast<const float4*>(a.bias + col);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 t = __ldg(b4 + i);
+            bb[4 * i] = t.x;
+            bb[4 * i + 1] = t.y;
+            bb[4 * i + 2] = t.z;
+            bb[4 * i + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) bb[i] = (a.bias && col + i < a.N) ? __ldg(a.bias + col + i) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = round_h(__uint_as_float(r[i])) + bb[i];
+    switch (a.act) {
+        case 1:
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = fmaxf(v[i], 0.0f);
+            break;
+        case 2:
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = gelu_erf(v[i]);
+            break;
+        case 3:
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = gelu_tanh(v[i]);
+            break;
+        case 4:
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = silu(v[i]);
+            break;
+        default: break;
+    }
+}
+
 // Direct stores for EPI_DIRECT (fully unrolled so v[] stays in registers).
 __device__ __forceinline__ void direct_store(const GemmArgs& a, int row, int col, float* v) {
     if (row >= a.M) return;
@@ -222,10 +264,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
-            for (int tile = blockIdx.x; tile < a.num_tiles && !aborted; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < a.num_units && !aborted; u += gridDim.x) {
+                const int tile = u % a.num_tiles, kb0 = (u / a.num_tiles) * a.kb_per;
+                const int kb1 = min(a.num_kb, kb0 + a.kb_per);
                 int m_blk, n_blk;
                 tile_coords(a, tile, m_blk, n_blk);
-                for (int kb = 0; kb < a.num_kb; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
                         record_error(a.err, abort_flag, kErrWaitEmpty);
                         aborted = true;
@@ -259,7 +303,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0, it = 0;
             uint32_t phase = 0;
             bool aborted = false;
-            for (int tile = blockIdx.x; tile < a.num_tiles && !aborted; tile += gridDim.x, it++) {
+            for (int u = blockIdx.x; u < a.num_units && !aborted; u += gridDim.x, it++) {
+                const int kb0 = (u / a.num_tiles) * a.kb_per, kb1 = min(a.num_kb, kb0 + a.kb_per);
                 const int acc = it & 1;
                 const uint32_t acc_par = (it >> 1) & 1;
                 if (!mbar_wait(acce_bar(acc), acc_par ^ 1, abort_flag)) {
@@ -268,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < a.num_kb; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
                         record_error(a.err, abort_flag, kErrWaitFull);
                         aborted = true;
@@ -279,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++)
                         tc_mma_f16(d_tmem, smem_desc_k128(a0 + k * 32), smem_desc_k128(b0 + k * 32), IDESC,
-                                   (kb | k) != 0);
+                                   ((kb - kb0) | k) != 0);
                     tc_commit(empty_bar(stage));
                     if (++stage == STAGES) {
                         stage = 0;
@@ -299,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sub = warp & 3;  // TMEM lane quarter (rows sub*32 .. +31) this warp may access
         uint8_t* stage0 = epi_smem + sub * 2 * EPI_BUF;
         int buf = 0, it = 0;
-        for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, it++) {
+        for (int u = blockIdx.x; u < a.num_units; u += gridDim.x, it++) {
+            const int tile = u % a.num_tiles;
             const int acc = it & 1;
             const uint32_t acc_par = (it >> 1) & 1;
             const bool ok = __all_sync(D1_FULL_MASK, mbar_wait(accf_bar(acc), acc_par, abort_flag));
@@ -329,12 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         tc_wait_ld();
                         if (EPI == EPI_BIAS_ACT) {
-                            const int col = col_base + c0;
-#pragma unroll
-                            for (int i = 0; i < 32; i++) {
-                                const float b = (a.bias && col + i < a.N) ? __ldg(a.bias + col + i) : 0.f;
-                                v[i] = apply_act(round_h(__uint_as_float(r[i])) + b, a.act);
-                            }
+                            bias_act32(a, col_base + c0, r, v);
                         } else {
 #pragma unroll
                             for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
@@ -468,12 +509,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int stage = 0;
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
-            for (int tile = pair; tile < a.num_tiles && !aborted; tile += npairs) {
+            for (int u = pair; u < a.num_units && !aborted; u += npairs) {
+                const int tile = u % a.num_tiles, kb0 = (u / a.num_tiles) * a.kb_per;
+                const int kb1 = min(a.num_kb, kb0 + a.kb_per);
                 int m_blk, n_blk;
                 tile_coords(a, tile, m_blk, n_blk);
                 const int arow = m_blk * 2 * BM + (int)rank * BM;
                 const int brow = EPI == EPI_SWIGLU ? (int)rank * a.F + n_blk * (BN / 2) : n_blk * BN + (int)rank * (BN / 2);
-                for (int kb = 0; kb < a.num_kb; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag)) {
                         record_error(a.err, abort_flag, kErrWaitEmpty);
                         aborted = true;
@@ -504,7 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int stage = 0, it = 0;
             uint32_t phase = 0;
             bool aborted = false;
-            for (int tile = pair; tile < a.num_tiles && !aborted; tile += npairs, it++) {
+            for (int u = pair; u < a.num_units && !aborted; u += npairs, it++) {
+                const int kb0 = (u / a.num_tiles) * a.kb_per, kb1 = min(a.num_kb, kb0 + a.kb_per);
                 const int acc = it & 1;
                 const uint32_t acc_par = (it >> 1) & 1;
                 if (!mbar_wait_cluster(acce_bar(acc), acc_par ^ 1, abort_flag)) {
@@ -513,7 +557,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * (TMEM_COLS / 2);
-                for (int kb = 0; kb < a.num_kb; kb++) {
+                for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
                         record_error(a.err, abort_flag, kErrWaitFull);
                         aborted = true;
@@ -524,7 +568,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++)
                         tc_mma_f16_pair(d_tmem, smem_desc_k128(a0 + k * 32), smem_desc_k128(b0 + k * 32), IDESC,
-                                        (kb | k) != 0);
+                                        ((kb - kb0) | k) != 0);
                     tc_commit_pair_both(empty_bar(stage));
                     if (++stage == STAGES) {
                         stage = 0;
@@ -546,7 +590,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         uint8_t* sbuf0 = epi_smem + ew * EPI_BUF;
         const uint32_t acce_leader0 = mapa_shared(acce_bar(0), 0), acce_leader1 = mapa_shared(acce_bar(1), 0);
         int sb = 0, it = 0;
-        for (int tile = pair; tile < a.num_tiles; tile += npairs, it++) {
+        for (int u = pair; u < a.num_units; u += npairs, it++) {
+            const int tile = u % a.num_tiles;
             const int acc = it & 1;
             const uint32_t acc_par = (it >> 1) & 1;
             const bool ok = __all_sync(D1_FULL_MASK, mbar_wait(accf_bar(acc), acc_par, abort_flag));
@@ -578,12 +623,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     } else {
                         tc_wait_ld();
                         if (EPI == EPI_BIAS_ACT) {
-                            const int col = col_base + c0;
-#pragma unroll
-                            for (int i = 0; i < 32; i++) {
-                                const float b = (a.bias && col + i < a.N) ? __ldg(a.bias + col + i) : 0.f;
-                                v[i] = apply_act(round_h(__uint_as_float(r[i])) + b, a.act);
-                            }
+                            bias_act32(a, col_base + c0, r, v);
                         } else {
 #pragma unroll
                             for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
@@ -727,7 +767,8 @@ struct TmapHash {
 // Tile plan: which kernel configuration runs a shape (the analogue of the reference's cuBLASLt algo choice).
 typedef std::tuple<int, int, int, int, int, int, int, int, int> PlanKey;  // N K ldx ldw ldy w_kn y_f32 epi bucket
 struct Plan {
-    int cfg;  // Cfg
+    int cfg;    // Cfg
+    int split;  // split-K factor (reduce-add epilogue only)
     float us;
 };
 
@@ -785,6 +826,14 @@ bool get_tmap(Ctx* c, CUtensorMap* out, const void* base, uint64_t inner, uint64
     return true;
 }
 
+// Split-K: a.kb_per holds the requested split on entry; every split gets a non-empty K range.
+void set_split(GemmArgs& a) {
+    int ks = a.kb_per < 1 ? 1 : a.kb_per;
+    if (ks > a.num_kb) ks = a.num_kb;
+    a.kb_per = (a.num_kb + ks - 1) / ks;
+    a.num_units = a.num_tiles * ((a.num_kb + a.kb_per - 1) / a.kb_per);
+}
+
 bool tc_ok(const void* X, int ldx, const void* W, int ldw, int w_kn, int K) {
     return !w_kn && K >= 1 && ldx % 8 == 0 && ldw % 8 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
 }
@@ -819,9 +868,10 @@ int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, i
     a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
     a.num_tiles = a.num_m * a.num_n;
     a.num_kb = (a.K + BK - 1) / BK;
+    set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    const int grid = a.num_tiles < c->num_sms ? a.num_tiles : c->num_sms;
+    const int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
     kern<<<grid, kThreads, S::BYTES, st>>>(ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
@@ -858,9 +908,10 @@ int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, 
     a.num_n = EPI == EPI_SWIGLU ? (a.F + BN / 2 - 1) / (BN / 2) : (a.N + BN - 1) / BN;
     a.num_tiles = a.num_m * a.num_n;
     a.num_kb = (a.K + BK - 1) / BK;
+    set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    const int pairs = a.num_tiles < c->pair_slots ? a.num_tiles : c->pair_slots;
+    const int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
     kern<<<2 * pairs, kPairThreads, S::BYTES, st>>>(ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
@@ -873,13 +924,13 @@ double wave_eff(long tiles, int sms) {
 
 // Kernel configurations a plan can name: the single-SM kernel with 128- or 256-column tiles, or the CTA-pair
 // kernel with 256 x 256 or 256 x 128 tiles.
-enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3 };
+enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3, CFG_1SM_64 = 4 };
 
 // Fraction of the SM-time the tiles keep busy (wave quantisation x column padding), per configuration.
 double cfg_eff(Ctx* c, int cfg, int M, int N) {
-    const bool pair = cfg >= CFG_PAIR_256;
+    const bool pair = cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128;
     const int bm = pair ? 2 * BM : BM;
-    const int bn = (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
+    const int bn = cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
     const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const int slots = pair ? c->pair_slots : c->num_sms;
     const double pad = (double)M * N / ((double)((M + bm - 1) / bm) * bm * ((N + bn - 1) / bn) * bn);
@@ -890,16 +941,35 @@ double cfg_eff(Ctx* c, int cfg, int M, int N) {
 // L2 operand bandwidth per FLOP), preferring the tile width that quantises better.
 int default_cfg(Ctx* c, int M, int N) {
     if (M >= 512) {
+        // 256x256 tiles read the fewest operand bytes per FLOP; 256x128 only for much better quantisation
         const double e256 = cfg_eff(c, CFG_PAIR_256, M, N), e128 = cfg_eff(c, CFG_PAIR_128, M, N);
-        return e128 > e256 + 0.05 ? CFG_PAIR_128 : CFG_PAIR_256;
+        return e128 > e256 + 0.15 ? CFG_PAIR_128 : CFG_PAIR_256;
     }
+    // small M is bound by reading W: narrow tiles put more SMs on it
+    const long mt = (M + BM - 1) / BM;
+    if (mt * ((N + 127) / 128) < c->num_sms / 2) return CFG_1SM_64;
+    if (mt * ((N + 255) / 256) < c->num_sms / 2) return CFG_1SM_128;
     const double e256 = cfg_eff(c, CFG_1SM_256, M, N), e128 = cfg_eff(c, CFG_1SM_128, M, N);
     return e128 > e256 + 0.08 ? CFG_1SM_128 : CFG_1SM_256;
 }
 
+// Split-K for the reduce-add epilogue (partial sums land in Y through TMA reduce-add): enough work units to
+// cover the SMs when the tiles alone leave most of them idle, keeping >= 4 K blocks per unit.
+int default_split(Ctx* c, int cfg, int M, int N, int K) {
+    const bool pair = cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128;
+    const int bm = pair ? 2 * BM : BM;
+    const int bn = cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
+    const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+    const int slots = pair ? c->pair_slots : c->num_sms;
+    const int kb = (K + BK - 1) / BK;
+    int split = 1;
+    while (tiles * split * 2 <= slots && kb / (split * 2) >= 4) split *= 2;
+    return split;
+}
+
 // Y = alpha X W^T + beta Y: TMA store (beta 0), TMA reduce-add (fp32 Y, beta 1), else direct stores.
-int run_store(Ctx* c, int cfg, int M, int N, int K, const void* X, int ldx, const void* W, int ldw, void* Y, int ldy,
-              int y_f32, float alpha, float beta, cudaStream_t st) {
+int run_store(Ctx* c, int cfg, int split, int M, int N, int K, const void* X, int ldx, const void* W, int ldw,
+              void* Y, int ldy, int y_f32, float alpha, float beta, cudaStream_t st) {
     GemmArgs a{};
     a.M = M;
     a.N = N;
@@ -911,6 +981,12 @@ int run_store(Ctx* c, int cfg, int M, int N, int K, const void* X, int ldx, cons
     a.beta = beta;
     const bool tma = tma_out_ok(Y, ldy, y_f32);
     const bool store = tma && beta == 0.f, add = tma && beta == 1.f && y_f32;
+    a.kb_per = add ? split : 1;  // split request (set_split turns it into K blocks per unit)
+    if (cfg == CFG_1SM_64 && (store || add)) {
+        if (add) return launch_tc<64, 8, EPI_ADD, true>(c, 20, X, ldx, W, ldw, N, a, st);
+        if (y_f32) return launch_tc<64, 8, EPI_STORE, true>(c, 21, X, ldx, W, ldw, N, a, st);
+        return launch_tc<64, 8, EPI_STORE, false>(c, 22, X, ldx, W, ldw, N, a, st);
+    }
     if (cfg == CFG_PAIR_256 && (store || add)) {
         if (add) return launch_tc2<256, 6, EPI_ADD, true>(c, 11, X, ldx, W, ldw, N, a, st);
         if (y_f32) return launch_tc2<256, 6, EPI_STORE, true>(c, 12, X, ldx, W, ldw, N, a, st);
@@ -921,7 +997,7 @@ int run_store(Ctx* c, int cfg, int M, int N, int K, const void* X, int ldx, cons
         if (y_f32) return launch_tc2<128, 8, EPI_STORE, true>(c, 15, X, ldx, W, ldw, N, a, st);
         return launch_tc2<128, 8, EPI_STORE, false>(c, 16, X, ldx, W, ldw, N, a, st);
     }
-    const bool b128 = cfg == CFG_1SM_128;
+    const bool b128 = cfg == CFG_1SM_128 || cfg == CFG_1SM_64;
     if (store) {
         if (y_f32)
             return b128 ? launch_tc<128, 6, EPI_STORE, true>(c, 0, X, ldx, W, ldw, N, a, st)
@@ -963,7 +1039,7 @@ void ensure(void** p, size_t* have, size_t need, uint32_t seed) {
 // ================================================================================================ C ABI
 extern "C" {
 
-const char* d1_build_id(void) { return "d1b200-tc-gemm-v3"; }
+const char* d1_build_id(void) { return "d1b200-tc-gemm-v4"; }
 
 void* d1_lt_init(size_t ws_bytes) {
     (void)ws_bytes;
@@ -1012,8 +1088,15 @@ int d1_lt_gemm(void* ctx, int M, int N, int K, const void* X, int ldx, const voi
     if (!tc_ok(X, ldx, W, ldw, w_kn, K))
         return run_simt(M, N, K, X, ldx, W, ldw, w_kn, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
     auto it = c->plans.find(PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, EPI_STORE, bucket_of(M)));
-    const int cfg = it != c->plans.end() ? it->second.cfg : default_cfg(c, M, N);
-    return run_store(c, cfg, M, N, K, X, ldx, W, ldw, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
+    int cfg, split;
+    if (it != c->plans.end()) {
+        cfg = it->second.cfg;
+        split = it->second.split;
+    } else {
+        cfg = default_cfg(c, M, N);
+        split = default_split(c, cfg, M, N, K);
+    }
+    return run_store(c, cfg, split, M, N, K, X, ldx, W, ldw, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
 }
 
 int d1_gemm_swiglu(void* ctx, int M, int F, int K, const d1_half* X, int ldx, const d1_half* W, int ldw,
@@ -1055,6 +1138,7 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
         case CFG_PAIR_256: return launch_tc2<256, 6, EPI_BIAS_ACT, false>(c, 18, X, ldx, W, ldw, N, a, st) ? -1 : 0;
         case CFG_PAIR_128: return launch_tc2<128, 8, EPI_BIAS_ACT, false>(c, 19, X, ldx, W, ldw, N, a, st) ? -1 : 0;
         case CFG_1SM_128: return launch_tc<128, 6, EPI_BIAS_ACT, false>(c, 9, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        case CFG_1SM_64: return launch_tc<64, 8, EPI_BIAS_ACT, false>(c, 23, X, ldx, W, ldw, N, a, st) ? -1 : 0;
         default: return launch_tc<256, 4, EPI_BIAS_ACT, false>(c, 10, X, ldx, W, ldw, N, a, st) ? -1 : 0;
     }
 }
@@ -1079,31 +1163,38 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
     cudaEventCreate(&e1);
     const int reps = M >= 4096 ? 5 : M >= 1024 ? 10 : 20;
     float best = 1e30f;
-    int best_cfg = CFG_1SM_256;
+    int best_cfg = CFG_1SM_256, best_split = 1;
     const bool tc = tc_ok(c->sx, ldx, c->sw, ldw, w_kn, K);
-    for (int cfg : {CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128}) {
-        auto run = [&]() {
-            return tc ? run_store(c, cfg, M, N, K, c->sx, ldx, c->sw, ldw, c->sy, ldy, y_f32, 1.f, y_f32 ? 1.f : 0.f, st)
-                      : run_simt(M, N, K, c->sx, ldx, c->sw, ldw, w_kn, c->sy, ldy, y_f32, 1.f, 0.f, st);
-        };
-        if (run() || run()) continue;
-        cudaEventRecord(e0, st);
-        for (int i = 0; i < reps; i++) run();
-        cudaEventRecord(e1, st);
-        cudaEventSynchronize(e1);
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, e0, e1);
-        const float us = ms * 1000.f / reps;
-        if (cudaGetLastError() == cudaSuccess && us < best) {
-            best = us;
-            best_cfg = cfg;
+    for (int cfg : {CFG_1SM_64, CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128}) {
+        for (int split : {1, 2, 4}) {
+            if (split > 1 && !y_f32) break;  // split-K only through the reduce-add epilogue
+            if ((K + BK - 1) / BK < 4 * split) break;
+            auto run = [&]() {
+                return tc ? run_store(c, cfg, split, M, N, K, c->sx, ldx, c->sw, ldw, c->sy, ldy, y_f32, 1.f,
+                                      y_f32 ? 1.f : 0.f, st)
+                          : run_simt(M, N, K, c->sx, ldx, c->sw, ldw, w_kn, c->sy, ldy, y_f32, 1.f, 0.f, st);
+            };
+            if (run() || run()) continue;
+            cudaEventRecord(e0, st);
+            for (int i = 0; i < reps; i++) run();
+            cudaEventRecord(e1, st);
+            cudaEventSynchronize(e1);
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, e0, e1);
+            const float us = ms * 1000.f / reps;
+            if (cudaGetLastError() == cudaSuccess && us < best) {
+                best = us;
+                best_cfg = cfg;
+                best_split = split;
+            }
+            if (!tc) break;
         }
         if (!tc) break;
     }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     if (best >= 1e29f) return -1.f;
-    c->plans[key] = Plan{best_cfg, best};
+    c->plans[key] = Plan{best_cfg, best_split, best};
     return best;
 }
 
@@ -1115,8 +1206,8 @@ int d1_lt_save(void* ctx, const char* path) {
     for (auto& kv : c->plans) {
         int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b;
         std::tie(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b) = kv.first;
-        fprintf(f, "%d %d %d %d %d %d %d %d %d %d %.2f\n", N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, kv.second.cfg,
-                kv.second.us);
+        fprintf(f, "%d %d %d %d %d %d %d %d %d %d %d %.2f\n", N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, kv.second.cfg,
+                kv.second.split, kv.second.us);
     }
     fclose(f);
     return 0;
@@ -1133,13 +1224,13 @@ int d1_lt_load(void* ctx, const char* path) {
     }
     int n = 0;
     while (true) {
-        int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, cfg;
+        int N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b, cfg, split;
         float us;
-        if (fscanf(f, "%d %d %d %d %d %d %d %d %d %d %f", &N, &K, &ldx, &ldw, &ldy, &w_kn, &y_f32, &epi, &b, &cfg,
-                   &us) != 11)
+        if (fscanf(f, "%d %d %d %d %d %d %d %d %d %d %d %f", &N, &K, &ldx, &ldw, &ldy, &w_kn, &y_f32, &epi, &b, &cfg,
+                   &split, &us) != 12)
             break;
-        if (cfg < CFG_1SM_128 || cfg > CFG_PAIR_128) continue;
-        c->plans[PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b)] = Plan{cfg, us};
+        if (cfg < CFG_1SM_128 || cfg > CFG_1SM_64 || split < 1 || split > 64) continue;
+        c->plans[PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b)] = Plan{cfg, split, us};
         n++;
     }
     fclose(f);

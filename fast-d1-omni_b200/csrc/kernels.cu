@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ s
 // keeps bx = b*u of the previous, current and next row in registers, so every row is read once by the CTA
 // (plus one halo row on each side) instead of three times. Sequence boundaries, the prefix's left state
 // (ext_bx) and the saved last state (save_bx) follow cuda/kernels.cu:224-259.
-constexpr int kConvRows = 16;
+constexpr int kConvRows = 8;
 
 struct ConvRow {
     float bx[8];

@@ -66,7 +66,7 @@ def test_config1_f16_out(gpu_lib, ctx, M, N, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("N,K", [(1024, 1024), (1024, 4608)])
-@pytest.mark.parametrize("M", [1, 3, 127, 129, 4096])
+@pytest.mark.parametrize("M", [1, 3, 127, 129, 512, 1000, 4096])
 def test_residual_f32(gpu_lib, ctx, M, N, K):
     """The trunk's residual projections: Y32 = X.W^T + Y32 (beta = 1, src/model.rs:373,390,396)."""
     g = torch.Generator(device="cuda").manual_seed(2)
