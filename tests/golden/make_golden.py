@@ -44,7 +44,7 @@ def main():
 
     out = {}
     for name, case in kernel_cases().items():
-        res = case.run(lib, pkg)
+        res = case.run(lib)
         for k, v in case.inputs.items():
             out[f"{name}/in/{k}"] = v
         for k, v in res.items():
