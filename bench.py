@@ -234,6 +234,9 @@ def main():
 
     w = text_weights(0)
     model = TextModel(w, device=local, cap_tokens=TOKENS)
+    # GEMM plan tuning at startup, as the reference's engine does (src/engine.rs:528-616): every trunk/head shape,
+    # every M bucket up to the batch budget; d1_lt_tune times this library's tile configurations and split-K.
+    n_tuned = model.tune(TOKENS)
     batches = [text_batch(1000 * rank + i, N_SEQS, SEQ_LEN) for i in range(4)]
     stream = torch.cuda.Stream(dev)
 
@@ -302,7 +305,8 @@ def main():
             "config": {"workload": f"text trunk+head forward (config-0 architecture), {TOKENS}-token batches of "
                                    f"{N_SEQS}x{SEQ_LEN} tokens, 3 markers per sequence",
                        "global_batch_tokens": TOKENS * world, "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2 (weights + activations > 700 MB)"},
+                       "l2": "inputs larger than L2 (weights + activations > 700 MB)",
+                       "gemm_plans": f"tuned at startup ({n_tuned} shape x bucket plans)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gemm_tflops_trunk_equiv": GEMM_FLOP_PER_TOKEN * value / world / 1e12,
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc2<256,6,EPI_SWIGLU> (w1|w3 + SwiGLU, CTA pair), M=8192",

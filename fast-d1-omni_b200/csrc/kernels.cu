@@ -245,23 +245,19 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ s
 }
 
 // ------------------------------------------------------------------------------------------------ short conv
-// bcu [T][3D] = [b | c | u]. Each CTA walks a run of kConvRows consecutive rows; a thread owns 8 channels and
-// keeps bx = b*u of the previous, current and next row in registers, so every row is read once by the CTA
-// (plus one halo row on each side) instead of three times. Sequence boundaries, the prefix's left state
+// bcu [T][3D] = [b | c | u]. Each CTA covers kConvRows consecutive rows; a thread owns 8 channels. All of the
+// thread's loads (b and u of rows t0-1 .. t0+kConvRows, c of its rows: 28 independent 16-byte loads) are issued
+// before any arithmetic, so the kernel runs at HBM bandwidth instead of one dependent row at a time; each row is
+// read once per CTA plus a one-row halo on each side (an L2 hit). Sequence boundaries, the prefix's left state
 // (ext_bx) and the saved last state (save_bx) follow cuda/kernels.cu:224-259.
 constexpr int kConvRows = 8;
 
-struct ConvRow {
-    float bx[8];
-};
-
-__device__ __forceinline__ void load_bx(const __half* bcu, size_t t, int D, int c, float* bx) {
-    float b[8], u[8];
-    const __half* row = bcu + t * 3 * D;
-    h8_to_f(__ldg(reinterpret_cast<const uint4*>(row + c)), b);
-    h8_to_f(__ldg(reinterpret_cast<const uint4*>(row + 2 * D + c)), u);
+__device__ __forceinline__ void mul8(const uint4& b, const uint4& u, float* bx) {
+    float fb[8], fu[8];
+    h8_to_f(b, fb);
+    h8_to_f(u, fu);
 #pragma unroll
-    for (int i = 0; i < 8; i++) bx[i] = b[i] * u[i];
+    for (int i = 0; i < 8; i++) bx[i] = fb[i] * fu[i];
 }
 
 __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bcu, const float* __restrict__ convw,
@@ -270,7 +266,21 @@ __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bc
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
     if (c >= D) return;
     const int t0 = blockIdx.x * kConvRows;
-    const int t1 = min(t0 + kConvRows, rows);
+    const size_t ld = (size_t)3 * D;
+    uint4 rb[kConvRows + 2], ru[kConvRows + 2], rc[kConvRows];
+    int sq[kConvRows];
+#pragma unroll
+    for (int j = 0; j < kConvRows + 2; j++) {
+        const int t = min(max(t0 - 1 + j, 0), rows - 1);
+        rb[j] = __ldg(reinterpret_cast<const uint4*>(bcu + t * ld + c));
+        ru[j] = __ldg(reinterpret_cast<const uint4*>(bcu + t * ld + 2 * D + c));
+    }
+#pragma unroll
+    for (int j = 0; j < kConvRows; j++) {
+        const int t = min(t0 + j, rows - 1);
+        rc[j] = __ldg(reinterpret_cast<const uint4*>(bcu + t * ld + D + c));
+        sq[j] = __ldg(tok_seq + t);
+    }
     float w0[8], w1[8], w2[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -278,55 +288,34 @@ __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bc
         w1[i] = __ldg(convw + (c + i) * 3 + 1);
         w2[i] = __ldg(convw + (c + i) * 3 + 2);
     }
-    float prev[8], cur[8], nxt[8];
-    load_bx(bcu, t0, D, c, cur);
-    int cur_seq = __ldg(tok_seq + t0);
-    if (t0 > 0 && __ldg(tok_seq + t0 - 1) == cur_seq) load_bx(bcu, t0 - 1, D, c, prev);
-#pragma unroll 1
-    for (int t = t0; t < t1; t++) {
-        const SeqInfo& s = seqs[cur_seq];
+#pragma unroll
+    for (int j = 0; j < kConvRows; j++) {
+        const int t = t0 + j;
+        if (t >= rows) break;
+        const SeqInfo& s = seqs[sq[j]];
         const int local = t - s.start;
         const bool has_left = local > 0, has_right = local + 1 < s.len;
-        float cc[8];
-        h8_to_f(__ldg(reinterpret_cast<const uint4*>(bcu + (size_t)t * 3 * D + D + c)), cc);
-        int nxt_seq = cur_seq;
-        if (has_right) {
-            load_bx(bcu, t + 1, D, c, nxt);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; i++) nxt[i] = 0.f;
-            if (s.save_bx) *reinterpret_cast<uint4*>(s.save_bx + (size_t)conv_idx * D + c) = f_to_h8(cur);
-            if (t + 1 < t1) {
-                nxt_seq = __ldg(tok_seq + t + 1);
-                load_bx(bcu, t + 1, D, c, nxt);
-            }
-        }
-        float l[8];
+        float cur[8], l[8], r[8], cc[8], y[8];
+        mul8(rb[j + 1], ru[j + 1], cur);
         if (has_left) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) l[i] = prev[i];
+            mul8(rb[j], ru[j], l);
         } else if (s.ext_bx) {
             h8_to_f(*reinterpret_cast<const uint4*>(s.ext_bx + (size_t)conv_idx * D + c), l);
         } else {
 #pragma unroll
             for (int i = 0; i < 8; i++) l[i] = 0.f;
         }
-        const float* r = nxt;
-        float y[8];
         if (has_right) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) y[i] = cc[i] * (w0[i] * l[i] + w1[i] * cur[i] + w2[i] * r[i]);
+            mul8(rb[j + 2], ru[j + 2], r);
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; i++) y[i] = cc[i] * (w0[i] * l[i] + w1[i] * cur[i] + w2[i] * 0.f);
+            for (int i = 0; i < 8; i++) r[i] = 0.f;
+            if (s.save_bx) *reinterpret_cast<uint4*>(s.save_bx + (size_t)conv_idx * D + c) = f_to_h8(cur);
         }
-        *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = f_to_h8(y);
+        h8_to_f(rc[j], cc);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            prev[i] = cur[i];
-            cur[i] = nxt[i];
-        }
-        cur_seq = nxt_seq;
+        for (int i = 0; i < 8; i++) y[i] = cc[i] * (w0[i] * l[i] + w1[i] * cur[i] + w2[i] * r[i]);
+        *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = f_to_h8(y);
     }
 }
 
