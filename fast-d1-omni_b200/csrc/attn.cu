@@ -5,7 +5,9 @@
 //   [ext prefix keys | local keys] of that sequence, kv head g = h / group, fp32 softmax, optional fp32 biases
 //   added to q/k/v as they are loaded.
 //
-// Design: one CTA per (64-query tile, kv head) runs all the query heads that share that kv head (GQA group 2:
+// Two kernels. Without biases (the trunk, media prefixes) the tcgen05 kernel below runs (S and O in TMEM, see
+// k_flash_attn_tc). With q/k/v biases (decision head, SigLIP2) an mma.sync kernel adds the biases as it loads:
+// one CTA per (64-query tile, kv head) runs all the query heads that share that kv head (GQA group 2:
 // 8 warps, two heads), so each K/V tile is fetched once for the group. Each warp owns 16 query rows of one head.
 // K/V tiles of 64 keys are double-buffered in shared memory with cp.async (bias-free case) so the next tile's
 // loads overlap this tile's math; QK^T and PV run on m16n8k16 fp16 tensor-core MMAs with fp32 accumulation,
@@ -272,6 +274,297 @@ __global__ void __launch_bounds__(128 * HPC) k_flash_attn(const FaArgs p) {
     }
 }
 
+// ---------------------------------------------------------------------------------------------- tcgen05 form
+// One CTA per (128-query tile, head), several CTAs per SM. TMEM holds S = Q.K^T (128 x 64 fp32, columns [0,64))
+// and the output accumulator O (128 x 64 fp32, columns [64,128)). Warps:
+//   0-3  softmax: thread t owns query row t (TMEM lane t): reads its S row, online softmax in the exp2 domain,
+//        writes P (fp16) to shared memory as the A operand of P.V, rescales its O row in TMEM when its running
+//        max rises, and finally writes O / l.
+//   4    loader: Q, then K/V tiles of 64 keys ([ext prefix keys | local keys]) into a 2-stage ring, cp.async into
+//        the 128-byte-swizzled K-major layout (V is read as the MN-major B operand of P.V: same bytes).
+//   5    TMEM allocation and the MMA issuer: S_j = Q.K_j^T (M=128, N=64, K=64), then O += P_j.V_j (M=128, N=64,
+//        K=64), with S_{j+1} issued as soon as the softmax has read S_j.
+// Work items are the reference's 64-row query tiles; a CTA whose tile starts at an odd multiple of 64 has nothing
+// to do (the even tile before it covers 128 rows).
+constexpr int TQ = 128;                  // query rows per CTA
+constexpr int TKV = 64;                  // keys per K/V tile
+constexpr int T_Q_BYTES = TQ * 128;      // 128 rows x 64 dims fp16
+constexpr int T_KV_BYTES = TKV * 128;
+constexpr int T_P_BYTES = TQ * TKV * 2;  // 64-key blocks of 128 rows x 128 B
+constexpr uint32_t T_TMEM_COLS = TKV + 64 <= 128 ? 128 : 256;
+constexpr int T_SMEM = T_Q_BYTES + 2 * 2 * T_KV_BYTES + T_P_BYTES + 16 * 8 + 16;  // 2 CTAs fit one SM
+
+// Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
+__device__ int g_fa_err = 0;
+
+struct FaTcArgs {
+    const __half* Q;
+    const __half* K;
+    const __half* V;
+    __half* O;
+    const AttnSeq* seqs;
+    const int2* work;
+    int ldq, ldkv, ext_ld, ldo, group;
+    float scale_log2;
+    int* err;
+};
+
+__device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void record_err(int* err, volatile int* abort_flag, int code) {
+    *abort_flag = 1;
+    if (err) atomicExch(err, code);
+}
+
+__device__ __forceinline__ bool mbar_wait_timed2(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    return true;
+}
+
+__device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+__global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
+    constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
+    constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw;  // the 128-byte swizzle needs 1024-byte aligned tiles: checked below
+    uint8_t* sQ = smem;
+    uint8_t* sKV = smem + T_Q_BYTES;                 // stage s: K at s * 2 * T_KV_BYTES, V right after
+    uint8_t* sP = sKV + 2 * 2 * T_KV_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + T_P_BYTES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const uint32_t q_full = smem_u32(bars + 0), s_full = smem_u32(bars + 1), s_free = smem_u32(bars + 2);
+    const uint32_t p_full = smem_u32(bars + 3), o_done = smem_u32(bars + 4);
+    auto kv_full = [&](int s) { return smem_u32(bars + 5 + s); };
+    auto kv_empty = [&](int s) { return smem_u32(bars + 7 + s); };
+
+    const int2 wi = a.work[blockIdx.x];
+    if (wi.y % TQ) return;  // covered by the 128-row tile before it
+    if (smem_u32(smem_raw) & 1023) {  // never expected: dynamic shared memory starts at the window base
+        if (threadIdx.x == 0 && a.err) atomicExch(a.err, kErrDrain);
+        return;
+    }
+    const AttnSeq sq = a.seqs[wi.x];
+    const int q0 = wi.y, h = blockIdx.y, g = h / a.group;
+    const int total = sq.ext_len + sq.kv_len;
+    const int nt = (total + TKV - 1) / TKV;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 32);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_done, 1);
+        mbar_init(smem_u32(bars + 9), 1);  // drain
+        for (int s = 0; s < 2; s++) {
+            mbar_init(kv_full(s), 32);
+            mbar_init(kv_empty(s), 1);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(smem_u32(tmem_slot), T_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------------ loader
+        bool ok = true;
+        for (int c = lane; c < TQ * 8; c += 32) {
+            const int r = c >> 3, ch = c & 7;
+            const bool v = q0 + r < sq.q_len;
+            const __half* src = v ? a.Q + (size_t)(sq.q_start + q0 + r) * a.ldq + h * 64 + ch * 8 : a.Q;
+            cp_async16z(smem_u32(sQ + r * 128 + ((ch ^ (r & 7)) << 4)), src, v ? 16 : 0);
+        }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        fence_async_smem_cta();
+        mbar_arrive(q_full);
+        for (int j = 0; j < nt && ok; j++) {
+            const int s = j & 1;
+            if (!__all_sync(D1_FULL_MASK, mbar_wait(kv_empty(s), ((j >> 1) & 1) ^ 1, abort_flag))) {
+                if (lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
+                break;
+            }
+            uint8_t* dK = sKV + s * 2 * T_KV_BYTES;
+            uint8_t* dV = dK + T_KV_BYTES;
+            for (int c = lane; c < TKV * 8; c += 32) {
+                const int r = c >> 3, ch = c & 7;
+                const int key = j * TKV + r;
+                const __half *srck = a.K, *srcv = a.V;
+                int bytes = 0;
+                if (key < sq.ext_len) {
+                    srck = sq.ext_k + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                    srcv = sq.ext_v + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                    bytes = 16;
+                } else if (key < total) {
+                    const size_t row = (size_t)(sq.kv_start + key - sq.ext_len) * a.ldkv + g * 64 + ch * 8;
+                    srck = a.K + row;
+                    srcv = a.V + row;
+                    bytes = 16;
+                }
+                const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
+                cp_async16z(smem_u32(dK + off), srck, bytes);
+                cp_async16z(smem_u32(dV + off), srcv, bytes);
+            }
+            asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+            fence_async_smem_cta();
+            mbar_arrive(kv_full(s));
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t tS = tmem, tO = tmem + TKV;
+            const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+            bool ok = mbar_wait(q_full, 0, abort_flag);
+            auto issue_s = [&](int j) {
+                const uint32_t k_addr = smem_u32(sKV + (j & 1) * 2 * T_KV_BYTES);
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    tc_mma_f16(tS, smem_desc_k128(q_addr + k * 32), smem_desc_k128(k_addr + k * 32), IDESC_S, k != 0);
+                tc_commit(s_full);
+            };
+            if (ok && nt > 0) {
+                ok = mbar_wait(kv_full(0), 0, abort_flag);
+                if (ok) {
+                    tc_fence_after();
+                    issue_s(0);
+                }
+            }
+            for (int j = 0; j < nt && ok; j++) {
+                if (j + 1 < nt) {
+                    ok = mbar_wait(kv_full((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag) && mbar_wait(s_free, j & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+                if (!(ok = mbar_wait(p_full, j & 1, abort_flag))) break;
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(sKV + (j & 1) * 2 * T_KV_BYTES + T_KV_BYTES);
+#pragma unroll
+                for (int k = 0; k < TKV / 16; k++)
+                    tc_mma_f16(tO, smem_desc_k128(p_addr + (k >> 2) * (TQ * 128) + (k & 3) * 32),
+                               smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
+                tc_commit(kv_empty(j & 1));
+                tc_commit(o_done);
+            }
+            if (!ok) record_err(a.err, abort_flag, kErrWaitFull);
+            tc_commit(s_free + 0 * 0 ? 0 : smem_u32(bars + 9));  // drain: every issued MMA completes
+            if (!mbar_wait_timed2(smem_u32(bars + 9), 0)) record_err(a.err, abort_flag, kErrDrain);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ softmax (warps 0-3, row = thread)
+        const int row = warp * 32 + lane;
+        const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16), tO = tS + TKV;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt; j++) {
+            if (!__all_sync(D1_FULL_MASK, mbar_wait(s_full, j & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[TKV];
+#pragma unroll
+            for (int c = 0; c < TKV / 32; c++) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+            const int kbase = j * TKV;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < TKV; c++) {
+                const float v = kbase + c < total ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
+                sr[c] = __float_as_uint(v);
+                mx = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m, mx);
+            const float alpha = exp2f(m - m_new);
+            float rs = 0.f;
+            // wait until P.V of the previous tile has consumed P and updated O
+            if (j > 0 && !__all_sync(D1_FULL_MASK, mbar_wait(o_done, (j - 1) & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {
+                uint32_t o[32];
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    tmem_ld32(tO + c * 32, o);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+                tc_wait_st();
+            }
+#pragma unroll
+            for (int half = 0; half < TKV / 64; half++) {
+                uint8_t* prow = sP + half * (TQ * 128) + row * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++) {
+                    float p[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        p[e] = exp2f(__uint_as_float(sr[half * 64 + ch * 8 + e]) - m_new);
+                        rs += p[e];
+                    }
+                    *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
+                        make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+                }
+            }
+            fence_async_smem_cta();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            l = l * alpha + rs;
+            m = m_new;
+        }
+        if (ok && nt > 0 && __all_sync(D1_FULL_MASK, mbar_wait(o_done, (nt - 1) & 1, abort_flag))) {
+            tc_fence_after();
+            const float il = l > 0.f ? 1.f / l : 0.f;
+            const bool store = q0 + row < sq.q_len;
+            __half* orow = a.O + (size_t)(sq.q_start + q0 + row) * a.ldo + h * 64;
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32, o);
+                tc_wait_ld();
+                if (store) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = make_uint4(
+                            pack_h2(__uint_as_float(o[8 * q]) * il, __uint_as_float(o[8 * q + 1]) * il),
+                            pack_h2(__uint_as_float(o[8 * q + 2]) * il, __uint_as_float(o[8 * q + 3]) * il),
+                            pack_h2(__uint_as_float(o[8 * q + 4]) * il, __uint_as_float(o[8 * q + 5]) * il),
+                            pack_h2(__uint_as_float(o[8 * q + 6]) * il, __uint_as_float(o[8 * q + 7]) * il));
+                }
+            }
+        } else if (nt > 0 && lane == 0) {
+            record_err(a.err, abort_flag, kErrWaitAccFull);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, T_TMEM_COLS);
+    }
+}
+
 template <int HPC, bool BIAS>
 int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
     constexpr size_t smem = (size_t)(HPC * FA_B * FA_LD + 4 * FA_B * FA_LD) * sizeof(__half);
@@ -291,7 +584,32 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
     return (int)cudaGetLastError();
 }
 
+int launch_fa_tc(const FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
+    static unsigned long long attr_done = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(__atomic_load_n(&attr_done, __ATOMIC_ACQUIRE) & bit)) {
+        if (cudaFuncSetAttribute(k_flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, T_SMEM) != cudaSuccess)
+            return -1;
+        __atomic_fetch_or(&attr_done, bit, __ATOMIC_RELEASE);
+    }
+    dim3 grid(n_work, heads);
+    k_flash_attn_tc<<<grid, 192, T_SMEM, st>>>(a);
+    return (int)cudaGetLastError();
+}
+
 }  // namespace
+
+extern "C" int d1_flash_attn_error(void) {
+    int e = 0;
+    if (cudaMemcpyFromSymbol(&e, g_fa_err, sizeof(int)) != cudaSuccess) return -1;
+    if (e) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_fa_err, &z, sizeof(int));
+    }
+    return e;
+}
 
 extern "C" int d1_flash_attn(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
                              const float* bq, const float* bk, const float* bv, d1_half* O, int ldo,
@@ -317,6 +635,28 @@ extern "C" int d1_flash_attn(const d1_half* Q, int ldq, const d1_half* K, const 
     a.group = group;
     a.scale_log2 = scale * 1.4426950408889634f;
     const bool bias = bq || bk || bv;
+    if (!bias) {  // the trunk and media-prefix forms: tcgen05 kernel
+        FaTcArgs t;
+        t.Q = Q;
+        t.K = K;
+        t.V = V;
+        t.O = O;
+        t.seqs = seqs;
+        t.work = reinterpret_cast<const int2*>(work);
+        t.ldq = ldq;
+        t.ldkv = ldkv;
+        t.ext_ld = ext_ld;
+        t.ldo = ldo;
+        t.group = group;
+        t.scale_log2 = scale * 1.4426950408889634f;
+        static int* err_addr[64] = {};  // device address of g_fa_err, per device
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!err_addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&err_addr[dev & 63]), g_fa_err) != cudaSuccess)
+            return -1;
+        t.err = err_addr[dev & 63];
+        return launch_fa_tc(t, n_work, heads, st);
+    }
     if (group == 2) {
         const int gy = heads / 2;
         return bias ? launch_fa<2, true>(a, n_work, gy, st) : launch_fa<2, false>(a, n_work, gy, st);

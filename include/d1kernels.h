@@ -213,6 +213,10 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
  * on a bounded wait (the kernel returns early instead of hanging; its output is then undefined). */
 int d1_lt_error(void* ctx);
 
+/* extension — reads and clears the attention kernels' device error word (nonzero: a kernel gave up on a bounded
+ * wait and returned early; its output is undefined). */
+int d1_flash_attn_error(void);
+
 /* extension — releases a context made by d1_lt_init (the reference never frees it). */
 void d1_lt_destroy(void* ctx);
 

@@ -45,6 +45,8 @@ def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, e
                           P(work), n_work, heads, group, 0.125, st)
     assert r == 0
     torch.cuda.synchronize()
+    if hasattr(lib, "d1_flash_attn_error"):
+        assert lib.d1_flash_attn_error() == 0
     return O_.float().cpu().numpy()
 
 
@@ -53,7 +55,7 @@ def lognormal(total, seed=2):
     return lognormal_lengths(seed, total)
 
 
-@pytest.mark.parametrize("total", [2048, 8192])
+@pytest.mark.parametrize("total", [2048, 8192, 16384])
 def test_config2_gqa(pkg, gpu_lib, ref_lib, total):
     lens = lognormal(total)
     g = torch.Generator(device="cuda").manual_seed(2)
