@@ -459,8 +459,9 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
                 tc_commit(o_done);
             }
             if (!ok) record_err(a.err, abort_flag, kErrWaitFull);
-            tc_commit(s_free + 0 * 0 ? 0 : smem_u32(bars + 9));  // drain: every issued MMA completes
-            if (!mbar_wait_timed2(smem_u32(bars + 9), 0)) record_err(a.err, abort_flag, kErrDrain);
+            const uint32_t drain = smem_u32(bars + 9);
+            tc_commit(drain);  // drain: every issued MMA has completed before TMEM is released
+            if (!mbar_wait_timed2(drain, 0)) record_err(a.err, abort_flag, kErrDrain);
         }
         __syncwarp();
     } else {
