@@ -275,24 +275,29 @@ __global__ void __launch_bounds__(128 * HPC) k_flash_attn(const FaArgs p) {
 }
 
 // ---------------------------------------------------------------------------------------------- tcgen05 form
-// One CTA per (128-query tile, head), several CTAs per SM. TMEM holds S = Q.K^T (128 x 64 fp32, columns [0,64))
-// and the output accumulator O (128 x 64 fp32, columns [64,128)). Warps:
+// Persistent CTAs (2 per SM) loop over units = (128-query tile, head); the reference's work list holds 64-row
+// tiles, so a unit starts at every item whose first row is a multiple of 128 and the other items are skipped.
+// TMEM per CTA: S = Q.K^T (128 x 64 fp32, columns [0,64)) and the output accumulator O (128 x 64 fp32, [64,128)).
+// Warps:
 //   0-3  softmax: thread t owns query row t (TMEM lane t): reads its S row, online softmax in the exp2 domain,
-//        writes P (fp16) to shared memory as the A operand of P.V, rescales its O row in TMEM when its running
-//        max rises, and finally writes O / l.
-//   4    loader: Q, then K/V tiles of 64 keys ([ext prefix keys | local keys]) into a 2-stage ring, cp.async into
-//        the 128-byte-swizzled K-major layout (V is read as the MN-major B operand of P.V: same bytes).
+//        writes P (fp16) into shared memory as the A operand of P.V, rescales its O row in TMEM when its running
+//        max rises, and at the end of a unit writes O / l to global memory.
+//   4    loader: Q of each unit into a 2-slot ring, K/V tiles of 64 keys ([ext prefix keys | local keys]) into a
+//        3-stage ring, with cp.async into the 128-byte-swizzled K-major layout (V is the MN-major B operand of
+//        P.V: same bytes). Several copy groups stay in flight; each is signalled when it lands.
 //   5    TMEM allocation and the MMA issuer: S_j = Q.K_j^T (M=128, N=64, K=64), then O += P_j.V_j (M=128, N=64,
-//        K=64), with S_{j+1} issued as soon as the softmax has read S_j.
-// Work items are the reference's 64-row query tiles; a CTA whose tile starts at an odd multiple of 64 has nothing
-// to do (the even tile before it covers 128 rows).
-constexpr int TQ = 128;                  // query rows per CTA
+//        K=64); S_{j+1} is issued as soon as the softmax has read S_j, so the tensor core works while it exps.
+// Loads for the next unit are issued while the current one is computed, which hides the copy latency that a
+// one-unit-per-CTA kernel exposes on short sequences.
+constexpr int TQ = 128;                  // query rows per unit
 constexpr int TKV = 64;                  // keys per K/V tile
+constexpr int T_QSLOTS = 2, T_KVSTAGES = 3;
 constexpr int T_Q_BYTES = TQ * 128;      // 128 rows x 64 dims fp16
 constexpr int T_KV_BYTES = TKV * 128;
-constexpr int T_P_BYTES = TQ * TKV * 2;  // 64-key blocks of 128 rows x 128 B
-constexpr uint32_t T_TMEM_COLS = TKV + 64 <= 128 ? 128 : 256;
-constexpr int T_SMEM = T_Q_BYTES + 2 * 2 * T_KV_BYTES + T_P_BYTES + 16 * 8 + 16;  // 2 CTAs fit one SM
+constexpr int T_P_BYTES = TQ * TKV * 2;
+constexpr uint32_t T_TMEM_COLS = 128;
+constexpr int T_NBARS = 2 * T_QSLOTS + 2 * T_KVSTAGES + 6;
+constexpr int T_SMEM = T_QSLOTS * T_Q_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + T_P_BYTES + T_NBARS * 8 + 16;
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
 __device__ int g_fa_err = 0;
@@ -304,6 +309,8 @@ struct FaTcArgs {
     __half* O;
     const AttnSeq* seqs;
     const int2* work;
+    int n_units;  // work items x heads
+    int heads;
     int ldq, ldkv, ext_ld, ldo, group;
     float scale_log2;
     int* err;
@@ -327,45 +334,66 @@ __device__ __forceinline__ void cp_async16z(uint32_t dst, const void* src, int b
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
 
+// 2^x with the hardware approximation (relative error ~2^-22, far below the fp16 rounding of P).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// A unit: work item w (its 64-row query tile must start at a multiple of 128) and head h.
+struct Unit {
+    AttnSeq s;
+    int q0, h, nt;
+};
+__device__ __forceinline__ bool unit_at(const FaTcArgs& a, int u, Unit& out) {
+    const int2 wi = a.work[u / a.heads];
+    if (wi.y % TQ) return false;
+    out.s = a.seqs[wi.x];
+    out.q0 = wi.y;
+    out.h = u % a.heads;
+    out.nt = (out.s.ext_len + out.s.kv_len + TKV - 1) / TKV;
+    return out.nt > 0 && out.s.q_len > out.q0;  // units with no keys or no queries are skipped by every role
+}
+
 __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = smem_raw;  // the 128-byte swizzle needs 1024-byte aligned tiles: checked below
-    uint8_t* sQ = smem;
-    uint8_t* sKV = smem + T_Q_BYTES;                 // stage s: K at s * 2 * T_KV_BYTES, V right after
-    uint8_t* sP = sKV + 2 * 2 * T_KV_BYTES;
+    uint8_t* sQ = smem_raw;  // the 128-byte swizzle needs 1024-byte aligned tiles: checked below
+    uint8_t* sKV = sQ + T_QSLOTS * T_Q_BYTES;  // stage s: K at s * 2 * T_KV_BYTES, V right after
+    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sP + T_P_BYTES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + T_NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    const uint32_t q_full = smem_u32(bars + 0), s_full = smem_u32(bars + 1), s_free = smem_u32(bars + 2);
-    const uint32_t p_full = smem_u32(bars + 3), o_done = smem_u32(bars + 4);
-    auto kv_full = [&](int s) { return smem_u32(bars + 5 + s); };
-    auto kv_empty = [&](int s) { return smem_u32(bars + 7 + s); };
+    auto q_full = [&](int i) { return smem_u32(bars + i); };
+    auto q_empty = [&](int i) { return smem_u32(bars + T_QSLOTS + i); };
+    auto kv_full = [&](int i) { return smem_u32(bars + 2 * T_QSLOTS + i); };
+    auto kv_empty = [&](int i) { return smem_u32(bars + 2 * T_QSLOTS + T_KVSTAGES + i); };
+    const uint32_t s_full = smem_u32(bars + 2 * T_QSLOTS + 2 * T_KVSTAGES);
+    const uint32_t s_free = s_full + 8, p_full = s_full + 16, o_done = s_full + 24, o_free = s_full + 32;
+    const uint32_t drain = s_full + 40;
 
-    const int2 wi = a.work[blockIdx.x];
-    if (wi.y % TQ) return;  // covered by the 128-row tile before it
     if (smem_u32(smem_raw) & 1023) {  // never expected: dynamic shared memory starts at the window base
         if (threadIdx.x == 0 && a.err) atomicExch(a.err, kErrDrain);
         return;
     }
-    const AttnSeq sq = a.seqs[wi.x];
-    const int q0 = wi.y, h = blockIdx.y, g = h / a.group;
-    const int total = sq.ext_len + sq.kv_len;
-    const int nt = (total + TKV - 1) / TKV;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 32);
+        for (int i = 0; i < T_QSLOTS; i++) {
+            mbar_init(q_full(i), 32);
+            mbar_init(q_empty(i), 1);
+        }
+        for (int i = 0; i < T_KVSTAGES; i++) {
+            mbar_init(kv_full(i), 32);
+            mbar_init(kv_empty(i), 1);
+        }
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
         mbar_init(p_full, 4);
         mbar_init(o_done, 1);
-        mbar_init(smem_u32(bars + 9), 1);  // drain
-        for (int s = 0; s < 2; s++) {
-            mbar_init(kv_full(s), 32);
-            mbar_init(kv_empty(s), 1);
-        }
+        mbar_init(o_free, 4);
+        mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -380,87 +408,135 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
 
     if (warp == 4) {
         // ------------------------------------------------------------------ loader
-        bool ok = true;
-        for (int c = lane; c < TQ * 8; c += 32) {
-            const int r = c >> 3, ch = c & 7;
-            const bool v = q0 + r < sq.q_len;
-            const __half* src = v ? a.Q + (size_t)(sq.q_start + q0 + r) * a.ldq + h * 64 + ch * 8 : a.Q;
-            cp_async16z(smem_u32(sQ + r * 128 + ((ch ^ (r & 7)) << 4)), src, v ? 16 : 0);
-        }
-        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-        fence_async_smem_cta();
-        mbar_arrive(q_full);
-        for (int j = 0; j < nt && ok; j++) {
-            const int s = j & 1;
-            if (!__all_sync(D1_FULL_MASK, mbar_wait(kv_empty(s), ((j >> 1) & 1) ^ 1, abort_flag))) {
-                if (lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
-                break;
-            }
-            uint8_t* dK = sKV + s * 2 * T_KV_BYTES;
-            uint8_t* dV = dK + T_KV_BYTES;
-            for (int c = lane; c < TKV * 8; c += 32) {
-                const int r = c >> 3, ch = c & 7;
-                const int key = j * TKV + r;
-                const __half *srck = a.K, *srcv = a.V;
-                int bytes = 0;
-                if (key < sq.ext_len) {
-                    srck = sq.ext_k + (size_t)key * a.ext_ld + g * 64 + ch * 8;
-                    srcv = sq.ext_v + (size_t)key * a.ext_ld + g * 64 + ch * 8;
-                    bytes = 16;
-                } else if (key < total) {
-                    const size_t row = (size_t)(sq.kv_start + key - sq.ext_len) * a.ldkv + g * 64 + ch * 8;
-                    srck = a.K + row;
-                    srcv = a.V + row;
-                    bytes = 16;
-                }
-                const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
-                cp_async16z(smem_u32(dK + off), srck, bytes);
-                cp_async16z(smem_u32(dV + off), srcv, bytes);
-            }
-            asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        // Copy groups in flight, oldest first: the barrier each one signals when it lands (at most 4).
+        uint32_t pend[4];
+        int npend = 0;
+        auto land_oldest = [&](bool all) {
+            if (all)
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+            else
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
             fence_async_smem_cta();
-            mbar_arrive(kv_full(s));
+            const int n = all ? npend : npend - 1;
+            for (int i = 0; i < n; i++) mbar_arrive(pend[i]);
+            for (int i = n; i < npend; i++) pend[i - n] = pend[i];
+            npend -= n;
+        };
+        // wait for a free slot; never block while a landed copy is still unsignalled
+        auto acquire = [&](uint32_t bar, uint32_t parity) -> bool {
+            if (!__all_sync(D1_FULL_MASK, mbar_try_wait(bar, parity))) {
+                if (npend) land_oldest(true);
+                return __all_sync(D1_FULL_MASK, mbar_wait(bar, parity, abort_flag)) != 0;
+            }
+            return true;
+        };
+        int qi = 0, ki = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
+            Unit un;
+            if (!unit_at(a, u, un)) continue;
+            const int g = un.h / a.group, total = un.s.ext_len + un.s.kv_len;
+            const int qs = qi % T_QSLOTS;
+            if (!(ok = acquire(q_empty(qs), ((qi / T_QSLOTS) & 1) ^ 1))) break;
+            uint8_t* dq = sQ + qs * T_Q_BYTES;
+            for (int c = lane; c < TQ * 8; c += 32) {
+                const int r = c >> 3, ch = c & 7;
+                const bool v = un.q0 + r < un.s.q_len;
+                const __half* src = v ? a.Q + (size_t)(un.s.q_start + un.q0 + r) * a.ldq + un.h * 64 + ch * 8 : a.Q;
+                cp_async16z(smem_u32(dq + r * 128 + ((ch ^ (r & 7)) << 4)), src, v ? 16 : 0);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            pend[npend++] = q_full(qs);
+            if (npend > 2) land_oldest(false);
+            qi++;
+            for (int j = 0; j < un.nt; j++) {
+                const int s = ki % T_KVSTAGES;
+                if (!(ok = acquire(kv_empty(s), ((ki / T_KVSTAGES) & 1) ^ 1))) break;
+                uint8_t* dK = sKV + s * 2 * T_KV_BYTES;
+                uint8_t* dV = dK + T_KV_BYTES;
+                for (int c = lane; c < TKV * 8; c += 32) {
+                    const int r = c >> 3, ch = c & 7;
+                    const int key = j * TKV + r;
+                    const __half *srck = a.K, *srcv = a.V;
+                    int bytes = 0;
+                    if (key < un.s.ext_len) {
+                        srck = un.s.ext_k + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                        srcv = un.s.ext_v + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                        bytes = 16;
+                    } else if (key < total) {
+                        const size_t row = (size_t)(un.s.kv_start + key - un.s.ext_len) * a.ldkv + g * 64 + ch * 8;
+                        srck = a.K + row;
+                        srcv = a.V + row;
+                        bytes = 16;
+                    }
+                    const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
+                    cp_async16z(smem_u32(dK + off), srck, bytes);
+                    cp_async16z(smem_u32(dV + off), srcv, bytes);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                pend[npend++] = kv_full(s);
+                if (npend > 2) land_oldest(false);
+                ki++;
+            }
         }
+        if (npend) land_oldest(true);
+        if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
     } else if (warp == 5) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t tS = tmem, tO = tmem + TKV;
-            const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
-            bool ok = mbar_wait(q_full, 0, abort_flag);
-            auto issue_s = [&](int j) {
-                const uint32_t k_addr = smem_u32(sKV + (j & 1) * 2 * T_KV_BYTES);
+            const uint32_t p_addr = smem_u32(sP);
+            int qi = 0, ki = 0, ui = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
+                Unit un;
+                if (!unit_at(a, u, un)) continue;
+                const int qs = qi % T_QSLOTS;
+                if (!(ok = mbar_wait(q_full(qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
+                const uint32_t q_addr = smem_u32(sQ + qs * T_Q_BYTES);
+                auto issue_s = [&](int kidx) {  // S = Q . K^T for the tile in ring slot kidx
+                    const uint32_t k_addr = smem_u32(sKV + (kidx % T_KVSTAGES) * 2 * T_KV_BYTES);
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    tc_mma_f16(tS, smem_desc_k128(q_addr + k * 32), smem_desc_k128(k_addr + k * 32), IDESC_S, k != 0);
-                tc_commit(s_full);
-            };
-            if (ok && nt > 0) {
-                ok = mbar_wait(kv_full(0), 0, abort_flag);
-                if (ok) {
-                    tc_fence_after();
-                    issue_s(0);
-                }
-            }
-            for (int j = 0; j < nt && ok; j++) {
-                if (j + 1 < nt) {
-                    ok = mbar_wait(kv_full((j + 1) & 1), ((j + 1) >> 1) & 1, abort_flag) && mbar_wait(s_free, j & 1, abort_flag);
+                    for (int k = 0; k < 4; k++)
+                        tc_mma_f16(tS, smem_desc_k128(q_addr + k * 32), smem_desc_k128(k_addr + k * 32), IDESC_S,
+                                   k != 0);
+                    tc_commit(s_full);
+                };
+                // S_0 of this unit: its K tile has landed and the softmax has read the previous S
+                ok = mbar_wait(kv_full(ki % T_KVSTAGES), (ki / T_KVSTAGES) & 1, abort_flag) &&
+                     (ki == 0 || mbar_wait(s_free, (ki - 1) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                issue_s(ki);
+                for (int j = 0; j < un.nt && ok; j++) {
+                    const int kj = ki + j;
+                    if (j + 1 < un.nt) {
+                        ok = mbar_wait(kv_full((kj + 1) % T_KVSTAGES), ((kj + 1) / T_KVSTAGES) & 1, abort_flag) &&
+                             mbar_wait(s_free, kj & 1, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(kj + 1);
+                    }
+                    ok = mbar_wait(p_full, kj & 1, abort_flag) &&
+                         (j > 0 || ui == 0 || mbar_wait(o_free, (ui - 1) & 1, abort_flag));
                     if (!ok) break;
                     tc_fence_after();
-                    issue_s(j + 1);
-                }
-                if (!(ok = mbar_wait(p_full, j & 1, abort_flag))) break;
-                tc_fence_after();
-                const uint32_t v_addr = smem_u32(sKV + (j & 1) * 2 * T_KV_BYTES + T_KV_BYTES);
+                    const uint32_t v_addr = smem_u32(sKV + (kj % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
 #pragma unroll
-                for (int k = 0; k < TKV / 16; k++)
-                    tc_mma_f16(tO, smem_desc_k128(p_addr + (k >> 2) * (TQ * 128) + (k & 3) * 32),
-                               smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                tc_commit(kv_empty(j & 1));
-                tc_commit(o_done);
+                    for (int k = 0; k < TKV / 16; k++)
+                        tc_mma_f16(tO, smem_desc_k128(p_addr + k * 32), smem_desc_k128(v_addr + k * 2048), IDESC_O,
+                                   (j | k) != 0);
+                    tc_commit(kv_empty(kj % T_KVSTAGES));
+                    tc_commit(o_done);
+                }
+                if (!ok) break;
+                tc_commit(q_empty(qs));
+                ki += un.nt;
+                qi++;
+                ui++;
             }
             if (!ok) record_err(a.err, abort_flag, kErrWaitFull);
-            const uint32_t drain = smem_u32(bars + 9);
-            tc_commit(drain);  // drain: every issued MMA has completed before TMEM is released
+            tc_commit(drain);  // every issued MMA has completed before TMEM is released
             if (!mbar_wait_timed2(drain, 0)) record_err(a.err, abort_flag, kErrDrain);
         }
         __syncwarp();
@@ -468,95 +544,98 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
         // ------------------------------------------------------------------ softmax (warps 0-3, row = thread)
         const int row = warp * 32 + lane;
         const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16), tO = tS + TKV;
-        float m = -INFINITY, l = 0.f;
+        int ki = 0;
         bool ok = true;
-        for (int j = 0; j < nt; j++) {
-            if (!__all_sync(D1_FULL_MASK, mbar_wait(s_full, j & 1, abort_flag))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[TKV];
+        for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
+            Unit un;
+            if (!unit_at(a, u, un)) continue;
+            const int total = un.s.ext_len + un.s.kv_len;
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < un.nt; j++) {
+                const int kj = ki + j;
+                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(s_full, kj & 1, abort_flag)))) break;
+                tc_fence_after();
+                uint32_t sr[TKV];
 #pragma unroll
-            for (int c = 0; c < TKV / 32; c++) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
-            const int kbase = j * TKV;
-            float mx = -INFINITY;
+                for (int c = 0; c < TKV / 32; c++)
+                    tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free);
+                const int kbase = j * TKV;
+                float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < TKV; c++) {
-                const float v = kbase + c < total ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
-                sr[c] = __float_as_uint(v);
-                mx = fmaxf(mx, v);
-            }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = exp2f(m - m_new);
-            float rs = 0.f;
-            // wait until P.V of the previous tile has consumed P and updated O
-            if (j > 0 && !__all_sync(D1_FULL_MASK, mbar_wait(o_done, (j - 1) & 1, abort_flag))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {
-                uint32_t o[32];
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    tmem_ld32(tO + c * 32, o);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(tO + c * 32, o);
+                for (int c = 0; c < TKV; c++) {
+                    const float v = kbase + c < total ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
+                    sr[c] = __float_as_uint(v);
+                    mx = fmaxf(mx, v);
                 }
-                tc_wait_st();
-            }
+                const float m_new = fmaxf(m, mx);
+                const float alpha = ex2(m - m_new);
+                // P.V of the previous tile (possibly the previous unit's last) has consumed P and updated O
+                if (kj > 0 && !(ok = __all_sync(D1_FULL_MASK, mbar_wait(o_done, (kj - 1) & 1, abort_flag)))) break;
+                tc_fence_after();
+                if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {
+                    uint32_t o[32];
 #pragma unroll
-            for (int half = 0; half < TKV / 64; half++) {
-                uint8_t* prow = sP + half * (TQ * 128) + row * 128;
+                    for (int c = 0; c < 2; c++) {
+                        tmem_ld32(tO + c * 32, o);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tc_wait_st();
+                }
+                float rs = 0.f;
+                uint8_t* prow = sP + row * 128;
 #pragma unroll
                 for (int ch = 0; ch < 8; ch++) {
                     float p[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
-                        p[e] = exp2f(__uint_as_float(sr[half * 64 + ch * 8 + e]) - m_new);
+                        p[e] = ex2(__uint_as_float(sr[ch * 8 + e]) - m_new);
                         rs += p[e];
                     }
                     *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
                         make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
                 }
+                fence_async_smem_cta();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full);
+                l = l * alpha + rs;
+                m = m_new;
             }
-            fence_async_smem_cta();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            l = l * alpha + rs;
-            m = m_new;
-        }
-        if (ok && nt > 0 && __all_sync(D1_FULL_MASK, mbar_wait(o_done, (nt - 1) & 1, abort_flag))) {
+            if (!ok) break;
+            ki += un.nt;
+            if (un.nt == 0) continue;
+            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(o_done, (ki - 1) & 1, abort_flag)))) break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;
-            const bool store = q0 + row < sq.q_len;
-            __half* orow = a.O + (size_t)(sq.q_start + q0 + row) * a.ldo + h * 64;
+            const bool store = un.q0 + row < un.s.q_len;
+            __half* orow = a.O + (size_t)(un.s.q_start + un.q0 + row) * a.ldo + un.h * 64;
+            uint32_t o[2][32];
+            tmem_ld32(tO, o[0]);
+            tmem_ld32(tO + 32, o[1]);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free);  // the next unit's first P.V may overwrite O
+            if (store) {
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                uint32_t o[32];
-                tmem_ld32(tO + c * 32, o);
-                tc_wait_ld();
-                if (store) {
+                for (int c = 0; c < 2; c++)
 #pragma unroll
                     for (int q = 0; q < 4; q++)
                         *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = make_uint4(
-                            pack_h2(__uint_as_float(o[8 * q]) * il, __uint_as_float(o[8 * q + 1]) * il),
-                            pack_h2(__uint_as_float(o[8 * q + 2]) * il, __uint_as_float(o[8 * q + 3]) * il),
-                            pack_h2(__uint_as_float(o[8 * q + 4]) * il, __uint_as_float(o[8 * q + 5]) * il),
-                            pack_h2(__uint_as_float(o[8 * q + 6]) * il, __uint_as_float(o[8 * q + 7]) * il));
-                }
+                            pack_h2(__uint_as_float(o[c][8 * q]) * il, __uint_as_float(o[c][8 * q + 1]) * il),
+                            pack_h2(__uint_as_float(o[c][8 * q + 2]) * il, __uint_as_float(o[c][8 * q + 3]) * il),
+                            pack_h2(__uint_as_float(o[c][8 * q + 4]) * il, __uint_as_float(o[c][8 * q + 5]) * il),
+                            pack_h2(__uint_as_float(o[c][8 * q + 6]) * il, __uint_as_float(o[c][8 * q + 7]) * il));
             }
-        } else if (nt > 0 && lane == 0) {
-            record_err(a.err, abort_flag, kErrWaitAccFull);
         }
+        if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitAccFull);
     }
     tc_fence_before();
     __syncthreads();
@@ -564,6 +643,25 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
         tc_fence_after();
         tmem_dealloc(tmem, T_TMEM_COLS);
     }
+}
+
+int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
+    static unsigned long long attr_done = 0;
+    static int sms[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(__atomic_load_n(&attr_done, __ATOMIC_ACQUIRE) & bit)) {
+        if (cudaFuncSetAttribute(k_flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, T_SMEM) != cudaSuccess)
+            return -1;
+        cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+        __atomic_fetch_or(&attr_done, bit, __ATOMIC_RELEASE);
+    }
+    a.n_units = n_work * heads;
+    a.heads = heads;
+    const int grid = a.n_units < 2 * sms[dev & 63] ? a.n_units : 2 * sms[dev & 63];
+    k_flash_attn_tc<<<grid, 192, T_SMEM, st>>>(a);
+    return (int)cudaGetLastError();
 }
 
 template <int HPC, bool BIAS>
@@ -582,21 +680,6 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
     }
     dim3 grid(n_work, gy);
     k_flash_attn<HPC, BIAS><<<grid, 128 * HPC, smem, st>>>(a);
-    return (int)cudaGetLastError();
-}
-
-int launch_fa_tc(const FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
-    static unsigned long long attr_done = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const unsigned long long bit = 1ull << (dev & 63);
-    if (!(__atomic_load_n(&attr_done, __ATOMIC_ACQUIRE) & bit)) {
-        if (cudaFuncSetAttribute(k_flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, T_SMEM) != cudaSuccess)
-            return -1;
-        __atomic_fetch_or(&attr_done, bit, __ATOMIC_RELEASE);
-    }
-    dim3 grid(n_work, heads);
-    k_flash_attn_tc<<<grid, 192, T_SMEM, st>>>(a);
     return (int)cudaGetLastError();
 }
 
