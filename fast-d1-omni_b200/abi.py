@@ -92,6 +92,7 @@ EXTENSIONS = {
     "d1_gemm_bias_act": (i32, [p, i32, i32, i32, p, i32, p, i32, p, i32, p, i32, p]),
     "d1_lt_error": (i32, [p]),
     "d1_flash_attn_error": (i32, []),
+    "d1_flash_attn_tc": (i32, [p, i32, p, p, i32, i32, p, i32, p, p, i32, i32, i32, f32, p]),
     "d1_lt_destroy": (None, [p]),
     "d1_build_id": (C.c_char_p, []),
 }

@@ -5,14 +5,19 @@
 //   [ext prefix keys | local keys] of that sequence, kv head g = h / group, fp32 softmax, optional fp32 biases
 //   added to q/k/v as they are loaded.
 //
-// Two kernels. Without biases (the trunk, media prefixes) the tcgen05 kernel below runs (S and O in TMEM, see
-// k_flash_attn_tc). With q/k/v biases (decision head, SigLIP2) an mma.sync kernel adds the biases as it loads:
-// one CTA per (64-query tile, kv head) runs all the query heads that share that kv head (GQA group 2:
+// d1_flash_attn runs an mma.sync kernel: one CTA per (64-query tile, kv head) runs all the query heads that share
+// that kv head (GQA group 2:
 // 8 warps, two heads), so each K/V tile is fetched once for the group. Each warp owns 16 query rows of one head.
 // K/V tiles of 64 keys are double-buffered in shared memory with cp.async (bias-free case) so the next tile's
 // loads overlap this tile's math; QK^T and PV run on m16n8k16 fp16 tensor-core MMAs with fp32 accumulation,
 // S stays in registers and is re-packed as the A operand of PV; the online softmax works in the exp2 domain.
-// The output tile is staged through shared memory for 16-byte coalesced stores.
+// The output tile is staged through shared memory for 16-byte coalesced stores; 2 CTAs per SM.
+//
+// d1_flash_attn_tc (extension) is the same computation for the bias-free forms on tcgen05 (S and O in TMEM;
+// k_flash_attn_tc below). Measured on B200 it is on par with the mma.sync kernel at 256-token sequences
+// (68.6 vs ~70 us for 32 x 256 tokens x 16 heads) and up to 2x slower on long ones: with 128 x 64 tiles its
+// per-tile S -> softmax -> P -> P.V handoffs are latency-bound (tensor pipe 5%, MUFU 10% busy). The remaining
+// steps to make it the default: 128-key tiles with two query tiles per CTA in ping-pong, lazy O rescaling.
 #include "common.cuh"
 
 using namespace d1;
@@ -81,7 +86,7 @@ struct FaArgs {
 
 // HPC query heads per CTA (all of them sharing one kv head), 4 warps per head.
 template <int HPC, bool BIAS>
-__global__ void __launch_bounds__(128 * HPC) k_flash_attn(const FaArgs p) {
+__global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
     extern __shared__ __align__(16) uint8_t fa_smem[];
     __half* sQ = reinterpret_cast<__half*>(fa_smem);                 // [HPC][64][FA_LD]
     __half* sK = sQ + HPC * FA_B * FA_LD;                           // [2][64][FA_LD]
@@ -685,6 +690,34 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
 
 }  // namespace
 
+extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
+                                d1_half* O, int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads,
+                                int group, float scale, cudaStream_t st) {
+    if (n_work <= 0) return n_work == 0 ? 0 : -1;
+    if (heads <= 0 || group <= 0 || heads % group) return -1;
+    if ((((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)O) & 15) || (ldq | ldkv | ldo | ext_ld) % 8) return -1;
+    FaTcArgs t;
+    t.Q = Q;
+    t.K = K;
+    t.V = V;
+    t.O = O;
+    t.seqs = seqs;
+    t.work = reinterpret_cast<const int2*>(work);
+    t.ldq = ldq;
+    t.ldkv = ldkv;
+    t.ext_ld = ext_ld;
+    t.ldo = ldo;
+    t.group = group;
+    t.scale_log2 = scale * 1.4426950408889634f;
+    static int* err_addr[64] = {};  // device address of g_fa_err, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!err_addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&err_addr[dev & 63]), g_fa_err) != cudaSuccess)
+        return -1;
+    t.err = err_addr[dev & 63];
+    return launch_fa_tc(t, n_work, heads, st);
+}
+
 extern "C" int d1_flash_attn_error(void) {
     int e = 0;
     if (cudaMemcpyFromSymbol(&e, g_fa_err, sizeof(int)) != cudaSuccess) return -1;
@@ -719,28 +752,6 @@ extern "C" int d1_flash_attn(const d1_half* Q, int ldq, const d1_half* K, const 
     a.group = group;
     a.scale_log2 = scale * 1.4426950408889634f;
     const bool bias = bq || bk || bv;
-    if (!bias) {  // the trunk and media-prefix forms: tcgen05 kernel
-        FaTcArgs t;
-        t.Q = Q;
-        t.K = K;
-        t.V = V;
-        t.O = O;
-        t.seqs = seqs;
-        t.work = reinterpret_cast<const int2*>(work);
-        t.ldq = ldq;
-        t.ldkv = ldkv;
-        t.ext_ld = ext_ld;
-        t.ldo = ldo;
-        t.group = group;
-        t.scale_log2 = scale * 1.4426950408889634f;
-        static int* err_addr[64] = {};  // device address of g_fa_err, per device
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (!err_addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&err_addr[dev & 63]), g_fa_err) != cudaSuccess)
-            return -1;
-        t.err = err_addr[dev & 63];
-        return launch_fa_tc(t, n_work, heads, st);
-    }
     if (group == 2) {
         const int gy = heads / 2;
         return bias ? launch_fa<2, true>(a, n_work, gy, st) : launch_fa<2, false>(a, n_work, gy, st);

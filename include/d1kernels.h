@@ -213,6 +213,12 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
  * on a bounded wait (the kernel returns early instead of hanging; its output is then undefined). */
 int d1_lt_error(void* ctx);
 
+/* extension — d1_flash_attn without biases on tcgen05 tensor cores (S and O in TMEM); same arguments and result
+ * as d1_flash_attn with bq = bk = bv = NULL. */
+int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld, d1_half* O,
+                     int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads, int group, float scale,
+                     cudaStream_t stream);
+
 /* extension — reads and clears the attention kernels' device error word (nonzero: a kernel gave up on a bounded
  * wait and returned early; its output is undefined). */
 int d1_flash_attn_error(void);

@@ -35,14 +35,19 @@ def attn_meta(pkg, seqs, ext=None):
     return meta, w, len(work)
 
 
-def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, ext_ld=0, q_rows=None):
+def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, ext_ld=0, q_rows=None, tc=False):
     meta, work, n_work = attn_meta(pkg, seqs, ext)
     rows = q_rows if q_rows is not None else Q.shape[0]
     O_ = torch.zeros(rows, heads * 64, dtype=torch.float16, device="cuda")
     bq, bk, bv = bias if bias is not None else (None, None, None)
     st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    r = lib.d1_flash_attn(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(bq), P(bk), P(bv), P(O_), heads * 64, P(meta),
-                          P(work), n_work, heads, group, 0.125, st)
+    if tc:  # the tcgen05 form (extension), bias-free only
+        assert bias is None
+        r = lib.d1_flash_attn_tc(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(O_), heads * 64, P(meta), P(work), n_work,
+                                 heads, group, 0.125, st)
+    else:
+        r = lib.d1_flash_attn(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(bq), P(bk), P(bv), P(O_), heads * 64, P(meta),
+                              P(work), n_work, heads, group, 0.125, st)
     assert r == 0
     torch.cuda.synchronize()
     if hasattr(lib, "d1_flash_attn_error"):
@@ -66,10 +71,12 @@ def test_config2_gqa(pkg, gpu_lib, ref_lib, total):
         s += n
     Q, K, V = qkv, qkv[:, 1024:], qkv[:, 1536:]
     got = run(gpu_lib, pkg, Q, 2048, K, V, 2048, spans, 16, 2)
+    got_tc = run(gpu_lib, pkg, Q, 2048, K, V, 2048, spans, 16, 2, tc=True)
     ref_k = run(ref_lib, pkg, Q, 2048, K, V, 2048, spans, 16, 2)
     q = qkv.float().cpu().numpy()
     want = O.attention(q[:, :1024], q[:, 1024:1536], q[:, 1536:], spans, 16, 2, 0.125)
     assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(got_tc - want).max() <= 4e-3
     assert np.abs(ref_k - want).max() <= 4e-3
     assert np.abs(got - ref_k).max() <= 4e-3
 
@@ -135,9 +142,11 @@ def test_prefix_keys(pkg, gpu_lib, ref_lib):
         s += n
     d = torch.from_numpy(qkv).cuda()
     got = run(gpu_lib, pkg, d, 2048, d[:, 1024:], d[:, 1536:], 2048, spans, 16, 2, ext=ext, ext_ld=512)
+    got_tc = run(gpu_lib, pkg, d, 2048, d[:, 1024:], d[:, 1536:], 2048, spans, 16, 2, ext=ext, ext_ld=512, tc=True)
     ref_k = run(ref_lib, pkg, d, 2048, d[:, 1024:], d[:, 1536:], 2048, spans, 16, 2, ext=ext, ext_ld=512)
     q = qkv.astype(np.float32)
     want = O.attention(q[:, :1024], q[:, 1024:1536], q[:, 1536:], spans, 16, 2, 0.125,
                        ext=[(k.astype(np.float32), v.astype(np.float32)) for k, v in ext_np])
     assert np.abs(got - want).max() <= 4e-3
+    assert np.abs(got_tc - want).max() <= 4e-3
     assert np.abs(got - ref_k).max() <= 4e-3
