@@ -256,11 +256,13 @@ def main():
         l0 = model.launches
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with Clocks(local) as clk:
+            torch.cuda.cudart().cudaProfilerStart()  # a profiler started with --profile-from-start off sees only this
             e0.record(stream)
             for i in range(args.steps):
                 model.launch(batches[i % 4], i % 2, stream)
             e1.record(stream)
             torch.cuda.synchronize(dev)
+            torch.cuda.cudart().cudaProfilerStop()
         for s in (0, 1):
             model._pending.pop(s, None)
         launches = model.launches - l0

@@ -43,6 +43,17 @@ class TextWeights(C.Structure):
                 ("out_b", f32), ("eps", f32), ("rope_theta", f32)]
 
 
+class VisionLayer(C.Structure):
+    _fields_ = [("ln1_w", p), ("ln1_b", p), ("qkv", p), ("qkv_b", p), ("out", p), ("out_b", p), ("ln2_w", p),
+                ("ln2_b", p), ("fc1", p), ("fc1_b", p), ("fc2", p), ("fc2_b", p)]
+
+
+class VisionWeights(C.Structure):
+    _fields_ = [("n_layers", i32), ("layers", C.POINTER(VisionLayer)), ("patch_w", p), ("patch_b", p), ("pos", p),
+                ("post_w", p), ("post_b", p), ("proj1", p), ("proj1_b", p), ("proj2", p), ("proj2_b", p),
+                ("eps", f32)]
+
+
 class PrefixCache(C.Structure):
     _fields_ = [("len", i32), ("k", p), ("v", p), ("bx", p)]
 
@@ -111,6 +122,9 @@ RUNNER = {
     "d1h_tune": (i32, [p, p, i32, p]),
     "d1h_launch_count": (C.c_longlong, [p]),
     "d1h_h2d_bytes": (C.c_longlong, [p, i32]),
+    "d1h_vision_create": (p, [C.POINTER(VisionWeights), C.c_char_p, i32, i32]),
+    "d1h_vision_destroy": (None, [p]),
+    "d1h_vision_encode": (i32, [p, i32, C.POINTER(i32), C.POINTER(i32), p, p, p]),
     "d1h_d2h_bytes": (C.c_longlong, [p, i32]),
 }
 

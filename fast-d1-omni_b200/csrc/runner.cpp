@@ -8,6 +8,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -52,6 +53,8 @@ struct Kt {
                       const float*, d1_half*, int, const AttnSeq*, const int*, int, int, int, float,
                       cudaStream_t) = nullptr;
     int (*scorer_out)(const d1_half*, const float*, const d1_half*, float, float*, int, int, cudaStream_t) = nullptr;
+    int (*unshuffle)(const d1_half*, d1_half*, int, int, int, cudaStream_t) = nullptr;
+    int (*fill_rows)(float*, const float*, const float*, int, int, cudaStream_t) = nullptr;
     void* (*lt_init)(size_t) = nullptr;
     int (*lt_gemm)(void*, int, int, int, const void*, int, const void*, int, int, void*, int, int, int, float, float,
                    cudaStream_t) = nullptr;
@@ -77,6 +80,8 @@ struct Kt {
         qk_norm_rope = d1_qk_norm_rope;
         flash_attn = d1_flash_attn;
         scorer_out = d1_scorer_out;
+        unshuffle = d1_unshuffle;
+        fill_rows = d1_fill_rows;
         lt_init = d1_lt_init;
         lt_gemm = d1_lt_gemm;
         lt_tune = d1_lt_tune;
@@ -108,7 +113,8 @@ struct Kt {
                sym(embed, "d1_embed") && sym(swiglu, "d1_swiglu") && sym(bias_act_h, "d1_bias_act_h") &&
                sym(gather_rows, "d1_gather_rows") && sym(shortconv, "d1_shortconv") &&
                sym(qk_norm_rope, "d1_qk_norm_rope") && sym(flash_attn, "d1_flash_attn") &&
-               sym(scorer_out, "d1_scorer_out") && sym(lt_init, "d1_lt_init") && sym(lt_gemm, "d1_lt_gemm") &&
+               sym(scorer_out, "d1_scorer_out") && sym(unshuffle, "d1_unshuffle") && sym(fill_rows, "d1_fill_rows") &&
+               sym(lt_init, "d1_lt_init") && sym(lt_gemm, "d1_lt_gemm") &&
                sym(lt_tune, "d1_lt_tune") && sym(lt_bucket, "d1_lt_bucket") &&
                sym(lt_free_scratch, "d1_lt_free_scratch") && sym(gemm_swiglu, "d1_gemm_swiglu", false) &&
                sym(gemm_bias_act, "d1_gemm_bias_act", false) && sym(lt_destroy, "d1_lt_destroy", false);
@@ -168,6 +174,22 @@ struct D1Model {
         return 0;
     }
 };
+
+// Blas::gemm over any kernel table and context (shared by the text model and the encoders).
+int kt_gemm(Kt& k, void* lt, long long& launches, int m, int n, int kk, const d1_half* x, int ldx, const d1_half* wt,
+            int ldw, void* y, int ldy, int y_f32, float alpha, float beta, cudaStream_t st) {
+    if (m == 0 || n == 0) return 0;
+    launches++;
+    int e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
+    if (e == -2) {
+        if (k.lt_tune(lt, m, n, kk, ldx, ldw, 0, ldy, y_f32, 0, 0, st) < 0.f)
+            return fail("GEMM tuning failed for m=" + std::to_string(m) + " n=" + std::to_string(n));
+        e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
+    }
+    if (e) return fail("d1_lt_gemm failed (" + std::to_string(e) + ") m=" + std::to_string(m) + " n=" +
+                       std::to_string(n) + " k=" + std::to_string(kk), e);
+    return 0;
+}
 
 struct D1Workspace {
     int cap_tokens = 0, cap_markers = 0;
@@ -687,6 +709,256 @@ int d1h_tune(D1Model* m, D1Workspace* ws, int max_tokens, cudaStream_t st) {
     cudaStreamSynchronize(st);
     m->k.lt_free_scratch(m->lt);
     return n;
+}
+
+}  // extern "C"
+
+// ================================================================================================ vision encoder
+// VisionModel (src/vision.rs:143-164) and VisionModel::encode (:305-385).
+
+namespace {
+constexpr int VD = 768;       // src/vision.rs:13
+constexpr int VHEADS = 12;    // :14
+constexpr int VFF = 3072;     // :15
+constexpr int VOUT = 1024;    // :16
+constexpr int VHID = 2048;    // projector hidden (src/vision.rs:379)
+constexpr size_t VMETA = 1 << 20;
+
+// Separable antialiased bilinear weights, as F.interpolate(antialias=True, align_corners=False) computes them
+// (src/vision.rs:173-196): for every output index, the first input index and the normalised weights.
+std::vector<std::pair<int, std::vector<float>>> aa_weights(int inp, int out) {
+    const double scale = (double)inp / (double)out;
+    const double support = scale >= 1.0 ? scale : 1.0;
+    const double invscale = scale >= 1.0 ? 1.0 / scale : 1.0;
+    std::vector<std::pair<int, std::vector<float>>> res;
+    for (int i = 0; i < out; i++) {
+        const double center = scale * (i + 0.5);
+        long long xmin = (long long)(center - support + 0.5);
+        long long xmax = (long long)(center + support + 0.5);
+        if (xmin < 0) xmin = 0;
+        if (xmax > inp) xmax = inp;
+        std::vector<double> w;
+        double t = 0.0;
+        for (long long j = xmin; j < xmax; j++) {
+            const double x = ((double)j - center + 0.5) * invscale;
+            const double v = fabs(x) < 1.0 ? 1.0 - fabs(x) : 0.0;
+            w.push_back(v);
+            t += v;
+        }
+        std::vector<float> wf;
+        for (double v : w) wf.push_back((float)(t != 0.0 ? v / t : v));
+        res.push_back({(int)xmin, wf});
+    }
+    return res;
+}
+}  // namespace
+
+struct D1Vision {
+    Kt k;
+    void* lt = nullptr;
+    D1VisionWeights w{};
+    std::vector<D1VisionLayer> layers;
+    std::vector<float> patch_b, pos;
+    std::map<std::pair<int, int>, float*> pos_cache;  // (ph, pw) -> device [ph*pw][768] pos + bias
+    bool fused = false;
+    long long launches = 0;
+    int max_patches = 0;
+    float* h = nullptr;
+    d1_half *xn = nullptr, *big = nullptr, *act = nullptr, *pix = nullptr;
+    uint8_t* meta = nullptr;
+    uint8_t* host_meta = nullptr;
+    cudaEvent_t done = nullptr;
+    bool busy = false;
+
+    // Resized position embeddings + patch bias for a (ph, pw) grid, computed on the host and cached on the
+    // device (src/vision.rs:263-302).
+    float* pos_for(int ph, int pw) {
+        auto it = pos_cache.find({ph, pw});
+        if (it != pos_cache.end()) return it->second;
+        auto wy = aa_weights(16, ph), wx = aa_weights(16, pw);
+        std::vector<float> tmp((size_t)16 * pw * VD, 0.f), out((size_t)ph * pw * VD, 0.f);
+        for (int y = 0; y < 16; y++)
+            for (int x = 0; x < pw; x++) {
+                const int s0 = wx[x].first;
+                const auto& ws = wx[x].second;
+                float* dst = &tmp[((size_t)y * pw + x) * VD];
+                for (size_t j = 0; j < ws.size(); j++) {
+                    const float* src = &pos[((size_t)y * 16 + s0 + j) * VD];
+                    for (int c = 0; c < VD; c++) dst[c] += ws[j] * src[c];
+                }
+            }
+        for (int y = 0; y < ph; y++) {
+            const int s0 = wy[y].first;
+            const auto& ws = wy[y].second;
+            for (int x = 0; x < pw; x++) {
+                float* dst = &out[((size_t)y * pw + x) * VD];
+                for (size_t j = 0; j < ws.size(); j++) {
+                    const float* src = &tmp[(((size_t)s0 + j) * pw + x) * VD];
+                    for (int c = 0; c < VD; c++) dst[c] += ws[j] * src[c];
+                }
+                for (int c = 0; c < VD; c++) dst[c] += patch_b[c];
+            }
+        }
+        float* d = nullptr;
+        if (cudaMalloc(&d, out.size() * 4) != cudaSuccess ||
+            cudaMemcpy(d, out.data(), out.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            fail("position embedding upload failed");
+            return nullptr;
+        }
+        pos_cache[{ph, pw}] = d;
+        return d;
+    }
+};
+
+extern "C" {
+
+D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, int fused, int max_patches) {
+    if (!w || w->n_layers <= 0 || !w->layers || !w->patch_b || !w->pos || max_patches <= 0) {
+        fail("invalid vision weights");
+        return nullptr;
+    }
+    D1Vision* v = new D1Vision();
+    if (!(kernel_lib ? v->k.load_lib(kernel_lib) : v->k.load_builtin())) {
+        delete v;
+        return nullptr;
+    }
+    v->w = *w;
+    v->layers.assign(w->layers, w->layers + w->n_layers);
+    v->w.layers = nullptr;
+    v->patch_b.assign(w->patch_b, w->patch_b + VD);
+    v->pos.assign(w->pos, w->pos + 256 * VD);
+    v->w.patch_b = v->w.pos = nullptr;
+    v->fused = fused != 0;
+    v->max_patches = max_patches;
+    v->lt = v->k.lt_init(32 << 20);
+    const size_t cap = max_patches;
+    int e = 0;
+    if (!v->lt) e = fail("d1_lt_init failed");
+    if (!e) e |= dmalloc(&v->h, cap * VD * 4);
+    if (!e) e |= dmalloc(&v->xn, cap * VD * 2);
+    if (!e) e |= dmalloc(&v->big, cap * VFF * 2);
+    if (!e) e |= dmalloc(&v->act, cap * VD * 2);
+    if (!e) e |= dmalloc(&v->pix, cap * VD * 2);
+    if (!e) e |= dmalloc(&v->meta, VMETA);
+    if (!e && (cudaMallocHost((void**)&v->host_meta, VMETA) != cudaSuccess ||
+               cudaEventCreateWithFlags(&v->done, cudaEventDisableTiming) != cudaSuccess))
+        e = fail("vision host allocation failed");
+    if (e) {
+        d1h_vision_destroy(v);
+        return nullptr;
+    }
+    return v;
+}
+
+void d1h_vision_destroy(D1Vision* v) {
+    if (!v) return;
+    if (v->busy) cudaEventSynchronize(v->done);
+    for (void* p : {(void*)v->h, (void*)v->xn, (void*)v->big, (void*)v->act, (void*)v->pix, (void*)v->meta})
+        if (p) cudaFree(p);
+    for (auto& kv : v->pos_cache) cudaFree(kv.second);
+    if (v->host_meta) cudaFreeHost(v->host_meta);
+    if (v->done) cudaEventDestroy(v->done);
+    if (v->lt && v->k.lt_destroy) v->k.lt_destroy(v->lt);
+    if (v->k.dl) dlclose(v->k.dl);
+    delete v;
+}
+
+int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, const d1_half* pixels, float* out,
+                      cudaStream_t st) {
+    if (!v || n_crops <= 0 || !ph || !pw || !pixels || !out) return fail("bad arguments");
+    Kt& k = v->k;
+    long long t = 0;
+    for (int i = 0; i < n_crops; i++) {
+        if (ph[i] <= 0 || pw[i] <= 0 || (ph[i] & 1) || (pw[i] & 1) || ph[i] > 1024 || pw[i] > 1024)
+            return fail("crop grids must be positive and even");
+        t += (long long)ph[i] * pw[i];
+    }
+    if (t > v->max_patches) return fail("patches exceed the vision batch capacity");
+    if (v->busy) {
+        if (cudaEventSynchronize(v->done) != cudaSuccess) return fail("event sync failed");
+        v->busy = false;
+    }
+    // metadata: one AttnSeq per crop and its 64-row query tiles (src/vision.rs:310-326)
+    std::vector<AttnSeq> seqs;
+    std::vector<std::pair<int, int>> spans;
+    int off = 0;
+    for (int i = 0; i < n_crops; i++) {
+        const int n = ph[i] * pw[i];
+        seqs.push_back(AttnSeq{off, n, off, n, 0, 0, nullptr, nullptr});
+        spans.push_back({off, n});
+        off += n;
+    }
+    std::vector<int> work = work_items(spans);
+    MetaWriter mw{v->host_meta, v->meta};
+    const AttnSeq* d_seqs = mw.put(seqs);
+    const int* d_work = mw.put(work);
+    if (mw.overflow || mw.off > VMETA) return fail("vision metadata too large");
+    if (cudaMemcpyAsync(v->meta, v->host_meta, mw.off, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(v->pix, pixels, (size_t)t * VD * 2, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail("vision upload failed");
+    const int ti = (int)t, n_work = (int)work.size() / 2;
+    // embeddings: h = pos + bias per crop, then += pixels . W^T
+    off = 0;
+    for (int i = 0; i < n_crops; i++) {
+        float* p = v->pos_for(ph[i], pw[i]);
+        if (!p) return -1;
+        if (cudaMemcpyAsync(v->h + (size_t)off * VD, p, (size_t)ph[i] * pw[i] * VD * 4, cudaMemcpyDeviceToDevice, st) !=
+            cudaSuccess)
+            return fail("position copy failed");
+        off += ph[i] * pw[i];
+    }
+    float* h = v->h;
+    d1_half *xn = v->xn, *big = v->big, *act = v->act;
+    long long& L = v->launches;
+    CK(kt_gemm(k, v->lt, L, ti, VD, VD, v->pix, VD, v->w.patch_w, VD, h, VD, 1, 1.f, 1.f, st));
+    const float* pend = nullptr;
+    const float eps = v->w.eps;
+    for (const auto& l : v->layers) {
+        L++;
+        CK(k.layernorm(h, pend, 1.f, l.ln1_w, l.ln1_b, xn, nullptr, ti, VD, eps, st));
+        CK(kt_gemm(k, v->lt, L, ti, 3 * VD, VD, xn, VD, l.qkv, VD, big, 3 * VD, 0, 1.f, 0.f, st));
+        L++;
+        CK(k.flash_attn(big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, l.qkv_b, l.qkv_b + VD, l.qkv_b + 2 * VD, act,
+                        VD, d_seqs, d_work, n_work, VHEADS, 1, 0.125f, st));
+        CK(kt_gemm(k, v->lt, L, ti, VD, VD, act, VD, l.out, VD, h, VD, 1, 1.f, 1.f, st));
+        L++;
+        CK(k.layernorm(h, l.out_b, 1.f, l.ln2_w, l.ln2_b, xn, nullptr, ti, VD, eps, st));
+        if (v->fused && k.gemm_bias_act) {
+            L++;
+            CK(k.gemm_bias_act(v->lt, ti, VFF, VD, xn, VD, l.fc1, VD, l.fc1_b, 3, big, VFF, st));
+        } else {
+            CK(kt_gemm(k, v->lt, L, ti, VFF, VD, xn, VD, l.fc1, VD, big, VFF, 0, 1.f, 0.f, st));
+            L++;
+            CK(k.bias_act_h(big, l.fc1_b, ti, VFF, 3, st));
+        }
+        CK(kt_gemm(k, v->lt, L, ti, VD, VFF, big, VFF, l.fc2, VFF, h, VD, 1, 1.f, 1.f, st));
+        pend = l.fc2_b;
+    }
+    L++;
+    CK(k.layernorm(h, pend, 1.f, v->w.post_w, v->w.post_b, xn, nullptr, ti, VD, eps, st));
+    // projector: unshuffle each crop -> big [P, 3072] -> linear_1 + GELU -> linear_2 (+bias) -> out
+    int src = 0, dst = 0;
+    for (int i = 0; i < n_crops; i++) {
+        L++;
+        CK(k.unshuffle(xn + (size_t)src * VD, big + (size_t)dst * 4 * VD, ph[i], pw[i], VD, st));
+        src += ph[i] * pw[i];
+        dst += ph[i] * pw[i] / 4;
+    }
+    const int p = dst;
+    if (v->fused && k.gemm_bias_act) {
+        L++;
+        CK(k.gemm_bias_act(v->lt, p, VHID, 4 * VD, big, 4 * VD, v->w.proj1, 4 * VD, v->w.proj1_b, 2, act, VHID, st));
+    } else {
+        CK(kt_gemm(k, v->lt, L, p, VHID, 4 * VD, big, 4 * VD, v->w.proj1, 4 * VD, act, VHID, 0, 1.f, 0.f, st));
+        L++;
+        CK(k.bias_act_h(act, v->w.proj1_b, p, VHID, 2, st));
+    }
+    L++;
+    CK(k.fill_rows(out, v->w.proj2_b, nullptr, p, VOUT, st));
+    CK(kt_gemm(k, v->lt, L, p, VOUT, VHID, act, VHID, v->w.proj2, VHID, out, VOUT, 1, 1.f, 1.f, st));
+    cudaEventRecord(v->done, st);
+    v->busy = true;
+    return 0;
 }
 
 }  // extern "C"

@@ -167,3 +167,78 @@ class TextModel:
             self.close()
         except Exception:
             pass
+
+
+class VisionModel:
+    """Device copy of `weights.vision_weights(...)` plus the vision runner (include/d1h.h d1h_vision_*)."""
+
+    def __init__(self, w: dict, device: int = 0, kernel_lib: str | None = None, fused: bool = True,
+                 max_patches: int = 16384):
+        self.device = torch.device("cuda", device)
+        self.L = lib()
+        self._keep = []
+
+        def h16(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float16)).to(self.device)
+            self._keep.append(t)
+            return _ptr(t)
+
+        def f32(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.device)
+            self._keep.append(t)
+            return _ptr(t)
+
+        def host32(a):
+            arr = np.ascontiguousarray(a, dtype=np.float32)
+            self._keep.append(arr)
+            return C.c_void_p(arr.ctypes.data)
+
+        with torch.cuda.device(self.device):
+            layers = (abi.VisionLayer * len(w["layers"]))()
+            for i, l in enumerate(w["layers"]):
+                x = layers[i]
+                x.ln1_w, x.ln1_b, x.qkv, x.qkv_b = f32(l["ln1_w"]), f32(l["ln1_b"]), h16(l["qkv"]), f32(l["qkv_b"])
+                x.out, x.out_b, x.ln2_w, x.ln2_b = h16(l["out"]), f32(l["out_b"]), f32(l["ln2_w"]), f32(l["ln2_b"])
+                x.fc1, x.fc1_b, x.fc2, x.fc2_b = h16(l["fc1"]), f32(l["fc1_b"]), h16(l["fc2"]), f32(l["fc2_b"])
+            vw = abi.VisionWeights()
+            vw.n_layers = len(w["layers"])
+            vw.layers = layers
+            vw.patch_w = h16(w["patch_w"])
+            vw.patch_b = host32(w["patch_b"])
+            vw.pos = host32(w["pos"])
+            vw.post_w, vw.post_b = f32(w["post_w"]), f32(w["post_b"])
+            vw.proj1, vw.proj1_b = h16(w["proj1"]), f32(w["proj1_b"])
+            vw.proj2, vw.proj2_b = h16(w["proj2"]), f32(w["proj2_b"])
+            vw.eps = float(w["eps"])
+            torch.cuda.synchronize(self.device)
+            self.v = self.L.d1h_vision_create(C.byref(vw), kernel_lib.encode() if kernel_lib else None, int(fused),
+                                              max_patches)
+            if not self.v:
+                raise RuntimeError(f"d1h_vision_create failed: {self.L.d1h_last_error().decode()}")
+
+    def encode(self, crops, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """crops: [(ph, pw, fp16 [ph*pw, 768] host patches)] -> fp32 [sum ph*pw/4, 1024] on the device."""
+        n = len(crops)
+        ph = (C.c_int * n)(*[c[0] for c in crops])
+        pw = (C.c_int * n)(*[c[1] for c in crops])
+        pix = np.ascontiguousarray(np.concatenate([c[2] for c in crops]), dtype=np.float16)
+        rows = sum(c[0] * c[1] // 4 for c in crops)
+        if out is None:
+            out = torch.empty(rows, 1024, device=self.device, dtype=torch.float32)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        with torch.cuda.device(self.device):
+            check(self.L.d1h_vision_encode(self.v, n, ph, pw, C.c_void_p(pix.ctypes.data), _ptr(out),
+                                           C.c_void_p(s.cuda_stream)), "vision_encode")
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "v", None):
+            self.L.d1h_vision_destroy(self.v)
+            self.v = None
+        self._keep.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

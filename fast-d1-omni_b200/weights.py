@@ -162,3 +162,42 @@ def loguniform_lengths(seed, total, lo=128, hi=2048):
         out.append(n)
         used += n
     return out
+
+
+# ---------------------------------------------------------------------------------------------------- vision
+VD, VFF, VHID, VOUT = 768, 3072, 2048, 1024
+
+
+def vision_weights(seed=3, n_layers=12, eps=1e-6):
+    """SigLIP2 tower + projector weights in the layout of src/vision.rs:198-260 (patch weight already in
+    (y, x, c) input order, fused QKV rows [q; k; v]); BASELINE config 3 uses seed 3."""
+    g = _Gen(seed)
+    w = {"eps": np.float32(eps), "patch_w": g.mat(VD, VD), "patch_b": g.vec(VD), "pos": g.vec(256 * VD).reshape(256, VD)}
+    layers = []
+    for _ in range(n_layers):
+        layers.append({"ln1_w": np.ones(VD, np.float32), "ln1_b": g.vec(VD), "qkv": g.mat(3 * VD, VD),
+                       "qkv_b": g.vec(3 * VD), "out": g.mat(VD, VD), "out_b": g.vec(VD),
+                       "ln2_w": np.ones(VD, np.float32), "ln2_b": g.vec(VD), "fc1": g.mat(VFF, VD), "fc1_b": g.vec(VFF),
+                       "fc2": g.mat(VD, VFF), "fc2_b": g.vec(VD)})
+    w["layers"] = layers
+    w["post_w"] = np.ones(VD, np.float32)
+    w["post_b"] = g.vec(VD)
+    w["proj1"] = g.mat(VHID, 4 * VD)
+    w["proj1_b"] = g.vec(VHID)
+    w["proj2"] = g.mat(VOUT, VHID)
+    w["proj2_b"] = g.vec(VOUT)
+    g.run()
+    return w
+
+
+def vision_crops(seed=3, n_images=16, lo=224, hi=768):
+    """images with sides uniform in [lo, hi] rounded to multiples of 32, pixels uniform in
+    [0, 1] fed directly as 16x16x3 patch rows in (y, x, c) order (the layout() tiling is bypassed).
+    Returns [(ph, pw, fp16 patches [ph*pw, 768])]."""
+    rng = np.random.default_rng(seed)
+    crops = []
+    for _ in range(n_images):
+        hh, ww = (int(round(rng.uniform(lo, hi) / 32.0)) * 32 for _ in range(2))
+        ph, pw = hh // 16, ww // 16
+        crops.append((ph, pw, rng.uniform(0.0, 1.0, size=(ph * pw, VD)).astype(np.float16)))
+    return crops

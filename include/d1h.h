@@ -136,6 +136,53 @@ int d1h_launch_prefix(D1Model* m, D1Workspace* ws, int slot, const D1PrefixSeq* 
  * Returns the number of shapes tuned or a negative status. */
 int d1h_tune(D1Model* m, D1Workspace* ws, int max_tokens, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------------------------------ vision
+ * SigLIP2-NaFlex tower + 2x2 pixel-unshuffle projector (src/vision.rs:128-164, 198-385): hidden 768, 12 heads,
+ * GELU-tanh MLP 3072, LayerNorm (eps from GGUF, 1e-6), projector 3072 -> 2048 (GELU-erf) -> 1024. */
+typedef struct D1VisionLayer {
+    const float* ln1_w;
+    const float* ln1_b;
+    const d1_half* qkv;      /* [q; k; v] rows [2304, 768] (src/vision.rs:217-219) */
+    const float* qkv_b;      /* [2304] */
+    const d1_half* out;      /* [768, 768] */
+    const float* out_b;
+    const float* ln2_w;
+    const float* ln2_b;
+    const d1_half* fc1;      /* [3072, 768] */
+    const float* fc1_b;
+    const d1_half* fc2;      /* [768, 3072] */
+    const float* fc2_b;
+} D1VisionLayer;
+
+typedef struct D1VisionWeights {
+    int n_layers;
+    const D1VisionLayer* layers;
+    const d1_half* patch_w;  /* [768, 768] with inputs in (y, x, c) patch order (src/vision.rs:202-213) */
+    const float* patch_b;    /* host [768] (folded into the position embeddings, src/vision.rs:293-295) */
+    const float* pos;        /* host [16*16][768] position embedding grid */
+    const float* post_w;
+    const float* post_b;
+    const d1_half* proj1;    /* [2048, 3072] */
+    const float* proj1_b;
+    const d1_half* proj2;    /* [1024, 2048] */
+    const float* proj2_b;
+    float eps;
+} D1VisionWeights;
+
+typedef struct D1Vision D1Vision;
+
+/* Creates the encoder over caller-owned device weights (host pointers for patch_b and pos, which are copied);
+ * max_patches bounds one call. kernel_lib / fused as d1h_model_create. NULL on failure. */
+D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, int fused, int max_patches);
+void d1h_vision_destroy(D1Vision* v);
+
+/* Runs crops through the tower and projector (src/vision.rs:305-385). ph, pw: each crop's patch grid (even);
+ * pixels: host fp16 [sum ph*pw][768] patch rows in (y, x, c) order; out: device fp32 [sum ph*pw/4][1024] in crop
+ * order. Asynchronous on `stream` (the host staging buffers are reused by the next call after it waits for
+ * this one). Returns 0 or an error status. */
+int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, const d1_half* pixels, float* out,
+                      cudaStream_t stream);
+
 /* Number of kernel launches the runner made since the model was created (a counter for benchmarks). */
 long long d1h_launch_count(const D1Model* m);
 /* Bytes the last launch on `slot` copied host->device (its batch metadata, token ids included) and

@@ -367,6 +367,75 @@ def launch_prefix(w, embs, prec="f16"):
             for i, (s, n) in enumerate(spans)]
 
 
+# ------------------------------------------------------------------------------------------------ vision
+
+def aa_weights(inp, out):
+    """src/vision.rs:173-196: separable antialiased bilinear weights (first input index, normalised weights)."""
+    scale = inp / out
+    support = scale if scale >= 1.0 else 1.0
+    invscale = 1.0 / scale if scale >= 1.0 else 1.0
+    res = []
+    for i in range(out):
+        center = scale * (i + 0.5)
+        xmin = max(int(center - support + 0.5), 0)
+        xmax = min(int(center + support + 0.5), inp)
+        w = [max(0.0, 1.0 - abs((j - center + 0.5) * invscale)) for j in range(xmin, xmax)]
+        t = sum(w)
+        res.append((xmin, np.asarray([v / t if t else v for v in w], np.float32)))
+    return res
+
+
+def vision_pos(pos, patch_b, ph, pw):
+    """src/vision.rs:263-302: the 16x16 position grid resized to (ph, pw) (horizontal then vertical pass) plus the
+    patch bias; fp32 [ph*pw, 768]."""
+    pos = np.asarray(pos, np.float32).reshape(16, 16, -1)
+    tmp = np.zeros((16, pw, pos.shape[-1]), np.float32)
+    for x, (s0, ws) in enumerate(aa_weights(16, pw)):
+        for j, wt in enumerate(ws):
+            tmp[:, x] += wt * pos[:, s0 + j]
+    out = np.zeros((ph, pw, pos.shape[-1]), np.float32)
+    for y, (s0, ws) in enumerate(aa_weights(16, ph)):
+        for j, wt in enumerate(ws):
+            out[y] += wt * tmp[s0 + j]
+    return (out + patch_b).reshape(ph * pw, -1)
+
+
+def vision_encode(w, crops, prec="f16"):
+    """src/vision.rs:305-385. crops: [(ph, pw, patches fp16 [ph*pw, 768])] -> fp32 [sum ph*pw/4, 1024]."""
+    VD = 768
+    eps = float(w["eps"])
+    h = np.concatenate([vision_pos(w["pos"], w["patch_b"], ph, pw) for ph, pw, _ in crops])
+    pix = np.concatenate([np.asarray(c[2], np.float32) for c in crops])
+    h = gemm(pix, w["patch_w"], h, 1.0, 1.0)
+    spans, s = [], 0
+    for ph, pw, _ in crops:
+        spans.append((s, ph * pw, s, ph * pw))
+        s += ph * pw
+    pend = None
+    for l in w["layers"]:
+        h, xn = layernorm(h, l["ln1_w"], l["ln1_b"], eps, pend)
+        xn = r16(xn, prec)
+        big = r16(gemm(xn, l["qkv"]), prec)
+        b = l["qkv_b"]
+        act = r16(attention(big[:, :VD], big[:, VD:2 * VD], big[:, 2 * VD:], spans, 12, 1, 0.125,
+                            b[:VD], b[VD:2 * VD], b[2 * VD:], prec=prec), prec)
+        h = gemm(act, l["out"], h, 1.0, 1.0)
+        h, xn = layernorm(h, l["ln2_w"], l["ln2_b"], eps, l["out_b"])
+        xn = r16(xn, prec)
+        big = r16(bias_act(r16(gemm(xn, l["fc1"]), prec), l["fc1_b"], 3), prec)
+        h = gemm(big, l["fc2"], h, 1.0, 1.0)
+        pend = l["fc2_b"]
+    h, xn = layernorm(h, w["post_w"], w["post_b"], eps, pend)
+    xn = r16(xn, prec)
+    parts, s = [], 0
+    for ph, pw, _ in crops:
+        parts.append(unshuffle(xn[s:s + ph * pw], ph, pw, VD))
+        s += ph * pw
+    big = np.concatenate(parts)
+    act = r16(bias_act(r16(gemm(big, w["proj1"]), prec), w["proj1_b"], 2), prec)
+    return gemm(act, w["proj2"], np.broadcast_to(w["proj2_b"], (act.shape[0], 1024)), 1.0, 1.0)
+
+
 # ------------------------------------------------------------------------------------------------ metrics
 
 def centred_logit_err(ref_logits, logits, group_sizes):
