@@ -67,6 +67,23 @@ class PrefixSeq(C.Structure):
     _fields_ = [("emb", p), ("cache", C.POINTER(PrefixCache))]
 
 
+class AudioLayer(C.Structure):
+    _fields_ = [("ff1_n_w", p), ("ff1_n_b", p), ("ff1_up", p), ("ff1_up_b", p), ("ff1_down", p), ("ff1_down_b", p),
+                ("att_n_w", p), ("att_n_b", p), ("qkv", p), ("bq", p), ("bk", p), ("bv", p), ("pu", p), ("pv", p),
+                ("pos", p), ("out", p), ("out_b", p), ("conv_n_w", p), ("conv_n_b", p), ("pw1", p), ("pw1_b", p),
+                ("dw", p), ("dw_b", p), ("bn_s", p), ("bn_b", p), ("pw2", p), ("pw2_b", p), ("ff2_n_w", p),
+                ("ff2_n_b", p), ("ff2_up", p), ("ff2_up_b", p), ("ff2_down", p), ("ff2_down_b", p), ("out_n_w", p),
+                ("out_n_b", p)]
+
+
+class AudioWeights(C.Structure):
+    _fields_ = [("n_layers", i32), ("layers", C.POINTER(AudioLayer)), ("c0_w", p), ("c0_b", p), ("c2_w", p),
+                ("c2_b", p), ("c3_w", p), ("c3_b", p), ("c5_w", p), ("c5_b", p), ("c6_w", p), ("c6_b", p),
+                ("pre_out", p), ("pre_out_b", p), ("ad_n_w", p), ("ad_n_b", p), ("ad1", p), ("ad1_b", p), ("ad2", p),
+                ("ad2_b", p), ("res_n_w", p), ("res_n_b", p), ("res_down", p), ("res_down_b", p), ("res_up", p),
+                ("res_up_b", p), ("eps", f32)]
+
+
 # name -> (restype, argtypes). The kernel ABI (d1kernels.h) first, then the runner (d1h.h).
 KERNELS = {
     "d1_rmsnorm": (i32, [p, p, p, i32, i32, f32, p]),
@@ -104,6 +121,9 @@ EXTENSIONS = {
     "d1_lt_error": (i32, [p]),
     "d1_flash_attn_error": (i32, []),
     "d1_flash_attn_tc": (i32, [p, i32, p, p, i32, i32, p, i32, p, p, i32, i32, i32, f32, p]),
+    "d1_sgemm": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, f32, p, i32, p]),
+    "d1_relpos_attn": (i32, [p, p, p, p, i32, p, i32, i32, i32, p, i32, p, i32, i32, i32, f32, p]),
+    "d1_relpos_attn_error": (i32, []),
     "d1_lt_destroy": (None, [p]),
     "d1_build_id": (C.c_char_p, []),
 }
@@ -126,6 +146,9 @@ RUNNER = {
     "d1h_vision_destroy": (None, [p]),
     "d1h_vision_encode": (i32, [p, i32, C.POINTER(i32), C.POINTER(i32), p, p, p]),
     "d1h_d2h_bytes": (C.c_longlong, [p, i32]),
+    "d1h_audio_create": (p, [C.POINTER(AudioWeights), i32, i32]),
+    "d1h_audio_destroy": (None, [p]),
+    "d1h_audio_encode": (i32, [p, i32, C.POINTER(i32), p, p, p]),
 }
 
 

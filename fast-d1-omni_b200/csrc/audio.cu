@@ -1,0 +1,481 @@
+// FastConformer audio-encoder kernels that the reference runs through cuBLAS from Rust (src/cuda.rs:493-527,
+// called from src/audio.rs:514-571), rebuilt for B200:
+//
+// d1_sgemm — fp32 row-major Y[M,N] = act(X[M,K] . W[N,K]^T + beta * Y + bias): Blas::sgemm (src/cuda.rs:493-505)
+//   with the d1_fill_rows / d1_bias_act_f calls around it (src/audio.rs:517-525) folded into the epilogue.
+//   fp32 FFMA (the reference asks cuBLAS for CUDA_R_32F with COMPUTE_32F, i.e. no TF32). 256 threads per CTA;
+//   128 x 128 tiles (8 x 8 outputs per thread) when they fill the GPU, else 64 x 64 tiles with the K range split
+//   across a thread-block cluster of up to 8 CTAs whose partial tiles are summed in rank order through
+//   distributed shared memory — deterministic, no global workspace, no atomics.
+//
+// d1_relpos_attn — the encoder's relative-position self-attention (src/audio.rs:565-571: three strided-batched
+//   GEMMs around d1_relpos_softmax, cuda/kernels.cu:583-616) as one kernel over packed clips. For clip c, head h
+//   and query i, key j < T:
+//       score(i, j) = (qu_i . k_j + qv_i . pp[center + j - i]) * scale,  P = softmax_j(score) rounded to fp16,
+//       O_i = P . V (fp32 accumulation, fp16 out)
+//   where row `center + j - i` of pp holds the projected sinusoid of relative position i - j (the reference's
+//   per-clip pp has center = T - 1; the runner passes a per-layer table for all positions of the longest clip).
+//   One CTA per (64-query tile, clip, head): the 64 x T score block lives in shared memory (fp32), the qu.k^T
+//   tiles are written into it, the qv.pp^T tiles of the 64-row pp chunks that the tile's band touches are added
+//   at their shifted columns, an exact row softmax (expf, like the reference) writes P in place as fp16, and P.V
+//   accumulates in registers. K tiles, pp chunks and V tiles stream through one double-buffered cp.async ring;
+//   the MMAs are m16n8k16 fp16 with fp32 accumulation. Clips up to 384 frames after subsampling
+//   (src/audio.rs:401 MAX_T) — the reference's limit.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "warp_mma.cuh"
+
+using namespace d1;
+namespace cg = cooperative_groups;
+
+namespace {
+
+// ================================================================================================ fp32 GEMM
+
+struct SgArgs {
+    const float* X;
+    const float* W;
+    float* Y;
+    const float* bias;
+    int M, N, K, ldx, ldw, ldy, act, kchunk;
+    float beta;
+};
+
+constexpr int SG_BK = 16;
+
+template <int BM, int BN>
+struct SgSmem {
+    static constexpr int A = 2 * SG_BK * (BM + 4);
+    static constexpr int B = 2 * SG_BK * (BN + 4);
+    static constexpr int TOTAL = A + B;
+};
+
+template <int BM, int BN, bool VEC, bool SPLIT>
+__global__ void __launch_bounds__(256) k_sgemm(const SgArgs a) {
+    constexpr int TM = BM / 16, TN = BN / 16;
+    constexpr int LX = BM / 64, LW = BN / 64;
+    __shared__ __align__(16) float sm[SgSmem<BM, BN>::TOTAL];
+    float(*As)[SG_BK][BM + 4] = reinterpret_cast<float(*)[SG_BK][BM + 4]>(sm);
+    float(*Bs)[SG_BK][BN + 4] = reinterpret_cast<float(*)[SG_BK][BN + 4]>(sm + SgSmem<BM, BN>::A);
+
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kb = SPLIT ? blockIdx.z * a.kchunk : 0;
+    const int ke = SPLIT ? min(a.K, kb + a.kchunk) : a.K;
+    const int nkt = ke > kb ? (ke - kb + SG_BK - 1) / SG_BK : 0;
+
+    float4 rx[LX], rw[LW];
+    auto ld4 = [&](const float* base, int ld, int r, int rmax, int k) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rmax && k < ke) {
+            const float* p = base + (size_t)r * ld + k;
+            if (VEC) {
+                v = __ldg(reinterpret_cast<const float4*>(p));
+            } else {
+                v.x = __ldg(p);
+                if (k + 1 < ke) v.y = __ldg(p + 1);
+                if (k + 2 < ke) v.z = __ldg(p + 2);
+                if (k + 3 < ke) v.w = __ldg(p + 3);
+            }
+        }
+        return v;
+    };
+    auto gload = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < LX; i++) {
+            const int f = tid + 256 * i;
+            rx[i] = ld4(a.X, a.ldx, m0 + (f >> 2), a.M, k0 + (f & 3) * 4);
+        }
+#pragma unroll
+        for (int i = 0; i < LW; i++) {
+            const int f = tid + 256 * i;
+            rw[i] = ld4(a.W, a.ldw, n0 + (f >> 2), a.N, k0 + (f & 3) * 4);
+        }
+    };
+    auto sstore = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < LX; i++) {
+            const int f = tid + 256 * i, r = f >> 2, k = (f & 3) * 4;
+            As[buf][k][r] = rx[i].x;
+            As[buf][k + 1][r] = rx[i].y;
+            As[buf][k + 2][r] = rx[i].z;
+            As[buf][k + 3][r] = rx[i].w;
+        }
+#pragma unroll
+        for (int i = 0; i < LW; i++) {
+            const int f = tid + 256 * i, r = f >> 2, k = (f & 3) * 4;
+            Bs[buf][k][r] = rw[i].x;
+            Bs[buf][k + 1][r] = rw[i].y;
+            Bs[buf][k + 2][r] = rw[i].z;
+            Bs[buf][k + 3][r] = rw[i].w;
+        }
+    };
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = 0.f;
+
+    if (nkt > 0) {
+        gload(kb);
+        sstore(0);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nkt; kt++) {
+        const int cur = kt & 1;
+        if (kt + 1 < nkt) gload(kb + (kt + 1) * SG_BK);
+#pragma unroll
+        for (int k = 0; k < SG_BK; k++) {
+            float av[TM], bv[TN];
+#pragma unroll
+            for (int g = 0; g < TM / 4; g++) {
+                const float4 t = *reinterpret_cast<const float4*>(&As[cur][k][g * 64 + ty * 4]);
+                av[g * 4] = t.x;
+                av[g * 4 + 1] = t.y;
+                av[g * 4 + 2] = t.z;
+                av[g * 4 + 3] = t.w;
+            }
+#pragma unroll
+            for (int g = 0; g < TN / 4; g++) {
+                const float4 t = *reinterpret_cast<const float4*>(&Bs[cur][k][g * 64 + tx * 4]);
+                bv[g * 4] = t.x;
+                bv[g * 4 + 1] = t.y;
+                bv[g * 4 + 2] = t.z;
+                bv[g * 4 + 3] = t.w;
+            }
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (kt + 1 < nkt) sstore(cur ^ 1);
+        __syncthreads();
+    }
+
+    auto epilogue = [&](int m, int n, float v) {
+        if (m < a.M && n < a.N) {
+            float* y = a.Y + (size_t)m * a.ldy + n;
+            if (a.beta != 0.f) v += a.beta * *y;
+            if (a.bias) v += __ldg(a.bias + n);
+            *y = apply_act(v, a.act);
+        }
+    };
+
+    if constexpr (!SPLIT) {
+#pragma unroll
+        for (int i = 0; i < TM; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++)
+                epilogue(m0 + (i / 4) * 64 + ty * 4 + (i & 3), n0 + (j / 4) * 64 + tx * 4 + (j & 3), acc[i][j]);
+    } else {
+        // partial tile -> own shared memory; rank r then sums rows [r*BM/S, (r+1)*BM/S) over all ranks in rank
+        // order (deterministic) and runs the epilogue for them
+        static_assert(BM * BN <= SgSmem<BM, BN>::TOTAL, "partial tile must fit the operand buffers");
+        cg::cluster_group cl = cg::this_cluster();
+        float* red = sm;
+#pragma unroll
+        for (int i = 0; i < TM; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++)
+                red[((i / 4) * 64 + ty * 4 + (i & 3)) * BN + (j / 4) * 64 + tx * 4 + (j & 3)] = acc[i][j];
+        cl.sync();
+        const int S = (int)cl.num_blocks(), r = (int)cl.block_rank();
+        const int rows = BM / S;
+        for (int e = tid; e < rows * BN; e += 256) {
+            const int row = r * rows + e / BN, col = e % BN;
+            float v = 0.f;
+            for (int q = 0; q < S; q++) v += cl.map_shared_rank(red, q)[row * BN + col];
+            epilogue(m0 + row, n0 + col, v);
+        }
+        cl.sync();  // keep this CTA's partial alive until every rank has read it
+    }
+}
+
+// ================================================================================================ rel-pos attention
+
+constexpr int RP_B = 64;     // query rows per CTA, keys / pp rows per tile
+constexpr int RP_LD = 72;    // padded shared row (halves): conflict-free ldmatrix
+constexpr int RP_MAXT = 384; // src/audio.rs:401
+
+struct RpArgs {
+    const __half* qu;
+    const __half* qv;
+    const __half* k;
+    const __half* v;
+    const __half* pp;
+    __half* o;
+    const int* offs;
+    int ld, ldp, pp_rows, pp_center, ldo, max_len, srow;
+    float scale;
+};
+
+__device__ int g_rp_err = 0;
+
+__global__ void __launch_bounds__(256) k_relpos_attn(const RpArgs a) {
+    extern __shared__ __align__(16) uint8_t rp_smem[];
+    __half* sQu = reinterpret_cast<__half*>(rp_smem);   // [64][RP_LD]
+    __half* sQv = sQu + RP_B * RP_LD;                    // [64][RP_LD]
+    __half* sT = sQv + RP_B * RP_LD;                     // [2][64][RP_LD] tile ring
+    float* sS = reinterpret_cast<float*>(sT + 2 * RP_B * RP_LD);  // [64][srow] scores; P aliases each row
+
+    const int clip = blockIdx.y, h = blockIdx.z;
+    const int start = a.offs[clip], len = a.offs[clip + 1] - start;
+    const int i0 = blockIdx.x * RP_B;
+    if (len > a.max_len || len < 0) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(&g_rp_err, 1);
+        return;
+    }
+    if (i0 >= len) return;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int nk = (len + RP_B - 1) / RP_B;
+    const int np = (len + 2 * RP_B - 2) / RP_B;        // pp rows center-(i0+63) .. center+len-1-i0
+    const int mbase = a.pp_center - i0 - (RP_B - 1);
+    const int ntiles = nk + np + nk;
+    const int hc = h * 64;
+
+    // Q tiles (qu, qv) of this head; committed together with tile 0
+    for (int i = tid; i < 2 * RP_B * 8; i += 256) {
+        const int which = i / (RP_B * 8), r = (i / 8) % RP_B, c = (i % 8) * 8;
+        const bool ok = i0 + r < len;
+        const __half* base = which ? a.qv : a.qu;
+        const __half* src = ok ? base + (size_t)(start + i0 + r) * a.ld + hc + c : base;
+        cp_async16(smem_u32((which ? sQv : sQu) + r * RP_LD + c), src, ok);
+    }
+    auto load_tile = [&](int q, int buf) {
+        __half* dst = sT + buf * RP_B * RP_LD;
+        for (int i = tid; i < RP_B * 8; i += 256) {
+            const int r = i / 8, c = (i % 8) * 8;
+            const __half* src = a.k;
+            bool ok;
+            if (q < nk) {
+                const int j = q * RP_B + r;
+                ok = j < len;
+                if (ok) src = a.k + (size_t)(start + j) * a.ld + hc + c;
+            } else if (q < nk + np) {
+                const int m = mbase + (q - nk) * RP_B + r;
+                ok = m >= 0 && m < a.pp_rows;
+                if (ok) src = a.pp + (size_t)m * a.ldp + hc + c;
+            } else {
+                const int j = (q - nk - np) * RP_B + r;
+                ok = j < len;
+                if (ok) src = a.v + (size_t)(start + j) * a.ld + hc + c;
+            }
+            cp_async16(smem_u32(dst + r * RP_LD + c), src, ok);
+        }
+        cp_async_commit();
+    };
+
+    const int wr = (warp & 3) * 16, wc = (warp >> 2) * 32;  // warp's 16 rows x 32 columns of a 64 x 64 tile
+    const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lc = (lane >> 4) * 8;
+    uint32_t qa[4][4];
+    float o[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    __half* sP = reinterpret_cast<__half*>(sS);
+    const int prow = a.srow * 2;  // P row pitch in halves (P row r overlays S row r)
+
+    load_tile(0, 0);
+    for (int q = 0; q < ntiles; q++) {
+        const int buf = q & 1;
+        if (q + 1 < ntiles) {
+            load_tile(q + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const __half* T = sT + buf * RP_B * RP_LD;
+
+        if (q == 0 || q == nk) {  // A fragments: qu for the qu.k^T tiles, qv for the qv.pp^T tiles
+            const __half* Qs = q == 0 ? sQu : sQv;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+                ldsm_x4(qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], smem_u32(Qs + (wr + lr) * RP_LD + kk * 16 + lc));
+        }
+        if (q < nk + np) {
+            float acc[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 4; nt++) {
+                acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(b0, b1, b2, b3, smem_u32(T + (wc + nt * 8 + (lane & 7)) * RP_LD + kk * 16 + (lane >> 3) * 8));
+                    mma16816(acc[nt], qa[kk], b0, b1);
+                    mma16816(acc[nt], qa[kk + 1], b2, b3);
+                }
+            }
+            if (q < nk) {  // ac tile -> S[:, q*64 + col]
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++) {
+                    const int col = q * RP_B + wc + nt * 8 + 2 * tig;
+                    *reinterpret_cast<float2*>(sS + (wr + gid) * a.srow + col) = make_float2(acc[nt][0], acc[nt][1]);
+                    *reinterpret_cast<float2*>(sS + (wr + gid + 8) * a.srow + col) = make_float2(acc[nt][2], acc[nt][3]);
+                }
+            } else {  // bd tile: pp row m = mbase + 64(q-nk) + col pairs with key j = m - center + i
+                const int jb = (q - nk) * RP_B - (RP_B - 1);
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int r = wr + gid + (e >> 1) * 8;
+                        const int j = jb + wc + nt * 8 + 2 * tig + (e & 1) + r;
+                        if (j >= 0 && j < len) sS[r * a.srow + j] += acc[nt][e];
+                    }
+            }
+        }
+        if (q == nk + np - 1) {
+            __syncthreads();  // the score block is complete
+            // exact row softmax (cuda/kernels.cu:583-616): max, sum of expf, P = fp16(expf(s - max) / sum)
+            for (int rr = 0; rr < 8; rr++) {
+                const int r = warp * 8 + rr;
+                const bool valid = i0 + r < len;
+                float* Srow = sS + r * a.srow;
+                float vals[RP_MAXT / 32];
+                float mx = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < RP_MAXT / 32; u++) {
+                    const int j = lane + 32 * u;
+                    vals[u] = valid && j < len ? Srow[j] * a.scale : -INFINITY;
+                    mx = fmaxf(mx, vals[u]);
+                }
+                mx = warp_max(mx);
+                float sum = 0.f;
+#pragma unroll
+                for (int u = 0; u < RP_MAXT / 32; u++)
+                    if (lane + 32 * u < len) sum += expf(vals[u] - mx);
+                sum = warp_sum(sum);
+                const float inv = 1.f / sum;
+                __syncwarp();  // every lane has read the row before P overwrites it
+                __half* Prow = sP + r * prow;
+#pragma unroll
+                for (int u = 0; u < RP_MAXT / 32; u++) {
+                    const int j = lane + 32 * u;
+                    if (j < nk * RP_B) Prow[j] = __float2half(valid && j < len ? expf(vals[u] - mx) * inv : 0.f);
+                }
+            }
+            __syncthreads();
+        }
+        if (q >= nk + np) {  // O += P[:, 64kt .. 64kt+63] . V tile
+            const int kt = q - nk - np;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                uint32_t pa[4];
+                ldsm_x4(pa[0], pa[1], pa[2], pa[3], smem_u32(sP + (wr + lr) * prow + kt * RP_B + kk * 16 + lc));
+#pragma unroll
+                for (int dt = 0; dt < 4; dt += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(b0, b1, b2, b3, smem_u32(T + (kk * 16 + lr) * RP_LD + wc + dt * 8 + lc));
+                    mma16816(o[dt], pa, b0, b1);
+                    mma16816(o[dt + 1], pa, b2, b3);
+                }
+            }
+        }
+        __syncthreads();  // tile buffer `buf` is free for the load issued next iteration
+    }
+
+    // fp16 output rows of this head
+#pragma unroll
+    for (int dt = 0; dt < 4; dt++) {
+        const int c = hc + wc + dt * 8 + 2 * tig;
+        const int r0 = i0 + wr + gid, r1 = r0 + 8;
+        if (r0 < len) *reinterpret_cast<uint32_t*>(a.o + (size_t)(start + r0) * a.ldo + c) = pack_h2(o[dt][0], o[dt][1]);
+        if (r1 < len) *reinterpret_cast<uint32_t*>(a.o + (size_t)(start + r1) * a.ldo + c) = pack_h2(o[dt][2], o[dt][3]);
+    }
+}
+
+int rp_smem_bytes(int max_len) {
+    const int srow = (max_len + RP_B - 1) / RP_B * RP_B + 4;
+    return 4 * RP_B * RP_LD * 2 + RP_B * srow * 4;
+}
+
+template <int BM, int BN, bool VEC, bool SPLIT>
+int launch_sgemm(const SgArgs& a, int split, cudaStream_t st) {
+    dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM, split);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (SPLIT) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = split;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaLaunchKernelEx(&cfg, k_sgemm<BM, BN, VEC, SPLIT>, a);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+int d1_sgemm(int M, int N, int K, const float* X, int ldx, const float* W, int ldw, float* Y, int ldy, float beta,
+             const float* bias, int act, cudaStream_t st) {
+    if (M < 0 || N < 0 || K < 0 || act < 0 || act > 4) return -1;
+    if (M == 0 || N == 0) return 0;
+    if (!X || !W || !Y || ldx < K || ldw < K || ldy < N) return -1;
+    SgArgs a{X, W, Y, bias, M, N, K, ldx, ldw, ldy, act, K, beta};
+    const bool vec = K % 4 == 0 && ldx % 4 == 0 && ldw % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
+    const long tiles128 = (long)((M + 127) / 128) * ((N + 127) / 128);
+    if (tiles128 >= 148) {
+        return vec ? launch_sgemm<128, 128, true, false>(a, 1, st) : launch_sgemm<128, 128, false, false>(a, 1, st);
+    }
+    const long tiles64 = (long)((M + 63) / 64) * ((N + 63) / 64);
+    int split = 1;
+    while (split < 8 && tiles64 * split < 2 * 148 && K / (2 * split) >= 128) split *= 2;
+    if (split == 1)
+        return vec ? launch_sgemm<64, 64, true, false>(a, 1, st) : launch_sgemm<64, 64, false, false>(a, 1, st);
+    a.kchunk = ((K + split - 1) / split + SG_BK - 1) / SG_BK * SG_BK;
+    return vec ? launch_sgemm<64, 64, true, true>(a, split, st) : launch_sgemm<64, 64, false, true>(a, split, st);
+}
+
+int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const d1_half* v, int ld,
+                   const d1_half* pp, int ldp, int pp_rows, int pp_center, d1_half* o, int ldo, const int* offs,
+                   int n_clips, int max_len, int heads, float scale, cudaStream_t st) {
+    if (n_clips < 0 || max_len < 0 || max_len > RP_MAXT || heads < 1) return -1;
+    if (n_clips == 0 || max_len == 0) return 0;
+    if (!qu || !qv || !k || !v || !pp || !o || !offs) return -1;
+    if (ld % 8 || ldp % 8 || ldo % 2 || ld < heads * 64 || ldp < heads * 64 || ldo < heads * 64 || pp_rows < 1)
+        return -1;
+    for (const void* p : {(const void*)qu, (const void*)qv, (const void*)k, (const void*)v, (const void*)pp})
+        if ((uintptr_t)p & 15) return -1;
+    if ((uintptr_t)o & 3) return -1;
+    const int smem = rp_smem_bytes(max_len);
+    static unsigned long long attr_done = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(__atomic_load_n(&attr_done, __ATOMIC_ACQUIRE) & bit)) {
+        if (cudaFuncSetAttribute(k_relpos_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, rp_smem_bytes(RP_MAXT)) !=
+            cudaSuccess)
+            return -1;
+        __atomic_fetch_or(&attr_done, bit, __ATOMIC_RELEASE);
+    }
+    RpArgs a{reinterpret_cast<const __half*>(qu), reinterpret_cast<const __half*>(qv),
+             reinterpret_cast<const __half*>(k),  reinterpret_cast<const __half*>(v),
+             reinterpret_cast<const __half*>(pp), reinterpret_cast<__half*>(o),
+             offs, ld, ldp, pp_rows, pp_center, ldo, max_len, (max_len + RP_B - 1) / RP_B * RP_B + 4, scale};
+    dim3 grid((max_len + RP_B - 1) / RP_B, n_clips, heads);
+    k_relpos_attn<<<grid, 256, smem, st>>>(a);
+    return (int)cudaGetLastError();
+}
+
+int d1_relpos_attn_error(void) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_rp_err, sizeof(int)) != cudaSuccess) return -1;
+    if (v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_rp_err, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // extern "C"

@@ -121,6 +121,29 @@ struct Kt {
     }
 };
 
+// IEEE binary32 -> binary16 bits, round to nearest even (overflow to infinity, gradual underflow).
+uint16_t f32_to_f16_bits(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000);
+    x &= 0x7fffffffu;
+    if (x >= 0x7f800000u) return sign | (x > 0x7f800000u ? 0x7e00 : 0x7c00);
+    if (x >= 0x477ff000u) return sign | 0x7c00;  // >= 65520 rounds past the largest half
+    if (x < 0x38800000u) {                      // half subnormal range (|f| < 2^-14)
+        if (x < 0x33000000u) return sign;        // below half of the smallest subnormal
+        const int shift = 126 - (int)(x >> 23);
+        const uint32_t m = (x & 0x7fffffu) | 0x800000u;
+        uint32_t r = m >> shift;
+        const uint32_t rem = m & ((1u << shift) - 1), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (r & 1))) r++;
+        return sign | (uint16_t)r;
+    }
+    uint32_t r = (x >> 13) - (112u << 10);      // rebias the exponent (127 -> 15)
+    const uint32_t rem = x & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1))) r++;
+    return sign | (uint16_t)r;
+}
+
 // RoPE table [pos][32] of (cos, sin), computed as src/model.rs:121-136 does: fp32 inverse frequency, fp32 angle
 // p * f, then cos/sin in double precision rounded to float.
 std::vector<float> rope_table(float theta) {
@@ -959,6 +982,258 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
     cudaEventRecord(v->done, st);
     v->busy = true;
     return 0;
+}
+
+}  // extern "C"
+
+// ================================================================================================ audio encoder
+// AudioModel (src/audio.rs:302-455) and AudioModel::encode (:505-594), with several clips per call: each clip's
+// subsampling runs on its own rows, then the conformer layers and the adapter run once over all clips' rows
+// (every op is row-wise except the depthwise conv, launched per clip, and the rel-pos attention, which takes the
+// clip offsets). The relative-position projections pp = pe . linear_pos^T depend only on the weights and the
+// relative position, so they are computed once at create for positions -(MAX_T-1) .. MAX_T-1 (one table per
+// layer) instead of per clip and layer (src/audio.rs:546-558, 568).
+
+namespace {
+constexpr int AD = 512;          // src/audio.rs:16
+constexpr int AHEADS = 8;        // :17
+constexpr int SUB_C = 256;       // :18
+constexpr int AOUT = 1024;       // :19
+constexpr int N_MELS = 128;      // :15
+constexpr int A_MAX_T = 384;     // :401
+constexpr int A_MAX_VALID = 3000;  // 30 s at hop 160 (src/audio.rs:11-14, 241-247)
+constexpr int PP_ROWS = 2 * A_MAX_T - 1;
+constexpr int PP_CENTER = A_MAX_T - 1;
+
+// pe rows for relative positions PP_CENTER - m, m = 0 .. PP_ROWS-1, as src/audio.rs:546-558 computes each row:
+// fp32 frequency exp(2i * -(ln 10000 / 512)), fp32 angle p * f, sin / cos in double, rounded to fp16.
+std::vector<uint16_t> audio_pe_table() {
+    std::vector<uint16_t> pe((size_t)PP_ROWS * AD);
+    const float c = (float)(-(log(10000.0) / (double)AD));
+    for (int m = 0; m < PP_ROWS; m++) {
+        const float p = (float)(PP_CENTER - m);
+        for (int i = 0; i < AD / 2; i++) {
+            const float div = expf((float)(2 * i) * c);
+            const double a = (double)(p * div);
+            pe[(size_t)m * AD + 2 * i] = f32_to_f16_bits((float)sin(a));
+            pe[(size_t)m * AD + 2 * i + 1] = f32_to_f16_bits((float)cos(a));
+        }
+    }
+    return pe;
+}
+
+int audio_out_len(int valid) {
+    const int l1 = (valid - 1) / 2 + 1, l2 = (l1 - 1) / 2 + 1;
+    return (l2 - 1) / 2 + 1;
+}
+}  // namespace
+
+struct D1Audio {
+    void* lt = nullptr;
+    D1AudioWeights w{};
+    std::vector<D1AudioLayer> layers;
+    bool fused = true;
+    int max_rows = 0;
+    long long launches = 0;
+    d1_half* pp = nullptr;          // [n_layers][PP_ROWS][512]
+    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *s3 = nullptr, *x = nullptr;
+    d1_half *xn = nullptr, *big = nullptr, *qu = nullptr, *qv = nullptr, *kk = nullptr, *vv = nullptr, *o = nullptr;
+    int* offs = nullptr;
+    int* host_offs = nullptr;
+    cudaEvent_t done = nullptr;
+    bool busy = false;
+};
+
+extern "C" {
+
+D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
+    if (!w || w->n_layers <= 0 || !w->layers || max_rows <= 0 || max_rows > (1 << 20)) {
+        fail("invalid audio weights or capacity");
+        return nullptr;
+    }
+    D1Audio* a = new D1Audio();
+    a->w = *w;
+    a->layers.assign(w->layers, w->layers + w->n_layers);
+    a->w.layers = nullptr;
+    a->fused = fused != 0;
+    a->max_rows = max_rows;
+    const size_t R = max_rows, L1 = (A_MAX_VALID - 1) / 2 + 1, L2 = (L1 - 1) / 2 + 1;
+    int e = 0;
+    a->lt = d1_lt_init(0);
+    if (!a->lt) e = fail("d1_lt_init failed");
+    if (!e) e |= dmalloc(&a->pp, (size_t)w->n_layers * PP_ROWS * AD * 2);
+    if (!e) e |= dmalloc(&a->mel, std::min<size_t>(R * 8, (size_t)64 * A_MAX_VALID) * N_MELS * 4);
+    if (!e) e |= dmalloc(&a->s1, L1 * 64 * SUB_C * 4);
+    if (!e) e |= dmalloc(&a->s2, L2 * 32 * SUB_C * 4);
+    if (!e) e |= dmalloc(&a->s3, L2 * 32 * SUB_C * 4);
+    if (!e) e |= dmalloc(&a->x, R * AD * 4);
+    if (!e) e |= dmalloc(&a->xn, R * AOUT * 2);
+    if (!e) e |= dmalloc(&a->big, R * 4 * AD * 2);
+    for (d1_half** p : {&a->qu, &a->qv, &a->kk, &a->vv, &a->o})
+        if (!e) e |= dmalloc(p, R * AD * 2);
+    if (!e) e |= dmalloc(&a->offs, 4096 * 4);
+    if (!e && (cudaMallocHost((void**)&a->host_offs, 4096 * 4) != cudaSuccess ||
+               cudaEventCreateWithFlags(&a->done, cudaEventDisableTiming) != cudaSuccess))
+        e = fail("audio host allocation failed");
+    if (!e) {  // per-layer relative-position projections
+        std::vector<uint16_t> pe = audio_pe_table();
+        d1_half* dpe = nullptr;
+        e |= dmalloc(&dpe, pe.size() * 2);
+        if (!e && cudaMemcpy(dpe, pe.data(), pe.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+            e = fail("pe upload failed");
+        for (int l = 0; l < w->n_layers && !e; l++) {
+            a->launches++;
+            if (d1_lt_gemm(a->lt, PP_ROWS, AD, AD, dpe, AD, a->layers[l].pos, AD, 0, a->pp + (size_t)l * PP_ROWS * AD,
+                           AD, 0, 0, 1.f, 0.f, 0))
+                e = fail("pp projection failed");
+        }
+        if (!e && cudaDeviceSynchronize() != cudaSuccess) e = fail("pp projection failed");
+        if (dpe) cudaFree(dpe);
+    }
+    if (e) {
+        d1h_audio_destroy(a);
+        return nullptr;
+    }
+    return a;
+}
+
+void d1h_audio_destroy(D1Audio* a) {
+    if (!a) return;
+    if (a->busy) cudaEventSynchronize(a->done);
+    for (void* p : {(void*)a->pp, (void*)a->mel, (void*)a->s1, (void*)a->s2, (void*)a->s3, (void*)a->x, (void*)a->xn,
+                    (void*)a->big, (void*)a->qu, (void*)a->qv, (void*)a->kk, (void*)a->vv, (void*)a->o,
+                    (void*)a->offs})
+        if (p) cudaFree(p);
+    if (a->host_offs) cudaFreeHost(a->host_offs);
+    if (a->done) cudaEventDestroy(a->done);
+    if (a->lt) d1_lt_destroy(a->lt);
+    delete a;
+}
+
+int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel, float* out, cudaStream_t st) {
+    if (!a || n_clips <= 0 || n_clips > 4095 || !valid || !mel || !out) return fail("bad arguments");
+    int rows = 0, max_t = 0;
+    long long frames = 0;
+    for (int c = 0; c < n_clips; c++) {
+        if (valid[c] < 1 || valid[c] > A_MAX_VALID) return fail("clip frames must be 1 .. 3000");
+        const int t = audio_out_len(valid[c]);
+        rows += t;
+        max_t = std::max(max_t, t);
+        frames += valid[c];
+    }
+    if (rows > a->max_rows || frames * N_MELS * 4 > (long long)std::min<size_t>((size_t)a->max_rows * 8,
+                                                                                    (size_t)64 * A_MAX_VALID) *
+                                                         N_MELS * 4)
+        return fail("clips exceed the audio batch capacity");
+    if (a->busy) {
+        if (cudaEventSynchronize(a->done) != cudaSuccess) return fail("event sync failed");
+        a->busy = false;
+    }
+    a->host_offs[0] = 0;
+    for (int c = 0; c < n_clips; c++) a->host_offs[c + 1] = a->host_offs[c] + audio_out_len(valid[c]);
+    if (cudaMemcpyAsync(a->offs, a->host_offs, (size_t)(n_clips + 1) * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(a->mel, mel, (size_t)frames * N_MELS * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail("audio upload failed");
+    long long& L = a->launches;
+    const D1AudioWeights& w = a->w;
+    const bool fz = a->fused;
+    // fp32 pointwise GEMM of the subsampling with bias (+ReLU), fused or in the reference's three calls
+    auto sgemm_ba = [&](int m, int n, int k, const float* x, const float* wt, float* y, const float* b, int act) -> int {
+        if (fz) {
+            L++;
+            return d1_sgemm(m, n, k, x, k, wt, k, y, n, 0.f, b, act, st);
+        }
+        L += 3;
+        int r = d1_fill_rows(y, b, nullptr, m, n, st);
+        if (!r) r = d1_sgemm(m, n, k, x, k, wt, k, y, n, 1.f, nullptr, 0, st);
+        if (!r && act) r = d1_bias_act_f(y, nullptr, m, n, act, st);
+        return r;
+    };
+    // ---- subsampling per clip (src/audio.rs:511-525) into rows offs[c] .. of x
+    const float* melc = a->mel;
+    for (int c = 0; c < n_clips; c++) {
+        const int v = valid[c], l1 = (v - 1) / 2 + 1, l2 = (l1 - 1) / 2 + 1, t = audio_out_len(v);
+        L += 3;
+        CK(d1_sub_conv0(melc, v, N_MELS, w.c0_w, w.c0_b, a->s1, l1, 64, st));
+        CK(d1_sub_dwconv(a->s1, l1, 64, w.c2_w, w.c2_b, a->s2, l2, 32, st));
+        CK(sgemm_ba(l2 * 32, SUB_C, SUB_C, a->s2, w.c3_w, a->s3, w.c3_b, 1));
+        CK(d1_sub_dwconv(a->s3, l2, 32, w.c5_w, w.c5_b, a->s2, t, 16, st));
+        CK(sgemm_ba(t * 16, SUB_C, SUB_C, a->s2, w.c6_w, a->s1, w.c6_b, 1));
+        CK(sgemm_ba(t, AD, 16 * SUB_C, a->s1, w.pre_out, a->x + (size_t)a->host_offs[c] * AD, w.pre_out_b, 0));
+        melc += (size_t)v * N_MELS;
+    }
+    // ---- conformer layers over all rows (src/audio.rs:561-588)
+    const int R = rows;
+    float* x = a->x;
+    d1_half *xn = a->xn, *big = a->big, *o = a->o;
+    auto ln = [&](float* xx, const float* pb, float ps, const float* g, const float* b, d1_half* y, float* yf,
+                  int d) -> int {
+        L++;
+        return d1_layernorm(xx, pb, ps, g, b, y, yf, R, d, w.eps, st);
+    };
+    auto gemm_h = [&](int n, int k, const d1_half* in, const d1_half* wt, d1_half* y, const float* b, int act) -> int {
+        if (fz && b) {
+            L++;
+            return d1_gemm_bias_act(a->lt, R, n, k, in, k, wt, k, b, act, y, n, st);
+        }
+        L++;
+        int r = d1_lt_gemm(a->lt, R, n, k, in, k, wt, k, 0, y, n, 0, 0, 1.f, 0.f, st);
+        if (!r && b) {
+            L++;
+            r = d1_bias_act_h(y, b, R, n, act, st);
+        }
+        return r;
+    };
+    auto gemm_add = [&](int n, int k, const d1_half* in, const d1_half* wt, float* y, float alpha) -> int {
+        L++;
+        return d1_lt_gemm(a->lt, R, n, k, in, k, wt, k, 0, y, n, 1, 0, alpha, 1.f, st);
+    };
+    const int ff = 4 * AD;
+    for (size_t li = 0; li < a->layers.size(); li++) {
+        const D1AudioLayer& l = a->layers[li];
+        // FF1 half step (pending bias of the previous layer's norm_out is none: it replaced x)
+        CK(ln(x, nullptr, 1.f, l.ff1_n_w, l.ff1_n_b, xn, nullptr, AD));
+        CK(gemm_h(ff, AD, xn, l.ff1_up, big, l.ff1_up_b, 4));
+        CK(gemm_add(AD, ff, big, l.ff1_down, x, 0.5f));
+        // rel-pos self-attention
+        CK(ln(x, l.ff1_down_b, 0.5f, l.att_n_w, l.att_n_b, xn, nullptr, AD));
+        CK(gemm_h(3 * AD, AD, xn, l.qkv, big, nullptr, 0));
+        L += 2;
+        CK(d1_relpos_prep(big, l.bq, l.bk, l.bv, l.pu, l.pv, a->qu, a->qv, a->kk, a->vv, R, AD, st));
+        CK(d1_relpos_attn(a->qu, a->qv, a->kk, a->vv, AD, a->pp + li * PP_ROWS * AD, AD, PP_ROWS, PP_CENTER, o, AD,
+                          a->offs, n_clips, max_t, AHEADS, 0.125f, st));
+        CK(gemm_add(AD, AD, o, l.out, x, 1.f));
+        // conv module: pw1 -> GLU / depthwise 9 / BN / SiLU (per clip: zero padding at the clip's edges) -> pw2
+        CK(ln(x, l.out_b, 1.f, l.conv_n_w, l.conv_n_b, xn, nullptr, AD));
+        CK(gemm_h(2 * AD, AD, xn, l.pw1, big, nullptr, 0));
+        for (int c = 0; c < n_clips; c++) {
+            const int s = a->host_offs[c], t = a->host_offs[c + 1] - s;
+            L++;
+            CK(d1_conformer_dw(big + (size_t)s * 2 * AD, l.pw1_b, l.dw, l.dw_b, l.bn_s, l.bn_b, o + (size_t)s * AD, t,
+                               AD, 9, st));
+        }
+        CK(gemm_add(AD, AD, o, l.pw2, x, 1.f));
+        // FF2 half step
+        CK(ln(x, l.pw2_b, 1.f, l.ff2_n_w, l.ff2_n_b, xn, nullptr, AD));
+        CK(gemm_h(ff, AD, xn, l.ff2_up, big, l.ff2_up_b, 4));
+        CK(gemm_add(AD, ff, big, l.ff2_down, x, 0.5f));
+        // norm_out replaces the residual stream
+        CK(ln(x, l.ff2_down_b, 0.5f, l.out_n_w, l.out_n_b, nullptr, x, AD));
+    }
+    // ---- adapter (src/audio.rs:589-593): LN -> Linear -> GELU -> Linear, then a + up(GELU(down(LN(a))))
+    CK(ln(x, nullptr, 1.f, w.ad_n_w, w.ad_n_b, xn, nullptr, AD));
+    CK(gemm_h(AOUT, AD, xn, w.ad1, big, w.ad1_b, 2));
+    L++;
+    CK(d1_fill_rows(out, w.ad2_b, nullptr, R, AOUT, st));
+    CK(gemm_add(AOUT, AOUT, big, w.ad2, out, 1.f));
+    CK(ln(out, nullptr, 1.f, w.res_n_w, w.res_n_b, xn, nullptr, AOUT));
+    CK(gemm_h(AD, AOUT, xn, w.res_down, big, w.res_down_b, 2));
+    CK(gemm_add(AOUT, AD, big, w.res_up, out, 1.f));
+    L++;
+    CK(d1_bias_act_f(out, w.res_up_b, R, AOUT, 0, st));
+    cudaEventRecord(a->done, st);
+    a->busy = true;
+    return R;
 }
 
 }  // extern "C"

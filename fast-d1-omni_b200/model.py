@@ -242,3 +242,75 @@ class VisionModel:
             self.close()
         except Exception:
             pass
+
+
+_AUDIO_F16 = {"ff1_up", "ff1_down", "qkv", "pos", "out", "pw1", "pw2", "ff2_up", "ff2_down", "ad1", "ad2", "res_down",
+              "res_up"}
+
+
+class AudioModel:
+    """Device copy of `weights.audio_weights(...)` plus the audio runner (include/d1h.h d1h_audio_*)."""
+
+    def __init__(self, w: dict, device: int = 0, fused: bool = True, max_rows: int = 1536):
+        self.device = torch.device("cuda", device)
+        self.L = lib()
+        self._keep = []
+
+        def dev(name, a):
+            dt = np.float16 if name in _AUDIO_F16 else np.float32
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=dt)).to(self.device)
+            self._keep.append(t)
+            return _ptr(t)
+
+        with torch.cuda.device(self.device):
+            layers = (abi.AudioLayer * len(w["layers"]))()
+            for i, l in enumerate(w["layers"]):
+                for name, _ in abi.AudioLayer._fields_:
+                    setattr(layers[i], name, dev(name, l[name]))
+            aw = abi.AudioWeights()
+            for name, _ in abi.AudioWeights._fields_:
+                if name not in ("n_layers", "layers", "eps"):
+                    setattr(aw, name, dev(name, w[name]))
+            aw.n_layers = len(w["layers"])
+            aw.layers = layers
+            aw.eps = float(w["eps"])
+            torch.cuda.synchronize(self.device)
+            self.a = self.L.d1h_audio_create(C.byref(aw), int(fused), max_rows)
+            if not self.a:
+                raise RuntimeError(f"d1h_audio_create failed: {self.L.d1h_last_error().decode()}")
+        self.max_rows = max_rows
+
+    @staticmethod
+    def out_len(valid: int) -> int:
+        l1 = (valid - 1) // 2 + 1
+        l2 = (l1 - 1) // 2 + 1
+        return (l2 - 1) // 2 + 1
+
+    def encode(self, clips, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """clips: [(mel fp32 [>= valid, 128], valid)] -> fp32 [sum ceil(valid/8), 1024] on the device."""
+        n = len(clips)
+        valid = (C.c_int * n)(*[int(v) for _, v in clips])
+        mel = np.ascontiguousarray(np.concatenate([np.asarray(m, np.float32)[:v] for m, v in clips]), np.float32)
+        rows = sum(self.out_len(v) for _, v in clips)
+        if out is None:
+            out = torch.empty(rows, 1024, device=self.device, dtype=torch.float32)
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        with torch.cuda.device(self.device):
+            r = self.L.d1h_audio_encode(self.a, n, valid, C.c_void_p(mel.ctypes.data), _ptr(out),
+                                        C.c_void_p(s.cuda_stream))
+        if r < 0:
+            raise RuntimeError(f"d1h_audio_encode failed: {self.L.d1h_last_error().decode()}")
+        assert r == rows
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "a", None):
+            self.L.d1h_audio_destroy(self.a)
+            self.a = None
+        self._keep.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

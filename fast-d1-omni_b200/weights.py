@@ -201,3 +201,78 @@ def vision_crops(seed=3, n_images=16, lo=224, hi=768):
         ph, pw = hh // 16, ww // 16
         crops.append((ph, pw, rng.uniform(0.0, 1.0, size=(ph * pw, VD)).astype(np.float16)))
     return crops
+
+
+# ------------------------------------------------------------------------------------------------ audio
+
+AD = 512        # src/audio.rs:16 (DM)
+AHEADS = 8      # :17
+SUB_C = 256     # :18
+AOUT = 1024     # :19
+N_MELS = 128    # :15
+A_MAX_T = 384   # :401
+
+
+def audio_weights(seed=4, n_layers=17, eps=1e-5):
+    """FastConformer encoder + adapter weights in the layout src/audio.rs:302-455 builds on the device: fused QKV
+    rows [q; k; v], pos_bias_u/v flattened [8*64], the pre-encode output weight with its columns already in the
+    (f, c) order the subsampled activations use, subsampling convs fp32 [256][9] / [256][256]. Subsampling
+    weights use std 1/sqrt(fan_in) so the fp32 front keeps unit scale; the rest follow the text weights' recipe
+    (matrices N(0, 0.02) as fp16 values, norm weights 1, batch-norm scale 1 + N(0, 0.02))."""
+    g = _Gen(seed)
+    w = {"eps": np.float32(eps)}
+    w["c0_w"], w["c0_b"] = g.vec(SUB_C * 9, 1 / 3).reshape(SUB_C, 9), g.vec(SUB_C)
+    w["c2_w"], w["c2_b"] = g.vec(SUB_C * 9, 1 / 3).reshape(SUB_C, 9), g.vec(SUB_C)
+    w["c3_w"], w["c3_b"] = g.vec(SUB_C * SUB_C, 1 / 16).reshape(SUB_C, SUB_C), g.vec(SUB_C)
+    w["c5_w"], w["c5_b"] = g.vec(SUB_C * 9, 1 / 3).reshape(SUB_C, 9), g.vec(SUB_C)
+    w["c6_w"], w["c6_b"] = g.vec(SUB_C * SUB_C, 1 / 16).reshape(SUB_C, SUB_C), g.vec(SUB_C)
+    w["pre_out"], w["pre_out_b"] = g.vec(AD * 16 * SUB_C, 1 / 64).reshape(AD, 16 * SUB_C), g.vec(AD)
+    one = lambda n: np.ones(n, np.float32)  # noqa: E731
+    layers = []
+    for _ in range(n_layers):
+        layers.append({
+            "ff1_n_w": one(AD), "ff1_n_b": g.vec(AD), "ff1_up": g.mat(4 * AD, AD), "ff1_up_b": g.vec(4 * AD),
+            "ff1_down": g.mat(AD, 4 * AD), "ff1_down_b": g.vec(AD),
+            "att_n_w": one(AD), "att_n_b": g.vec(AD), "qkv": g.mat(3 * AD, AD),
+            "bq": g.vec(AD), "bk": g.vec(AD), "bv": g.vec(AD), "pu": g.vec(AD), "pv": g.vec(AD),
+            "pos": g.mat(AD, AD), "out": g.mat(AD, AD), "out_b": g.vec(AD),
+            "conv_n_w": one(AD), "conv_n_b": g.vec(AD), "pw1": g.mat(2 * AD, AD), "pw1_b": g.vec(2 * AD),
+            "dw": g.vec(AD * 9, 1 / 3).reshape(AD, 9), "dw_b": g.vec(AD), "bn_s": g.vec(AD), "bn_b": g.vec(AD),
+            "pw2": g.mat(AD, AD), "pw2_b": g.vec(AD),
+            "ff2_n_w": one(AD), "ff2_n_b": g.vec(AD), "ff2_up": g.mat(4 * AD, AD), "ff2_up_b": g.vec(4 * AD),
+            "ff2_down": g.mat(AD, 4 * AD), "ff2_down_b": g.vec(AD),
+            "out_n_w": one(AD), "out_n_b": g.vec(AD)})
+    w["layers"] = layers
+    w["ad_n_w"], w["ad_n_b"] = one(AD), g.vec(AD)
+    w["ad1"], w["ad1_b"] = g.mat(AOUT, AD), g.vec(AOUT)
+    w["ad2"], w["ad2_b"] = g.mat(AOUT, AOUT), g.vec(AOUT)
+    w["res_n_w"], w["res_n_b"] = one(AOUT), g.vec(AOUT)
+    w["res_down"], w["res_down_b"] = g.mat(AD, AOUT), g.vec(AD)
+    w["res_up"], w["res_up_b"] = g.mat(AOUT, AD), g.vec(AOUT)
+    g.run()
+    for l in layers:
+        l["bn_s"] += np.float32(1.0)
+    return w
+
+
+def audio_clip_frames(n_samples: int) -> int:
+    """Valid mel frames of a clip (src/audio.rs:241-249: capped at 30 s, padded to 0.5 s, hop 160)."""
+    n = min(max(n_samples, 8000), 30 * 16000)
+    return n // 160
+
+
+def audio_out_len(valid: int) -> int:
+    """Encoder output rows for `valid` mel frames: three stride-2 stages (src/audio.rs:506-509)."""
+    l1 = (valid - 1) // 2 + 1
+    l2 = (l1 - 1) // 2 + 1
+    return (l2 - 1) // 2 + 1
+
+
+def audio_clips(seed=4, n_clips=4, lo_s=1.0, hi_s=30.0):
+    """BASELINE config 4's audio: clips of 1-30 s of N(0, 0.1) waveform at 16 kHz (float32 samples)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_clips):
+        n = int(round(rng.uniform(lo_s, hi_s) * 16000))
+        out.append((rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32))
+    return out

@@ -183,6 +183,93 @@ void d1h_vision_destroy(D1Vision* v);
 int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, const d1_half* pixels, float* out,
                       cudaStream_t stream);
 
+/* ------------------------------------------------------------------------------------------------ audio
+ * FastConformer encoder + adapter (src/audio.rs:302-594): 8x conv subsampling of 128-bin log-mel frames
+ * (fp32, 256 channels), 17 layers of hidden 512 with 8-head rel-pos attention, depthwise conv kernel 9 and
+ * half-step SiLU FFNs of width 2048, adapter LN -> 1024 GELU -> 1024 plus LN -> 512 GELU -> 1024 residual.
+ * Matrices fp16 [out, in] (fused QKV rows [q; k; v]); vectors and subsampling weights fp32. */
+typedef struct D1AudioLayer {
+    const float* ff1_n_w;
+    const float* ff1_n_b;
+    const d1_half* ff1_up;     /* [2048, 512] */
+    const float* ff1_up_b;
+    const d1_half* ff1_down;   /* [512, 2048] */
+    const float* ff1_down_b;
+    const float* att_n_w;
+    const float* att_n_b;
+    const d1_half* qkv;        /* [1536, 512] */
+    const float* bq;
+    const float* bk;
+    const float* bv;
+    const float* pu;           /* pos_bias_u [8*64] */
+    const float* pv;           /* pos_bias_v [8*64] */
+    const d1_half* pos;        /* linear_pos [512, 512] */
+    const d1_half* out;        /* [512, 512] */
+    const float* out_b;
+    const float* conv_n_w;
+    const float* conv_n_b;
+    const d1_half* pw1;        /* [1024, 512] */
+    const float* pw1_b;
+    const float* dw;           /* [512][9] */
+    const float* dw_b;
+    const float* bn_s;         /* batch-norm folded scale / shift */
+    const float* bn_b;
+    const d1_half* pw2;        /* [512, 512] */
+    const float* pw2_b;
+    const float* ff2_n_w;
+    const float* ff2_n_b;
+    const d1_half* ff2_up;
+    const float* ff2_up_b;
+    const d1_half* ff2_down;
+    const float* ff2_down_b;
+    const float* out_n_w;
+    const float* out_n_b;
+} D1AudioLayer;
+
+typedef struct D1AudioWeights {
+    int n_layers;
+    const D1AudioLayer* layers;
+    const float* c0_w;         /* conv 1 -> 256, 3x3 stride 2: [256][9] */
+    const float* c0_b;
+    const float* c2_w;         /* depthwise 3x3 stride 2: [256][9] */
+    const float* c2_b;
+    const float* c3_w;         /* pointwise [256, 256] */
+    const float* c3_b;
+    const float* c5_w;
+    const float* c5_b;
+    const float* c6_w;
+    const float* c6_b;
+    const float* pre_out;      /* [512, 16*256] with columns in (f, c) order (src/audio.rs:434-442) */
+    const float* pre_out_b;
+    const float* ad_n_w;
+    const float* ad_n_b;
+    const d1_half* ad1;        /* [1024, 512] */
+    const float* ad1_b;
+    const d1_half* ad2;        /* [1024, 1024] */
+    const float* ad2_b;
+    const float* res_n_w;
+    const float* res_n_b;
+    const d1_half* res_down;   /* [512, 1024] */
+    const float* res_down_b;
+    const d1_half* res_up;     /* [1024, 512] */
+    const float* res_up_b;
+    float eps;
+} D1AudioWeights;
+
+typedef struct D1Audio D1Audio;
+
+/* Creates the encoder over caller-owned device weights, with this library's kernels; max_rows bounds the encoder
+ * output rows (sum over clips of ceil(valid / 8)) of one call. fused: fold biases / activations into the GEMM
+ * epilogues (0: the reference's separate d1_fill_rows / d1_bias_act_* calls). NULL on failure. */
+D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows);
+void d1h_audio_destroy(D1Audio* a);
+
+/* Encodes clips (src/audio.rs:505-594) packed into one pass: clip c contributes valid[c] (1 .. 3000) normalised
+ * log-mel frames, mel is host fp32 [sum valid][128] in clip order; out: device fp32 [sum T_c][1024] in clip
+ * order, T_c = ceil(valid[c] / 8) <= 375. Asynchronous on `stream` (the host staging is reused by the next call
+ * after it waits for this one). Returns the number of output rows or a negative status. */
+int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel, float* out, cudaStream_t stream);
+
 /* Number of kernel launches the runner made since the model was created (a counter for benchmarks). */
 long long d1h_launch_count(const D1Model* m);
 /* Bytes the last launch on `slot` copied host->device (its batch metadata, token ids included) and

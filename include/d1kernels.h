@@ -223,6 +223,29 @@ int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half*
  * wait and returned early; its output is undefined). */
 int d1_flash_attn_error(void);
 
+/* extension — fp32 GEMM with the bias / activation folded in: row-major
+ * Y[M,N] = act(X[M,K] . W[N,K]^T + beta * Y + bias) (bias fp32 [N] or NULL; act as d1_bias_act_f).
+ * Replaces Blas::sgemm (src/cuda.rs:493-505, a cublasGemmEx call made from Rust) and the d1_fill_rows /
+ * d1_bias_act_f around it in the audio subsampling (src/audio.rs:517-525). fp32 FFMA, no TF32; results do not
+ * depend on the launch (split-K partials are summed in a fixed order). */
+int d1_sgemm(int M, int N, int K, const float* X, int ldx, const float* W, int ldw, float* Y, int ldy, float beta,
+             const float* bias, int act, cudaStream_t stream);
+
+/* extension — the FastConformer rel-pos self-attention of packed clips in one kernel. Replaces the three
+ * Blas::gemm_batched calls (src/cuda.rs:507-527, cuBLAS from Rust) and d1_relpos_softmax of src/audio.rs:567-570.
+ * Clip c holds rows offs[c] .. offs[c+1]-1 (offs: device int [n_clips + 1], every clip <= max_len <= 384 rows);
+ * for head h (64 columns at h*64 of each operand), query i and key j of the clip:
+ *   P[i][j] = fp16(softmax_j((qu_i . k_j + qv_i . pp[pp_center + j - i]) * scale)),  O_i = fp16(sum_j P[i][j] v_j)
+ * where pp row pp_center + j - i (of pp_rows rows; rows outside read as zero) is the projected sinusoid of
+ * relative position i - j: the reference's per-clip pp has pp_center = T - 1. qu/qv/k/v share row pitch ld. */
+int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const d1_half* v, int ld,
+                   const d1_half* pp, int ldp, int pp_rows, int pp_center, d1_half* o, int ldo, const int* offs,
+                   int n_clips, int max_len, int heads, float scale, cudaStream_t stream);
+
+/* extension — reads and clears d1_relpos_attn's device error word (nonzero: a clip longer than max_len was
+ * skipped). */
+int d1_relpos_attn_error(void);
+
 /* extension — releases a context made by d1_lt_init (the reference never frees it). */
 void d1_lt_destroy(void* ctx);
 

@@ -436,6 +436,191 @@ def vision_encode(w, crops, prec="f16"):
     return gemm(act, w["proj2"], np.broadcast_to(w["proj2_b"], (act.shape[0], 1024)), 1.0, 1.0)
 
 
+# ------------------------------------------------------------------------------------------------ audio
+
+AD = 512          # src/audio.rs:16
+AHEADS = 8        # :17
+SUB_C = 256       # :18
+N_MELS = 128      # :15
+A_MAX_T = 384     # :401
+
+
+def sub_conv0(mel, valid, w, b, Tout, Fout):
+    """cuda/kernels.cu:529-545: 3x3 stride-2 conv (pad 1) from 1 to 256 channels over the valid mel rows, ReLU;
+    mel [>= valid, F] -> [Tout, Fout, 256] fp32."""
+    mel = np.asarray(mel, np.float32)
+    F = mel.shape[1]
+    xp = np.zeros((2 * Tout + 2, max(F, 2 * Fout) + 2), np.float32)
+    xp[1:1 + min(valid, 2 * Tout + 1), 1:1 + F] = mel[:min(valid, 2 * Tout + 1)]
+    patches = np.stack([xp[dt:dt + 2 * Tout:2, df:df + 2 * Fout:2] for dt in range(3) for df in range(3)], -1)
+    return np.maximum(patches @ np.asarray(w, np.float32).T + b, 0).astype(np.float32)
+
+
+def sub_dwconv(x, tin_valid, w, b, Tout, Fout):
+    """cuda/kernels.cu:548-564: depthwise 3x3 stride-2 conv (pad 1) on [Tin, Fin, 256] -> [Tout, Fout, 256]."""
+    x = np.asarray(x, np.float32)
+    Fin = x.shape[1]
+    xp = np.zeros((2 * Tout + 2, max(Fin, 2 * Fout) + 2, x.shape[2]), np.float32)
+    n = min(tin_valid, 2 * Tout + 1)
+    xp[1:1 + n, 1:1 + Fin] = x[:n]
+    out = np.broadcast_to(np.asarray(b, np.float32), (Tout, Fout, x.shape[2])).copy()
+    for dt in range(3):
+        for df in range(3):
+            out += w[:, dt * 3 + df] * xp[dt:dt + 2 * Tout:2, df:df + 2 * Fout:2]
+    return out
+
+
+def relpos_prep(qkv, bq, bk, bv, pu, pv, prec="f16"):
+    """cuda/kernels.cu:567-580: qu = q+bq+u, qv = q+bq+v, k+bk, v+bv (fp16 outputs in the F16 engine)."""
+    qkv = np.asarray(qkv, np.float32)
+    q = qkv[:, :AD] + bq
+    return (r16(q + pu, prec), r16(q + pv, prec), r16(qkv[:, AD:2 * AD] + bk, prec), r16(qkv[:, 2 * AD:] + bv, prec))
+
+
+def relpos_pe(t):
+    """src/audio.rs:546-558: sinusoid rows for relative positions t-1 .. -(t-1), [2t-1, 512] (fp16 values):
+    row n, columns (2i, 2i+1) = sin, cos of (t-1-n) * exp(2i * -(ln 10000 / 512)) (fp32 angle, f64 sin/cos)."""
+    c = np.float32(-(math.log(10000.0) / AD))
+    div = np.exp(np.arange(0, AD, 2, dtype=np.float32) * c).astype(np.float32)
+    p = (t - 1 - np.arange(2 * t - 1)).astype(np.float32)
+    a = (p[:, None] * div[None, :]).astype(np.float32).astype(np.float64)
+    pe = np.empty((2 * t - 1, AD), np.float32)
+    pe[:, 0::2] = np.sin(a).astype(np.float32)
+    pe[:, 1::2] = np.cos(a).astype(np.float32)
+    return pe.astype(np.float16).astype(np.float32)
+
+
+def relpos_attention(qu, qv, k, v, pp, scale=0.125, prec="f16"):
+    """src/audio.rs:567-571 with cuda/kernels.cu:583-616: per head, ac = qu.k^T and bd = qv.pp^T (fp32), score
+    (i, j) = (ac[i, j] + bd[i, j + T-1-i]) * scale, row softmax, probs fp16, O = probs.V (fp16 out)."""
+    T = qu.shape[0]
+    i = np.arange(T)[:, None]
+    j = np.arange(T)[None, :]
+    out = np.empty((T, AD), np.float32)
+    for h in range(AHEADS):
+        c = slice(h * 64, h * 64 + 64)
+        ac = np.asarray(qu[:, c], np.float32) @ np.asarray(k[:, c], np.float32).T
+        bd = np.asarray(qv[:, c], np.float32) @ np.asarray(pp[:, c], np.float32).T
+        s = (ac + bd[i, j + T - 1 - i]) * np.float32(scale)
+        e = np.exp(s - s.max(-1, keepdims=True))
+        p = r16(e / e.sum(-1, keepdims=True), prec)
+        out[:, c] = p @ np.asarray(v[:, c], np.float32)
+    return r16(out, prec)
+
+
+def conformer_dw(a, b1, dw, dwb, bn_s, bn_b, ksize=9, prec="f16"):
+    """cuda/kernels.cu:620-637: GLU of the pw1 output (+bias), depthwise conv (zero pad, 'same'), bias, batch-norm
+    affine, SiLU; a [T, 2C] -> [T, C]."""
+    a = np.asarray(a, np.float32)
+    C = a.shape[1] // 2
+    T = a.shape[0]
+    x = a[:, :C] + b1[:C]
+    g = a[:, C:] + b1[C:]
+    glu = (x / (np.float32(1) + np.exp(-g))).astype(np.float32)
+    pad = (ksize - 1) // 2
+    gp = np.zeros((T + 2 * pad, C), np.float32)
+    gp[pad:pad + T] = glu
+    acc = np.broadcast_to(np.asarray(dwb, np.float32), (T, C)).copy()
+    for kk in range(ksize):
+        acc += dw[:, kk] * gp[kk:kk + T]
+    return r16(silu(acc * bn_s + bn_b), prec)
+
+
+def audio_encode(w, mel, valid, prec="f16"):
+    """src/audio.rs:505-594: one clip's normalised log-mel rows (the first `valid` of mel [frames, 128]) ->
+    fp32 prefix embeddings [T, 1024], T = ceil(valid / 8)."""
+    eps = float(w["eps"])
+    l1 = (valid - 1) // 2 + 1
+    l2 = (l1 - 1) // 2 + 1
+    t = (l2 - 1) // 2 + 1
+    s1 = sub_conv0(mel, valid, w["c0_w"], w["c0_b"], l1, 64)
+    s2 = sub_dwconv(s1, l1, w["c2_w"], w["c2_b"], l2, 32)
+    s3 = np.maximum(s2.reshape(-1, SUB_C) @ w["c3_w"].T + w["c3_b"], 0).astype(np.float32).reshape(l2, 32, SUB_C)
+    s2 = sub_dwconv(s3, l2, w["c5_w"], w["c5_b"], t, 16)
+    s1 = np.maximum(s2.reshape(-1, SUB_C) @ w["c6_w"].T + w["c6_b"], 0).astype(np.float32)
+    x = (s1.reshape(t, 16 * SUB_C) @ w["pre_out"].T + w["pre_out_b"]).astype(np.float32)
+    pe = relpos_pe(t)
+    pend, pscale = None, 1.0
+    for l in w["layers"]:
+        x, xn = layernorm(x, l["ff1_n_w"], l["ff1_n_b"], eps, pend, pscale)
+        big = r16(bias_act(r16(gemm(r16(xn, prec), l["ff1_up"]), prec), l["ff1_up_b"], 4), prec)
+        x = gemm(big, l["ff1_down"], x, 0.5, 1.0)
+        x, xn = layernorm(x, l["att_n_w"], l["att_n_b"], eps, l["ff1_down_b"], 0.5)
+        big = r16(gemm(r16(xn, prec), l["qkv"]), prec)
+        qu, qv, kk, vv = relpos_prep(big, l["bq"], l["bk"], l["bv"], l["pu"], l["pv"], prec)
+        pp = r16(gemm(pe, l["pos"]), prec)
+        o = relpos_attention(qu, qv, kk, vv, pp, 0.125, prec)
+        x = gemm(o, l["out"], x, 1.0, 1.0)
+        x, xn = layernorm(x, l["conv_n_w"], l["conv_n_b"], eps, l["out_b"])
+        big = r16(gemm(r16(xn, prec), l["pw1"]), prec)
+        o = conformer_dw(big, l["pw1_b"], l["dw"], l["dw_b"], l["bn_s"], l["bn_b"], 9, prec)
+        x = gemm(o, l["pw2"], x, 1.0, 1.0)
+        x, xn = layernorm(x, l["ff2_n_w"], l["ff2_n_b"], eps, l["pw2_b"])
+        big = r16(bias_act(r16(gemm(r16(xn, prec), l["ff2_up"]), prec), l["ff2_up_b"], 4), prec)
+        x = gemm(big, l["ff2_down"], x, 0.5, 1.0)
+        _, x = layernorm(x, l["out_n_w"], l["out_n_b"], eps, l["ff2_down_b"], 0.5)  # norm_out replaces x
+        pend, pscale = None, 1.0
+    _, xn = layernorm(x, w["ad_n_w"], w["ad_n_b"], eps)
+    big = r16(bias_act(r16(gemm(r16(xn, prec), w["ad1"]), prec), w["ad1_b"], 2), prec)
+    out = gemm(big, w["ad2"], np.broadcast_to(w["ad2_b"], (t, 1024)), 1.0, 1.0)
+    _, xn = layernorm(out, w["res_n_w"], w["res_n_b"], eps)
+    big = r16(bias_act(r16(gemm(r16(xn, prec), w["res_down"]), prec), w["res_down_b"], 2), prec)
+    out = gemm(big, w["res_up"], out, 1.0, 1.0)
+    return bias_act(out, w["res_up_b"], 0)
+
+
+def slaney_filterbank(n_fft=512, sr=16000, n_mels=N_MELS):
+    """src/audio.rs:151-176: Slaney-scale triangular filters with area normalisation, [n_mels, n_fft/2+1] fp32."""
+    f_sp, min_log_hz, logstep = 200.0 / 3.0, 1000.0, math.log(6.4) / 27.0
+    min_log_mel = min_log_hz / f_sp
+
+    def hz_to_mel(f):
+        return min_log_mel + math.log(f / min_log_hz) / logstep if f >= min_log_hz else f / f_sp
+
+    def mel_to_hz(m):
+        return min_log_hz * math.exp(logstep * (m - min_log_mel)) if m >= min_log_mel else f_sp * m
+
+    nb = n_fft // 2 + 1
+    m0, m1 = hz_to_mel(0.0), hz_to_mel(sr / 2.0)
+    mel_f = np.array([mel_to_hz(m0 + (m1 - m0) * i / (n_mels + 1)) for i in range(n_mels + 2)])
+    freqs = np.arange(nb) * sr / n_fft
+    w = np.zeros((n_mels, nb), np.float32)
+    for i in range(n_mels):
+        lower = -(mel_f[i] - freqs) / (mel_f[i + 1] - mel_f[i])
+        upper = (mel_f[i + 2] - freqs) / (mel_f[i + 2] - mel_f[i + 1])
+        enorm = np.float32(2.0 / (mel_f[i + 2] - mel_f[i]))
+        w[i] = np.maximum(np.minimum(lower, upper), 0.0).astype(np.float32) * enorm
+    return w
+
+
+def log_mel(samples):
+    """src/audio.rs:238-299: pre-emphasis 0.97, centred 512-point frames (hop 160, 400-sample periodic-free Hann
+    window centred in the frame), power spectrum, Slaney mel, ln(x + 2^-24), per-channel normalisation over the
+    valid frames (unbiased std + 1e-5). Returns (fp32 [frames, 128], valid)."""
+    x = np.asarray(samples, np.float32)[:30 * 16000]
+    if x.shape[0] < 8000:
+        x = np.concatenate([x, np.zeros(8000 - x.shape[0], np.float32)])
+    n = x.shape[0]
+    valid, frames = n // 160, 1 + n // 160
+    y = np.empty(n, np.float32)
+    y[0] = x[0]
+    y[1:] = x[1:] - np.float32(0.97) * x[:-1]
+    win = np.zeros(512)
+    win[56:456] = 0.5 - 0.5 * np.cos(2.0 * math.pi * np.arange(400) / 399.0)
+    yp = np.concatenate([np.zeros(256), y.astype(np.float64), np.zeros(512)])
+    idx = np.arange(frames)[:, None] * 160 + np.arange(512)[None, :]
+    spec = np.fft.rfft(yp[idx] * win, axis=1)
+    pw = (spec.real ** 2 + spec.imag ** 2).astype(np.float32)
+    out = np.log((pw @ slaney_filterbank().T).astype(np.float32) + np.float32(2.0 ** -24)).astype(np.float32)
+    v = out[:valid].astype(np.float64)
+    mean = v.mean(0)
+    std = np.sqrt(((v - mean) ** 2).sum(0) / (valid - 1.0))
+    std = np.where(np.isnan(std), 0.0, std)
+    res = np.zeros_like(out)
+    res[:valid] = ((v - mean) / (std + 1e-5)).astype(np.float32)
+    return res, valid
+
+
 # ------------------------------------------------------------------------------------------------ metrics
 
 def centred_logit_err(ref_logits, logits, group_sizes):
