@@ -16,7 +16,11 @@ peak. One step = one Runner::launch_text (src/model.rs:470-599) of an 8192-token
 
 --impl reference: the reference's CPU implementation of the path. The reference has none (its forward is CUDA
 only; its fp32 PyTorch path needs remote code and weights that are not available offline), so this arm times the
-oracle port (fp32 numpy restatement of the reference's arithmetic) on all host threads, on bounded samples.
+oracle port (fp32 numpy restatement of the reference's arithmetic) on all host threads, on bounded samples. When a
+GPU and oracle/_ref/libd1ref.so (the reference's cuda/*.cu built unchanged) are present, the line also carries
+`reference_gpu_engine`: the reference's own F16 engine (its kernels + cuBLASLt) timed on the same batches.
+
+--gemm-sweep: BASELINE config 1, every projection GEMM shape, one JSON line per shape.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own replica on its own batches (the model is
 replicated and requests are sharded; no collective on the data path); value = all ranks' tokens / max time.
@@ -164,7 +168,61 @@ def run_reference(args, rank, world):
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"{n_sample} sequences x {SEQ_LEN} tokens per step, oracle/d1_oracle.py fp32"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    gpu = reference_gpu_engine(w, args.steps, args.warmup)
+    if gpu is not None:
+        line["reference_gpu_engine"] = gpu
     print(json.dumps(line), flush=True)
+
+
+REF_LIB = ROOT / "oracle" / "_ref" / "libd1ref.so"
+
+
+def reference_gpu_engine(w, steps, warmup):
+    """The reference's own F16 CUDA engine on this GPU: cuda/kernels.cu + cuda/gemm.cu (cuBLASLt autotuner) built
+    unchanged into oracle/_ref/libd1ref.so, driven by the same host runner (src/model.rs restated), on the same
+    8192-token batches as this library's arm. Its GEMM plans come from d1_lt_tune at effort 0 (cuBLASLt heuristic
+    candidates, each timed) on first use of each shape during the warm-up steps: the effort-1 search of
+    src/engine.rs:593 (every cuBLASLt algorithm x tile) crashed the process with SIGSEGV on B200 and is not run.
+    Device time over `steps` back-to-back launch_text steps (CUDA events). None when there is no GPU or the
+    reference library was not built."""
+    try:
+        import torch
+        if not torch.cuda.is_available() or not REF_LIB.exists():
+            return None
+    except Exception:
+        return None
+    load_package()
+    from fast_d1_omni_b200.model import TextModel
+    from fast_d1_omni_b200.weights import text_batch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    print("reference GPU engine: loading", file=sys.stderr, flush=True)
+    model = TextModel(w, device=0, kernel_lib=str(REF_LIB), fused=False, cap_tokens=TOKENS)
+    try:
+        print("reference GPU engine: warm-up (effort-0 plans on first use)", file=sys.stderr, flush=True)
+        batches = [text_batch(i, N_SEQS, SEQ_LEN) for i in range(4)]
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for i in range(warmup):
+                model.launch(batches[i % 4], i % 2, stream)
+            torch.cuda.synchronize(dev)
+            model._pending.clear()
+            print("reference GPU engine: timing", file=sys.stderr, flush=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(steps):
+                model.launch(batches[i % 4], i % 2, stream)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            model._pending.clear()
+        ms = e0.elapsed_time(e1)
+        return {"value": TOKENS * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
+                "device": torch.cuda.get_device_name(dev),
+                "gemm_plans": "d1_lt_tune effort 0 on first use (cuBLASLt heuristic candidates, timed)",
+                "source": "oracle/_ref/libd1ref.so: the reference's cuda/kernels.cu + cuda/gemm.cu (cuBLASLt) built "
+                          "unchanged, through this repository's restatement of src/model.rs"}
+    finally:
+        model.close()
 
 
 def swiglu_gemm_ms(pkg, dev, stream, reps=20):
@@ -195,6 +253,65 @@ def swiglu_gemm_ms(pkg, dev, stream, reps=20):
     return g0.elapsed_time(g1) / reps
 
 
+SWEEP_M = (256, 1024, 4096, 8192, 16384)
+SWEEP_NK = ((3072, 1024, "conv in_proj"), (2048, 1024, "fused QKV"), (1024, 1024, "out_proj"),
+            (9216, 1024, "w1|w3"), (1024, 4608, "w2"))
+
+
+def gemm_sweep(pkg, dev, stream, reps=20):
+    """C = A.W^T for every M x (N, K), fp16 in, fp32 accumulate, after d1_lt_tune (effort 1).
+    Per shape: the plain fp16-store GEMM and the trunk's own form of that projection (residual add into the fp32
+    stream for out_proj / w2, the fused SwiGLU for w1|w3). One JSON line per shape; CUDA-event averages over
+    `reps` launches of inputs larger than L2 at M >= 8192 (the smaller shapes are L2-resident by nature)."""
+    import ctypes as C
+    import torch
+    lib = pkg.lib()
+    ctx = lib.d1_lt_init(0)
+    st = C.c_void_p(stream.cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    _, tflops, kind = peaks()
+    g = torch.Generator(device=dev).manual_seed(1)
+    out = []
+    for (N, K, name) in SWEEP_NK:
+        wt = (torch.randn(N, K, device=dev, generator=g) * 0.02).half()
+        for M in SWEEP_M:
+            x = torch.randn(M, K, device=dev, generator=g).half()
+            y16 = torch.empty(M, N, device=dev, dtype=torch.float16)
+            forms = {"store_f16": lambda: lib.d1_lt_gemm(ctx, M, N, K, P(x), K, P(wt), K, 0, P(y16), N, 0, 0, 1.0,
+                                                         0.0, st)}
+            if N == 1024:
+                y32 = torch.zeros(M, N, device=dev)
+                forms["trunk_residual_f32"] = lambda: lib.d1_lt_gemm(ctx, M, N, K, P(x), K, P(wt), K, 0, P(y32), N, 1,
+                                                                     0, 1.0, 1.0, st)
+                lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, 1, 0, 1, st)
+            if N == 9216:
+                act = torch.empty(M, N // 2, device=dev, dtype=torch.float16)
+                forms["trunk_swiglu"] = lambda: lib.d1_gemm_swiglu(ctx, M, N // 2, K, P(x), K, P(wt), K, P(act),
+                                                                   N // 2, st)
+            lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, 0, 0, 1, st)
+            rec = {"sweep": "config1", "shape": name, "M": M, "N": N, "K": K}
+            for fname, fn in forms.items():
+                for _ in range(3):
+                    assert fn() == 0
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    fn()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                us = e0.elapsed_time(e1) / reps * 1e3
+                tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+                rec[fname] = {"us": round(us, 2), "tflops": round(tf, 1), "frac_of_peak": round(tf / tflops, 3)}
+            rec["peak"] = f"{tflops} TFLOP/s ({kind}, bf16 cuBLAS burst)"
+            out.append(rec)
+            print(json.dumps(rec), flush=True)
+    err = lib.d1_lt_error(ctx)
+    lib.d1_lt_destroy(ctx)
+    if err:
+        raise RuntimeError(f"GEMM kernel reported error {err}")
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -202,6 +319,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="d1", choices=["d1", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="BASELINE config 1: time every GEMM shape (one JSON line each) instead of the forward")
     ap.add_argument("--only-roofline", action="store_true",
                     help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
     args = ap.parse_args()
@@ -223,6 +342,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     pkg = load_package()
+    if args.gemm_sweep:
+        if rank == 0:
+            gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
+        return
     if args.only_roofline:
         ms = swiglu_gemm_ms(pkg, dev, torch.cuda.Stream(dev))
         if rank == 0:
