@@ -84,6 +84,30 @@ class AudioWeights(C.Structure):
                 ("res_up_b", p), ("eps", f32)]
 
 
+
+class EngineConfig(C.Structure):
+    _fields_ = [("max_batch_tokens", i32), ("cap_tokens", i32), ("media_cache_bytes", C.c_longlong)]
+
+
+class Row(C.Structure):
+    _fields_ = [("ids", C.POINTER(i32)), ("n_ids", i32), ("markers", C.POINTER(i32)), ("n_markers", i32),
+                ("qtype", i32)]
+
+
+class Media(C.Structure):
+    _fields_ = [("kind", i32), ("n_crops", i32), ("ph", C.POINTER(i32)), ("pw", C.POINTER(i32)), ("patches", p),
+                ("mel", C.POINTER(f32)), ("valid", i32), ("pcm", C.POINTER(f32)), ("n_samples", i32)]
+
+
+class Job(C.Structure):
+    _fields_ = [("rows", C.POINTER(Row)), ("n_rows", i32), ("media", Media)]
+
+
+class EngineStats(C.Structure):
+    _fields_ = [("tokens", C.c_longlong), ("media_tokens", C.c_longlong), ("batches", C.c_longlong),
+                ("media_jobs", C.c_longlong), ("rows", C.c_longlong)]
+
+
 # name -> (restype, argtypes). The kernel ABI (d1kernels.h) first, then the runner (d1h.h).
 KERNELS = {
     "d1_rmsnorm": (i32, [p, p, p, i32, i32, f32, p]),
@@ -124,6 +148,7 @@ EXTENSIONS = {
     "d1_sgemm": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, f32, p, i32, p]),
     "d1_relpos_attn": (i32, [p, p, p, p, i32, p, i32, i32, i32, p, i32, p, i32, i32, i32, f32, p]),
     "d1_relpos_attn_error": (i32, []),
+    "d1_log_mel": (i32, [p, i32, p, p]),
     "d1_lt_destroy": (None, [p]),
     "d1_build_id": (C.c_char_p, []),
 }
@@ -149,6 +174,19 @@ RUNNER = {
     "d1h_audio_create": (p, [C.POINTER(AudioWeights), i32, i32]),
     "d1h_audio_destroy": (None, [p]),
     "d1h_audio_encode": (i32, [p, i32, C.POINTER(i32), p, p, p]),
+    "d1h_audio_encode_pcm": (i32, [p, i32, C.POINTER(i32), p, p, C.POINTER(i32), p]),
+    "d1h_vision_capacity": (i32, [p]),
+    "d1h_model_layers": (i32, [p, i32]),
+    "d1e_create": (p, [p, p, p, C.POINTER(EngineConfig), p]),
+    "d1e_destroy": (None, [p]),
+    "d1e_submit": (C.c_longlong, [p, C.POINTER(Job)]),
+    "d1e_step": (i32, [p]),
+    "d1e_pending": (i32, [p]),
+    "d1e_queued_tokens": (C.c_longlong, [p]),
+    "d1e_next_logits": (i32, [p]),
+    "d1e_take": (i32, [p, C.POINTER(C.c_longlong), C.POINTER(f32), i32, C.c_char_p, i32]),
+    "d1e_stats": (None, [p, C.POINTER(EngineStats)]),
+    "d1e_last_error": (C.c_char_p, []),
 }
 
 

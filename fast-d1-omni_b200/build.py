@@ -20,7 +20,7 @@ OBJ = HERE / "_build"
 SO = HERE / "libd1kernels.so"
 ARCHIVE = HERE / "libd1kernels.a"
 
-SOURCES = ["gemm.cu", "kernels.cu", "attn.cu", "audio.cu", "runner.cpp"]
+SOURCES = ["gemm.cu", "kernels.cu", "attn.cu", "audio.cu", "runner.cpp", "engine.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall", f"-I{INCLUDE}"]
 

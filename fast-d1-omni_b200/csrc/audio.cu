@@ -479,3 +479,149 @@ int d1_relpos_attn_error(void) {
 }
 
 }  // extern "C"
+
+// ================================================================================================ log-mel front end
+// src/audio.rs:238-299 (the reference computes it on the host) on the GPU, in the reference's precision and
+// operation order: fp32 pre-emphasis y[i] = x[i] - 0.97 x[i-1]; 512-sample frames centred every 160 samples (zero
+// outside the clip) times a 400-point Hann window centred in the frame (f64); an iterative radix-2 FFT in f64 with
+// the same bit-reversal, twiddle table (e^{-2 pi i k / 512}) and butterfly expressions; power spectrum rounded to
+// fp32; 128 Slaney mel filters summed in fp32 over each filter's nonzero bins in order; ln(s + 2^-24); then each mel
+// channel normalised over the valid frames with f64 mean and unbiased std (std + 1e-5), frames past `valid` zero.
+// Explicit _rn intrinsics keep the compiler from contracting multiply-adds the reference evaluates separately.
+
+namespace {
+
+constexpr int MEL_NFFT = 512, MEL_HOP = 160, MEL_WIN = 400, MEL_N = 128, MEL_NB = MEL_NFFT / 2 + 1;
+
+__device__ double g_mel_tw[MEL_NFFT];      // (cos, sin) pairs of -2 pi k / 512, k < 256
+__device__ double g_mel_win[MEL_NFFT];
+__device__ float g_mel_fb[MEL_N * MEL_NB];
+__device__ int g_mel_rng[MEL_N * 2];        // nonzero bin range [lo, hi) per filter
+
+__global__ void __launch_bounds__(256) k_mel_frames(const float* __restrict__ x, int n, float* __restrict__ out) {
+    __shared__ double re[MEL_NFFT], im[MEL_NFFT];
+    __shared__ float pw[MEL_NB];
+    const int f = blockIdx.x, tid = threadIdx.x;
+    for (int i = tid; i < MEL_NFFT; i += 256) {
+        const long si = (long)f * MEL_HOP + i - MEL_NFFT / 2;
+        float y = 0.f;
+        if (si >= 0 && si < n) y = si == 0 ? x[0] : __fsub_rn(x[si], __fmul_rn(0.97f, x[si - 1]));
+        const int r = (int)(__brev((unsigned)i) >> (32 - 9));
+        re[r] = __dmul_rn((double)y, g_mel_win[i]);
+        im[r] = 0.0;
+    }
+    __syncthreads();
+    for (int len = 2; len <= MEL_NFFT; len <<= 1) {
+        const int half = len >> 1, step = MEL_NFFT / len;
+        const int b = tid;  // 256 butterflies per stage, one per thread
+        const int a = (b / half) * len + (b % half), c = a + half, k = b % half;
+        const double wr = g_mel_tw[2 * (k * step)], wi = g_mel_tw[2 * (k * step) + 1];
+        const double xr = __dsub_rn(__dmul_rn(re[c], wr), __dmul_rn(im[c], wi));
+        const double xi = __dadd_rn(__dmul_rn(re[c], wi), __dmul_rn(im[c], wr));
+        const double ar = re[a], ai = im[a];
+        re[c] = __dsub_rn(ar, xr);
+        im[c] = __dsub_rn(ai, xi);
+        re[a] = __dadd_rn(ar, xr);
+        im[a] = __dadd_rn(ai, xi);
+        __syncthreads();
+    }
+    for (int kk = tid; kk < MEL_NB; kk += 256)
+        pw[kk] = __double2float_rn(__dadd_rn(__dmul_rn(re[kk], re[kk]), __dmul_rn(im[kk], im[kk])));
+    __syncthreads();
+    if (tid < MEL_N) {
+        float s = 0.f;
+        const int lo = g_mel_rng[2 * tid], hi = g_mel_rng[2 * tid + 1];
+        for (int kk = lo; kk < hi; kk++) s = __fadd_rn(s, __fmul_rn(g_mel_fb[tid * MEL_NB + kk], pw[kk]));
+        out[(size_t)f * MEL_N + tid] = logf(__fadd_rn(s, 5.9604644775390625e-8f));  // 2^-24
+    }
+}
+
+// one thread per mel channel, frames in order (the reference's f64 summation order)
+__global__ void __launch_bounds__(MEL_N) k_mel_norm(float* __restrict__ mel, int frames, int valid) {
+    const int m = threadIdx.x;
+    double mean = 0.0;
+    for (int f = 0; f < valid; f++) mean = __dadd_rn(mean, (double)mel[(size_t)f * MEL_N + m]);
+    mean = __ddiv_rn(mean, (double)valid);
+    double var = 0.0;
+    for (int f = 0; f < valid; f++) {
+        const double d = __dsub_rn((double)mel[(size_t)f * MEL_N + m], mean);
+        var = __dadd_rn(var, __dmul_rn(d, d));
+    }
+    double sd = sqrt(__ddiv_rn(var, __dsub_rn((double)valid, 1.0)));
+    if (isnan(sd)) sd = 0.0;
+    const double den = __dadd_rn(sd, 1e-5);
+    for (int f = 0; f < frames; f++) {
+        float* p = mel + (size_t)f * MEL_N + m;
+        *p = f < valid ? __double2float_rn(__ddiv_rn(__dsub_rn((double)*p, mean), den)) : 0.f;
+    }
+}
+
+// Host tables, as src/audio.rs:151-205 builds them (f64 math, Slaney scale, area normalisation).
+struct MelTables {
+    double tw[MEL_NFFT], win[MEL_NFFT];
+    float fb[MEL_N * MEL_NB];
+    int rng[MEL_N * 2];
+    MelTables() {
+        const double PI = 3.14159265358979323846;
+        for (int k = 0; k < MEL_NFFT / 2; k++) {
+            const double a = -2.0 * PI * (double)k / (double)MEL_NFFT;
+            tw[2 * k] = cos(a);
+            tw[2 * k + 1] = sin(a);
+        }
+        for (int i = 0; i < MEL_NFFT; i++) win[i] = 0.0;
+        const int off = (MEL_NFFT - MEL_WIN) / 2;
+        for (int i = 0; i < MEL_WIN; i++) win[off + i] = 0.5 - 0.5 * cos(2.0 * PI * (double)i / (double)(MEL_WIN - 1));
+        const double f_sp = 200.0 / 3.0, min_log_hz = 1000.0, logstep = log(6.4) / 27.0;
+        const double min_log_mel = min_log_hz / f_sp;
+        auto hz_to_mel = [&](double f) { return f >= min_log_hz ? min_log_mel + log(f / min_log_hz) / logstep : f / f_sp; };
+        auto mel_to_hz = [&](double m) { return m >= min_log_mel ? min_log_hz * exp(logstep * (m - min_log_mel)) : f_sp * m; };
+        const double m0 = hz_to_mel(0.0), m1 = hz_to_mel(16000.0 / 2.0);
+        double mel_f[MEL_N + 2];
+        for (int i = 0; i < MEL_N + 2; i++) mel_f[i] = mel_to_hz(m0 + (m1 - m0) * (double)i / (double)(MEL_N + 1));
+        for (int i = 0; i < MEL_N; i++) {
+            const double fd0 = mel_f[i + 1] - mel_f[i], fd1 = mel_f[i + 2] - mel_f[i + 1];
+            const double enorm = 2.0 / (mel_f[i + 2] - mel_f[i]);
+            int lo = -1, hi = 0;
+            for (int j = 0; j < MEL_NB; j++) {
+                const double f = (double)j * 16000.0 / (double)MEL_NFFT;
+                const double lower = -(mel_f[i] - f) / fd0, upper = (mel_f[i + 2] - f) / fd1;
+                const float v = (float)std::max(std::min(lower, upper), 0.0);
+                fb[i * MEL_NB + j] = v * (float)enorm;
+                if (fb[i * MEL_NB + j] != 0.f) {
+                    if (lo < 0) lo = j;
+                    hi = j + 1;
+                }
+            }
+            if (lo < 0) lo = 0;
+            rng[2 * i] = lo;
+            rng[2 * i + 1] = std::max(hi, lo);
+        }
+    }
+};
+
+int mel_tables_ready() {
+    static unsigned long long done = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return 0;
+    static const MelTables t;
+    if (cudaMemcpyToSymbol(g_mel_tw, t.tw, sizeof(t.tw)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_mel_win, t.win, sizeof(t.win)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_mel_fb, t.fb, sizeof(t.fb)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_mel_rng, t.rng, sizeof(t.rng)) != cudaSuccess)
+        return -1;
+    __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int d1_log_mel(const float* x, int n, float* mel, cudaStream_t st) {
+    if (!x || !mel || n < 1) return -1;
+    if (mel_tables_ready()) return -1;
+    const int frames = 1 + n / MEL_HOP, valid = n / MEL_HOP;
+    k_mel_frames<<<frames, 256, 0, st>>>(x, n, mel);
+    k_mel_norm<<<1, MEL_N, 0, st>>>(mel, frames, valid);
+    return (int)cudaGetLastError();
+}

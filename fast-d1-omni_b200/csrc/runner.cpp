@@ -1002,6 +1002,8 @@ constexpr int AOUT = 1024;       // :19
 constexpr int N_MELS = 128;      // :15
 constexpr int A_MAX_T = 384;     // :401
 constexpr int A_MAX_VALID = 3000;  // 30 s at hop 160 (src/audio.rs:11-14, 241-247)
+constexpr int A_MAX_SAMPLES = 30 * 16000;  // src/audio.rs:10-11
+constexpr int A_MIN_SAMPLES = 8000;
 constexpr int PP_ROWS = 2 * A_MAX_T - 1;
 constexpr int PP_CENTER = A_MAX_T - 1;
 
@@ -1036,7 +1038,9 @@ struct D1Audio {
     int max_rows = 0;
     long long launches = 0;
     d1_half* pp = nullptr;          // [n_layers][PP_ROWS][512]
-    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *s3 = nullptr, *x = nullptr;
+    float *mel = nullptr, *s1 = nullptr, *s2 = nullptr, *s3 = nullptr, *x = nullptr, *pcm = nullptr;
+    long long mel_rows = 0;  // capacity of mel in frames
+    size_t pcm_cap = 0;      // capacity of pcm in samples
     d1_half *xn = nullptr, *big = nullptr, *qu = nullptr, *qv = nullptr, *kk = nullptr, *vv = nullptr, *o = nullptr;
     int* offs = nullptr;
     int* host_offs = nullptr;
@@ -1062,7 +1066,8 @@ D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
     a->lt = d1_lt_init(0);
     if (!a->lt) e = fail("d1_lt_init failed");
     if (!e) e |= dmalloc(&a->pp, (size_t)w->n_layers * PP_ROWS * AD * 2);
-    if (!e) e |= dmalloc(&a->mel, std::min<size_t>(R * 8, (size_t)64 * A_MAX_VALID) * N_MELS * 4);
+    a->mel_rows = (long long)R * 8 + 4096;  // sum of valid <= 8 * rows, plus one spare frame per clip
+    if (!e) e |= dmalloc(&a->mel, (size_t)a->mel_rows * N_MELS * 4);
     if (!e) e |= dmalloc(&a->s1, L1 * 64 * SUB_C * 4);
     if (!e) e |= dmalloc(&a->s2, L2 * 32 * SUB_C * 4);
     if (!e) e |= dmalloc(&a->s3, L2 * 32 * SUB_C * 4);
@@ -1100,7 +1105,7 @@ D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
 void d1h_audio_destroy(D1Audio* a) {
     if (!a) return;
     if (a->busy) cudaEventSynchronize(a->done);
-    for (void* p : {(void*)a->pp, (void*)a->mel, (void*)a->s1, (void*)a->s2, (void*)a->s3, (void*)a->x, (void*)a->xn,
+    for (void* p : {(void*)a->pp, (void*)a->mel, (void*)a->pcm, (void*)a->s1, (void*)a->s2, (void*)a->s3, (void*)a->x, (void*)a->xn,
                     (void*)a->big, (void*)a->qu, (void*)a->qv, (void*)a->kk, (void*)a->vv, (void*)a->o,
                     (void*)a->offs})
         if (p) cudaFree(p);
@@ -1110,30 +1115,108 @@ void d1h_audio_destroy(D1Audio* a) {
     delete a;
 }
 
-int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel, float* out, cudaStream_t st) {
-    if (!a || n_clips <= 0 || n_clips > 4095 || !valid || !mel || !out) return fail("bad arguments");
-    int rows = 0, max_t = 0;
-    long long frames = 0;
+}  // extern "C"
+
+namespace {
+
+// Checks the clips, waits for the previous call, uploads the clip offsets; returns the output rows (or < 0).
+int audio_prepare(D1Audio* a, int n_clips, const int* valid, int& max_t, cudaStream_t st) {
+    int rows = 0;
+    max_t = 0;
     for (int c = 0; c < n_clips; c++) {
         if (valid[c] < 1 || valid[c] > A_MAX_VALID) return fail("clip frames must be 1 .. 3000");
         const int t = audio_out_len(valid[c]);
         rows += t;
         max_t = std::max(max_t, t);
-        frames += valid[c];
     }
-    if (rows > a->max_rows || frames * N_MELS * 4 > (long long)std::min<size_t>((size_t)a->max_rows * 8,
-                                                                                    (size_t)64 * A_MAX_VALID) *
-                                                         N_MELS * 4)
-        return fail("clips exceed the audio batch capacity");
+    if (rows > a->max_rows) return fail("clips exceed the audio batch capacity");
     if (a->busy) {
         if (cudaEventSynchronize(a->done) != cudaSuccess) return fail("event sync failed");
         a->busy = false;
     }
     a->host_offs[0] = 0;
     for (int c = 0; c < n_clips; c++) a->host_offs[c + 1] = a->host_offs[c] + audio_out_len(valid[c]);
-    if (cudaMemcpyAsync(a->offs, a->host_offs, (size_t)(n_clips + 1) * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(a->mel, mel, (size_t)frames * N_MELS * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    if (cudaMemcpyAsync(a->offs, a->host_offs, (size_t)(n_clips + 1) * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
         return fail("audio upload failed");
+    return rows;
+}
+
+int audio_encode_core(D1Audio* a, int n_clips, const int* valid, const float* const* melc_dev, int rows, int max_t,
+                      float* out, cudaStream_t st);
+
+}  // namespace
+
+extern "C" {
+
+int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel, float* out, cudaStream_t st) {
+    if (!a || n_clips <= 0 || n_clips > 4095 || !valid || !mel || !out) return fail("bad arguments");
+    int max_t = 0;
+    const int rows = audio_prepare(a, n_clips, valid, max_t, st);
+    if (rows < 0) return rows;
+    long long frames = 0;
+    for (int c = 0; c < n_clips; c++) frames += valid[c];
+    if (frames > a->mel_rows) return fail("clips exceed the audio batch capacity");
+    if (cudaMemcpyAsync(a->mel, mel, (size_t)frames * N_MELS * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail("audio upload failed");
+    std::vector<const float*> mp(n_clips);
+    const float* p = a->mel;
+    for (int c = 0; c < n_clips; c++) {
+        mp[c] = p;
+        p += (size_t)valid[c] * N_MELS;
+    }
+    return audio_encode_core(a, n_clips, valid, mp.data(), rows, max_t, out, st);
+}
+
+int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const float* pcm, float* out, int* valid_out,
+                         cudaStream_t st) {
+    if (!a || n_clips <= 0 || n_clips > 4095 || !n_samples || !pcm || !out) return fail("bad arguments");
+    // src/audio.rs:238-247: at most 30 s, zero-padded to at least 0.5 s; valid = n / 160 frames
+    std::vector<int> valid(n_clips), used(n_clips);
+    size_t total = 0, frames = 0;
+    for (int c = 0; c < n_clips; c++) {
+        if (n_samples[c] < 0) return fail("negative sample count");
+        used[c] = std::min(n_samples[c], A_MAX_SAMPLES);
+        const int n = std::max(used[c], A_MIN_SAMPLES);
+        valid[c] = n / 160;
+        total += (size_t)n;
+        frames += (size_t)valid[c] + 1;
+    }
+    if ((long long)frames > a->mel_rows) return fail("clips exceed the audio batch capacity");
+    int max_t = 0;
+    const int rows = audio_prepare(a, n_clips, valid.data(), max_t, st);
+    if (rows < 0) return rows;
+    if (total > a->pcm_cap) {
+        if (a->pcm) cudaFree(a->pcm);
+        a->pcm = nullptr;
+        a->pcm_cap = 0;
+        if (dmalloc(&a->pcm, total * 4)) return -1;
+        a->pcm_cap = total;
+    }
+    std::vector<const float*> mp(n_clips);
+    const float* src = pcm;
+    size_t off = 0, moff = 0;
+    for (int c = 0; c < n_clips; c++) {
+        const int n = std::max(used[c], A_MIN_SAMPLES);
+        if (cudaMemcpyAsync(a->pcm + off, src, (size_t)used[c] * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            (n > used[c] && cudaMemsetAsync(a->pcm + off + used[c], 0, (size_t)(n - used[c]) * 4, st) != cudaSuccess))
+            return fail("audio upload failed");
+        a->launches += 2;
+        if (d1_log_mel(a->pcm + off, n, a->mel + moff * N_MELS, st)) return fail("log-mel front end failed");
+        mp[c] = a->mel + moff * N_MELS;
+        src += n_samples[c];
+        off += (size_t)n;
+        moff += (size_t)valid[c] + 1;
+        if (valid_out) valid_out[c] = valid[c];
+    }
+    return audio_encode_core(a, n_clips, valid.data(), mp.data(), rows, max_t, out, st);
+}
+
+}  // extern "C"
+
+namespace {
+
+int audio_encode_core(D1Audio* a, int n_clips, const int* valid, const float* const* melc_dev, int rows, int max_t,
+                      float* out, cudaStream_t st) {
     long long& L = a->launches;
     const D1AudioWeights& w = a->w;
     const bool fz = a->fused;
@@ -1150,17 +1233,15 @@ int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel
         return r;
     };
     // ---- subsampling per clip (src/audio.rs:511-525) into rows offs[c] .. of x
-    const float* melc = a->mel;
     for (int c = 0; c < n_clips; c++) {
         const int v = valid[c], l1 = (v - 1) / 2 + 1, l2 = (l1 - 1) / 2 + 1, t = audio_out_len(v);
         L += 3;
-        CK(d1_sub_conv0(melc, v, N_MELS, w.c0_w, w.c0_b, a->s1, l1, 64, st));
+        CK(d1_sub_conv0(melc_dev[c], v, N_MELS, w.c0_w, w.c0_b, a->s1, l1, 64, st));
         CK(d1_sub_dwconv(a->s1, l1, 64, w.c2_w, w.c2_b, a->s2, l2, 32, st));
         CK(sgemm_ba(l2 * 32, SUB_C, SUB_C, a->s2, w.c3_w, a->s3, w.c3_b, 1));
         CK(d1_sub_dwconv(a->s3, l2, 32, w.c5_w, w.c5_b, a->s2, t, 16, st));
         CK(sgemm_ba(t * 16, SUB_C, SUB_C, a->s2, w.c6_w, a->s1, w.c6_b, 1));
         CK(sgemm_ba(t, AD, 16 * SUB_C, a->s1, w.pre_out, a->x + (size_t)a->host_offs[c] * AD, w.pre_out_b, 0));
-        melc += (size_t)v * N_MELS;
     }
     // ---- conformer layers over all rows (src/audio.rs:561-588)
     const int R = rows;
@@ -1234,6 +1315,19 @@ int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel
     cudaEventRecord(a->done, st);
     a->busy = true;
     return R;
+}
+
+}  // namespace
+
+extern "C" {
+
+int d1h_vision_capacity(const D1Vision* v) { return v ? v->max_patches : 0; }
+
+int d1h_model_layers(const D1Model* m, int is_attn) {
+    if (!m) return 0;
+    int n = 0;
+    for (const auto& l : m->layers) n += (l.is_attn != 0) == (is_attn != 0);
+    return n;
 }
 
 }  // extern "C"

@@ -276,3 +276,34 @@ def audio_clips(seed=4, n_clips=4, lo_s=1.0, hi_s=30.0):
         n = int(round(rng.uniform(lo_s, hi_s) * 16000))
         out.append((rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32))
     return out
+
+
+def mixed_requests(seed=4, n_requests=64, vocab=65536, n_types=4, questions=3, options=4):
+    """a mixed request stream for the continuous-batching engine (engine.py request dicts).
+    70% text (each question 128-2048 tokens, log-uniform), 20% text+image (one image with config-3 sides, uniform
+    in 224-768 px rounded to 32, pixels U[0, 1] as 16x16x3 patch rows; questions 128-896 tokens, the reference's
+    image_text_length), 10% text+audio (1-30 s of N(0, 0.1) waveform at 16 kHz, features computed by the engine;
+    questions 128-2048 tokens). Every request carries `questions` questions with `options` answer markers each,
+    at distinct sorted positions; question types uniform in [0, n_types)."""
+    rng = np.random.default_rng(seed)
+    reqs = []
+    for _ in range(n_requests):
+        u = rng.uniform()
+        kind = "text" if u < 0.7 else "images" if u < 0.9 else "audio"
+        hi = 896 if kind == "images" else 2048
+        rows = []
+        for _ in range(questions):
+            n = int(round(np.exp(rng.uniform(np.log(128), np.log(hi)))))
+            ids = rng.integers(0, vocab, size=n, dtype=np.int32)
+            markers = np.sort(rng.choice(n, size=options, replace=False)).astype(np.int32)
+            rows.append({"ids": ids, "markers": markers, "qtype": int(rng.integers(0, n_types))})
+        media = None
+        if kind == "images":
+            hh, ww = (int(round(rng.uniform(224, 768) / 32.0)) * 32 for _ in range(2))
+            ph, pw = hh // 16, ww // 16
+            media = {"kind": "images", "crops": [(ph, pw, rng.uniform(0.0, 1.0, size=(ph * pw, VD)).astype(np.float16))]}
+        elif kind == "audio":
+            n = int(round(rng.uniform(1.0, 30.0) * 16000))
+            media = {"kind": "audio", "pcm": (rng.standard_normal(n, dtype=np.float32) * np.float32(0.1))}
+        reqs.append({"rows": rows, "media": media})
+    return reqs

@@ -270,6 +270,88 @@ void d1h_audio_destroy(D1Audio* a);
  * after it waits for this one). Returns the number of output rows or a negative status. */
 int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel, float* out, cudaStream_t stream);
 
+/* As d1h_audio_encode from 16 kHz waveforms: clip c has n_samples[c] host fp32 samples (pcm holds the clips back to
+ * back); each clip is cut to 30 s and zero-padded to 0.5 s (src/audio.rs:238-247) and its log-mel features are
+ * computed on the device (d1_log_mel). valid_out (optional, [n_clips]) receives each clip's mel frame count. */
+int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const float* pcm, float* out, int* valid_out,
+                         cudaStream_t stream);
+
+/* Vision batch capacity in patches (max_patches of d1h_vision_create). */
+int d1h_vision_capacity(const D1Vision* v);
+/* Number of attention (is_attn = 1) or conv (is_attn = 0) trunk layers of the model. */
+int d1h_model_layers(const D1Model* m, int is_attn);
+
+/* ------------------------------------------------------------------------------------------------ engine
+ * Continuous batching over one device's runners (src/engine.rs:149-525): requests (jobs) of question rows and
+ * optional media; every d1e_step packs question rows FIFO across requests into one varlen batch under the token
+ * budget and launches it, encodes at most one media group and runs its prefixes through the trunk once, keeps up
+ * to two batches in flight, and moves finished requests to a completion queue (d1e_take). One engine per
+ * device, driven from one host thread; engines of different devices are independent. */
+enum { D1_MEDIA_NONE = 0, D1_MEDIA_IMAGES = 1, D1_MEDIA_AUDIO = 2 };
+
+typedef struct D1EngineConfig {
+    int max_batch_tokens;        /* token budget per text batch (src/main.rs:153, default 8192) */
+    int cap_tokens;              /* workspace capacity in tokens (>= max_batch_tokens, >= the longest question) */
+    long long media_cache_bytes; /* budget for live prefix caches (src/main.rs:155, default 1536 MiB) */
+} D1EngineConfig;
+
+typedef struct D1Row {           /* one question (src/engine.rs:21-25) */
+    const int* ids;
+    int n_ids;
+    const int* markers;          /* option-marker rows within the question */
+    int n_markers;
+    int qtype;
+} D1Row;
+
+typedef struct D1Media {         /* src/engine.rs:27-31 */
+    int kind;                    /* D1_MEDIA_* */
+    int n_crops;                 /* images: crops of all the request's images, in order */
+    const int* ph;
+    const int* pw;
+    const d1_half* patches;      /* host fp16 [sum ph*pw][768] */
+    const float* mel;            /* audio: host fp32 [valid][128] normalised log-mel frames, or NULL with pcm */
+    int valid;                   /* 1 .. 3000 */
+    const float* pcm;            /* audio as a 16 kHz waveform (features computed on the device), or NULL */
+    int n_samples;
+} D1Media;
+
+typedef struct D1Job {           /* src/engine.rs:49-53 */
+    const D1Row* rows;
+    int n_rows;
+    D1Media media;
+} D1Job;
+
+typedef struct D1EngineStats {
+    long long tokens;            /* question tokens launched */
+    long long media_tokens;      /* prefix positions run through the trunk */
+    long long batches;
+    long long media_jobs;          /* requests whose media were encoded */
+    long long rows;
+} D1EngineStats;
+
+typedef struct D1Engine D1Engine;
+
+/* Creates an engine on the current device over a text model and optional encoders (NULL: requests with that
+ * media fail), with its own workspace; all work goes to `stream`. NULL on failure (d1e_last_error). */
+D1Engine* d1e_create(D1Model* m, D1Vision* vision, D1Audio* audio, const D1EngineConfig* cfg, cudaStream_t stream);
+void d1e_destroy(D1Engine* e);
+/* Copies a request into the engine; returns its id (>= 0) or a negative status. */
+long long d1e_submit(D1Engine* e, const D1Job* job);
+/* One engine iteration (src/engine.rs:182-221). Returns the number of requests that finished in it, or a
+ * negative status. */
+int d1e_step(D1Engine* e);
+/* Requests submitted and not finished. */
+int d1e_pending(const D1Engine* e);
+/* Question tokens (plus unencoded media positions) still queued: the dispatcher's load measure. */
+long long d1e_queued_tokens(const D1Engine* e);
+/* Logit count of the next finished request, or -1 if none. */
+int d1e_next_logits(const D1Engine* e);
+/* Pops the next finished request: its id, its logits (rows in order, one per option marker) and its error text
+ * (empty on success). Returns the number of logits, -1 if none finished, -2 if cap is too small. */
+int d1e_take(D1Engine* e, long long* id, float* logits, int cap, char* err, int err_cap);
+void d1e_stats(const D1Engine* e, D1EngineStats* out);
+const char* d1e_last_error(void);
+
 /* Number of kernel launches the runner made since the model was created (a counter for benchmarks). */
 long long d1h_launch_count(const D1Model* m);
 /* Bytes the last launch on `slot` copied host->device (its batch metadata, token ids included) and

@@ -242,6 +242,14 @@ int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const
                    const d1_half* pp, int ldp, int pp_rows, int pp_center, d1_half* o, int ldo, const int* offs,
                    int n_clips, int max_len, int heads, float scale, cudaStream_t stream);
 
+/* extension — the audio front end on the GPU: normalised log-mel features of n (>= 1) samples at 16 kHz, device x
+ * -> device mel fp32 [1 + n/160][128], of which the first n/160 frames are valid (the rest zero). Replaces
+ * audio::mel (src/audio.rs:238-299, host code in the reference), with the caller doing its truncation to 30 s and
+ * zero-padding to 0.5 s: pre-emphasis 0.97, 512-point frames every 160 samples under a centred 400-point Hann
+ * window, f64 radix-2 FFT, power, 128 Slaney mel filters, ln(x + 2^-24), per-channel normalisation over the valid
+ * frames (f64 mean, unbiased std + 1e-5). Same operation order and precision as the reference. */
+int d1_log_mel(const float* x, int n, float* mel, cudaStream_t stream);
+
 /* extension — reads and clears d1_relpos_attn's device error word (nonzero: a clip longer than max_len was
  * skipped). */
 int d1_relpos_attn_error(void);
