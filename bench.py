@@ -21,6 +21,8 @@ GPU and oracle/_ref/libd1ref.so (the reference's cuda/*.cu built unchanged) are 
 `reference_gpu_engine`: the reference's own F16 engine (its kernels + cuBLASLt) timed on the same batches.
 
 --gemm-sweep: BASELINE config 1, every projection GEMM shape, one JSON line per shape.
+--workload mixed: BASELINE config 4 — the mixed text / image / audio request stream through the continuous-batching
+engine, one replica per GPU (torchrun for N > 1).
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own replica on its own batches (the model is
 replicated and requests are sharded; no collective on the data path); value = all ranks' tokens / max time.
@@ -312,6 +314,81 @@ def gemm_sweep(pkg, dev, stream, reps=20):
     return out
 
 
+MIXED_PER_GPU = 48  # config-4 requests per GPU (weak scaling): ~90K trunk tokens, ~11 batches of 8192
+
+
+def run_mixed(args, rank, world, local, dev):
+    """the mixed request stream (70% text, 20% text+image, 10% text+audio; 3 questions each)
+    through the continuous-batching engine (csrc/engine.cpp) at max-batch-tokens 8192, one replica per GPU; every
+    rank takes its deterministic least-loaded share of the stream (engine.assign) and runs it on its own engine.
+    value = trunk tokens (questions + media prefixes) of all ranks / the slowest rank's device time."""
+    import torch
+    import torch.distributed as dist
+    pkg = load_package()
+    from fast_d1_omni_b200.engine import Engine, assign, request_tokens
+    from fast_d1_omni_b200.model import AudioModel, TextModel, VisionModel
+    from fast_d1_omni_b200.weights import audio_weights, mixed_requests, text_weights, vision_weights
+    text = TextModel(text_weights(0), device=local, cap_tokens=TOKENS)
+    n_tuned = text.tune(TOKENS)
+    vision = VisionModel(vision_weights(3), device=local, max_patches=16384)
+    audio = AudioModel(audio_weights(4), device=local, max_rows=1536)
+    eng = Engine(text, vision, audio, max_batch_tokens=TOKENS)
+    reqs = mixed_requests(4, MIXED_PER_GPU * world)
+    mine = [r for r, d in zip(reqs, assign(reqs, world)) if d == rank]
+    warm = mixed_requests(99, 6)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(1, args.warmup // 3)):
+        eng.run(warm)
+    torch.cuda.synchronize(dev)
+    s0 = eng.stats()
+    l0 = text.launches
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        e0.record(eng.stream)
+        res = eng.run(mine)
+        e1.record(eng.stream)
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    s1 = eng.stats()
+    dev_s = e0.elapsed_time(e1) / 1e3
+    tokens = (s1["tokens"] - s0["tokens"]) + (s1["media_tokens"] - s0["media_tokens"])
+    assert tokens == sum(request_tokens(r) for r in mine) and all(e == "" for _, e in res)
+    t = torch.tensor([dev_s, wall, float(tokens), float(len(mine))], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t[:2].clone()
+        sm = t[2:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        t = torch.cat([mx, sm])
+    if rank == 0:
+        dev_max, wall_max, tok_all, nreq = (float(x) for x in t)
+        line = {"metric": "mixed continuous-batching trunk tokens/s (BASELINE config 4)", "value": tok_all / dev_max,
+                "unit": "tokens/s", "n_gpus": world, "steps": 1, "warmup": args.warmup,
+                "ms_per_step": dev_max * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16", "data": "synthetic (seeded random weights, token ids, images and waveforms)",
+                "config": {"workload": f"config 4: {MIXED_PER_GPU} requests per GPU (70% text 128-2048 tokens per "
+                                       "question, 20% text+image of config-3 sides, 10% text+audio 1-30 s through the "
+                                       "GPU log-mel front end), 3 questions x 4 options, max-batch-tokens 8192",
+                           "parallelism": f"replicas x{world}, deterministic least-loaded request split",
+                           "gemm_plans": f"tuned at startup ({n_tuned} plans)"},
+                "requests": int(nreq), "requests_per_s": nreq / dev_max,
+                "e2e": {"value": tok_all / wall_max, "unit": "tokens/s", "note": "wall clock, host request buffers"},
+                "engine": {k: s1[k] - s0[k] for k in s1}, "gpu_launches_text_runner": text.launches - l0,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    audio.close()
+    vision.close()
+    text.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -319,6 +396,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="d1", choices=["d1", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="text", choices=["text", "mixed"],
+                    help="text: the metric's 8192-token text batches; mixed: BASELINE config 4 through the engine")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="BASELINE config 1: time every GEMM shape (one JSON line each) instead of the forward")
     ap.add_argument("--only-roofline", action="store_true",
@@ -342,6 +421,12 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     pkg = load_package()
+    if args.workload == "mixed":
+        run_mixed(args, rank, world, local, dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.gemm_sweep:
         if rank == 0:
             gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
