@@ -350,12 +350,14 @@ def run_mixed(args, rank, world, local, dev):
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        torch.cuda.cudart().cudaProfilerStart()  # a profiler started with --profile-from-start off sees only this
         t0 = time.perf_counter()
         e0.record(eng.stream)
         res = eng.run(mine)
         e1.record(eng.stream)
         torch.cuda.synchronize(dev)
         wall = time.perf_counter() - t0
+        torch.cuda.cudart().cudaProfilerStop()
     s1 = eng.stats()
     dev_s = e0.elapsed_time(e1) / 1e3
     tokens = (s1["tokens"] - s0["tokens"]) + (s1["media_tokens"] - s0["media_tokens"])
