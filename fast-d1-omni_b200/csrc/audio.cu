@@ -488,6 +488,8 @@ int d1_relpos_attn_error(void) {
 // fp32; 128 Slaney mel filters summed in fp32 over each filter's nonzero bins in order; ln(s + 2^-24); then each mel
 // channel normalised over the valid frames with f64 mean and unbiased std (std + 1e-5), frames past `valid` zero.
 // Explicit _rn intrinsics keep the compiler from contracting multiply-adds the reference evaluates separately.
+// Everything per frame follows the reference's order; the channel statistics are f64 sums taken in 8 interleaved
+// parts (the reference sums the frames in sequence), a difference at f64 rounding level.
 
 namespace {
 
@@ -536,23 +538,48 @@ __global__ void __launch_bounds__(256) k_mel_frames(const float* __restrict__ x,
     }
 }
 
-// one thread per mel channel, frames in order (the reference's f64 summation order)
-__global__ void __launch_bounds__(MEL_N) k_mel_norm(float* __restrict__ mel, int frames, int valid) {
-    const int m = threadIdx.x;
-    double mean = 0.0;
-    for (int f = 0; f < valid; f++) mean = __dadd_rn(mean, (double)mel[(size_t)f * MEL_N + m]);
-    mean = __ddiv_rn(mean, (double)valid);
-    double var = 0.0;
-    for (int f = 0; f < valid; f++) {
-        const double d = __dsub_rn((double)mel[(size_t)f * MEL_N + m], mean);
-        var = __dadd_rn(var, __dmul_rn(d, d));
+// Per-channel normalisation over the valid frames: 1024 threads, thread (part, channel) sums the frames
+// f = part (mod 8) in f64, the 8 partial sums are combined in part order (the reference sums frames sequentially in
+// f64; the orders differ by f64 rounding only, ~1e-16 relative), then every element is normalised in parallel.
+constexpr int MEL_PARTS = 8;
+
+__global__ void __launch_bounds__(MEL_N * MEL_PARTS) k_mel_norm(float* __restrict__ mel, int frames, int valid) {
+    __shared__ double part_sum[MEL_PARTS][MEL_N];
+    __shared__ double stat[2][MEL_N];  // mean, 1 / (std + 1e-5)
+    const int m = threadIdx.x % MEL_N, part = threadIdx.x / MEL_N;
+    double acc = 0.0;
+#pragma unroll 4
+    for (int f = part; f < valid; f += MEL_PARTS) acc = __dadd_rn(acc, (double)mel[(size_t)f * MEL_N + m]);
+    part_sum[part][m] = acc;
+    __syncthreads();
+    if (part == 0) {
+        double t = 0.0;
+        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][m]);
+        stat[0][m] = __ddiv_rn(t, (double)valid);
     }
-    double sd = sqrt(__ddiv_rn(var, __dsub_rn((double)valid, 1.0)));
-    if (isnan(sd)) sd = 0.0;
-    const double den = __dadd_rn(sd, 1e-5);
-    for (int f = 0; f < frames; f++) {
-        float* p = mel + (size_t)f * MEL_N + m;
-        *p = f < valid ? __double2float_rn(__ddiv_rn(__dsub_rn((double)*p, mean), den)) : 0.f;
+    __syncthreads();
+    const double mean = stat[0][m];
+    acc = 0.0;
+#pragma unroll 4
+    for (int f = part; f < valid; f += MEL_PARTS) {
+        const double d = __dsub_rn((double)mel[(size_t)f * MEL_N + m], mean);
+        acc = __dadd_rn(acc, __dmul_rn(d, d));
+    }
+    __syncthreads();
+    part_sum[part][m] = acc;
+    __syncthreads();
+    if (part == 0) {
+        double t = 0.0;
+        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][m]);
+        double sd = sqrt(__ddiv_rn(t, __dsub_rn((double)valid, 1.0)));
+        if (isnan(sd)) sd = 0.0;
+        stat[1][m] = __dadd_rn(sd, 1e-5);
+    }
+    __syncthreads();
+    for (size_t i = threadIdx.x; i < (size_t)frames * MEL_N; i += MEL_N * MEL_PARTS) {
+        const int c = (int)(i % MEL_N);
+        const int f = (int)(i / MEL_N);
+        mel[i] = f < valid ? __double2float_rn(__ddiv_rn(__dsub_rn((double)mel[i], stat[0][c]), stat[1][c])) : 0.f;
     }
 }
 
@@ -622,6 +649,6 @@ extern "C" int d1_log_mel(const float* x, int n, float* mel, cudaStream_t st) {
     if (mel_tables_ready()) return -1;
     const int frames = 1 + n / MEL_HOP, valid = n / MEL_HOP;
     k_mel_frames<<<frames, 256, 0, st>>>(x, n, mel);
-    k_mel_norm<<<1, MEL_N, 0, st>>>(mel, frames, valid);
+    k_mel_norm<<<1, MEL_N * MEL_PARTS, 0, st>>>(mel, frames, valid);
     return (int)cudaGetLastError();
 }

@@ -627,12 +627,23 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
         const D1HeadLayer& l = m->head[li];
         m->launches++;
         CK(k.layernorm(h, pend, 1.f, l.n1_w, l.n1_b, xn, nullptr, t, D, 1e-5f, st));
-        CK(m->gemm(t, qkv_ld, D, xn, D, l.qkv, D, big, qkv_ld, 0, 1.f, 0.f, st));
-        const float* qb = l.qkv_b;
+        // q/k/v biases: the reference adds them as flash attention loads q/k/v (fp32 add, rounded to fp16); with
+        // the fused epilogue the QKV GEMM adds them to its fp16-rounded output instead — the same values — and the
+        // attention runs its bias-free path.
+        const bool fold = m->fused && k.gemm_bias_act;
+        if (fold) {
+            m->launches++;
+            CK(k.gemm_bias_act(m->lt, t, qkv_ld, D, xn, D, l.qkv, D, l.qkv_b, 0, big, qkv_ld, st));
+        } else {
+            CK(m->gemm(t, qkv_ld, D, xn, D, l.qkv, D, big, qkv_ld, 0, 1.f, 0.f, st));
+        }
+        const float* bq = fold ? nullptr : l.qkv_b;
+        const float* bk = fold ? nullptr : l.qkv_b + D;
+        const float* bv = fold ? nullptr : l.qkv_b + 2 * D;
         if (li + 1 < nh) {
             m->launches++;
-            CK(k.flash_attn(big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, qb, qb + D, qb + 2 * D, act, D, d_head_attn,
-                            d_work, n_work, HEADS, 1, 0.125f, st));
+            CK(k.flash_attn(big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, act, D, d_head_attn, d_work,
+                            n_work, HEADS, 1, 0.125f, st));
             CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
             m->launches++;
             CK(k.layernorm(h, l.out_b, 1.f, l.n2_w, l.n2_b, xn, nullptr, t, D, 1e-5f, st));
@@ -647,8 +658,8 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
                 m->launches += 3;
                 CK(k.gather_rows(big, ws->mq, d_mrows, nm, qkv_ld * 2, st));
                 CK(k.gather_rows(h, ws->mh, d_mrows, nm, D * 4, st));
-                CK(k.flash_attn(ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, qb, qb + D, qb + 2 * D, ws->mo, D,
-                                d_last_attn, d_mwork, n_mwork, HEADS, 1, 0.125f, st));
+                CK(k.flash_attn(ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, ws->mo, D, d_last_attn,
+                                d_mwork, n_mwork, HEADS, 1, 0.125f, st));
                 CK(m->gemm(nm, D, D, ws->mo, D, l.out, D, ws->mh, D, 1, 1.f, 1.f, st));
                 m->launches++;
                 CK(k.layernorm(ws->mh, l.out_b, 1.f, l.n2_w, l.n2_b, ws->mx, nullptr, nm, D, 1e-5f, st));
@@ -939,10 +950,18 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
     for (const auto& l : v->layers) {
         L++;
         CK(k.layernorm(h, pend, 1.f, l.ln1_w, l.ln1_b, xn, nullptr, ti, VD, eps, st));
-        CK(kt_gemm(k, v->lt, L, ti, 3 * VD, VD, xn, VD, l.qkv, VD, big, 3 * VD, 0, 1.f, 0.f, st));
+        // q/k/v biases folded into the QKV GEMM epilogue when fused (same fp16 values as adding them on load)
+        const bool fold = v->fused && k.gemm_bias_act;
+        if (fold) {
+            L++;
+            CK(k.gemm_bias_act(v->lt, ti, 3 * VD, VD, xn, VD, l.qkv, VD, l.qkv_b, 0, big, 3 * VD, st));
+        } else {
+            CK(kt_gemm(k, v->lt, L, ti, 3 * VD, VD, xn, VD, l.qkv, VD, big, 3 * VD, 0, 1.f, 0.f, st));
+        }
         L++;
-        CK(k.flash_attn(big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, l.qkv_b, l.qkv_b + VD, l.qkv_b + 2 * VD, act,
-                        VD, d_seqs, d_work, n_work, VHEADS, 1, 0.125f, st));
+        CK(k.flash_attn(big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, fold ? nullptr : l.qkv_b,
+                        fold ? nullptr : l.qkv_b + VD, fold ? nullptr : l.qkv_b + 2 * VD, act, VD, d_seqs, d_work,
+                        n_work, VHEADS, 1, 0.125f, st));
         CK(kt_gemm(k, v->lt, L, ti, VD, VD, act, VD, l.out, VD, h, VD, 1, 1.f, 1.f, st));
         L++;
         CK(k.layernorm(h, l.out_b, 1.f, l.ln2_w, l.ln2_b, xn, nullptr, ti, VD, eps, st));

@@ -247,7 +247,8 @@ int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const
  * audio::mel (src/audio.rs:238-299, host code in the reference), with the caller doing its truncation to 30 s and
  * zero-padding to 0.5 s: pre-emphasis 0.97, 512-point frames every 160 samples under a centred 400-point Hann
  * window, f64 radix-2 FFT, power, 128 Slaney mel filters, ln(x + 2^-24), per-channel normalisation over the valid
- * frames (f64 mean, unbiased std + 1e-5). Same operation order and precision as the reference. */
+ * frames (f64 mean, unbiased std + 1e-5). The reference's precision and per-frame operation order; the channel
+ * statistics are f64 sums in 8 interleaved parts (the reference sums sequentially). */
 int d1_log_mel(const float* x, int n, float* mel, cudaStream_t stream);
 
 /* extension — reads and clears d1_relpos_attn's device error word (nonzero: a clip longer than max_len was
