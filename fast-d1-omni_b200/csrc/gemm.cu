@@ -772,7 +772,10 @@ struct Plan {
     float us;
 };
 
+// One per device. Several host threads may share a context (engines of one device over one model): `mu` guards the
+// plan table, the tensor-map cache and the lazily set kernel attributes during each call's host work.
 struct Ctx {
+    std::mutex mu;
     int dev = 0;
     int num_sms = 148;
     int* d_err = nullptr;
@@ -1084,6 +1087,7 @@ int d1_lt_gemm(void* ctx, int M, int N, int K, const void* X, int ldx, const voi
     (void)f16acc;
     Ctx* c = (Ctx*)ctx;
     if (!c || M < 0 || N < 0 || K < 0) return -1;
+    std::lock_guard<std::mutex> lock(c->mu);
     if (M == 0 || N == 0) return 0;
     if (!tc_ok(X, ldx, W, ldw, w_kn, K))
         return run_simt(M, N, K, X, ldx, W, ldw, w_kn, Y, ldy, y_f32, alpha, beta, st) ? -1 : 0;
@@ -1103,6 +1107,7 @@ int d1_gemm_swiglu(void* ctx, int M, int F, int K, const d1_half* X, int ldx, co
                    d1_half* out, int ldo, cudaStream_t st) {
     Ctx* c = (Ctx*)ctx;
     if (!c || M < 0 || F <= 0 || K <= 0) return M == 0 ? 0 : -1;
+    std::lock_guard<std::mutex> lock(c->mu);
     if (M == 0) return 0;
     if (!tc_ok(X, ldx, W, ldw, 0, K)) return -1;
     GemmArgs a{};
@@ -1122,6 +1127,7 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
                      const float* bias, int act, d1_half* Y, int ldy, cudaStream_t st) {
     Ctx* c = (Ctx*)ctx;
     if (!c || M < 0 || N < 0 || K <= 0 || act < 0 || act > 4) return -1;
+    std::lock_guard<std::mutex> lock(c->mu);
     if (M == 0 || N == 0) return 0;
     if (!tc_ok(X, ldx, W, ldw, 0, K)) return -1;
     GemmArgs a{};
@@ -1149,6 +1155,7 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
     (void)effort;
     Ctx* c = (Ctx*)ctx;
     if (!c || M <= 0 || N <= 0 || K <= 0) return -1.f;
+    std::lock_guard<std::mutex> lock(c->mu);
     const int bm = bucket_of(M);
     PlanKey key(N, K, ldx, ldw, ldy, w_kn, y_f32, EPI_STORE, bm);
     auto it = c->plans.find(key);
@@ -1200,6 +1207,8 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
 
 int d1_lt_save(void* ctx, const char* path) {
     Ctx* c = (Ctx*)ctx;
+    if (!c) return -1;
+    std::lock_guard<std::mutex> lock(c->mu);
     FILE* f = fopen(path, "w");
     if (!f) return -1;
     fprintf(f, "d1b200-gemm-plans v1 %s\n", d1_build_id());
@@ -1215,6 +1224,8 @@ int d1_lt_save(void* ctx, const char* path) {
 
 int d1_lt_load(void* ctx, const char* path) {
     Ctx* c = (Ctx*)ctx;
+    if (!c) return -1;
+    std::lock_guard<std::mutex> lock(c->mu);
     FILE* f = fopen(path, "r");
     if (!f) return -1;
     char tag[64], ver[16], id[128];
@@ -1242,6 +1253,7 @@ int d1_lt_bucket(int m) { return bucket_of(m); }
 void d1_lt_free_scratch(void* ctx) {
     Ctx* c = (Ctx*)ctx;
     if (!c) return;
+    std::lock_guard<std::mutex> lock(c->mu);
     for (void** p : {&c->sx, &c->sw, &c->sy})
         if (*p) {
             cudaFree(*p);

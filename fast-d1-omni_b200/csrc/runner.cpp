@@ -8,6 +8,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <string>
 #include <vector>
@@ -177,7 +178,7 @@ struct D1Model {
     int n_attn = 0, n_conv = 0, max_ffn = 0;
     float* rope = nullptr;
     bool fused = false;
-    long long launches = 0;
+    std::atomic<long long> launches{0};  // engines of one device may share the model
     int dev = 0;
 
     // Blas::gemm (src/cuda.rs:433-490): Y = alpha X W^T + beta Y. A library without a plan for the shape

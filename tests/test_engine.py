@@ -130,6 +130,7 @@ def test_engine_media_vs_oracle(tmodel, vmodel, amodel, tw, vw, aw):
 
 
 def test_dispatcher_two_engines(tmodel):
+    """Two engines of one device sharing one model (and its GEMM context), stepped by two host threads."""
     from fast_d1_omni_b200.engine import Dispatcher, Engine
     reqs = text_requests(43, 10)
     single = Engine(tmodel, max_batch_tokens=4096)
