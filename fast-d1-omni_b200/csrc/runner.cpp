@@ -409,7 +409,7 @@ void d1h_model_destroy(D1Model* m) {
     delete m;
 }
 
-long long d1h_launch_count(const D1Model* m) { return m ? m->launches : 0; }
+long long d1h_launch_count(const D1Model* m) { return m ? m->launches.load() : 0LL; }
 
 long long d1h_h2d_bytes(const D1Workspace* ws, int slot) {
     return ws && slot >= 0 && slot < SLOTS ? ws->h2d[slot] : -1;
