@@ -458,6 +458,13 @@ D1Engine* d1e_create(D1Model* m, D1Vision* vision, D1Audio* audio, const D1Engin
     e->n_conv = d1h_model_layers(m, 0);
     e->vision_patches = vision ? d1h_vision_capacity(vision) : 0;
     cudaGetDevice(&e->device);
+    // media prefixes and their embeddings are stream-ordered allocations from the device's default pool; keep
+    // freed blocks in the pool instead of unmapping them at every synchronisation (a process-local setting)
+    cudaMemPool_t pool = nullptr;
+    if (cudaDeviceGetDefaultMemPool(&pool, e->device) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
     e->ws = d1h_workspace_create(m, cfg->cap_tokens);
     if (!e->ws) {
         efail(std::string("workspace: ") + d1h_last_error());

@@ -1088,6 +1088,9 @@ D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
     if (!e) e |= dmalloc(&a->pp, (size_t)w->n_layers * PP_ROWS * AD * 2);
     a->mel_rows = (long long)R * 8 + 4096;  // sum of valid <= 8 * rows, plus one spare frame per clip
     if (!e) e |= dmalloc(&a->mel, (size_t)a->mel_rows * N_MELS * 4);
+    // waveform staging for d1h_audio_encode_pcm: R rows need at most 8 * 160 * R samples plus the 0.5 s padding
+    a->pcm_cap = std::min<size_t>(R * 8 * 160 + 4 * (size_t)A_MIN_SAMPLES, (size_t)64 * A_MAX_SAMPLES);
+    if (!e) e |= dmalloc(&a->pcm, a->pcm_cap * 4);
     if (!e) e |= dmalloc(&a->s1, L1 * 64 * SUB_C * 4);
     if (!e) e |= dmalloc(&a->s2, L2 * 32 * SUB_C * 4);
     if (!e) e |= dmalloc(&a->s3, L2 * 32 * SUB_C * 4);
