@@ -399,6 +399,30 @@ __global__ void __launch_bounds__(256) k_scorer_out(const __half* __restrict__ x
 
 // ------------------------------------------------------------------------------------------------ vision
 // 2x2 pixel unshuffle x [ph*pw][C] -> out [(ph/2)*(pw/2)][4C] (cuda/kernels.cu:517-525), uint4 copies.
+// Resized position embeddings of one crop (src/vision.rs:263-302, host code in the reference): the 16x16 grid of
+// position vectors resampled to (ph, pw) by separable antialiased-bilinear taps — horizontal pass, then vertical
+// pass, each a sum from zero of weight * value in tap order (fp32, multiply then add, as the reference's host
+// loops) — plus the patch bias. spans: (first input index, taps) for the ph output rows then the pw output
+// columns; w: their weights, `taps` per entry. One CTA per output patch row, threads over channels.
+__global__ void __launch_bounds__(256) k_vision_pos(const float* __restrict__ grid, const float* __restrict__ bias,
+                                                    const int2* __restrict__ spans, const float* __restrict__ w,
+                                                    int taps, int ph, int pw, int C, float* __restrict__ out) {
+    const int p = blockIdx.x, y = p / pw, x = p % pw;
+    const int2 sy = spans[y], sx = spans[ph + x];
+    const float* wy = w + (size_t)y * taps;
+    const float* wx = w + (size_t)(ph + x) * taps;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < sy.y; j++) {
+            const float* row = grid + ((size_t)(sy.x + j) * 16 + sx.x) * C + c;
+            float t = 0.f;
+            for (int i = 0; i < sx.y; i++) t = __fadd_rn(t, __fmul_rn(__ldg(wx + i), __ldg(row + (size_t)i * C)));
+            acc = __fadd_rn(acc, __fmul_rn(__ldg(wy + j), t));
+        }
+        out[(size_t)p * C + c] = __fadd_rn(acc, __ldg(bias + c));
+    }
+}
+
 __global__ void k_unshuffle(const __half* __restrict__ x, __half* __restrict__ out, int ph, int pw, int C) {
     const int o = blockIdx.x;
     const int i = o / (pw / 2), jj = o % (pw / 2);
@@ -646,6 +670,15 @@ int d1_scorer_out(const d1_half* x, const float* b1, const d1_half* w2, float b2
                   cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
     k_scorer_out<<<nblk(rows, 8), 256, 0, st>>>(x, b1, w2, b2, logits, rows, D);
+    return (int)cudaGetLastError();
+}
+
+int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, const float* w, int taps, int ph,
+                  int pw, int C, float* out, cudaStream_t st) {
+    if (ph <= 0 || pw <= 0) return 0;
+    if (!grid || !patch_b || !spans || !w || !out || taps < 1 || C < 1 || ((uintptr_t)spans & 7)) return -1;
+    k_vision_pos<<<ph * pw, 256, 0, st>>>(grid, patch_b, reinterpret_cast<const int2*>(spans), w, taps, ph, pw, C,
+                                           out);
     return (int)cudaGetLastError();
 }
 

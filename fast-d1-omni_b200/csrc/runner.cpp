@@ -794,6 +794,10 @@ struct D1Vision {
     D1VisionWeights w{};
     std::vector<D1VisionLayer> layers;
     std::vector<float> patch_b, pos;
+    bool builtin = true;               // this library's kernels: position embeddings resized on the GPU
+    float* d_grid = nullptr;           // device [256][768] position grid
+    float* d_patch_b = nullptr;        // device [768]
+    // another kernel library (the reference's): the reference's host resize, cached per grid shape
     std::map<std::pair<int, int>, float*> pos_cache;  // (ph, pw) -> device [ph*pw][768] pos + bias
     bool fused = false;
     long long launches = 0;
@@ -805,7 +809,8 @@ struct D1Vision {
     cudaEvent_t done = nullptr;
     bool busy = false;
 
-    // Resized position embeddings + patch bias for a (ph, pw) grid, computed on the host and cached on the
+    // With another kernel library (the reference's): resized position embeddings + patch bias for a (ph, pw) grid,
+    // computed on the host and cached on the
     // device (src/vision.rs:263-302).
     float* pos_for(int ph, int pw) {
         auto it = pos_cache.find({ph, pw});
@@ -863,6 +868,7 @@ D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, in
     v->patch_b.assign(w->patch_b, w->patch_b + VD);
     v->pos.assign(w->pos, w->pos + 256 * VD);
     v->w.patch_b = v->w.pos = nullptr;
+    v->builtin = kernel_lib == nullptr;
     v->fused = fused != 0;
     v->max_patches = max_patches;
     v->lt = v->k.lt_init(32 << 20);
@@ -875,6 +881,13 @@ D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, in
     if (!e) e |= dmalloc(&v->act, cap * VD * 2);
     if (!e) e |= dmalloc(&v->pix, cap * VD * 2);
     if (!e) e |= dmalloc(&v->meta, VMETA);
+    if (!e && v->builtin) {
+        e |= dmalloc(&v->d_grid, v->pos.size() * 4);
+        if (!e) e |= dmalloc(&v->d_patch_b, VD * 4);
+        if (!e && (cudaMemcpy(v->d_grid, v->pos.data(), v->pos.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                   cudaMemcpy(v->d_patch_b, v->patch_b.data(), VD * 4, cudaMemcpyHostToDevice) != cudaSuccess))
+            e = fail("position grid upload failed");
+    }
     if (!e && (cudaMallocHost((void**)&v->host_meta, VMETA) != cudaSuccess ||
                cudaEventCreateWithFlags(&v->done, cudaEventDisableTiming) != cudaSuccess))
         e = fail("vision host allocation failed");
@@ -888,7 +901,8 @@ D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, in
 void d1h_vision_destroy(D1Vision* v) {
     if (!v) return;
     if (v->busy) cudaEventSynchronize(v->done);
-    for (void* p : {(void*)v->h, (void*)v->xn, (void*)v->big, (void*)v->act, (void*)v->pix, (void*)v->meta})
+    for (void* p : {(void*)v->h, (void*)v->xn, (void*)v->big, (void*)v->act, (void*)v->pix, (void*)v->meta,
+                    (void*)v->d_grid, (void*)v->d_patch_b})
         if (p) cudaFree(p);
     for (auto& kv : v->pos_cache) cudaFree(kv.second);
     if (v->host_meta) cudaFreeHost(v->host_meta);
@@ -927,6 +941,31 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
     MetaWriter mw{v->host_meta, v->meta};
     const AttnSeq* d_seqs = mw.put(seqs);
     const int* d_work = mw.put(work);
+    // per crop: the separable resize taps of its position embeddings (src/vision.rs:173-196), for d1_vision_pos
+    std::vector<const int*> pos_spans(n_crops);
+    std::vector<const float*> pos_w(n_crops);
+    std::vector<int> pos_taps(n_crops);
+    if (v->builtin) {
+        for (int i = 0; i < n_crops; i++) {
+            auto wy = aa_weights(16, ph[i]), wx = aa_weights(16, pw[i]);
+            size_t taps = 1;
+            for (auto& e : wy) taps = std::max(taps, e.second.size());
+            for (auto& e : wx) taps = std::max(taps, e.second.size());
+            std::vector<int> sp;
+            std::vector<float> wt((size_t)(ph[i] + pw[i]) * taps, 0.f);
+            size_t r = 0;
+            for (auto* tab : {&wy, &wx})
+                for (auto& e : *tab) {
+                    sp.push_back(e.first);
+                    sp.push_back((int)e.second.size());
+                    std::copy(e.second.begin(), e.second.end(), wt.begin() + r * taps);
+                    r++;
+                }
+            pos_spans[i] = mw.put(sp);
+            pos_w[i] = mw.put(wt);
+            pos_taps[i] = (int)taps;
+        }
+    }
     if (mw.overflow || mw.off > VMETA) return fail("vision metadata too large");
     if (cudaMemcpyAsync(v->meta, v->host_meta, mw.off, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemcpyAsync(v->pix, pixels, (size_t)t * VD * 2, cudaMemcpyHostToDevice, st) != cudaSuccess)
@@ -935,11 +974,17 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
     // embeddings: h = pos + bias per crop, then += pixels . W^T
     off = 0;
     for (int i = 0; i < n_crops; i++) {
-        float* p = v->pos_for(ph[i], pw[i]);
-        if (!p) return -1;
-        if (cudaMemcpyAsync(v->h + (size_t)off * VD, p, (size_t)ph[i] * pw[i] * VD * 4, cudaMemcpyDeviceToDevice, st) !=
-            cudaSuccess)
-            return fail("position copy failed");
+        if (v->builtin) {
+            v->launches++;
+            CK(d1_vision_pos(v->d_grid, v->d_patch_b, pos_spans[i], pos_w[i], pos_taps[i], ph[i], pw[i], VD,
+                             v->h + (size_t)off * VD, st));
+        } else {
+            float* p = v->pos_for(ph[i], pw[i]);
+            if (!p) return -1;
+            if (cudaMemcpyAsync(v->h + (size_t)off * VD, p, (size_t)ph[i] * pw[i] * VD * 4, cudaMemcpyDeviceToDevice,
+                                st) != cudaSuccess)
+                return fail("position copy failed");
+        }
         off += ph[i] * pw[i];
     }
     float* h = v->h;

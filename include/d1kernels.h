@@ -242,6 +242,15 @@ int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const
                    const d1_half* pp, int ldp, int pp_rows, int pp_center, d1_half* o, int ldo, const int* offs,
                    int n_clips, int max_len, int heads, float scale, cudaStream_t stream);
 
+/* extension — resized position embeddings of one vision crop, written as the crop's initial residual rows:
+ * out[y*pw + x][c] = sum_j wy_j * (sum_i wx_i * grid[(sy+j)*16 + sx+i][c]) + patch_b[c], with the separable
+ * antialiased-bilinear taps of src/vision.rs:173-196 given per output row y (entries 0..ph-1) and column x (entries
+ * ph..ph+pw-1): spans int2 (first input index, tap count), w [ph+pw][taps] weights. grid fp32 [256][C]. Replaces
+ * VisionModel::pos_for (src/vision.rs:263-302, computed on the host and cached per grid shape in the reference),
+ * with the same fp32 operation order. */
+int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, const float* w, int taps, int ph, int pw,
+                  int C, float* out, cudaStream_t stream);
+
 /* extension — the audio front end on the GPU: normalised log-mel features of n (>= 1) samples at 16 kHz, device x
  * -> device mel fp32 [1 + n/160][128], of which the first n/160 frames are valid (the rest zero). Replaces
  * audio::mel (src/audio.rs:238-299, host code in the reference), with the caller doing its truncation to 30 s and

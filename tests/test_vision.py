@@ -91,3 +91,22 @@ def test_config3(pkg, ref_lib, vmodel, vw):
     # the fp32 oracle on the first 4 crops (a packed batch gives each crop the same result as alone)
     want = O.vision_encode(vw, crops[:4], "f32")
     assert rel_rms(got[:want.shape[0]], want) <= 1e-2
+
+
+@pytest.mark.parametrize("ph,pw", [(14, 22), (2, 2), (48, 48), (16, 16), (4, 40)])
+def test_vision_pos_kernel_bit_exact(gpu_lib, vw, ph, pw):
+    """d1_vision_pos (the GPU form of src/vision.rs:263-302) against the oracle's restatement: same fp32 order."""
+    import ctypes as C
+    taps_y, taps_x = O.aa_weights(16, ph), O.aa_weights(16, pw)
+    taps = max(len(w) for _, w in taps_y + taps_x)
+    spans = np.array([[s, len(w)] for s, w in taps_y + taps_x], np.int32)
+    wts = np.zeros((ph + pw, taps), np.float32)
+    for r, (_, w) in enumerate(taps_y + taps_x):
+        wts[r, :len(w)] = w
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    grid, pb, sp, wt = d(np.asarray(vw["pos"], np.float32)), d(vw["patch_b"]), d(spans), d(wts)
+    out = torch.full((ph * pw, 768), float("nan"), device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    assert gpu_lib.d1_vision_pos(P(grid), P(pb), P(sp), P(wt), taps, ph, pw, 768, P(out),
+                                 C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    assert np.array_equal(out.cpu().numpy(), O.vision_pos(vw["pos"], vw["patch_b"], ph, pw))
