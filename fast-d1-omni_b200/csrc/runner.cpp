@@ -806,7 +806,9 @@ struct D1Vision {
     d1_half *xn = nullptr, *big = nullptr, *act = nullptr, *pix = nullptr;
     uint8_t* meta = nullptr;
     uint8_t* host_meta = nullptr;
-    cudaEvent_t done = nullptr;
+    uint8_t* host_pix = nullptr;       // pinned staging of the patch rows
+    cudaEvent_t done = nullptr;        // the previous call's last kernel
+    cudaEvent_t staged = nullptr;      // the previous call's host->device copies
     bool busy = false;
 
     // With another kernel library (the reference's): resized position embeddings + patch bias for a (ph, pw) grid,
@@ -889,7 +891,9 @@ D1Vision* d1h_vision_create(const D1VisionWeights* w, const char* kernel_lib, in
             e = fail("position grid upload failed");
     }
     if (!e && (cudaMallocHost((void**)&v->host_meta, VMETA) != cudaSuccess ||
-               cudaEventCreateWithFlags(&v->done, cudaEventDisableTiming) != cudaSuccess))
+               cudaMallocHost((void**)&v->host_pix, cap * VD * 2) != cudaSuccess ||
+               cudaEventCreateWithFlags(&v->done, cudaEventDisableTiming) != cudaSuccess ||
+               cudaEventCreateWithFlags(&v->staged, cudaEventDisableTiming) != cudaSuccess))
         e = fail("vision host allocation failed");
     if (e) {
         d1h_vision_destroy(v);
@@ -906,7 +910,9 @@ void d1h_vision_destroy(D1Vision* v) {
         if (p) cudaFree(p);
     for (auto& kv : v->pos_cache) cudaFree(kv.second);
     if (v->host_meta) cudaFreeHost(v->host_meta);
+    if (v->host_pix) cudaFreeHost(v->host_pix);
     if (v->done) cudaEventDestroy(v->done);
+    if (v->staged) cudaEventDestroy(v->staged);
     if (v->lt && v->k.lt_destroy) v->k.lt_destroy(v->lt);
     if (v->k.dl) dlclose(v->k.dl);
     delete v;
@@ -924,7 +930,10 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
     }
     if (t > v->max_patches) return fail("patches exceed the vision batch capacity");
     if (v->busy) {
-        if (cudaEventSynchronize(v->done) != cudaSuccess) return fail("event sync failed");
+        // the host staging may be refilled once the previous call's copies are done; its device buffers are
+        // reused in stream order after its last kernel
+        if (cudaEventSynchronize(v->staged) != cudaSuccess || cudaStreamWaitEvent(st, v->done, 0) != cudaSuccess)
+            return fail("event sync failed");
         v->busy = false;
     }
     // metadata: one AttnSeq per crop and its 64-row query tiles (src/vision.rs:310-326)
@@ -967,8 +976,10 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
         }
     }
     if (mw.overflow || mw.off > VMETA) return fail("vision metadata too large");
+    memcpy(v->host_pix, pixels, (size_t)t * VD * 2);
     if (cudaMemcpyAsync(v->meta, v->host_meta, mw.off, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(v->pix, pixels, (size_t)t * VD * 2, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        cudaMemcpyAsync(v->pix, v->host_pix, (size_t)t * VD * 2, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaEventRecord(v->staged, st) != cudaSuccess)
         return fail("vision upload failed");
     const int ti = (int)t, n_work = (int)work.size() / 2;
     // embeddings: h = pos + bias per crop, then += pixels . W^T
@@ -1108,8 +1119,11 @@ struct D1Audio {
     size_t pcm_cap = 0;      // capacity of pcm in samples
     d1_half *xn = nullptr, *big = nullptr, *qu = nullptr, *qv = nullptr, *kk = nullptr, *vv = nullptr, *o = nullptr;
     int* offs = nullptr;
-    int* host_offs = nullptr;
-    cudaEvent_t done = nullptr;
+    int* host_offs = nullptr;          // pinned: clip offsets
+    float* host_mel = nullptr;         // pinned staging of log-mel frames [mel_rows][128]
+    float* host_pcm = nullptr;         // pinned staging of waveforms [pcm_cap]
+    cudaEvent_t done = nullptr;        // the previous call's last kernel
+    cudaEvent_t staged = nullptr;      // the previous call's host->device copies
     bool busy = false;
 };
 
@@ -1133,8 +1147,9 @@ D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
     if (!e) e |= dmalloc(&a->pp, (size_t)w->n_layers * PP_ROWS * AD * 2);
     a->mel_rows = (long long)R * 8 + 4096;  // sum of valid <= 8 * rows, plus one spare frame per clip
     if (!e) e |= dmalloc(&a->mel, (size_t)a->mel_rows * N_MELS * 4);
-    // waveform staging for d1h_audio_encode_pcm: R rows need at most 8 * 160 * R samples plus the 0.5 s padding
-    a->pcm_cap = std::min<size_t>(R * 8 * 160 + 4 * (size_t)A_MIN_SAMPLES, (size_t)64 * A_MAX_SAMPLES);
+    // waveform staging for d1h_audio_encode_pcm: a clip of T rows has valid <= 8T frames and fewer than
+    // 160 (valid + 1) samples, and a call has at most R / 7 clips (0.5 s minimum -> 7 rows): < 1303 R samples
+    a->pcm_cap = std::min<size_t>(R * 1304 + 2 * (size_t)A_MIN_SAMPLES, (size_t)64 * A_MAX_SAMPLES);
     if (!e) e |= dmalloc(&a->pcm, a->pcm_cap * 4);
     if (!e) e |= dmalloc(&a->s1, L1 * 64 * SUB_C * 4);
     if (!e) e |= dmalloc(&a->s2, L2 * 32 * SUB_C * 4);
@@ -1146,7 +1161,10 @@ D1Audio* d1h_audio_create(const D1AudioWeights* w, int fused, int max_rows) {
         if (!e) e |= dmalloc(p, R * AD * 2);
     if (!e) e |= dmalloc(&a->offs, 4096 * 4);
     if (!e && (cudaMallocHost((void**)&a->host_offs, 4096 * 4) != cudaSuccess ||
-               cudaEventCreateWithFlags(&a->done, cudaEventDisableTiming) != cudaSuccess))
+               cudaMallocHost((void**)&a->host_mel, (size_t)a->mel_rows * N_MELS * 4) != cudaSuccess ||
+               cudaMallocHost((void**)&a->host_pcm, a->pcm_cap * 4) != cudaSuccess ||
+               cudaEventCreateWithFlags(&a->done, cudaEventDisableTiming) != cudaSuccess ||
+               cudaEventCreateWithFlags(&a->staged, cudaEventDisableTiming) != cudaSuccess))
         e = fail("audio host allocation failed");
     if (!e) {  // per-layer relative-position projections
         std::vector<uint16_t> pe = audio_pe_table();
@@ -1177,8 +1195,10 @@ void d1h_audio_destroy(D1Audio* a) {
                     (void*)a->big, (void*)a->qu, (void*)a->qv, (void*)a->kk, (void*)a->vv, (void*)a->o,
                     (void*)a->offs})
         if (p) cudaFree(p);
-    if (a->host_offs) cudaFreeHost(a->host_offs);
+    for (void* p : {(void*)a->host_offs, (void*)a->host_mel, (void*)a->host_pcm})
+        if (p) cudaFreeHost(p);
     if (a->done) cudaEventDestroy(a->done);
+    if (a->staged) cudaEventDestroy(a->staged);
     if (a->lt) d1_lt_destroy(a->lt);
     delete a;
 }
@@ -1199,7 +1219,9 @@ int audio_prepare(D1Audio* a, int n_clips, const int* valid, int& max_t, cudaStr
     }
     if (rows > a->max_rows) return fail("clips exceed the audio batch capacity");
     if (a->busy) {
-        if (cudaEventSynchronize(a->done) != cudaSuccess) return fail("event sync failed");
+        // host staging refilled once the previous call's copies are done; device buffers reused in stream order
+        if (cudaEventSynchronize(a->staged) != cudaSuccess || cudaStreamWaitEvent(st, a->done, 0) != cudaSuccess)
+            return fail("event sync failed");
         a->busy = false;
     }
     a->host_offs[0] = 0;
@@ -1224,7 +1246,9 @@ int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel
     long long frames = 0;
     for (int c = 0; c < n_clips; c++) frames += valid[c];
     if (frames > a->mel_rows) return fail("clips exceed the audio batch capacity");
-    if (cudaMemcpyAsync(a->mel, mel, (size_t)frames * N_MELS * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    memcpy(a->host_mel, mel, (size_t)frames * N_MELS * 4);
+    if (cudaMemcpyAsync(a->mel, a->host_mel, (size_t)frames * N_MELS * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaEventRecord(a->staged, st) != cudaSuccess)
         return fail("audio upload failed");
     std::vector<const float*> mp(n_clips);
     const float* p = a->mel;
@@ -1253,25 +1277,28 @@ int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const fl
     int max_t = 0;
     const int rows = audio_prepare(a, n_clips, valid.data(), max_t, st);
     if (rows < 0) return rows;
-    if (total > a->pcm_cap) {
-        if (a->pcm) cudaFree(a->pcm);
-        a->pcm = nullptr;
-        a->pcm_cap = 0;
-        if (dmalloc(&a->pcm, total * 4)) return -1;
-        a->pcm_cap = total;
-    }
-    std::vector<const float*> mp(n_clips);
+    if (total > a->pcm_cap) return fail("clips exceed the audio waveform staging capacity");
+    // stage every clip (cut, zero-padded) in pinned memory, one copy, then the front end per clip
     const float* src = pcm;
-    size_t off = 0, moff = 0;
+    size_t off = 0;
     for (int c = 0; c < n_clips; c++) {
         const int n = std::max(used[c], A_MIN_SAMPLES);
-        if (cudaMemcpyAsync(a->pcm + off, src, (size_t)used[c] * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            (n > used[c] && cudaMemsetAsync(a->pcm + off + used[c], 0, (size_t)(n - used[c]) * 4, st) != cudaSuccess))
-            return fail("audio upload failed");
+        memcpy(a->host_pcm + off, src, (size_t)used[c] * 4);
+        if (n > used[c]) memset(a->host_pcm + off + used[c], 0, (size_t)(n - used[c]) * 4);
+        src += n_samples[c];
+        off += (size_t)n;
+    }
+    if (cudaMemcpyAsync(a->pcm, a->host_pcm, total * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaEventRecord(a->staged, st) != cudaSuccess)
+        return fail("audio upload failed");
+    std::vector<const float*> mp(n_clips);
+    off = 0;
+    size_t moff = 0;
+    for (int c = 0; c < n_clips; c++) {
+        const int n = std::max(used[c], A_MIN_SAMPLES);
         a->launches += 2;
         if (d1_log_mel(a->pcm + off, n, a->mel + moff * N_MELS, st)) return fail("log-mel front end failed");
         mp[c] = a->mel + moff * N_MELS;
-        src += n_samples[c];
         off += (size_t)n;
         moff += (size_t)valid[c] + 1;
         if (valid_out) valid_out[c] = valid[c];
