@@ -150,6 +150,7 @@ EXTENSIONS = {
     "d1_relpos_attn_error": (i32, []),
     "d1_log_mel": (i32, [p, i32, p, p]),
     "d1_vision_pos": (i32, [p, p, p, p, i32, i32, i32, i32, p, p]),
+    "d1_gemm_noalloc": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, i32, p]),
     "d1_lt_destroy": (None, [p]),
     "d1_build_id": (C.c_char_p, []),
 }

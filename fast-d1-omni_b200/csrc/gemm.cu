@@ -1263,3 +1263,117 @@ void d1_lt_free_scratch(void* ctx) {
 }
 
 }  // extern "C"
+
+// ================================================================================================ allocation-free form
+// d1_gemm_noalloc: an fp16-output GEMM whose only scratch — the fp32 split-K accumulator and the kernels' error word
+// — lives in a file-scope static device buffer, so the call allocates nothing (no context, no cudaMalloc, no
+// cached tensor maps). The K range of every output tile is split across CTAs; each CTA reduce-adds its partial
+// tile into the buffer through the same tcgen05 kernel the residual GEMMs use, then one pass rounds the sums to
+// fp16 into Y. The buffer is cleared (cudaMemsetAsync) before every call. Overlapping calls on one device race on
+// the buffer.
+
+namespace {
+
+constexpr size_t kNoallocMaxElems = (size_t)1 << 20;  // fp32 partial sums: 4 MiB
+constexpr size_t kNoallocErrOff = kNoallocMaxElems;   // error word right after the accumulator
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocMaxElems + 64];
+
+__global__ void __launch_bounds__(256) k_noalloc_to_f16(const float* __restrict__ acc, int M, int N,
+                                                        __half* __restrict__ Y, int ldy) {
+    const size_t total = (size_t)M * N;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = i / N, n = i % N;
+        Y[m * ldy + n] = __float2half_rn(acc[i]);
+    }
+}
+
+struct NoallocDev {
+    float* scratch = nullptr;
+    int num_sms = 0;
+};
+
+// Per-device set-up, once: the buffer's device address (cudaGetSymbolAddress, checked), the SM count and the
+// kernel's shared-memory attribute.
+bool noalloc_setup(NoallocDev& d) {
+    static NoallocDev devs[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    NoallocDev& s = devs[dev];
+    if (!s.scratch) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return false;
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return false;
+        using S = Smem<128, 6>;
+        if (cudaFuncSetAttribute(k_gemm_tc<128, 6, EPI_ADD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)S::BYTES) != cudaSuccess)
+            return false;
+        s.num_sms = sms;
+        s.scratch = static_cast<float*>(p);
+    }
+    d = s;
+    return true;
+}
+
+bool encode_nocache(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_bytes,
+                    uint32_t box_inner, uint32_t box_outer, bool f32) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" int d1_gemm_noalloc(int M, int N, int K, const d1_half* X, int ldx, const d1_half* W, int ldw, d1_half* Y,
+                               int ldy, int split, cudaStream_t st) {
+    if (M < 0 || N < 0 || K < 0 || split < 1 || split > 64) return -1;
+    if (M == 0 || N == 0) return 0;
+    if ((size_t)M * (size_t)N > kNoallocMaxElems) return -1;  // beyond the static accumulator
+    if (!Y || ldy < N || N % 4 || !tc_ok(X, ldx, W, ldw, 0, K)) return -1;
+    NoallocDev d;
+    if (!noalloc_setup(d)) return -1;
+    float* acc = d.scratch;
+    int* err = reinterpret_cast<int*>(d.scratch + kNoallocErrOff);
+    // what must start at zero: the reduce-add accumulator and the error word
+    if (cudaMemsetAsync(acc, 0, (size_t)M * N * sizeof(float), st) != cudaSuccess ||
+        cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
+        return -1;
+    CUtensorMap ta, tb, ty;
+    if (!encode_nocache(&ta, X, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, BK, BM, false) ||
+        !encode_nocache(&tb, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw * 2, BK, 128, false) ||
+        !encode_nocache(&ty, acc, (uint64_t)N, (uint64_t)M, (uint64_t)N * 4, 32, 32, true))
+        return -1;
+    GemmArgs a{};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.Y = acc;
+    a.ldy = N;
+    a.y_f32 = 1;
+    a.alpha = 1.f;
+    a.beta = 1.f;
+    a.kb_per = split;
+    a.num_m = (M + BM - 1) / BM;
+    a.num_n = (N + 127) / 128;
+    a.num_tiles = a.num_m * a.num_n;
+    a.num_kb = (K + BK - 1) / BK;
+    set_split(a);
+    a.n_fast = M > N;
+    a.err = err;
+    const int grid = a.num_units < d.num_sms ? a.num_units : d.num_sms;
+    k_gemm_tc<128, 6, EPI_ADD, true><<<grid, kThreads, Smem<128, 6>::BYTES, st>>>(ta, tb, ty, a);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    const size_t total = (size_t)M * N;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)d.num_sms * 8);
+    k_noalloc_to_f16<<<blocks, 256, 0, st>>>(acc, M, N, reinterpret_cast<__half*>(Y), ldy);
+    return (int)cudaGetLastError();
+}

@@ -264,6 +264,15 @@ int d1_log_mel(const float* x, int n, float* mel, cudaStream_t stream);
  * skipped). */
 int d1_relpos_attn_error(void);
 
+/* extension, no reference counterpart — fp16-output GEMM that allocates nothing: Y[M,N] = fp16(X[M,K] . W[N,K]^T)
+ * (W nn.Linear, fp32 accumulation), the K range of every 128x128 output tile split across up to `split` CTAs
+ * (1 .. 64). Needs no context: its scratch — the fp32 partial sums and the kernels' error word — is a file-scope
+ * static device buffer of 2^20 floats (4 MiB), cleared at the start of every call; M*N above 2^20 is rejected
+ * (-1), as are N not a multiple of 4 and X/W rows that are not 16-byte aligned. Calls that overlap on one device
+ * (other streams or threads) race on that buffer and must not be issued. Returns 0 or an error status. */
+int d1_gemm_noalloc(int M, int N, int K, const d1_half* X, int ldx, const d1_half* W, int ldw, d1_half* Y, int ldy,
+                    int split, cudaStream_t stream);
+
 /* extension — releases a context made by d1_lt_init (the reference never frees it). */
 void d1_lt_destroy(void* ctx);
 
