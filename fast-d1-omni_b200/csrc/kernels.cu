@@ -323,73 +323,93 @@ __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bc
 // qkv row = [q (H*64) | k (KVH*64) | v (KVH*64)], in place. Half a warp per 64-wide head vector: lane j of the
 // half holds dims (2j, 2j+1) and (2j+32, 2j+33), i.e. both halves of the rotate-half pairs (l, l+32), l = 2j, 2j+1
 // (cuda/kernels.cu:263-303).
-// QK-norm + RoPE with 16-byte accesses: 8 lanes per 64-element head vector, lane k of a group holds elements
-// 8k .. 8k+7, so the rotate-half partner of element e (e ^ 32) sits in lane k ^ 4 of the same group. Units per row:
-// H query heads, KVH key heads, then KVH value heads (copied to the prefix cache when the sequence saves one, else
-// idle). Needs 16-byte aligned rows; d1_qk_norm_rope falls back to k_qk_norm_rope otherwise.
+// QK-norm + RoPE with 16-byte accesses, one warp per row: 8 lanes per 64-element head vector (lane k of a group holds
+// elements 8k .. 8k+7, so the rotate-half partner of element e, e ^ 32, sits in lane k ^ 4 of the same group); the
+// warp's 4 groups walk the row's H query and KVH key heads with every head load issued up front, and share the
+// row's sequence lookup and RoPE (cos, sin) values. The KVH value heads are copied to the prefix cache when the
+// sequence saves one. Needs 16-byte aligned rows and H + KVH <= 32; d1_qk_norm_rope falls back to k_qk_norm_rope
+// otherwise.
+constexpr int kQkMaxPerGroup = 8;  // (H + KVH) / 4 heads per group at most
+
 __global__ void __launch_bounds__(256) k_qk_norm_rope8(__half* __restrict__ qkv, int ld, int H, int KVH,
                                                        const float* __restrict__ qn, const float* __restrict__ kn,
                                                        const float* __restrict__ rope,
                                                        const int* __restrict__ tok_seq,
                                                        const SeqInfo* __restrict__ seqs, int attn_idx, int rows,
                                                        float eps) {
-    const int units = H + 2 * KVH;
-    const long g = (long)blockIdx.x * 32 + (threadIdx.x >> 3);
-    const int k = threadIdx.x & 7;
-    const bool valid = g < (long)rows * units;
-    const int t = valid ? (int)(g / units) : 0, u = valid ? (int)(g % units) : 0;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= rows) return;  // whole warps leave together
+    const int lane = threadIdx.x & 31, grp = lane >> 3, k = lane & 7;
+    const int nh = H + KVH;
+    uint4* row = reinterpret_cast<uint4*>(qkv + (size_t)t * ld);
+    uint4 raw[kQkMaxPerGroup];
+#pragma unroll
+    for (int j = 0; j < kQkMaxPerGroup; j++) {
+        const int u = grp + 4 * j;
+        raw[j] = u < nh ? row[u * 8 + k] : make_uint4(0, 0, 0, 0);
+    }
     const SeqInfo s = seqs[__ldg(tok_seq + t)];
     const int local = t - s.start, pos = local + s.pos_off;
-    const bool normed = valid && u < H + KVH, isq = u < H;
-    uint4* p = reinterpret_cast<uint4*>(qkv + (size_t)t * ld + u * 64) + k;
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (valid && (normed || s.save_v)) raw = *p;
-    if (valid && !normed && s.save_v)  // raw V into the prefix cache
-        reinterpret_cast<uint4*>(s.save_v + ((size_t)attn_idx * s.len + local) * (KVH * 64) + (u - H - KVH) * 64)[k] =
-            raw;
-    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-    float x[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float2 f = __half22float2(h2[i]);
-        x[2 * i] = f.x;
-        x[2 * i + 1] = f.y;
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) ss += x[i] * x[i];
-    ss += __shfl_xor_sync(D1_FULL_MASK, ss, 1);
-    ss += __shfl_xor_sync(D1_FULL_MASK, ss, 2);
-    ss += __shfl_xor_sync(D1_FULL_MASK, ss, 4);
-    const float r = rsqrtf(ss / 64.f + eps);
-    const float* w = (isq ? qn : kn) + 8 * k;
-    float y[8], q[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) y[i] = normed ? x[i] * r * __ldg(w + i) : 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) q[i] = __shfl_xor_sync(D1_FULL_MASK, y[i], 4);
-    if (!normed) return;
-    // (cos, sin) of pairs 8(k & 3) .. +7 at this position: 16 contiguous floats
+    float cs[16];  // (cos, sin) of pairs 8(k & 3) .. +7 at this position
     const float4* cs4 = reinterpret_cast<const float4*>(rope + ((size_t)pos * 32 + 8 * (k & 3)) * 2);
-    float o[8];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const float4 cs = __ldg(cs4 + i);  // (c, s) of pairs 2i, 2i+1 of this lane
-        if (k < 4) {  // first half: a = own value, b = partner
-            o[2 * i] = y[2 * i] * cs.x - q[2 * i] * cs.y;
-            o[2 * i + 1] = y[2 * i + 1] * cs.z - q[2 * i + 1] * cs.w;
-        } else {      // second half: b = own value, a = partner
-            o[2 * i] = y[2 * i] * cs.x + q[2 * i] * cs.y;
-            o[2 * i + 1] = y[2 * i + 1] * cs.z + q[2 * i + 1] * cs.w;
-        }
+        const float4 c = __ldg(cs4 + i);
+        cs[4 * i] = c.x;
+        cs[4 * i + 1] = c.y;
+        cs[4 * i + 2] = c.z;
+        cs[4 * i + 3] = c.w;
     }
-    uint4 out;
-    __half2* oh = reinterpret_cast<__half2*>(&out);
 #pragma unroll
-    for (int i = 0; i < 4; i++) oh[i] = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
-    *p = out;
-    if (!isq && s.save_k)
-        reinterpret_cast<uint4*>(s.save_k + ((size_t)attn_idx * s.len + local) * (KVH * 64) + (u - H) * 64)[k] = out;
+    for (int j = 0; j < kQkMaxPerGroup; j++) {
+        const int u = grp + 4 * j;
+        if (4 * j >= nh) break;  // uniform across the warp
+        const bool active = u < nh, isq = u < H;
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw[j]);
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = __half22float2(h2[i]);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss += x[i] * x[i];
+        ss += __shfl_xor_sync(D1_FULL_MASK, ss, 1);
+        ss += __shfl_xor_sync(D1_FULL_MASK, ss, 2);
+        ss += __shfl_xor_sync(D1_FULL_MASK, ss, 4);
+        const float r = rsqrtf(ss / 64.f + eps);
+        const float* w = (isq ? qn : kn) + 8 * k;
+        float y[8], q[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) y[i] = active ? x[i] * r * __ldg(w + i) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = __shfl_xor_sync(D1_FULL_MASK, y[i], 4);
+        if (!active) continue;
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            if (k < 4) {  // first half: a = own value, b = partner
+                o[i] = y[i] * cs[2 * i] - q[i] * cs[2 * i + 1];
+                o[i + 1] = y[i + 1] * cs[2 * i + 2] - q[i + 1] * cs[2 * i + 3];
+            } else {      // second half: b = own value, a = partner
+                o[i] = y[i] * cs[2 * i] + q[i] * cs[2 * i + 1];
+                o[i + 1] = y[i + 1] * cs[2 * i + 2] + q[i + 1] * cs[2 * i + 3];
+            }
+        }
+        uint4 out;
+        __half2* oh = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+        for (int i = 0; i < 4; i++) oh[i] = __floats2half2_rn(o[2 * i], o[2 * i + 1]);
+        row[u * 8 + k] = out;
+        if (!isq && s.save_k)
+            reinterpret_cast<uint4*>(s.save_k + ((size_t)attn_idx * s.len + local) * (KVH * 64) + (u - H) * 64)[k] = out;
+    }
+    if (s.save_v)  // raw V heads into the prefix cache
+        for (int g = grp; g < KVH; g += 4)
+            reinterpret_cast<uint4*>(s.save_v + ((size_t)attn_idx * s.len + local) * (KVH * 64) + g * 64)[k] =
+                row[(nh + g) * 8 + k];
 }
 
 __global__ void __launch_bounds__(256) k_qk_norm_rope(__half* __restrict__ qkv, int ld, int H, int KVH,
@@ -731,10 +751,9 @@ int d1_qk_norm_rope(d1_half* qkv, int ld, int H, int KVH, const float* qn, const
                     const int* tok_seq, const SeqInfo* seqs, int attn_idx, int rows, float eps, cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
     if (((uintptr_t)qkv & 3) || (ld & 1) || !al16(rope)) return -1;
-    if (al16(qkv) && ld % 8 == 0) {
-        const long groups = (long)rows * (H + 2 * KVH);
-        k_qk_norm_rope8<<<(unsigned)((groups + 31) / 32), 256, 0, st>>>(qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs,
-                                                                       attn_idx, rows, eps);
+    if (al16(qkv) && ld % 8 == 0 && H + KVH <= 4 * kQkMaxPerGroup) {
+        k_qk_norm_rope8<<<nblk(rows, 8), 256, 0, st>>>(qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows,
+                                                       eps);
         return (int)cudaGetLastError();
     }
     k_qk_norm_rope<<<rows, 256, 0, st>>>(qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows, eps);
