@@ -248,29 +248,49 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 }
 
 // ---------------------------------------------------------------------------------------------- tcgen05 form
-// Persistent CTAs (2 per SM) loop over units = (128-query tile, head); the reference's work list holds 64-row
-// tiles, so a unit starts at every item whose first row is a multiple of 128 and the other items are skipped.
-// TMEM per CTA: S = Q.K^T (128 x 64 fp32, columns [0,64)) and the output accumulator O (128 x 64 fp32, [64,128)).
+// Persistent CTAs (one per SM) loop over units = (256-query block, head): the reference's work list holds 64-row
+// tiles, so a unit starts at every item whose first row is a multiple of 256 and the other items are skipped (the
+// list must cover every tile, as the runner's does). A unit is two 128-row query tiles that share each K/V tile;
+// two softmax warpgroups work on them in turn, so the tensor core computes one tile's S and P.V while the other's
+// exponentials run. TMEM (512 columns): S0 = Q0.K^T [0,128), S1 [128,256), O0 [256,320), O1 [320,384).
 // Warps:
-//   0-3  softmax: thread t owns query row t (TMEM lane t): reads its S row, online softmax in the exp2 domain,
-//        writes P (fp16) into shared memory as the A operand of P.V, rescales its O row in TMEM when its running
-//        max rises, and at the end of a unit writes O / l to global memory.
-//   4    loader: Q of each unit into a 2-slot ring, K/V tiles of 64 keys ([ext prefix keys | local keys]) into a
-//        3-stage ring, with cp.async into the 128-byte-swizzled K-major layout (V is the MN-major B operand of
-//        P.V: same bytes). Several copy groups stay in flight; each is signalled when it lands.
-//   5    TMEM allocation and the MMA issuer: S_j = Q.K_j^T (M=128, N=64, K=64), then O += P_j.V_j (M=128, N=64,
-//        K=64); S_{j+1} is issued as soon as the softmax has read S_j, so the tensor core works while it exps.
-// Loads for the next unit are issued while the current one is computed, which hides the copy latency that a
-// one-unit-per-CTA kernel exposes on short sequences.
-constexpr int TQ = 128;                  // query rows per unit
-constexpr int TKV = 64;                  // keys per K/V tile
+//   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 128-key tile it
+//        reads its S row, takes the row max in the exp2 domain, writes P = 2^(s - m) as fp16 into shared memory
+//        (two 64-key blocks, 128-byte swizzle: the A operand of P.V), and accumulates the row sum. O is rescaled
+//        in TMEM only when the row max grows by more than 8 (log2 units); otherwise P is taken against the old
+//        max (P <= 2^8, exact in fp16's range) and the final O / l is unchanged. At the end of a unit it reads O
+//        and writes O / l to global memory.
+//   8    loader: the unit's two Q tiles into a 2-slot ring, K/V tiles of 128 keys ([ext prefix keys | local keys])
+//        into a 3-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V: same
+//        bytes). Copy groups stay in flight and are signalled when they land; the next unit's loads overlap the
+//        current unit's math.
+//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=128, K=64) and
+//        O_w += P_w(j).V_j (M=128, N=64, K=128) for both tiles w, S_w(j+1) issued as soon as warpgroup w has
+//        written P_w(j).
+constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
+constexpr int TQU = 2 * TQ;               // query rows per unit
+constexpr int TKV = 128;                  // keys per K/V tile
 constexpr int T_QSLOTS = 2, T_KVSTAGES = 3;
-constexpr int T_Q_BYTES = TQ * 128;      // 128 rows x 64 dims fp16
-constexpr int T_KV_BYTES = TKV * 128;
-constexpr int T_P_BYTES = TQ * TKV * 2;
-constexpr uint32_t T_TMEM_COLS = 128;
-constexpr int T_NBARS = 2 * T_QSLOTS + 2 * T_KVSTAGES + 6;
-constexpr int T_SMEM = T_QSLOTS * T_Q_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + T_P_BYTES + T_NBARS * 8 + 16;
+constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
+constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
+constexpr int T_PBLK = TQ * 128;          // one 64-key block of P
+constexpr int T_P_BYTES = 2 * T_PBLK;     // P of one query tile
+constexpr uint32_t T_TMEM_COLS = 512;
+constexpr float kLazyRescale = 8.f;
+enum : int {
+    B_QFULL = 0,
+    B_QEMPTY = B_QFULL + T_QSLOTS,
+    B_KVFULL = B_QEMPTY + T_QSLOTS,
+    B_KVEMPTY = B_KVFULL + T_KVSTAGES,
+    B_SFULL = B_KVEMPTY + T_KVSTAGES,
+    B_PFULL = B_SFULL + 2,
+    B_ODONE = B_PFULL + 2,
+    B_OFREE = B_ODONE + 2,
+    B_DRAIN = B_OFREE + 2,
+    T_NBARS = B_DRAIN + 1
+};
+constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_P_BYTES + T_NBARS * 8 + 16;
+static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
 __device__ int g_fa_err = 0;
@@ -314,38 +334,34 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// A unit: work item w (its 64-row query tile must start at a multiple of 128) and head h.
+// A unit: work item w (its 64-row query tile must start at a multiple of 256) and head h.
 struct Unit {
     AttnSeq s;
     int q0, h, nt;
+    bool two;  // the second 128-row tile has queries
 };
 __device__ __forceinline__ bool unit_at(const FaTcArgs& a, int u, Unit& out) {
     const int2 wi = a.work[u / a.heads];
-    if (wi.y % TQ) return false;
+    if (wi.y % TQU) return false;
     out.s = a.seqs[wi.x];
     out.q0 = wi.y;
     out.h = u % a.heads;
     out.nt = (out.s.ext_len + out.s.kv_len + TKV - 1) / TKV;
+    out.two = out.s.q_len > out.q0 + TQ;
     return out.nt > 0 && out.s.q_len > out.q0;  // units with no keys or no queries are skipped by every role
 }
 
-__global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
+__global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* sQ = smem_raw;  // the 128-byte swizzle needs 1024-byte aligned tiles: checked below
-    uint8_t* sKV = sQ + T_QSLOTS * T_Q_BYTES;  // stage s: K at s * 2 * T_KV_BYTES, V right after
-    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + T_P_BYTES);
+    uint8_t* sQ = smem_raw;                                    // slot q: Q0 at q * 2 * T_QT_BYTES, Q1 after it
+    uint8_t* sKV = sQ + T_QSLOTS * 2 * T_QT_BYTES;             // stage s: K at s * 2 * T_KV_BYTES, V after it
+    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // warpgroup w: P at w * T_P_BYTES
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * T_P_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + T_NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    auto q_full = [&](int i) { return smem_u32(bars + i); };
-    auto q_empty = [&](int i) { return smem_u32(bars + T_QSLOTS + i); };
-    auto kv_full = [&](int i) { return smem_u32(bars + 2 * T_QSLOTS + i); };
-    auto kv_empty = [&](int i) { return smem_u32(bars + 2 * T_QSLOTS + T_KVSTAGES + i); };
-    const uint32_t s_full = smem_u32(bars + 2 * T_QSLOTS + 2 * T_KVSTAGES);
-    const uint32_t s_free = s_full + 8, p_full = s_full + 16, o_done = s_full + 24, o_free = s_full + 32;
-    const uint32_t drain = s_full + 40;
+    auto bar = [&](int i) { return smem_u32(bars + i); };
 
     if (smem_u32(smem_raw) & 1023) {  // never expected: dynamic shared memory starts at the window base
         if (threadIdx.x == 0 && a.err) atomicExch(a.err, kErrDrain);
@@ -354,23 +370,24 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < T_QSLOTS; i++) {
-            mbar_init(q_full(i), 32);
-            mbar_init(q_empty(i), 1);
+            mbar_init(bar(B_QFULL + i), 32);
+            mbar_init(bar(B_QEMPTY + i), 1);
         }
         for (int i = 0; i < T_KVSTAGES; i++) {
-            mbar_init(kv_full(i), 32);
-            mbar_init(kv_empty(i), 1);
+            mbar_init(bar(B_KVFULL + i), 32);
+            mbar_init(bar(B_KVEMPTY + i), 1);
         }
-        mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
-        mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
-        mbar_init(o_free, 4);
-        mbar_init(drain, 1);
+        for (int w = 0; w < 2; w++) {
+            mbar_init(bar(B_SFULL + w), 1);
+            mbar_init(bar(B_PFULL + w), 4);
+            mbar_init(bar(B_ODONE + w), 1);
+            mbar_init(bar(B_OFREE + w), 4);
+        }
+        mbar_init(bar(B_DRAIN), 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         tmem_alloc(smem_u32(tmem_slot), T_TMEM_COLS);
         tmem_relinquish();
     }
@@ -379,10 +396,9 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ------------------------------------------------------------------ loader
-        // Copy groups in flight, oldest first: the barrier each one signals when it lands (at most 4).
-        uint32_t pend[4];
+        uint32_t pend[4];  // barriers of the copy groups in flight, oldest first
         int npend = 0;
         auto land_oldest = [&](bool all) {
             if (all)
@@ -395,11 +411,10 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
             for (int i = n; i < npend; i++) pend[i - n] = pend[i];
             npend -= n;
         };
-        // wait for a free slot; never block while a landed copy is still unsignalled
-        auto acquire = [&](uint32_t bar, uint32_t parity) -> bool {
-            if (!__all_sync(D1_FULL_MASK, mbar_try_wait(bar, parity))) {
+        auto acquire = [&](uint32_t b, uint32_t parity) -> bool {  // never block with a landed copy unsignalled
+            if (!__all_sync(D1_FULL_MASK, mbar_try_wait(b, parity))) {
                 if (npend) land_oldest(true);
-                return __all_sync(D1_FULL_MASK, mbar_wait(bar, parity, abort_flag)) != 0;
+                return __all_sync(D1_FULL_MASK, mbar_wait(b, parity, abort_flag)) != 0;
             }
             return true;
         };
@@ -410,22 +425,23 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
             if (!unit_at(a, u, un)) continue;
             const int g = un.h / a.group, total = un.s.ext_len + un.s.kv_len;
             const int qs = qi % T_QSLOTS;
-            if (!(ok = acquire(q_empty(qs), ((qi / T_QSLOTS) & 1) ^ 1))) break;
-            uint8_t* dq = sQ + qs * T_Q_BYTES;
-            for (int c = lane; c < TQ * 8; c += 32) {
-                const int r = c >> 3, ch = c & 7;
+            if (!(ok = acquire(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1))) break;
+            uint8_t* dq = sQ + qs * 2 * T_QT_BYTES;
+            for (int c = lane; c < (un.two ? 2 : 1) * TQ * 8; c += 32) {
+                const int r = c >> 3, ch = c & 7;  // r < 256: tile r / 128, row r % 128
                 const bool v = un.q0 + r < un.s.q_len;
                 const __half* src = v ? a.Q + (size_t)(un.s.q_start + un.q0 + r) * a.ldq + un.h * 64 + ch * 8 : a.Q;
-                cp_async16z(smem_u32(dq + r * 128 + ((ch ^ (r & 7)) << 4)), src, v ? 16 : 0);
+                cp_async16z(smem_u32(dq + (r >> 7) * T_QT_BYTES + (r & 127) * 128 + ((ch ^ (r & 7)) << 4)), src,
+                            v ? 16 : 0);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
-            pend[npend++] = q_full(qs);
+            pend[npend++] = bar(B_QFULL + qs);
             if (npend > 2) land_oldest(false);
             qi++;
             for (int j = 0; j < un.nt; j++) {
-                const int s = ki % T_KVSTAGES;
-                if (!(ok = acquire(kv_empty(s), ((ki / T_KVSTAGES) & 1) ^ 1))) break;
-                uint8_t* dK = sKV + s * 2 * T_KV_BYTES;
+                const int st = ki % T_KVSTAGES;
+                if (!(ok = acquire(bar(B_KVEMPTY + st), ((ki / T_KVSTAGES) & 1) ^ 1))) break;
+                uint8_t* dK = sKV + st * 2 * T_KV_BYTES;
                 uint8_t* dV = dK + T_KV_BYTES;
                 for (int c = lane; c < TKV * 8; c += 32) {
                     const int r = c >> 3, ch = c & 7;
@@ -447,111 +463,127 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
                     cp_async16z(smem_u32(dV + off), srcv, bytes);
                 }
                 asm volatile("cp.async.commit_group;" ::: "memory");
-                pend[npend++] = kv_full(s);
+                pend[npend++] = bar(B_KVFULL + st);
                 if (npend > 2) land_oldest(false);
                 ki++;
             }
         }
         if (npend) land_oldest(true);
         if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t tS = tmem, tO = tmem + TKV;
-            const uint32_t p_addr = smem_u32(sP);
-            int qi = 0, ki = 0, ui = 0;
+            int cnt[2] = {0, 0}, units[2] = {0, 0};  // tiles and units each warpgroup has been given so far
+            int qi = 0, ki = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
                 Unit un;
                 if (!unit_at(a, u, un)) continue;
+                const int nw = un.two ? 2 : 1;
                 const int qs = qi % T_QSLOTS;
-                if (!(ok = mbar_wait(q_full(qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
-                const uint32_t q_addr = smem_u32(sQ + qs * T_Q_BYTES);
-                auto issue_s = [&](int kidx) {  // S = Q . K^T for the tile in ring slot kidx
+                if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
+                const uint32_t q_addr = smem_u32(sQ + qs * 2 * T_QT_BYTES);
+                auto issue_s = [&](int w, int kidx) {  // S_w = Q_w . K^T for the K tile in ring slot kidx
                     const uint32_t k_addr = smem_u32(sKV + (kidx % T_KVSTAGES) * 2 * T_KV_BYTES);
+                    const uint32_t qa = q_addr + w * T_QT_BYTES;
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        tc_mma_f16(tS, smem_desc_k128(q_addr + k * 32), smem_desc_k128(k_addr + k * 32), IDESC_S,
-                                   k != 0);
-                    tc_commit(s_full);
+                        tc_mma_f16(tmem + w * TKV, smem_desc_k128(qa + k * 32), smem_desc_k128(k_addr + k * 32),
+                                   IDESC_S, k != 0);
+                    tc_commit(bar(B_SFULL + w));
                 };
-                // S_0 of this unit: its K tile has landed and the softmax has read the previous S
-                ok = mbar_wait(kv_full(ki % T_KVSTAGES), (ki / T_KVSTAGES) & 1, abort_flag) &&
-                     (ki == 0 || mbar_wait(s_free, (ki - 1) & 1, abort_flag));
-                if (!ok) break;
+                if (!(ok = mbar_wait(bar(B_KVFULL + ki % T_KVSTAGES), (ki / T_KVSTAGES) & 1, abort_flag))) break;
                 tc_fence_after();
-                issue_s(ki);
+                for (int w = 0; w < nw; w++) issue_s(w, ki);  // S buffers are free: P of their last tile is written
                 for (int j = 0; j < un.nt && ok; j++) {
                     const int kj = ki + j;
-                    if (j + 1 < un.nt) {
-                        ok = mbar_wait(kv_full((kj + 1) % T_KVSTAGES), ((kj + 1) / T_KVSTAGES) & 1, abort_flag) &&
-                             mbar_wait(s_free, kj & 1, abort_flag);
-                        if (!ok) break;
+                    bool next_ready = false;
+                    for (int w = 0; w < nw && ok; w++) {
+                        // warpgroup w has read S_w(j) and written P_w(j)
+                        if (!(ok = mbar_wait(bar(B_PFULL + w), cnt[w] & 1, abort_flag))) break;
                         tc_fence_after();
-                        issue_s(kj + 1);
-                    }
-                    ok = mbar_wait(p_full, kj & 1, abort_flag) &&
-                         (j > 0 || ui == 0 || mbar_wait(o_free, (ui - 1) & 1, abort_flag));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sKV + (kj % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
+                        if (j + 1 < un.nt) {
+                            if (!next_ready) {
+                                if (!(ok = mbar_wait(bar(B_KVFULL + (kj + 1) % T_KVSTAGES),
+                                                     ((kj + 1) / T_KVSTAGES) & 1, abort_flag)))
+                                    break;
+                                tc_fence_after();
+                                next_ready = true;
+                            }
+                            issue_s(w, kj + 1);
+                        }
+                        // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
+                        if (j == 0 && units[w] > 0 &&
+                            !(ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag)))
+                            break;
+                        tc_fence_after();
+                        const uint32_t p_addr = smem_u32(sP + w * T_P_BYTES);
+                        const uint32_t v_addr = smem_u32(sKV + (kj % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
 #pragma unroll
-                    for (int k = 0; k < TKV / 16; k++)
-                        tc_mma_f16(tO, smem_desc_k128(p_addr + k * 32), smem_desc_k128(v_addr + k * 2048), IDESC_O,
-                                   (j | k) != 0);
-                    tc_commit(kv_empty(kj % T_KVSTAGES));
-                    tc_commit(o_done);
+                        for (int k = 0; k < TKV / 16; k++)
+                            tc_mma_f16(tmem + 2 * TKV + w * 64,
+                                       smem_desc_k128(p_addr + (k >> 2) * T_PBLK + (k & 3) * 32),
+                                       smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
+                        tc_commit(bar(B_ODONE + w));
+                        cnt[w]++;
+                    }
+                    if (!ok) break;
+                    tc_commit(bar(B_KVEMPTY + kj % T_KVSTAGES));
                 }
                 if (!ok) break;
-                tc_commit(q_empty(qs));
+                tc_commit(bar(B_QEMPTY + qs));
                 ki += un.nt;
                 qi++;
-                ui++;
+                for (int w = 0; w < nw; w++) units[w]++;
             }
             if (!ok) record_err(a.err, abort_flag, kErrWaitFull);
-            tc_commit(drain);  // every issued MMA has completed before TMEM is released
-            if (!mbar_wait_timed2(drain, 0)) record_err(a.err, abort_flag, kErrDrain);
+            tc_commit(bar(B_DRAIN));  // every issued MMA has completed before TMEM is released
+            if (!mbar_wait_timed2(bar(B_DRAIN), 0)) record_err(a.err, abort_flag, kErrDrain);
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------------------------ softmax (warps 0-3, row = thread)
-        const int row = warp * 32 + lane;
-        const uint32_t tS = tmem + ((uint32_t)(warp * 32) << 16), tO = tS + TKV;
-        int ki = 0;
+        // ------------------------------------------------------------------ softmax (warpgroups 0 and 1)
+        const int w = warp >> 2, row = (warp & 3) * 32 + lane;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + w * TKV + lane_off, tO = tmem + 2 * TKV + w * 64 + lane_off;
+        uint8_t* prow = sP + w * T_P_BYTES + row * 128;
+        int cnt = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
             Unit un;
-            if (!unit_at(a, u, un)) continue;
+            if (!unit_at(a, u, un) || (w == 1 && !un.two)) continue;
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
-                const int kj = ki + j;
-                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(s_full, kj & 1, abort_flag)))) break;
+                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + w), cnt & 1, abort_flag)))) break;
                 tc_fence_after();
-                uint32_t sr[TKV];
-#pragma unroll
-                for (int c = 0; c < TKV / 32; c++)
-                    tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
-                tc_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_free);
+                // S stays in TMEM until this warpgroup signals P: read it twice, 32 columns at a time (row max,
+                // then the exponentials) instead of holding 128 values in registers
                 const int kbase = j * TKV;
                 float mx = -INFINITY;
+#pragma unroll 1
+                for (int c = 0; c < TKV / 32; c++) {
+                    uint32_t sr[32];
+                    tmem_ld32(tS + c * 32, sr);
+                    tc_wait_ld();
 #pragma unroll
-                for (int c = 0; c < TKV; c++) {
-                    const float v = kbase + c < total ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
-                    sr[c] = __float_as_uint(v);
-                    mx = fmaxf(mx, v);
+                    for (int i = 0; i < 32; i++)
+                        if (kbase + c * 32 + i < total) mx = fmaxf(mx, __uint_as_float(sr[i]) * a.scale_log2);
                 }
-                const float m_new = fmaxf(m, mx);
-                const float alpha = ex2(m - m_new);
-                // P.V of the previous tile (possibly the previous unit's last) has consumed P and updated O
-                if (kj > 0 && !(ok = __all_sync(D1_FULL_MASK, mbar_wait(o_done, (kj - 1) & 1, abort_flag)))) break;
+                float m_use = m, alpha = 1.f;
+                if (j == 0) {
+                    m_use = mx;
+                } else if (mx > m + kLazyRescale) {
+                    m_use = mx;
+                    alpha = ex2(m - mx);
+                }
+                // P.V of this warpgroup's previous tile has consumed P and updated O
+                if (cnt > 0 && !(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), (cnt - 1) & 1, abort_flag))))
+                    break;
                 tc_fence_after();
                 if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {
                     uint32_t o[32];
-#pragma unroll
+#pragma unroll 1
                     for (int c = 0; c < 2; c++) {
                         tmem_ld32(tO + c * 32, o);
                         tc_wait_ld();
@@ -562,57 +594,63 @@ __global__ void __launch_bounds__(192, 2) k_flash_attn_tc(const FaTcArgs a) {
                     tc_wait_st();
                 }
                 float rs = 0.f;
-                uint8_t* prow = sP + row * 128;
+#pragma unroll 1
+                for (int c = 0; c < TKV / 32; c++) {
+                    uint32_t sr[32];
+                    tmem_ld32(tS + c * 32, sr);
+                    tc_wait_ld();
 #pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    float p[8];
+                    for (int q8 = 0; q8 < 4; q8++) {
+                        const int ch = c * 4 + q8;  // 8-key chunk of the row
+                        float p[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        p[e] = ex2(__uint_as_float(sr[ch * 8 + e]) - m_new);
-                        rs += p[e];
+                        for (int e = 0; e < 8; e++) {
+                            const int i = q8 * 8 + e;
+                            p[e] = kbase + c * 32 + i < total ? ex2(__uint_as_float(sr[i]) * a.scale_log2 - m_use) : 0.f;
+                            rs += p[e];
+                        }
+                        *reinterpret_cast<uint4*>(prow + (ch >> 3) * T_PBLK + (((ch & 7) ^ (row & 7)) << 4)) =
+                            make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]),
+                                       pack_h2(p[6], p[7]));
                     }
-                    *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
-                        make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
                 }
                 fence_async_smem_cta();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(p_full);
+                if (lane == 0) mbar_arrive(bar(B_PFULL + w));
                 l = l * alpha + rs;
-                m = m_new;
+                m = m_use;
+                cnt++;
             }
             if (!ok) break;
-            ki += un.nt;
-            if (un.nt == 0) continue;
-            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(o_done, (ki - 1) & 1, abort_flag)))) break;
+            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), (cnt - 1) & 1, abort_flag)))) break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;
-            const bool store = un.q0 + row < un.s.q_len;
-            __half* orow = a.O + (size_t)(un.s.q_start + un.q0 + row) * a.ldo + un.h * 64;
-            uint32_t o[2][32];
-            tmem_ld32(tO, o[0]);
-            tmem_ld32(tO + 32, o[1]);
-            tc_wait_ld();
+            const int q = un.q0 + w * TQ + row;
+            __half* orow = a.O + (size_t)(un.s.q_start + (q < un.s.q_len ? q : 0)) * a.ldo + un.h * 64;
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {  // O in two 32-column pieces
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32, o);
+                tc_wait_ld();
+                if (q < un.s.q_len)
+#pragma unroll
+                    for (int k8 = 0; k8 < 4; k8++)
+                        *reinterpret_cast<uint4*>(orow + c * 32 + k8 * 8) = make_uint4(
+                            pack_h2(__uint_as_float(o[8 * k8]) * il, __uint_as_float(o[8 * k8 + 1]) * il),
+                            pack_h2(__uint_as_float(o[8 * k8 + 2]) * il, __uint_as_float(o[8 * k8 + 3]) * il),
+                            pack_h2(__uint_as_float(o[8 * k8 + 4]) * il, __uint_as_float(o[8 * k8 + 5]) * il),
+                            pack_h2(__uint_as_float(o[8 * k8 + 6]) * il, __uint_as_float(o[8 * k8 + 7]) * il));
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(o_free);  // the next unit's first P.V may overwrite O
-            if (store) {
-#pragma unroll
-                for (int c = 0; c < 2; c++)
-#pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = make_uint4(
-                            pack_h2(__uint_as_float(o[c][8 * q]) * il, __uint_as_float(o[c][8 * q + 1]) * il),
-                            pack_h2(__uint_as_float(o[c][8 * q + 2]) * il, __uint_as_float(o[c][8 * q + 3]) * il),
-                            pack_h2(__uint_as_float(o[c][8 * q + 4]) * il, __uint_as_float(o[c][8 * q + 5]) * il),
-                            pack_h2(__uint_as_float(o[c][8 * q + 6]) * il, __uint_as_float(o[c][8 * q + 7]) * il));
-            }
+            if (lane == 0) mbar_arrive(bar(B_OFREE + w));  // the next unit's first P.V may overwrite O
         }
         if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitAccFull);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem, T_TMEM_COLS);
     }
@@ -632,8 +670,8 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
     }
     a.n_units = n_work * heads;
     a.heads = heads;
-    const int grid = a.n_units < 2 * sms[dev & 63] ? a.n_units : 2 * sms[dev & 63];
-    k_flash_attn_tc<<<grid, 192, T_SMEM, st>>>(a);
+    const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
+    k_flash_attn_tc<<<grid, 320, T_SMEM, st>>>(a);
     return (int)cudaGetLastError();
 }
 

@@ -103,6 +103,51 @@ def test_edge_lengths_mha_bias(pkg, gpu_lib, ref_lib, lens):
     assert np.abs(got - ref_k).max() <= 4e-3
 
 
+@pytest.mark.parametrize("group", [1, 2])
+@pytest.mark.parametrize("lens", [[1], [63, 64, 65], [127, 128, 129, 255, 256, 257], [300, 1, 513, 2]])
+def test_tc_edge_lengths(pkg, gpu_lib, lens, group):
+    """d1_flash_attn_tc on ragged lengths around its 128-row tiles and 256-row units (units whose second tile is
+    empty, single-tile units, partial key tiles), MHA and GQA, against the oracle and the mma.sync kernel."""
+    rng = np.random.default_rng(sum(lens) + group)
+    T = sum(lens)
+    ld = 1024 + 2 * 1024 // group
+    qkv = rng.standard_normal((T, ld)).astype(np.float16)
+    spans, s = [], 0
+    for n in lens:
+        spans.append((s, n, s, n))
+        s += n
+    d = torch.from_numpy(qkv).cuda()
+    kvw = 1024 // group
+    K, V = d[:, 1024:], d[:, 1024 + kvw:]
+    got_tc = run(gpu_lib, pkg, d, ld, K, V, ld, spans, 16, group, tc=True)
+    got = run(gpu_lib, pkg, d, ld, K, V, ld, spans, 16, group)
+    q = qkv.astype(np.float32)
+    want = O.attention(q[:, :1024], q[:, 1024:1024 + kvw], q[:, 1024 + kvw:], spans, 16, group, 0.125)
+    assert np.abs(got_tc - want).max() <= 4e-3
+    assert np.abs(got_tc - got).max() <= 4e-3
+
+
+def test_tc_marker_queries(pkg, gpu_lib):
+    """d1_flash_attn_tc with fewer query rows than keys (gathered marker rows, the last head layer's form)."""
+    rng = np.random.default_rng(12)
+    lens, marks = [700, 40, 300], [list(range(0, 700, 3)), [0, 39], [1, 2, 150, 299]]
+    T = sum(lens)
+    qkv = rng.standard_normal((T, 3072)).astype(np.float16)
+    rows, seqs, s, ms = [], [], 0, 0
+    for n, mk in zip(lens, marks):
+        rows += [s + m for m in mk]
+        seqs.append((ms, len(mk), s, n))
+        s += n
+        ms += len(mk)
+    mq = qkv[rows]
+    d = torch.from_numpy(qkv).cuda()
+    dq = torch.from_numpy(np.ascontiguousarray(mq)).cuda()
+    got = run(gpu_lib, pkg, dq, 3072, d[:, 1024:], d[:, 2048:], 3072, seqs, 16, 1, tc=True)
+    q = qkv.astype(np.float32)
+    want = O.attention(mq.astype(np.float32)[:, :1024], q[:, 1024:2048], q[:, 2048:], seqs, 16, 1, 0.125)
+    assert np.abs(got - want).max() <= 4e-3
+
+
 def test_marker_queries(pkg, gpu_lib, ref_lib):
     """Last head layer: queries are gathered marker rows (q_start indexes the gathered buffer), keys cover every
     row of the sequence (src/model.rs:534-539)."""
