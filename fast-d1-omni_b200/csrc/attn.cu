@@ -250,31 +250,33 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // ---------------------------------------------------------------------------------------------- tcgen05 form
 // Persistent CTAs (one per SM) loop over units = (256-query block, head): the reference's work list holds 64-row
 // tiles, so a unit starts at every item whose first row is a multiple of 256 and the other items are skipped (the
-// list must cover every tile, as the runner's does). A unit is two 128-row query tiles that share each K/V tile;
-// two softmax warpgroups work on them in turn, so the tensor core computes one tile's S and P.V while the other's
-// exponentials run. TMEM (512 columns): S0 = Q0.K^T [0,128), S1 [128,256), O0 [256,320), O1 [320,384).
+// list must cover every tile, as the runner's does). A unit is two 128-row query tiles that share each K/V tile,
+// one per softmax warpgroup.
+//
+// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM and
+// two P buffers in shared memory, so S(j+2) is issued as soon as P(j) is written and the softmax never waits for
+// the tensor core; its only other wait is for the P.V that last read the P buffer it is about to refill (two tiles
+// back). Every handoff has its own barrier per buffer, so no wait can confuse two phases of one barrier.
+// TMEM (512 columns): S[w][b] at (2w + b) * 64, O[w] at 256 + 64w.
 // Warps:
-//   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 128-key tile it
-//        reads its S row, takes the row max in the exp2 domain, writes P = 2^(s - m) as fp16 into shared memory
-//        (two 64-key blocks, 128-byte swizzle: the A operand of P.V), and accumulates the row sum. O is rescaled
-//        in TMEM only when the row max grows by more than 8 (log2 units); otherwise P is taken against the old
-//        max (P <= 2^8, exact in fp16's range) and the final O / l is unchanged. At the end of a unit it reads O
-//        and writes O / l to global memory.
-//   8    loader: the unit's two Q tiles into a 2-slot ring, K/V tiles of 128 keys ([ext prefix keys | local keys])
-//        into a 3-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V: same
-//        bytes). Copy groups stay in flight and are signalled when they land; the next unit's loads overlap the
-//        current unit's math.
-//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=128, K=64) and
-//        O_w += P_w(j).V_j (M=128, N=64, K=128) for both tiles w, S_w(j+1) issued as soon as warpgroup w has
-//        written P_w(j).
+//   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
+//        reads its S row (one TMEM round trip), takes the row max in the exp2 domain, writes P = 2^(s - m) as fp16
+//        (128-byte swizzle: the A operand of P.V) and accumulates the row sum. O is rescaled in TMEM only when the
+//        row max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well
+//        inside fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory.
+//   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring, K/V tiles of 64 keys ([ext prefix keys | local
+//        keys]) into a 4-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V:
+//        same bytes); each lane's copies complete the slot's barrier when they land (cp.async.mbarrier.arrive), and
+//        the next unit's loads overlap the current unit's math.
+//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64) and
+//        O_w += P_w(j).V_j (M=128, N=64, K=64).
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
-constexpr int TKV = 128;                  // keys per K/V tile
-constexpr int T_QSLOTS = 2, T_KVSTAGES = 3;
+constexpr int TKV = 64;                   // keys per K/V tile
+constexpr int T_QSLOTS = 2, T_KVSTAGES = 4;
 constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
-constexpr int T_PBLK = TQ * 128;          // one 64-key block of P
-constexpr int T_P_BYTES = 2 * T_PBLK;     // P of one query tile
+constexpr int T_P_BYTES = TQ * 128;       // P of one query tile and K/V tile (64 keys: one swizzle block)
 constexpr uint32_t T_TMEM_COLS = 512;
 constexpr float kLazyRescale = 8.f;
 enum : int {
@@ -282,14 +284,14 @@ enum : int {
     B_QEMPTY = B_QFULL + T_QSLOTS,
     B_KVFULL = B_QEMPTY + T_QSLOTS,
     B_KVEMPTY = B_KVFULL + T_KVSTAGES,
-    B_SFULL = B_KVEMPTY + T_KVSTAGES,
-    B_PFULL = B_SFULL + 2,
-    B_ODONE = B_PFULL + 2,
-    B_OFREE = B_ODONE + 2,
+    B_SFULL = B_KVEMPTY + T_KVSTAGES,  // [w][b]
+    B_PFULL = B_SFULL + 4,             // [w][b]
+    B_ODONE = B_PFULL + 4,             // [w][b]: the P.V that read P[w][b]
+    B_OFREE = B_ODONE + 4,             // [w]
     B_DRAIN = B_OFREE + 2,
     T_NBARS = B_DRAIN + 1
 };
-constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_P_BYTES + T_NBARS * 8 + 16;
+constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 4 * T_P_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
@@ -351,14 +353,17 @@ __device__ __forceinline__ bool unit_at(const FaTcArgs& a, int u, Unit& out) {
     return out.nt > 0 && out.s.q_len > out.q0;  // units with no keys or no queries are skipped by every role
 }
 
-__global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
+constexpr int T_LOADERS = 3;             // loader warps (8, 10, 11): K/V copy issue is instruction-bound
+constexpr int T_THREADS = 384;
+
+__global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sQ = smem_raw;                                    // slot q: Q0 at q * 2 * T_QT_BYTES, Q1 after it
     uint8_t* sKV = sQ + T_QSLOTS * 2 * T_QT_BYTES;             // stage s: K at s * 2 * T_KV_BYTES, V after it
-    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // warpgroup w: P at w * T_P_BYTES
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * T_P_BYTES);
+    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // P[w][b] at (2w + b) * T_P_BYTES
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * T_P_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + T_NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     auto bar = [&](int i) { return smem_u32(bars + i); };
@@ -370,19 +375,20 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < T_QSLOTS; i++) {
-            mbar_init(bar(B_QFULL + i), 32);
+            mbar_init(bar(B_QFULL + i), 32 * T_LOADERS);
             mbar_init(bar(B_QEMPTY + i), 1);
         }
         for (int i = 0; i < T_KVSTAGES; i++) {
-            mbar_init(bar(B_KVFULL + i), 32);
+            mbar_init(bar(B_KVFULL + i), 32 * T_LOADERS);
             mbar_init(bar(B_KVEMPTY + i), 1);
         }
-        for (int w = 0; w < 2; w++) {
-            mbar_init(bar(B_SFULL + w), 1);
-            mbar_init(bar(B_PFULL + w), 4);
-            mbar_init(bar(B_ODONE + w), 1);
-            mbar_init(bar(B_OFREE + w), 4);
+        for (int i = 0; i < 4; i++) {
+            mbar_init(bar(B_SFULL + i), 1);
+            mbar_init(bar(B_PFULL + i), 4);
+            mbar_init(bar(B_ODONE + i), 1);
         }
+        mbar_init(bar(B_OFREE + 0), 4);
+        mbar_init(bar(B_OFREE + 1), 4);
         mbar_init(bar(B_DRAIN), 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -396,27 +402,14 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 8) {
-        // ------------------------------------------------------------------ loader
-        uint32_t pend[4];  // barriers of the copy groups in flight, oldest first
-        int npend = 0;
-        auto land_oldest = [&](bool all) {
-            if (all)
-                asm volatile("cp.async.wait_group 0;" ::: "memory");
-            else
-                asm volatile("cp.async.wait_group 1;" ::: "memory");
-            fence_async_smem_cta();
-            const int n = all ? npend : npend - 1;
-            for (int i = 0; i < n; i++) mbar_arrive(pend[i]);
-            for (int i = n; i < npend; i++) pend[i - n] = pend[i];
-            npend -= n;
-        };
-        auto acquire = [&](uint32_t b, uint32_t parity) -> bool {  // never block with a landed copy unsignalled
-            if (!__all_sync(D1_FULL_MASK, mbar_try_wait(b, parity))) {
-                if (npend) land_oldest(true);
-                return __all_sync(D1_FULL_MASK, mbar_wait(b, parity, abort_flag)) != 0;
-            }
-            return true;
+    if (warp == 8 || warp >= 10) {
+        // ------------------------------------------------------------------ loaders (warps 8, 10, 11)
+        const int lt = (warp == 8 ? 0 : warp - 9) * 32 + lane;  // loader thread 0 .. 32 * T_LOADERS - 1
+        // Each lane's copies complete the stage's barrier by themselves (cp.async.mbarrier.arrive.noinc: the
+        // barrier counts the lane once all of its earlier cp.async have landed), so the loader only ever waits for
+        // free slots.
+        auto landed_arrive = [&](uint32_t b) {
+            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(b) : "memory");
         };
         int qi = 0, ki = 0;
         bool ok = true;
@@ -425,25 +418,26 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
             if (!unit_at(a, u, un)) continue;
             const int g = un.h / a.group, total = un.s.ext_len + un.s.kv_len;
             const int qs = qi % T_QSLOTS;
-            if (!(ok = acquire(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1))) break;
+            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1, abort_flag))))
+                break;
             uint8_t* dq = sQ + qs * 2 * T_QT_BYTES;
-            for (int c = lane; c < (un.two ? 2 : 1) * TQ * 8; c += 32) {
+            for (int c = lt; c < (un.two ? 2 : 1) * TQ * 8; c += 32 * T_LOADERS) {
                 const int r = c >> 3, ch = c & 7;  // r < 256: tile r / 128, row r % 128
                 const bool v = un.q0 + r < un.s.q_len;
                 const __half* src = v ? a.Q + (size_t)(un.s.q_start + un.q0 + r) * a.ldq + un.h * 64 + ch * 8 : a.Q;
                 cp_async16z(smem_u32(dq + (r >> 7) * T_QT_BYTES + (r & 127) * 128 + ((ch ^ (r & 7)) << 4)), src,
                             v ? 16 : 0);
             }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-            pend[npend++] = bar(B_QFULL + qs);
-            if (npend > 2) land_oldest(false);
+            landed_arrive(bar(B_QFULL + qs));
             qi++;
             for (int j = 0; j < un.nt; j++) {
                 const int st = ki % T_KVSTAGES;
-                if (!(ok = acquire(bar(B_KVEMPTY + st), ((ki / T_KVSTAGES) & 1) ^ 1))) break;
+                if (!(ok = __all_sync(D1_FULL_MASK,
+                                      mbar_wait(bar(B_KVEMPTY + st), ((ki / T_KVSTAGES) & 1) ^ 1, abort_flag))))
+                    break;
                 uint8_t* dK = sKV + st * 2 * T_KV_BYTES;
                 uint8_t* dV = dK + T_KV_BYTES;
-                for (int c = lane; c < TKV * 8; c += 32) {
+                for (int c = lt; c < TKV * 8; c += 32 * T_LOADERS) {
                     const int r = c >> 3, ch = c & 7;
                     const int key = j * TKV + r;
                     const __half *srck = a.K, *srcv = a.V;
@@ -462,18 +456,16 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
                     cp_async16z(smem_u32(dK + off), srck, bytes);
                     cp_async16z(smem_u32(dV + off), srcv, bytes);
                 }
-                asm volatile("cp.async.commit_group;" ::: "memory");
-                pend[npend++] = bar(B_KVFULL + st);
-                if (npend > 2) land_oldest(false);
+                landed_arrive(bar(B_KVFULL + st));
                 ki++;
             }
         }
-        if (npend) land_oldest(true);
+        asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight when the CTA exits
         if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
     } else if (warp == 9) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            int cnt[2] = {0, 0}, units[2] = {0, 0};  // tiles and units each warpgroup has been given so far
+            int cnt[2] = {0, 0}, units[2] = {0, 0};  // tiles and units given to each warpgroup so far
             int qi = 0, ki = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
@@ -483,58 +475,68 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
                 const int qs = qi % T_QSLOTS;
                 if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
                 const uint32_t q_addr = smem_u32(sQ + qs * 2 * T_QT_BYTES);
-                auto issue_s = [&](int w, int kidx) {  // S_w = Q_w . K^T for the K tile in ring slot kidx
-                    const uint32_t k_addr = smem_u32(sKV + (kidx % T_KVSTAGES) * 2 * T_KV_BYTES);
+                // S_w for tile j of this unit (global tile index c = cnt[w] + j) into buffer c % 2, once the
+                // softmax has written P(c - 2) (it has read S(c - 2) from that buffer)
+                auto issue_s = [&](int w, int j) -> bool {
+                    const int c = cnt[w] + j, b = c & 1;
+                    if (c >= 2 && !mbar_wait(bar(B_PFULL + 2 * w + b), ((c - 2) >> 1) & 1, abort_flag)) return false;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES);
                     const uint32_t qa = q_addr + w * T_QT_BYTES;
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        tc_mma_f16(tmem + w * TKV, smem_desc_k128(qa + k * 32), smem_desc_k128(k_addr + k * 32),
+                        tc_mma_f16(tmem + (2 * w + b) * TKV, smem_desc_k128(qa + k * 32), smem_desc_k128(k_addr + k * 32),
                                    IDESC_S, k != 0);
-                    tc_commit(bar(B_SFULL + w));
+                    tc_commit(bar(B_SFULL + 2 * w + b));
+                    return true;
                 };
-                if (!(ok = mbar_wait(bar(B_KVFULL + ki % T_KVSTAGES), (ki / T_KVSTAGES) & 1, abort_flag))) break;
-                tc_fence_after();
-                for (int w = 0; w < nw; w++) issue_s(w, ki);  // S buffers are free: P of their last tile is written
+                auto kv_ready = [&](int j) {
+                    return mbar_wait(bar(B_KVFULL + (ki + j) % T_KVSTAGES), ((ki + j) / T_KVSTAGES) & 1, abort_flag);
+                };
+                for (int j = 0; j < 2 && j < un.nt && ok; j++) {  // prologue: S for tiles 0 and 1
+                    if (!(ok = kv_ready(j))) break;
+                    tc_fence_after();
+                    for (int w = 0; w < nw && ok; w++) ok = issue_s(w, j);
+                }
                 for (int j = 0; j < un.nt && ok; j++) {
-                    const int kj = ki + j;
-                    bool next_ready = false;
+                    bool k2_ready = false;
                     for (int w = 0; w < nw && ok; w++) {
-                        // warpgroup w has read S_w(j) and written P_w(j)
-                        if (!(ok = mbar_wait(bar(B_PFULL + w), cnt[w] & 1, abort_flag))) break;
+                        const int c = cnt[w] + j, b = c & 1;
+                        // P_w(j) written (so S_w(j) has been read)
+                        if (!(ok = mbar_wait(bar(B_PFULL + 2 * w + b), (c >> 1) & 1, abort_flag))) break;
                         tc_fence_after();
-                        if (j + 1 < un.nt) {
-                            if (!next_ready) {
-                                if (!(ok = mbar_wait(bar(B_KVFULL + (kj + 1) % T_KVSTAGES),
-                                                     ((kj + 1) / T_KVSTAGES) & 1, abort_flag)))
-                                    break;
-                                tc_fence_after();
-                                next_ready = true;
-                            }
-                            issue_s(w, kj + 1);
-                        }
                         // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
                         if (j == 0 && units[w] > 0 &&
                             !(ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag)))
                             break;
                         tc_fence_after();
-                        const uint32_t p_addr = smem_u32(sP + w * T_P_BYTES);
-                        const uint32_t v_addr = smem_u32(sKV + (kj % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
+                        const uint32_t p_addr = smem_u32(sP + (2 * w + b) * T_P_BYTES);
+                        const uint32_t v_addr = smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
 #pragma unroll
                         for (int k = 0; k < TKV / 16; k++)
-                            tc_mma_f16(tmem + 2 * TKV + w * 64,
-                                       smem_desc_k128(p_addr + (k >> 2) * T_PBLK + (k & 3) * 32),
+                            tc_mma_f16(tmem + 4 * TKV + w * 64, smem_desc_k128(p_addr + k * 32),
                                        smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                        tc_commit(bar(B_ODONE + w));
-                        cnt[w]++;
+                        tc_commit(bar(B_ODONE + 2 * w + b));
+                        if (j + 2 < un.nt) {  // S two tiles ahead, into the buffer P(j) just released
+                            if (!k2_ready) {
+                                if (!(ok = kv_ready(j + 2))) break;
+                                tc_fence_after();
+                                k2_ready = true;
+                            }
+                            if (!(ok = issue_s(w, j + 2))) break;
+                        }
                     }
                     if (!ok) break;
-                    tc_commit(bar(B_KVEMPTY + kj % T_KVSTAGES));
+                    tc_commit(bar(B_KVEMPTY + (ki + j) % T_KVSTAGES));
                 }
                 if (!ok) break;
                 tc_commit(bar(B_QEMPTY + qs));
                 ki += un.nt;
                 qi++;
-                for (int w = 0; w < nw; w++) units[w]++;
+                for (int w = 0; w < nw; w++) {
+                    cnt[w] += un.nt;
+                    units[w]++;
+                }
             }
             if (!ok) record_err(a.err, abort_flag, kErrWaitFull);
             tc_commit(bar(B_DRAIN));  // every issued MMA has completed before TMEM is released
@@ -545,8 +547,7 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
         // ------------------------------------------------------------------ softmax (warpgroups 0 and 1)
         const int w = warp >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + w * TKV + lane_off, tO = tmem + 2 * TKV + w * 64 + lane_off;
-        uint8_t* prow = sP + w * T_P_BYTES + row * 128;
+        const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
         int cnt = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
@@ -555,20 +556,22 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
-                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + w), cnt & 1, abort_flag)))) break;
+                const int c = cnt + j, b = c & 1;
+                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + 2 * w + b), (c >> 1) & 1, abort_flag))))
+                    break;
                 tc_fence_after();
-                // S stays in TMEM until this warpgroup signals P: read it twice, 32 columns at a time (row max,
-                // then the exponentials) instead of holding 128 values in registers
+                uint32_t sr[TKV];
+                const uint32_t tS = tmem + (2 * w + b) * TKV + lane_off;
+                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                tc_wait_ld();
                 const int kbase = j * TKV;
                 float mx = -INFINITY;
-#pragma unroll 1
-                for (int c = 0; c < TKV / 32; c++) {
-                    uint32_t sr[32];
-                    tmem_ld32(tS + c * 32, sr);
-                    tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (kbase + c * 32 + i < total) mx = fmaxf(mx, __uint_as_float(sr[i]) * a.scale_log2);
+                for (int i = 0; i < TKV; i++) {
+                    const float v = kbase + i < total ? __uint_as_float(sr[i]) * a.scale_log2 : -INFINITY;
+                    sr[i] = __float_as_uint(v);
+                    mx = fmaxf(mx, v);
                 }
                 float m_use = m, alpha = 1.f;
                 if (j == 0) {
@@ -577,66 +580,65 @@ __global__ void __launch_bounds__(320, 1) k_flash_attn_tc(const FaTcArgs a) {
                     m_use = mx;
                     alpha = ex2(m - mx);
                 }
-                // P.V of this warpgroup's previous tile has consumed P and updated O
-                if (cnt > 0 && !(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), (cnt - 1) & 1, abort_flag))))
+                // the P.V that last read this P buffer (tile c - 2) is done
+                if (c >= 2 &&
+                    !(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + b), ((c - 2) >> 1) & 1, abort_flag))))
                     break;
-                tc_fence_after();
-                if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {
-                    uint32_t o[32];
+                if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {  // rare: O must hold P.V up to tile c - 1
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + (b ^ 1)), ((c - 1) >> 1) & 1,
+                                                                  abort_flag))))
+                        break;
+                    tc_fence_after();
 #pragma unroll 1
-                    for (int c = 0; c < 2; c++) {
-                        tmem_ld32(tO + c * 32, o);
+                    for (int q = 0; q < 8; q++) {
+                        uint32_t o[8];
+                        tmem_ld8(tO + q * 8, o);
                         tc_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        tmem_st32(tO + c * 32, o);
+                        for (int i = 0; i < 8; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st8(tO + q * 8, o);
                     }
                     tc_wait_st();
                 }
                 float rs = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < TKV / 32; c++) {
-                    uint32_t sr[32];
-                    tmem_ld32(tS + c * 32, sr);
-                    tc_wait_ld();
+                uint8_t* prow = sP + (2 * w + b) * T_P_BYTES + row * 128;
 #pragma unroll
-                    for (int q8 = 0; q8 < 4; q8++) {
-                        const int ch = c * 4 + q8;  // 8-key chunk of the row
-                        float p[8];
+                for (int ch = 0; ch < TKV / 8; ch++) {
+                    float p[8];
 #pragma unroll
-                        for (int e = 0; e < 8; e++) {
-                            const int i = q8 * 8 + e;
-                            p[e] = kbase + c * 32 + i < total ? ex2(__uint_as_float(sr[i]) * a.scale_log2 - m_use) : 0.f;
-                            rs += p[e];
-                        }
-                        *reinterpret_cast<uint4*>(prow + (ch >> 3) * T_PBLK + (((ch & 7) ^ (row & 7)) << 4)) =
-                            make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]),
-                                       pack_h2(p[6], p[7]));
+                    for (int e = 0; e < 8; e++) {
+                        p[e] = ex2(__uint_as_float(sr[ch * 8 + e]) - m_use);
+                        rs += p[e];
                     }
+                    *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
+                        make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
                 }
                 fence_async_smem_cta();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(B_PFULL + w));
+                if (lane == 0) mbar_arrive(bar(B_PFULL + 2 * w + b));
                 l = l * alpha + rs;
                 m = m_use;
-                cnt++;
             }
             if (!ok) break;
-            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), (cnt - 1) & 1, abort_flag)))) break;
+            cnt += un.nt;
+            // the unit's last P.V (the earlier ones completed before it)
+            const int cl = cnt - 1;
+            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + (cl & 1)), (cl >> 1) & 1, abort_flag))))
+                break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;
             const int q = un.q0 + w * TQ + row;
             __half* orow = a.O + (size_t)(un.s.q_start + (q < un.s.q_len ? q : 0)) * a.ldo + un.h * 64;
 #pragma unroll 1
-            for (int c = 0; c < 2; c++) {  // O in two 32-column pieces
+            for (int c2 = 0; c2 < 2; c2++) {  // O in two 32-column pieces
                 uint32_t o[32];
-                tmem_ld32(tO + c * 32, o);
+                tmem_ld32(tO + c2 * 32, o);
                 tc_wait_ld();
                 if (q < un.s.q_len)
 #pragma unroll
                     for (int k8 = 0; k8 < 4; k8++)
-                        *reinterpret_cast<uint4*>(orow + c * 32 + k8 * 8) = make_uint4(
+                        *reinterpret_cast<uint4*>(orow + c2 * 32 + k8 * 8) = make_uint4(
                             pack_h2(__uint_as_float(o[8 * k8]) * il, __uint_as_float(o[8 * k8 + 1]) * il),
                             pack_h2(__uint_as_float(o[8 * k8 + 2]) * il, __uint_as_float(o[8 * k8 + 3]) * il),
                             pack_h2(__uint_as_float(o[8 * k8 + 4]) * il, __uint_as_float(o[8 * k8 + 5]) * il),
@@ -671,7 +673,7 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
     a.n_units = n_work * heads;
     a.heads = heads;
     const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
-    k_flash_attn_tc<<<grid, 320, T_SMEM, st>>>(a);
+    k_flash_attn_tc<<<grid, T_THREADS, T_SMEM, st>>>(a);
     return (int)cudaGetLastError();
 }
 
