@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 //        row max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well
 //        inside fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory.
 //   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring, K/V tiles of 64 keys ([ext prefix keys | local
-//        keys]) into a 4-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V:
+//        keys]) into a 6-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V:
 //        same bytes); each lane's copies complete the slot's barrier when they land (cp.async.mbarrier.arrive), and
 //        the next unit's loads overlap the current unit's math.
 //   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64) and
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
-constexpr int T_QSLOTS = 2, T_KVSTAGES = 4;
+constexpr int T_QSLOTS = 2, T_KVSTAGES = 6;
 constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
 constexpr int T_P_BYTES = TQ * 128;       // P of one query tile and K/V tile (64 keys: one swizzle block)
@@ -475,58 +475,67 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
                 const int qs = qi % T_QSLOTS;
                 if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
                 const uint32_t q_addr = smem_u32(sQ + qs * 2 * T_QT_BYTES);
-                // S_w for tile j of this unit (global tile index c = cnt[w] + j) into buffer c % 2, once the
-                // softmax has written P(c - 2) (it has read S(c - 2) from that buffer)
-                auto issue_s = [&](int w, int j) -> bool {
-                    const int c = cnt[w] + j, b = c & 1;
-                    if (c >= 2 && !mbar_wait(bar(B_PFULL + 2 * w + b), ((c - 2) >> 1) & 1, abort_flag)) return false;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES);
-                    const uint32_t qa = q_addr + w * T_QT_BYTES;
-#pragma unroll
-                    for (int k = 0; k < 4; k++)
-                        tc_mma_f16(tmem + (2 * w + b) * TKV, smem_desc_k128(qa + k * 32), smem_desc_k128(k_addr + k * 32),
-                                   IDESC_S, k != 0);
-                    tc_commit(bar(B_SFULL + 2 * w + b));
-                    return true;
-                };
+                // One step's MMAs are issued k-slice by k-slice across the independent accumulators (both
+                // warpgroups' P.V and S), so the tensor pipe overlaps their dependent chains.
+                auto k_addr = [&](int j) { return smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES); };
                 auto kv_ready = [&](int j) {
                     return mbar_wait(bar(B_KVFULL + (ki + j) % T_KVSTAGES), ((ki + j) / T_KVSTAGES) & 1, abort_flag);
                 };
+                // S_w(j) goes to buffer (cnt[w] + j) % 2, which P(cnt[w] + j - 2) has released (its softmax read it)
+                auto s_buffer_free = [&](int w, int j) {
+                    const int c = cnt[w] + j;
+                    return c < 2 || mbar_wait(bar(B_PFULL + 2 * w + (c & 1)), ((c - 2) >> 1) & 1, abort_flag);
+                };
+                auto issue_s_pair = [&](int j) {  // S_w(j) for every active warpgroup, interleaved
+                    const uint32_t ka = k_addr(j);
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        for (int w = 0; w < nw; w++)
+                            tc_mma_f16(tmem + (2 * w + ((cnt[w] + j) & 1)) * TKV,
+                                       smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32), smem_desc_k128(ka + k * 32),
+                                       IDESC_S, k != 0);
+                    for (int w = 0; w < nw; w++) tc_commit(bar(B_SFULL + 2 * w + ((cnt[w] + j) & 1)));
+                };
                 for (int j = 0; j < 2 && j < un.nt && ok; j++) {  // prologue: S for tiles 0 and 1
                     if (!(ok = kv_ready(j))) break;
+                    for (int w = 0; w < nw && ok; w++) ok = s_buffer_free(w, j);
+                    if (!ok) break;
                     tc_fence_after();
-                    for (int w = 0; w < nw && ok; w++) ok = issue_s(w, j);
+                    issue_s_pair(j);
                 }
                 for (int j = 0; j < un.nt && ok; j++) {
-                    bool k2_ready = false;
+                    // P_w(j) written for every active warpgroup (so S_w(j) has been read and its buffer is free)
                     for (int w = 0; w < nw && ok; w++) {
-                        const int c = cnt[w] + j, b = c & 1;
-                        // P_w(j) written (so S_w(j) has been read)
-                        if (!(ok = mbar_wait(bar(B_PFULL + 2 * w + b), (c >> 1) & 1, abort_flag))) break;
-                        tc_fence_after();
+                        const int c = cnt[w] + j;
+                        ok = mbar_wait(bar(B_PFULL + 2 * w + (c & 1)), (c >> 1) & 1, abort_flag);
                         // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
-                        if (j == 0 && units[w] > 0 &&
-                            !(ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag)))
-                            break;
-                        tc_fence_after();
-                        const uint32_t p_addr = smem_u32(sP + (2 * w + b) * T_P_BYTES);
-                        const uint32_t v_addr = smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES + T_KV_BYTES);
-#pragma unroll
-                        for (int k = 0; k < TKV / 16; k++)
-                            tc_mma_f16(tmem + 4 * TKV + w * 64, smem_desc_k128(p_addr + k * 32),
-                                       smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                        tc_commit(bar(B_ODONE + 2 * w + b));
-                        if (j + 2 < un.nt) {  // S two tiles ahead, into the buffer P(j) just released
-                            if (!k2_ready) {
-                                if (!(ok = kv_ready(j + 2))) break;
-                                tc_fence_after();
-                                k2_ready = true;
-                            }
-                            if (!(ok = issue_s(w, j + 2))) break;
-                        }
+                        if (ok && j == 0 && units[w] > 0) ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag);
                     }
+                    const bool ahead = j + 2 < un.nt;
+                    if (ok && ahead) ok = kv_ready(j + 2);
                     if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = k_addr(j) + T_KV_BYTES;
+                    const uint32_t ka2 = ahead ? k_addr(j + 2) : 0;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        for (int w = 0; w < nw; w++) {
+                            const int c = cnt[w] + j;
+                            tc_mma_f16(tmem + 4 * TKV + w * 64,
+                                       smem_desc_k128(smem_u32(sP + (2 * w + (c & 1)) * T_P_BYTES) + k * 32),
+                                       smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
+                        }
+                        if (ahead)
+                            for (int w = 0; w < nw; w++)
+                                tc_mma_f16(tmem + (2 * w + ((cnt[w] + j) & 1)) * TKV,
+                                           smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32), smem_desc_k128(ka2 + k * 32),
+                                           IDESC_S, k != 0);
+                    }
+                    for (int w = 0; w < nw; w++) {
+                        const int c = cnt[w] + j;
+                        tc_commit(bar(B_ODONE + 2 * w + (c & 1)));
+                        if (ahead) tc_commit(bar(B_SFULL + 2 * w + (c & 1)));  // S(j+2) shares buffer c % 2
+                    }
                     tc_commit(bar(B_KVEMPTY + (ki + j) % T_KVSTAGES));
                 }
                 if (!ok) break;
@@ -566,13 +575,26 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
                 tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                 tc_wait_ld();
                 const int kbase = j * TKV;
-                float mx = -INFINITY;
+                // eight independent partial maxima (short dependency chains); keys past the sequence only in its
+                // last tile
+                float mx8[8];
 #pragma unroll
-                for (int i = 0; i < TKV; i++) {
-                    const float v = kbase + i < total ? __uint_as_float(sr[i]) * a.scale_log2 : -INFINITY;
-                    sr[i] = __float_as_uint(v);
-                    mx = fmaxf(mx, v);
+                for (int i = 0; i < 8; i++) mx8[i] = -INFINITY;
+                // the max of the raw scores (the scale is positive), scaled once; the exponent below folds the
+                // scale in: P = 2^(s * scale - m)
+                if (kbase + TKV <= total) {
+#pragma unroll
+                    for (int i = 0; i < TKV; i++) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < TKV; i++) {
+                        if (kbase + i >= total) sr[i] = __float_as_uint(-INFINITY);
+                        mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+                    }
                 }
+                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                                 a.scale_log2;
                 float m_use = m, alpha = 1.f;
                 if (j == 0) {
                     m_use = mx;
@@ -600,15 +622,17 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
                     }
                     tc_wait_st();
                 }
-                float rs = 0.f;
+                float rs8[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) rs8[e] = 0.f;
                 uint8_t* prow = sP + (2 * w + b) * T_P_BYTES + row * 128;
 #pragma unroll
                 for (int ch = 0; ch < TKV / 8; ch++) {
                     float p[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
-                        p[e] = ex2(__uint_as_float(sr[ch * 8 + e]) - m_use);
-                        rs += p[e];
+                        p[e] = ex2(fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use));
+                        rs8[e] += p[e];
                     }
                     *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
                         make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
@@ -617,6 +641,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(B_PFULL + 2 * w + b));
+                const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
                 l = l * alpha + rs;
                 m = m_use;
             }
