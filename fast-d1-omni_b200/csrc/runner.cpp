@@ -67,7 +67,20 @@ struct Kt {
                        cudaStream_t) = nullptr;
     int (*gemm_bias_act)(void*, int, int, int, const d1_half*, int, const d1_half*, int, const float*, int, d1_half*,
                          int, cudaStream_t) = nullptr;
+    int (*flash_attn_tc)(const d1_half*, int, const d1_half*, const d1_half*, int, int, d1_half*, int, const AttnSeq*,
+                         const int*, int, int, int, float, cudaStream_t) = nullptr;
     void (*lt_destroy)(void*) = nullptr;
+
+    // Bidirectional attention over a complete work list (every 64-row tile of every sequence, as the runners
+    // build it): the tcgen05 kernel when the library has it, fused forms are on and there are no biases to add
+    // on load; d1_flash_attn otherwise.
+    int attention(bool fused, const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
+                  const float* bq, const float* bk, const float* bv, d1_half* O, int ldo, const AttnSeq* seqs,
+                  const int* work, int n_work, int heads, int group, float scale, cudaStream_t st) const {
+        if (fused && flash_attn_tc && !bq && !bk && !bv)
+            return flash_attn_tc(Q, ldq, K, V, ldkv, ext_ld, O, ldo, seqs, work, n_work, heads, group, scale, st);
+        return flash_attn(Q, ldq, K, V, ldkv, ext_ld, bq, bk, bv, O, ldo, seqs, work, n_work, heads, group, scale, st);
+    }
 
     bool load_builtin() {
         rmsnorm = d1_rmsnorm;
@@ -90,6 +103,7 @@ struct Kt {
         lt_free_scratch = d1_lt_free_scratch;
         gemm_swiglu = d1_gemm_swiglu;
         gemm_bias_act = d1_gemm_bias_act;
+        flash_attn_tc = d1_flash_attn_tc;
         lt_destroy = d1_lt_destroy;
         return true;
     }
@@ -118,7 +132,8 @@ struct Kt {
                sym(lt_init, "d1_lt_init") && sym(lt_gemm, "d1_lt_gemm") &&
                sym(lt_tune, "d1_lt_tune") && sym(lt_bucket, "d1_lt_bucket") &&
                sym(lt_free_scratch, "d1_lt_free_scratch") && sym(gemm_swiglu, "d1_gemm_swiglu", false) &&
-               sym(gemm_bias_act, "d1_gemm_bias_act", false) && sym(lt_destroy, "d1_lt_destroy", false);
+               sym(gemm_bias_act, "d1_gemm_bias_act", false) && sym(flash_attn_tc, "d1_flash_attn_tc", false) &&
+               sym(lt_destroy, "d1_lt_destroy", false);
     }
 };
 
@@ -322,8 +337,8 @@ int trunk(D1Model* m, D1Workspace* ws, int t, const int* tok_seq, const SeqInfo*
             CK(m->gemm(t, ld, D, xn, D, l.qkv, D, big, ld, 0, 1.f, 0.f, st));
             m->launches += 2;
             CK(k.qk_norm_rope(big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq, seqs, idx, t, m->w.eps, st));
-            CK(k.flash_attn(big, ld, big + D, big + D + KV_DIM, ld, KV_DIM, nullptr, nullptr, nullptr, act, D, attn[idx],
-                            work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, st));
+            CK(k.attention(m->fused, big, ld, big + D, big + D + KV_DIM, ld, KV_DIM, nullptr, nullptr, nullptr, act, D,
+                           attn[idx], work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, st));
             if (prefix_pass && last) return 0;
             CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
         }
@@ -643,8 +658,8 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
         const float* bv = fold ? nullptr : l.qkv_b + 2 * D;
         if (li + 1 < nh) {
             m->launches++;
-            CK(k.flash_attn(big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, act, D, d_head_attn, d_work,
-                            n_work, HEADS, 1, 0.125f, st));
+            CK(k.attention(m->fused, big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, act, D, d_head_attn,
+                           d_work, n_work, HEADS, 1, 0.125f, st));
             CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
             m->launches++;
             CK(k.layernorm(h, l.out_b, 1.f, l.n2_w, l.n2_b, xn, nullptr, t, D, 1e-5f, st));
@@ -659,8 +674,8 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
                 m->launches += 3;
                 CK(k.gather_rows(big, ws->mq, d_mrows, nm, qkv_ld * 2, st));
                 CK(k.gather_rows(h, ws->mh, d_mrows, nm, D * 4, st));
-                CK(k.flash_attn(ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, ws->mo, D, d_last_attn,
-                                d_mwork, n_mwork, HEADS, 1, 0.125f, st));
+                CK(k.attention(m->fused, ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, ws->mo, D,
+                               d_last_attn, d_mwork, n_mwork, HEADS, 1, 0.125f, st));
                 CK(m->gemm(nm, D, D, ws->mo, D, l.out, D, ws->mh, D, 1, 1.f, 1.f, st));
                 m->launches++;
                 CK(k.layernorm(ws->mh, l.out_b, 1.f, l.n2_w, l.n2_b, ws->mx, nullptr, nm, D, 1e-5f, st));
@@ -1016,9 +1031,9 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
             CK(kt_gemm(k, v->lt, L, ti, 3 * VD, VD, xn, VD, l.qkv, VD, big, 3 * VD, 0, 1.f, 0.f, st));
         }
         L++;
-        CK(k.flash_attn(big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, fold ? nullptr : l.qkv_b,
-                        fold ? nullptr : l.qkv_b + VD, fold ? nullptr : l.qkv_b + 2 * VD, act, VD, d_seqs, d_work,
-                        n_work, VHEADS, 1, 0.125f, st));
+        CK(k.attention(v->fused, big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, fold ? nullptr : l.qkv_b,
+                       fold ? nullptr : l.qkv_b + VD, fold ? nullptr : l.qkv_b + 2 * VD, act, VD, d_seqs, d_work,
+                       n_work, VHEADS, 1, 0.125f, st));
         CK(kt_gemm(k, v->lt, L, ti, VD, VD, act, VD, l.out, VD, h, VD, 1, 1.f, 1.f, st));
         L++;
         CK(k.layernorm(h, l.out_b, 1.f, l.ln2_w, l.ln2_b, xn, nullptr, ti, VD, eps, st));
