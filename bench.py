@@ -400,6 +400,42 @@ def run_mixed(args, rank, world, local, dev):
     text.close()
 
 
+def attention_launches(pkg, dev, seq_len, reps=20, warm=3):
+    """The runners' attention (d1_flash_attn_tc: trunk shapes, 16 heads, GQA 2, head dim 64) on 8192 / seq_len packed
+    sequences of seq_len tokens; average CUDA-event time per launch. The small case for an ncu capture."""
+    import ctypes as C
+    import torch
+    lib = pkg.lib()
+    n = TOKENS // seq_len
+    arr = (pkg.abi.AttnSeq * n)()
+    work = []
+    for i in range(n):
+        arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = i * seq_len, seq_len, i * seq_len, seq_len
+        work += [(i, q) for q in range(0, seq_len, 64)]
+    meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
+    wk = torch.tensor(np.asarray(work, np.int32).reshape(-1), device=dev)
+    g = torch.Generator(device=dev).manual_seed(2)
+    qkv = torch.randn(TOKENS, 2048, device=dev, generator=g).half()
+    out = torch.empty(TOKENS, 1024, device=dev, dtype=torch.float16)
+    st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    f = lambda: lib.d1_flash_attn_tc(P(qkv), 2048, P(qkv[:, 1024:]), P(qkv[:, 1536:]), 2048, 512, P(out), 1024,  # noqa: E731
+                                     P(meta), P(wk), len(work), 16, 2, 0.125, st)
+    for _ in range(warm):
+        assert f() == 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        f()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    if lib.d1_flash_attn_error():
+        raise RuntimeError("attention kernel reported a wait that gave up")
+    us = e0.elapsed_time(e1) / reps * 1e3
+    flops = n * 4.0 * seq_len * seq_len * 64 * 16
+    return us, flops / (us * 1e-6) / 1e12
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,6 +447,8 @@ def main():
                     help="text: the metric's 8192-token text batches; mixed: BASELINE config 4 through the engine")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="BASELINE config 1: time every GEMM shape (one JSON line each) instead of the forward")
+    ap.add_argument("--only-attention", type=int, default=0, metavar="L",
+                    help="run only the runners' attention kernel on 8192/L sequences of L tokens (an ncu case)")
     ap.add_argument("--only-roofline", action="store_true",
                     help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
     args = ap.parse_args()
@@ -441,6 +479,12 @@ def main():
     if args.gemm_sweep:
         if rank == 0:
             gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
+        return
+    if args.only_attention:
+        us, tf = attention_launches(pkg, dev, args.only_attention, reps=args.steps, warm=args.warmup)
+        if rank == 0:
+            print(json.dumps({"kernel": "k_flash_attn_tc", "seq_len": args.only_attention, "us": us, "tflops": tf}),
+                  flush=True)
         return
     if args.only_roofline:
         ms = swiglu_gemm_ms(pkg, dev, torch.cuda.Stream(dev))

@@ -214,7 +214,9 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
 int d1_lt_error(void* ctx);
 
 /* extension — d1_flash_attn without biases on tcgen05 tensor cores (S and O in TMEM); same arguments and result
- * as d1_flash_attn with bq = bk = bv = NULL. */
+ * as d1_flash_attn with bq = bk = bv = NULL, for a work list that covers every 64-row tile of every sequence (as
+ * src/model.rs builds it): the kernel works in 256-row blocks, each starting at an item whose q0 is a multiple of
+ * 256. Pointers 16-byte aligned, leading dimensions multiples of 8. */
 int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld, d1_half* O,
                      int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads, int group, float scale,
                      cudaStream_t stream);
