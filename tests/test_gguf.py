@@ -4,8 +4,11 @@ The writer below emits GGUF v2/v3 containers as the format defines them (header,
 ggml dims, aligned tensor data) with the tensor names the reference's loaders read (src/model.rs:139-231,
 src/vision.rs:198-260, src/audio.rs:403-455). CPU tests: every metadata type, every tensor type the reference
 decodes (F32, F16, BF16, Q8_0; src/gguf.rs:186-214) against the reference's conversion formulas restated in numpy,
-the error cases, and each model mapping back to the dict it was written from. GPU tests: a TextModel, VisionModel
-and AudioModel loaded from GGUF give bit-identical outputs to the same models built from the dicts.
+the error cases, and each model mapping back to the dict it was written from. GPU tests: models loaded from GGUF against
+the same models built from the dicts. The two are not bit-identical: split-K tiles add into fp32 residuals in
+arrival order, and the encoders tune their GEMM plans per instance by timing, so the text logits agree within 2e-3
+(the engine tests' run-to-run bound) and the encoder outputs to a relative RMS of 5e-3 — a wrong mapping (a
+transposed patch or pre-encode weight, swapped q/k/v) is off by O(1).
 """
 import struct
 
@@ -384,7 +387,7 @@ def test_text_model_from_gguf_identical(tmp_path, gpu_lib):
         got = b(batch)
     finally:
         b.close()
-    assert np.array_equal(got, want)
+    assert got.shape == want.shape and np.abs(got - want).max() <= 2e-3
 
 
 @pytest.mark.gpu
@@ -404,4 +407,6 @@ def test_media_models_from_gguf_identical(tmp_path, gpu_lib):
         finally:
             v.close()
             a.close()
-    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+    for want, got in zip(outs[0], outs[1]):
+        assert got.shape == want.shape
+        assert np.sqrt(((got - want) ** 2).mean() / (want ** 2).mean()) <= 5e-3
