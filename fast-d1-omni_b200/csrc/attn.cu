@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
     __half* sK = sQ + HPC * FA_B * FA_LD;                           // [2][64][FA_LD]
     __half* sV = sK + 2 * FA_B * FA_LD;                             // [2][64][FA_LD]
 
+    pdl_entry();
     const int2 wi = p.work[blockIdx.x];
     const AttnSeq s = p.seqs[wi.x];
     const int q0 = wi.y;
@@ -369,6 +370,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
     auto bar = [&](int i) { return smem_u32(bars + i); };
 
     if (smem_u32(smem_raw) & 1023) {  // never expected: dynamic shared memory starts at the window base
+        pdl_wait();
         if (threadIdx.x == 0 && a.err) atomicExch(a.err, kErrDrain);
         return;
     }
@@ -401,6 +403,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_entry();  // barriers and TMEM are set up; global memory is touched only after this
 
     if (warp == 8 || warp >= 10) {
         // ------------------------------------------------------------------ loaders (warps 8, 10, 11)
@@ -698,7 +701,7 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
     a.n_units = n_work * heads;
     a.heads = heads;
     const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
-    k_flash_attn_tc<<<grid, T_THREADS, T_SMEM, st>>>(a);
+    launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, a);
     return (int)cudaGetLastError();
 }
 
@@ -717,7 +720,7 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
         __atomic_fetch_or(&attr_done, bit, __ATOMIC_RELEASE);
     }
     dim3 grid(n_work, gy);
-    k_flash_attn<HPC, BIAS><<<grid, 128 * HPC, smem, st>>>(a);
+    launch_pdl(k_flash_attn<HPC, BIAS>, grid, 128 * HPC, smem, st, a);
     return (int)cudaGetLastError();
 }
 

@@ -310,3 +310,50 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                  : "memory");
 }
 }  // namespace d1
+
+#include <stdlib.h>
+
+#include <utility>
+
+namespace d1 {
+// ------------------------------------------------------------------------- programmatic dependent launch
+// The forward's kernels are launched with programmatic stream serialization: a kernel's CTAs may be scheduled while
+// the kernel before it in the stream is still finishing, so its prologue (barrier set-up, TMEM allocation, tensor-map
+// prefetch) and its launch latency overlap the previous kernel's tail. Every kernel launched this way calls
+// pdl_wait() in every CTA, on every path, before its first access to global memory: it returns once the previous
+// grid has completed and its writes are visible, so each kernel's completion still implies its predecessors'. After
+// the wait, pdl_trigger() lets the next kernel's CTAs launch. Both are no-ops in a kernel launched the ordinary way.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+    pdl_wait();
+    pdl_trigger();
+}
+
+// D1_PDL=0 in the environment launches every kernel the ordinary way (fully serialised).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("D1_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// kernel<<<grid, block, smem, st>>>(args...) with programmatic stream serialization; the kernel must call pdl_wait()
+// (pdl_entry()) as described above.
+template <typename... KP, typename... A>
+inline cudaError_t launch_pdl(void (*kernel)(KP...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+}  // namespace d1

@@ -257,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_entry();  // barriers, TMEM and tensor maps are set up; global memory is touched only after this
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -502,6 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     cluster_sync();  // both CTAs' barriers are initialised before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_entry();
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer (both CTAs)
@@ -875,7 +877,7 @@ int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, i
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
     const int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
-    kern<<<grid, kThreads, S::BYTES, st>>>(ta, tb, ty, a);
+    launch_pdl(kern, grid, kThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
 
@@ -915,7 +917,7 @@ int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, 
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
     const int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
-    kern<<<2 * pairs, kPairThreads, S::BYTES, st>>>(ta, tb, ty, a);
+    launch_pdl(kern, 2 * pairs, kPairThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
 

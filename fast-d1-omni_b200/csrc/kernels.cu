@@ -44,6 +44,7 @@ __device__ __forceinline__ uint4 f_to_h8(const float* f) {
 template <int NV>
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
                                                  __half* __restrict__ y, int rows, float eps) {
+    pdl_entry();
     constexpr int D = NV * 128;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -70,6 +71,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) k_layernorm(float* x, const float* __restrict__ pend, float pend_scale,
                                                    const float* __restrict__ w, const float* __restrict__ b,
                                                    __half* __restrict__ y, float* yf, int rows, float eps) {
+    pdl_entry();
     constexpr int D = NV * 128;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -115,6 +117,7 @@ __global__ void __launch_bounds__(256) k_layernorm(float* x, const float* __rest
 __global__ void __launch_bounds__(256) k_head_init(const float* h, const float* __restrict__ w,
                                                    const float* __restrict__ type_emb, const int* __restrict__ tok_seq,
                                                    const SeqInfo* __restrict__ seqs, float* out, int rows, float eps) {
+    pdl_entry();
     constexpr int NV = 8, D = 1024;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(256) k_head_init(const float* h, const float* 
 // h[row] = table[ids[row]] (fp16 -> fp32); a warp per row, 8 halves per access.
 __global__ void __launch_bounds__(256) k_embed(const __half* __restrict__ table, const int* __restrict__ ids,
                                                float* __restrict__ h, int rows, int D) {
+    pdl_entry();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)ids[row] * D);
@@ -156,12 +160,14 @@ __global__ void __launch_bounds__(256) k_embed(const __half* __restrict__ table,
 
 __global__ void k_embed_scalar(const __half* __restrict__ table, const int* __restrict__ ids, float* __restrict__ h,
                                int rows, int D) {
+    pdl_entry();
     const int row = blockIdx.x;
     for (int c = threadIdx.x; c < D; c += blockDim.x) h[(size_t)row * D + c] = __half2float(table[(size_t)ids[row] * D + c]);
 }
 
 // out[t][i] = silu(gu[t][i]) * gu[t][F + i], 8 columns per step (F % 8 == 0).
 __global__ void k_swiglu8(const __half* __restrict__ gu, __half* __restrict__ out, int rows, int F) {
+    pdl_entry();
     const int f8 = F / 8;
     const size_t n = (size_t)rows * f8;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
@@ -177,6 +183,7 @@ __global__ void k_swiglu8(const __half* __restrict__ gu, __half* __restrict__ ou
 }
 
 __global__ void k_swiglu_scalar(const __half* __restrict__ gu, __half* __restrict__ out, int rows, int F) {
+    pdl_entry();
     const size_t n = (size_t)rows * F;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const size_t r = idx / F;
@@ -187,6 +194,7 @@ __global__ void k_swiglu_scalar(const __half* __restrict__ gu, __half* __restric
 
 // x = act(x + bias), fp16 in place, 8 columns per step (N % 8 == 0).
 __global__ void k_bias_act_h8(__half* __restrict__ x, const float* __restrict__ bias, int rows, int N, int act) {
+    pdl_entry();
     const int n8 = N / 8;
     const size_t n = (size_t)rows * n8;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
@@ -201,6 +209,7 @@ __global__ void k_bias_act_h8(__half* __restrict__ x, const float* __restrict__ 
 }
 
 __global__ void k_bias_act_h_scalar(__half* __restrict__ x, const float* __restrict__ bias, int rows, int N, int act) {
+    pdl_entry();
     const size_t n = (size_t)rows * N;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(idx % N);
@@ -210,6 +219,7 @@ __global__ void k_bias_act_h_scalar(__half* __restrict__ x, const float* __restr
 
 // x = act(x + bias), fp32 in place.
 __global__ void k_bias_act_f(float* __restrict__ x, const float* __restrict__ bias, int rows, int N, int act) {
+    pdl_entry();
     const size_t n = (size_t)rows * N;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(idx % N);
@@ -220,6 +230,7 @@ __global__ void k_bias_act_f(float* __restrict__ x, const float* __restrict__ bi
 // out[t][i] = bias[i] (+ add[t][i]).
 __global__ void k_fill_rows(float* __restrict__ out, const float* __restrict__ bias, const float* __restrict__ add,
                             int rows, int N) {
+    pdl_entry();
     const size_t n = (size_t)rows * N;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(idx % N);
@@ -230,6 +241,7 @@ __global__ void k_fill_rows(float* __restrict__ out, const float* __restrict__ b
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+    pdl_entry();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         y[i] = __float2half(x[i]);
 }
@@ -237,6 +249,7 @@ __global__ void k_f32_to_f16(const float* __restrict__ x, __half* __restrict__ y
 // dst[i] = src[idx[i]]: a warp per row of width16 x 16 bytes.
 __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                      const int* __restrict__ idx, int n, int width16) {
+    pdl_entry();
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= n) return;
     const uint4* s = src + (size_t)idx[r] * width16;
@@ -263,6 +276,7 @@ __device__ __forceinline__ void mul8(const uint4& b, const uint4& u, float* bx) 
 __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bcu, const float* __restrict__ convw,
                                                    const int* __restrict__ tok_seq, const SeqInfo* __restrict__ seqs,
                                                    __half* __restrict__ out, int rows, int D, int conv_idx) {
+    pdl_entry();
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
     if (c >= D) return;
     const int t0 = blockIdx.x * kConvRows;
@@ -337,6 +351,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope8(__half* __restrict__ qkv,
                                                        const int* __restrict__ tok_seq,
                                                        const SeqInfo* __restrict__ seqs, int attn_idx, int rows,
                                                        float eps) {
+    pdl_entry();
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (t >= rows) return;  // whole warps leave together
     const int lane = threadIdx.x & 31, grp = lane >> 3, k = lane & 7;
@@ -417,6 +432,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(__half* __restrict__ qkv, 
                                                       const float* __restrict__ rope, const int* __restrict__ tok_seq,
                                                       const SeqInfo* __restrict__ seqs, int attn_idx, int rows,
                                                       float eps) {
+    pdl_entry();
     const int t = blockIdx.x;
     const int half_id = threadIdx.x >> 4, j = threadIdx.x & 15;
     const SeqInfo s = seqs[tok_seq[t]];
@@ -468,6 +484,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(__half* __restrict__ qkv, 
 __global__ void __launch_bounds__(256) k_scorer_out(const __half* __restrict__ x, const float* __restrict__ b1,
                                                     const __half* __restrict__ w2, float b2, float* __restrict__ logits,
                                                     int rows, int D) {
+    pdl_entry();
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     float s = 0.f;
@@ -496,6 +513,7 @@ __global__ void __launch_bounds__(256) k_scorer_out(const __half* __restrict__ x
 __global__ void __launch_bounds__(256) k_vision_pos(const float* __restrict__ grid, const float* __restrict__ bias,
                                                     const int2* __restrict__ spans, const float* __restrict__ w,
                                                     int taps, int ph, int pw, int C, float* __restrict__ out) {
+    pdl_entry();
     const int p = blockIdx.x, y = p / pw, x = p % pw;
     const int2 sy = spans[y], sx = spans[ph + x];
     const float* wy = w + (size_t)y * taps;
@@ -513,6 +531,7 @@ __global__ void __launch_bounds__(256) k_vision_pos(const float* __restrict__ gr
 }
 
 __global__ void k_unshuffle(const __half* __restrict__ x, __half* __restrict__ out, int ph, int pw, int C) {
+    pdl_entry();
     const int o = blockIdx.x;
     const int i = o / (pw / 2), jj = o % (pw / 2);
     for (int k = threadIdx.x * 8; k < 4 * C; k += blockDim.x * 8) {
@@ -528,6 +547,7 @@ __global__ void k_unshuffle(const __half* __restrict__ x, __half* __restrict__ o
 __global__ void __launch_bounds__(256) k_sub_conv0(const float* __restrict__ mel, int tin_valid, int F,
                                                    const float* __restrict__ w, const float* __restrict__ b,
                                                    float* __restrict__ out, int Tout, int Fout) {
+    pdl_entry();
     const int t = blockIdx.x, f = blockIdx.y, c = threadIdx.x;
     __shared__ float patch[9];
     if (threadIdx.x < 9) {
@@ -554,6 +574,7 @@ __global__ void __launch_bounds__(256) k_sub_conv0(const float* __restrict__ mel
 __global__ void __launch_bounds__(256) k_sub_dwconv(const float* __restrict__ x, int tin_valid, int Fin,
                                                     const float* __restrict__ w, const float* __restrict__ b,
                                                     float* __restrict__ out, int Fout) {
+    pdl_entry();
     const int t = blockIdx.x, f = blockIdx.y, c = threadIdx.x;
     float acc = b[c];
 #pragma unroll
@@ -575,6 +596,7 @@ __global__ void k_relpos_prep(const __half* __restrict__ qkv, const float* __res
                               const float* __restrict__ bk, const float* __restrict__ bv, const float* __restrict__ pu,
                               const float* __restrict__ pv, __half* __restrict__ qu, __half* __restrict__ qvv,
                               __half* __restrict__ k, __half* __restrict__ v, int T, int Dm) {
+    pdl_entry();
     const int t = blockIdx.x;
     const __half* r = qkv + (size_t)t * 3 * Dm;
     for (int c = threadIdx.x; c < Dm; c += blockDim.x) {
@@ -589,6 +611,7 @@ __global__ void k_relpos_prep(const __half* __restrict__ qkv, const float* __res
 // p[h][i][j] = softmax_j((ac[h][i][j] + bd[h][i][j + T-1-i]) * scale) (cuda/kernels.cu:582-616).
 __global__ void __launch_bounds__(256) k_relpos_softmax(const float* __restrict__ ac, const float* __restrict__ bd,
                                                         __half* __restrict__ p, int T, float scale) {
+    pdl_entry();
     const int h = blockIdx.y, i = blockIdx.x;
     const float* a = ac + ((size_t)h * T + i) * T;
     const float* b = bd + ((size_t)h * T + i) * (2 * T - 1) + (T - 1 - i);
@@ -626,6 +649,7 @@ __global__ void __launch_bounds__(256) k_relpos_softmax(const float* __restrict_
 __global__ void k_conformer_dw(const __half* __restrict__ a, const float* __restrict__ b1, const float* __restrict__ dw,
                                const float* __restrict__ dwb, const float* __restrict__ bn_s,
                                const float* __restrict__ bn_b, __half* __restrict__ out, int T, int C, int ksize) {
+    pdl_entry();
     const int t = blockIdx.x;
     const int pad = (ksize - 1) / 2;
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
@@ -654,9 +678,9 @@ int d1_rmsnorm(const float* x, const float* w, d1_half* y, int rows, int D, floa
     if (!al16(x) || !al16(w) || ((uintptr_t)y & 7)) return -1;
     const int grid = nblk(rows, 8);
     switch (D) {
-        case 1024: k_rmsnorm<8><<<grid, 256, 0, st>>>(x, w, y, rows, eps); break;
-        case 768: k_rmsnorm<6><<<grid, 256, 0, st>>>(x, w, y, rows, eps); break;
-        case 512: k_rmsnorm<4><<<grid, 256, 0, st>>>(x, w, y, rows, eps); break;
+        case 1024: launch_pdl(k_rmsnorm<8>, grid, 256, 0, st, x, w, y, rows, eps); break;
+        case 768: launch_pdl(k_rmsnorm<6>, grid, 256, 0, st, x, w, y, rows, eps); break;
+        case 512: launch_pdl(k_rmsnorm<4>, grid, 256, 0, st, x, w, y, rows, eps); break;
         default: return -1;
     }
     return (int)cudaGetLastError();
@@ -669,9 +693,9 @@ int d1_layernorm(float* x, const float* pend_bias, float pend_scale, const float
         return -1;
     const int grid = nblk(rows, 8);
     switch (D) {
-        case 1024: k_layernorm<8><<<grid, 256, 0, st>>>(x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
-        case 768: k_layernorm<6><<<grid, 256, 0, st>>>(x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
-        case 512: k_layernorm<4><<<grid, 256, 0, st>>>(x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
+        case 1024: launch_pdl(k_layernorm<8>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
+        case 768: launch_pdl(k_layernorm<6>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
+        case 512: launch_pdl(k_layernorm<4>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
         default: return -1;
     }
     return (int)cudaGetLastError();
@@ -681,59 +705,59 @@ int d1_head_init(const float* h, const float* w, const float* type_emb, const in
                  float* out, int rows, float eps, cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
     if (!al16(h) || !al16(w) || !al16(type_emb) || !al16(out)) return -1;
-    k_head_init<<<nblk(rows, 8), 256, 0, st>>>(h, w, type_emb, tok_seq, seqs, out, rows, eps);
+    launch_pdl(k_head_init, nblk(rows, 8), 256, 0, st, h, w, type_emb, tok_seq, seqs, out, rows, eps);
     return (int)cudaGetLastError();
 }
 
 int d1_embed(const d1_half* table, const int* ids, float* h, int rows, int D, cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
     if (D % 8 == 0 && al16(table) && al16(h))
-        k_embed<<<nblk(rows, 8), 256, 0, st>>>(table, ids, h, rows, D);
+        launch_pdl(k_embed, nblk(rows, 8), 256, 0, st, table, ids, h, rows, D);
     else
-        k_embed_scalar<<<rows, 256, 0, st>>>(table, ids, h, rows, D);
+        launch_pdl(k_embed_scalar, rows, 256, 0, st, table, ids, h, rows, D);
     return (int)cudaGetLastError();
 }
 
 int d1_swiglu(const d1_half* gu, d1_half* out, int rows, int F, cudaStream_t st) {
     if (rows <= 0 || F <= 0) return rows == 0 || F == 0 ? 0 : -1;
     if (F % 8 == 0 && al16(gu) && al16(out))
-        k_swiglu8<<<egrid((size_t)rows * F / 8, 256), 256, 0, st>>>(gu, out, rows, F);
+        launch_pdl(k_swiglu8, egrid((size_t)rows * F / 8, 256), 256, 0, st, gu, out, rows, F);
     else
-        k_swiglu_scalar<<<egrid((size_t)rows * F, 256), 256, 0, st>>>(gu, out, rows, F);
+        launch_pdl(k_swiglu_scalar, egrid((size_t)rows * F, 256), 256, 0, st, gu, out, rows, F);
     return (int)cudaGetLastError();
 }
 
 int d1_bias_act_h(d1_half* x, const float* bias, int rows, int N, int act, cudaStream_t st) {
     if (rows <= 0 || N <= 0) return rows == 0 || N == 0 ? 0 : -1;
     if (N % 8 == 0 && al16(x))
-        k_bias_act_h8<<<egrid((size_t)rows * N / 8, 256), 256, 0, st>>>(x, bias, rows, N, act);
+        launch_pdl(k_bias_act_h8, egrid((size_t)rows * N / 8, 256), 256, 0, st, x, bias, rows, N, act);
     else
-        k_bias_act_h_scalar<<<egrid((size_t)rows * N, 256), 256, 0, st>>>(x, bias, rows, N, act);
+        launch_pdl(k_bias_act_h_scalar, egrid((size_t)rows * N, 256), 256, 0, st, x, bias, rows, N, act);
     return (int)cudaGetLastError();
 }
 
 int d1_bias_act_f(float* x, const float* bias, int rows, int N, int act, cudaStream_t st) {
     if (rows <= 0 || N <= 0) return rows == 0 || N == 0 ? 0 : -1;
-    k_bias_act_f<<<egrid((size_t)rows * N, 256), 256, 0, st>>>(x, bias, rows, N, act);
+    launch_pdl(k_bias_act_f, egrid((size_t)rows * N, 256), 256, 0, st, x, bias, rows, N, act);
     return (int)cudaGetLastError();
 }
 
 int d1_fill_rows(float* out, const float* bias, const float* add, int rows, int N, cudaStream_t st) {
     if (rows <= 0 || N <= 0) return rows == 0 || N == 0 ? 0 : -1;
-    k_fill_rows<<<egrid((size_t)rows * N, 256), 256, 0, st>>>(out, bias, add, rows, N);
+    launch_pdl(k_fill_rows, egrid((size_t)rows * N, 256), 256, 0, st, out, bias, add, rows, N);
     return (int)cudaGetLastError();
 }
 
 int d1_f32_to_f16(const float* x, d1_half* y, size_t n, cudaStream_t st) {
     if (n == 0) return 0;
-    k_f32_to_f16<<<egrid(n, 256), 256, 0, st>>>(x, y, n);
+    launch_pdl(k_f32_to_f16, egrid(n, 256), 256, 0, st, x, y, n);
     return (int)cudaGetLastError();
 }
 
 int d1_gather_rows(const void* src, void* dst, const int* idx, int n, int row_bytes, cudaStream_t st) {
     if (n <= 0) return n == 0 ? 0 : -1;
     if (row_bytes % 16 || !al16(src) || !al16(dst)) return -1;
-    k_gather_rows<<<nblk(n, 8), 256, 0, st>>>((const uint4*)src, (uint4*)dst, idx, n, row_bytes / 16);
+    launch_pdl(k_gather_rows, nblk(n, 8), 256, 0, st, (const uint4*)src, (uint4*)dst, idx, n, row_bytes / 16);
     return (int)cudaGetLastError();
 }
 
@@ -743,7 +767,7 @@ int d1_shortconv(const d1_half* bcu, const float* convw, const int* tok_seq, con
     if (D % 8 || !al16(bcu) || !al16(out)) return -1;
     const int threads = D / 8 < 128 ? D / 8 : 128;
     dim3 grid(nblk(rows, kConvRows), nblk(D / 8, threads));
-    k_shortconv<<<grid, threads, 0, st>>>(bcu, convw, tok_seq, seqs, out, rows, D, conv_idx);
+    launch_pdl(k_shortconv, grid, threads, 0, st, bcu, convw, tok_seq, seqs, out, rows, D, conv_idx);
     return (int)cudaGetLastError();
 }
 
@@ -752,18 +776,18 @@ int d1_qk_norm_rope(d1_half* qkv, int ld, int H, int KVH, const float* qn, const
     if (rows <= 0) return rows == 0 ? 0 : -1;
     if (((uintptr_t)qkv & 3) || (ld & 1) || !al16(rope)) return -1;
     if (al16(qkv) && ld % 8 == 0 && H + KVH <= 4 * kQkMaxPerGroup) {
-        k_qk_norm_rope8<<<nblk(rows, 8), 256, 0, st>>>(qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows,
+        launch_pdl(k_qk_norm_rope8, nblk(rows, 8), 256, 0, st, qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows,
                                                        eps);
         return (int)cudaGetLastError();
     }
-    k_qk_norm_rope<<<rows, 256, 0, st>>>(qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows, eps);
+    launch_pdl(k_qk_norm_rope, rows, 256, 0, st, qkv, ld, H, KVH, qn, kn, rope, tok_seq, seqs, attn_idx, rows, eps);
     return (int)cudaGetLastError();
 }
 
 int d1_scorer_out(const d1_half* x, const float* b1, const d1_half* w2, float b2, float* logits, int rows, int D,
                   cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
-    k_scorer_out<<<nblk(rows, 8), 256, 0, st>>>(x, b1, w2, b2, logits, rows, D);
+    launch_pdl(k_scorer_out, nblk(rows, 8), 256, 0, st, x, b1, w2, b2, logits, rows, D);
     return (int)cudaGetLastError();
 }
 
@@ -771,7 +795,7 @@ int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, con
                   int pw, int C, float* out, cudaStream_t st) {
     if (ph <= 0 || pw <= 0) return 0;
     if (!grid || !patch_b || !spans || !w || !out || taps < 1 || C < 1 || ((uintptr_t)spans & 7)) return -1;
-    k_vision_pos<<<ph * pw, 256, 0, st>>>(grid, patch_b, reinterpret_cast<const int2*>(spans), w, taps, ph, pw, C,
+    launch_pdl(k_vision_pos, ph * pw, 256, 0, st, grid, patch_b, reinterpret_cast<const int2*>(spans), w, taps, ph, pw, C,
                                            out);
     return (int)cudaGetLastError();
 }
@@ -779,7 +803,7 @@ int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, con
 int d1_unshuffle(const d1_half* x, d1_half* out, int ph, int pw, int C, cudaStream_t st) {
     if (ph <= 0 || pw <= 0) return 0;
     if (C % 8 || !al16(x) || !al16(out)) return -1;
-    k_unshuffle<<<(ph / 2) * (pw / 2), 128, 0, st>>>(x, out, ph, pw, C);
+    launch_pdl(k_unshuffle, (ph / 2) * (pw / 2), 128, 0, st, x, out, ph, pw, C);
     return (int)cudaGetLastError();
 }
 
@@ -787,7 +811,7 @@ int d1_sub_conv0(const float* mel, int tin_valid, int F, const float* w, const f
                  cudaStream_t st) {
     if (Tout <= 0 || Fout <= 0) return 0;
     dim3 grid(Tout, Fout);
-    k_sub_conv0<<<grid, 256, 0, st>>>(mel, tin_valid, F, w, b, out, Tout, Fout);
+    launch_pdl(k_sub_conv0, grid, 256, 0, st, mel, tin_valid, F, w, b, out, Tout, Fout);
     return (int)cudaGetLastError();
 }
 
@@ -795,28 +819,28 @@ int d1_sub_dwconv(const float* x, int tin_valid, int Fin, const float* w, const 
                   int Fout, cudaStream_t st) {
     if (Tout <= 0 || Fout <= 0) return 0;
     dim3 grid(Tout, Fout);
-    k_sub_dwconv<<<grid, 256, 0, st>>>(x, tin_valid, Fin, w, b, out, Fout);
+    launch_pdl(k_sub_dwconv, grid, 256, 0, st, x, tin_valid, Fin, w, b, out, Fout);
     return (int)cudaGetLastError();
 }
 
 int d1_relpos_prep(const d1_half* qkv, const float* bq, const float* bk, const float* bv, const float* pu,
                    const float* pv, d1_half* qu, d1_half* qv, d1_half* k, d1_half* v, int T, int Dm, cudaStream_t st) {
     if (T <= 0) return 0;
-    k_relpos_prep<<<T, 256, 0, st>>>(qkv, bq, bk, bv, pu, pv, qu, qv, k, v, T, Dm);
+    launch_pdl(k_relpos_prep, T, 256, 0, st, qkv, bq, bk, bv, pu, pv, qu, qv, k, v, T, Dm);
     return (int)cudaGetLastError();
 }
 
 int d1_relpos_softmax(const float* ac, const float* bd, d1_half* p, int T, int H, float scale, cudaStream_t st) {
     if (T <= 0 || H <= 0) return 0;
     dim3 grid(T, H);
-    k_relpos_softmax<<<grid, 256, 0, st>>>(ac, bd, p, T, scale);
+    launch_pdl(k_relpos_softmax, grid, 256, 0, st, ac, bd, p, T, scale);
     return (int)cudaGetLastError();
 }
 
 int d1_conformer_dw(const d1_half* a, const float* b1, const float* dw, const float* dwb, const float* bn_s,
                     const float* bn_b, d1_half* out, int T, int C, int ksize, cudaStream_t st) {
     if (T <= 0) return 0;
-    k_conformer_dw<<<T, 256, 0, st>>>(a, b1, dw, dwb, bn_s, bn_b, out, T, C, ksize);
+    launch_pdl(k_conformer_dw, T, 256, 0, st, a, b1, dw, dwb, bn_s, bn_b, out, T, C, ksize);
     return (int)cudaGetLastError();
 }
 
