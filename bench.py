@@ -411,7 +411,7 @@ def attention_launches(pkg, dev, seq_len, reps=20, warm=3):
     work = []
     for i in range(n):
         arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = i * seq_len, seq_len, i * seq_len, seq_len
-        work += [(i, q) for q in range(0, seq_len, 64)]
+        work += [(i, q) for q in range(0, seq_len, 256)]  # one item per 256-row block, as the runners pass it
     meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
     wk = torch.tensor(np.asarray(work, np.int32).reshape(-1), device=dev)
     g = torch.Generator(device=dev).manual_seed(2)
@@ -420,7 +420,7 @@ def attention_launches(pkg, dev, seq_len, reps=20, warm=3):
     st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
     f = lambda: lib.d1_flash_attn_tc(P(qkv), 2048, P(qkv[:, 1024:]), P(qkv[:, 1536:]), 2048, 512, P(out), 1024,  # noqa: E731
-                                     P(meta), P(wk), len(work), 16, 2, 0.125, st)
+                                     P(meta), P(wk), len(work), 16, 2, 0.125, TOKENS, TOKENS, st)
     for _ in range(warm):
         assert f() == 0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -144,7 +144,7 @@ EXTENSIONS = {
     "d1_gemm_bias_act": (i32, [p, i32, i32, i32, p, i32, p, i32, p, i32, p, i32, p]),
     "d1_lt_error": (i32, [p]),
     "d1_flash_attn_error": (i32, []),
-    "d1_flash_attn_tc": (i32, [p, i32, p, p, i32, i32, p, i32, p, p, i32, i32, i32, f32, p]),
+    "d1_flash_attn_tc": (i32, [p, i32, p, p, i32, i32, p, i32, p, p, i32, i32, i32, f32, i32, i32, p]),
     "d1_sgemm": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, f32, p, i32, p]),
     "d1_relpos_attn": (i32, [p, p, p, p, i32, p, i32, i32, i32, p, i32, p, i32, i32, i32, f32, p]),
     "d1_relpos_attn_error": (i32, []),
@@ -179,6 +179,7 @@ RUNNER = {
     "d1h_audio_encode_pcm": (i32, [p, i32, C.POINTER(i32), p, p, C.POINTER(i32), p]),
     "d1h_vision_capacity": (i32, [p]),
     "d1h_model_layers": (i32, [p, i32]),
+    "d1h_gemm_ctx": (p, [p]),
     "d1e_create": (p, [p, p, p, C.POINTER(EngineConfig), p]),
     "d1e_destroy": (None, [p]),
     "d1e_submit": (C.c_longlong, [p, C.POINTER(Job)]),

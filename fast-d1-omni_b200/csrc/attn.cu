@@ -249,10 +249,10 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 }
 
 // ---------------------------------------------------------------------------------------------- tcgen05 form
-// Persistent CTAs (one per SM) loop over units = (256-query block, head): the reference's work list holds 64-row
-// tiles, so a unit starts at every item whose first row is a multiple of 256 and the other items are skipped (the
-// list must cover every tile, as the runner's does). A unit is two 128-row query tiles that share each K/V tile,
-// one per softmax warpgroup.
+// Persistent CTAs (one per SM) loop over units = (256-query block, head). A unit starts at every work item whose
+// first row is a multiple of 256; other items are skipped, so the reference's list of 64-row tiles works as it is
+// (it must cover every tile) and the runners pass one item per 256-row block. A unit is two 128-row query tiles
+// that share each K/V tile, one per softmax warpgroup.
 //
 // The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM and
 // two P buffers in shared memory, so S(j+2) is issued as soon as P(j) is written and the softmax never waits for
@@ -343,21 +343,28 @@ struct Unit {
     int q0, h, nt;
     bool two;  // the second 128-row tile has queries
 };
-__device__ __forceinline__ bool unit_at(const FaTcArgs& a, int u, Unit& out) {
-    const int2 wi = a.work[u / a.heads];
-    if (wi.y % TQU) return false;
-    out.s = a.seqs[wi.x];
-    out.q0 = wi.y;
-    out.h = u % a.heads;
-    out.nt = (out.s.ext_len + out.s.kv_len + TKV - 1) / TKV;
-    out.two = out.s.q_len > out.q0 + TQ;
-    return out.nt > 0 && out.s.q_len > out.q0;  // units with no keys or no queries are skipped by every role
+// This CTA's next unit at or after candidate u (its candidates are u, u + gridDim.x, ...); false when none is left.
+// Every role walks the same sequence.
+__device__ __forceinline__ bool next_unit(const FaTcArgs& a, int& u, Unit& out) {
+    for (; u < a.n_units; u += gridDim.x) {
+        const int2 wi = a.work[u / a.heads];
+        if (wi.y % TQU) continue;
+        out.s = a.seqs[wi.x];
+        out.q0 = wi.y;
+        out.h = u % a.heads;
+        out.nt = (out.s.ext_len + out.s.kv_len + TKV - 1) / TKV;
+        out.two = out.s.q_len > out.q0 + TQ;
+        if (out.nt > 0 && out.s.q_len > out.q0) return true;  // units with no keys or no queries are skipped
+    }
+    return false;
 }
 
 constexpr int T_LOADERS = 3;             // loader warps (8, 10, 11): K/V copy issue is instruction-bound
 constexpr int T_THREADS = 384;
 
-__global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a) {
+__global__ void __launch_bounds__(T_THREADS, 1)
+    k_flash_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < T_QSLOTS; i++) {
-            mbar_init(bar(B_QFULL + i), 32 * T_LOADERS);
+            mbar_init(bar(B_QFULL + i), 1);
             mbar_init(bar(B_QEMPTY + i), 1);
         }
         for (int i = 0; i < T_KVSTAGES; i++) {
@@ -395,6 +402,11 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
         *abort_flag = 0;
         fence_mbar_init();
     }
+    if (warp == 8 && lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
     if (warp == 9) {
         tmem_alloc(smem_u32(tmem_slot), T_TMEM_COLS);
         tmem_relinquish();
@@ -407,31 +419,34 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
 
     if (warp == 8 || warp >= 10) {
         // ------------------------------------------------------------------ loaders (warps 8, 10, 11)
+        // Q tiles and K/V tiles of local keys come in by TMA, issued by one thread (warp 8, lane 0) into the
+        // 128-byte-swizzled layouts the MMAs read. A K/V tile with prefix keys (their rows live in a per-sequence
+        // buffer) or with keys past the sequence end (they must read as zeros) is copied by all three loader warps
+        // with cp.async instead; each lane's copies complete the stage's barrier by themselves
+        // (cp.async.mbarrier.arrive.noinc counts the lane once its earlier copies have landed). A TMA stage
+        // completes on its byte count plus the other 95 lanes' plain arrivals, so both kinds use one barrier count.
         const int lt = (warp == 8 ? 0 : warp - 9) * 32 + lane;  // loader thread 0 .. 32 * T_LOADERS - 1
-        // Each lane's copies complete the stage's barrier by themselves (cp.async.mbarrier.arrive.noinc: the
-        // barrier counts the lane once all of its earlier cp.async have landed), so the loader only ever waits for
-        // free slots.
+        const bool issuer = warp == 8 && lane == 0;
         auto landed_arrive = [&](uint32_t b) {
             asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(b) : "memory");
         };
         int qi = 0, ki = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
-            Unit un;
-            if (!unit_at(a, u, un)) continue;
+        Unit un;
+        for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
             const int g = un.h / a.group, total = un.s.ext_len + un.s.kv_len;
             const int qs = qi % T_QSLOTS;
-            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1, abort_flag))))
-                break;
-            uint8_t* dq = sQ + qs * 2 * T_QT_BYTES;
-            for (int c = lt; c < (un.two ? 2 : 1) * TQ * 8; c += 32 * T_LOADERS) {
-                const int r = c >> 3, ch = c & 7;  // r < 256: tile r / 128, row r % 128
-                const bool v = un.q0 + r < un.s.q_len;
-                const __half* src = v ? a.Q + (size_t)(un.s.q_start + un.q0 + r) * a.ldq + un.h * 64 + ch * 8 : a.Q;
-                cp_async16z(smem_u32(dq + (r >> 7) * T_QT_BYTES + (r & 127) * 128 + ((ch ^ (r & 7)) << 4)), src,
-                            v ? 16 : 0);
+            if (warp == 8) {
+                if (!(ok = __all_sync(D1_FULL_MASK,
+                                      mbar_wait(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1, abort_flag))))
+                    break;
+                if (issuer) {
+                    const uint32_t dq = smem_u32(sQ + qs * 2 * T_QT_BYTES);
+                    mbar_arrive_expect_tx(bar(B_QFULL + qs), (un.two ? 2 : 1) * T_QT_BYTES);
+                    tma_load_2d(dq, &tmQ, un.h * 64, un.s.q_start + un.q0, bar(B_QFULL + qs));
+                    if (un.two) tma_load_2d(dq + T_QT_BYTES, &tmQ, un.h * 64, un.s.q_start + un.q0 + TQ, bar(B_QFULL + qs));
+                }
             }
-            landed_arrive(bar(B_QFULL + qs));
             qi++;
             for (int j = 0; j < un.nt; j++) {
                 const int st = ki % T_KVSTAGES;
@@ -440,40 +455,59 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
                     break;
                 uint8_t* dK = sKV + st * 2 * T_KV_BYTES;
                 uint8_t* dV = dK + T_KV_BYTES;
-                for (int c = lt; c < TKV * 8; c += 32 * T_LOADERS) {
-                    const int r = c >> 3, ch = c & 7;
-                    const int key = j * TKV + r;
-                    const __half *srck = a.K, *srcv = a.V;
-                    int bytes = 0;
-                    if (key < un.s.ext_len) {
-                        srck = un.s.ext_k + (size_t)key * a.ext_ld + g * 64 + ch * 8;
-                        srcv = un.s.ext_v + (size_t)key * a.ext_ld + g * 64 + ch * 8;
-                        bytes = 16;
-                    } else if (key < total) {
-                        const size_t row = (size_t)(un.s.kv_start + key - un.s.ext_len) * a.ldkv + g * 64 + ch * 8;
-                        srck = a.K + row;
-                        srcv = a.V + row;
-                        bytes = 16;
+                const int key0 = j * TKV;
+                if (key0 >= un.s.ext_len && key0 + TKV <= total) {
+                    if (issuer) {
+                        const int row = un.s.kv_start + key0 - un.s.ext_len;
+                        mbar_arrive_expect_tx(bar(B_KVFULL + st), 2 * T_KV_BYTES);
+                        tma_load_2d(smem_u32(dK), &tmK, g * 64, row, bar(B_KVFULL + st));
+                        tma_load_2d(smem_u32(dV), &tmV, g * 64, row, bar(B_KVFULL + st));
+                    } else {
+                        mbar_arrive(bar(B_KVFULL + st));
                     }
-                    const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
-                    cp_async16z(smem_u32(dK + off), srck, bytes);
-                    cp_async16z(smem_u32(dV + off), srcv, bytes);
+                } else {
+                    for (int c = lt; c < TKV * 8; c += 32 * T_LOADERS) {
+                        const int r = c >> 3, ch = c & 7;
+                        const int key = key0 + r;
+                        const __half *srck = a.K, *srcv = a.V;
+                        int bytes = 0;
+                        if (key < un.s.ext_len) {
+                            srck = un.s.ext_k + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                            srcv = un.s.ext_v + (size_t)key * a.ext_ld + g * 64 + ch * 8;
+                            bytes = 16;
+                        } else if (key < total) {
+                            const size_t row = (size_t)(un.s.kv_start + key - un.s.ext_len) * a.ldkv + g * 64 + ch * 8;
+                            srck = a.K + row;
+                            srcv = a.V + row;
+                            bytes = 16;
+                        }
+                        const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
+                        cp_async16z(smem_u32(dK + off), srck, bytes);
+                        cp_async16z(smem_u32(dV + off), srcv, bytes);
+                    }
+                    landed_arrive(bar(B_KVFULL + st));
                 }
-                landed_arrive(bar(B_KVFULL + st));
                 ki++;
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // nothing in flight when the CTA exits
         if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitEmpty);
+        if (issuer) {
+            // TMA copies still in flight (only after an abort) land before the CTA exits: wait (bounded) for the
+            // last use of every stage and Q slot
+            for (int i = ki > T_KVSTAGES ? ki - T_KVSTAGES : 0; i < ki; i++)
+                if (!mbar_wait_timed2(bar(B_KVFULL + i % T_KVSTAGES), (i / T_KVSTAGES) & 1)) break;
+            for (int i = qi > T_QSLOTS ? qi - T_QSLOTS : 0; i < qi; i++)
+                if (!mbar_wait_timed2(bar(B_QFULL + i % T_QSLOTS), (i / T_QSLOTS) & 1)) break;
+        }
     } else if (warp == 9) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             int cnt[2] = {0, 0}, units[2] = {0, 0};  // tiles and units given to each warpgroup so far
             int qi = 0, ki = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
-                Unit un;
-                if (!unit_at(a, u, un)) continue;
+            Unit un;
+            for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
                 const int nw = un.two ? 2 : 1;
                 const int qs = qi % T_QSLOTS;
                 if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
@@ -562,9 +596,9 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
         const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
         int cnt = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
-            Unit un;
-            if (!unit_at(a, u, un) || (w == 1 && !un.two)) continue;
+        Unit un;
+        for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
+            if (w == 1 && !un.two) continue;
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
@@ -686,7 +720,21 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_flash_attn_tc(const FaTcArgs a
     }
 }
 
-int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
+// A 2-D fp16 tensor map over rows x cols (row pitch ld elements) with 64-column x box_rows boxes in the 128-byte
+// swizzle; rows past `rows` read as zeros.
+bool attn_tmap(CUtensorMap* m, const void* base, int cols, int rows, int ld, uint32_t box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_fa_tc(FaTcArgs& a, int n_work, int heads, int q_rows, int kv_rows, cudaStream_t st) {
     static unsigned long long attr_done = 0;
     static int sms[64] = {};
     int dev = 0;
@@ -700,8 +748,13 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, cudaStream_t st) {
     }
     a.n_units = n_work * heads;
     a.heads = heads;
+    CUtensorMap tq, tk, tv;
+    const int kv_cols = heads / a.group * 64;
+    if (!attn_tmap(&tq, a.Q, heads * 64, q_rows, a.ldq, TQ) || !attn_tmap(&tk, a.K, kv_cols, kv_rows, a.ldkv, TKV) ||
+        !attn_tmap(&tv, a.V, kv_cols, kv_rows, a.ldkv, TKV))
+        return -1;
     const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
-    launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, a);
+    launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, tq, tk, tv, a);
     return (int)cudaGetLastError();
 }
 
@@ -728,9 +781,10 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
 
 extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
                                 d1_half* O, int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads,
-                                int group, float scale, cudaStream_t st) {
+                                int group, float scale, int q_rows, int kv_rows, cudaStream_t st) {
     if (n_work <= 0) return n_work == 0 ? 0 : -1;
-    if (heads <= 0 || group <= 0 || heads % group) return -1;
+    if (heads <= 0 || group <= 0 || heads % group || q_rows <= 0 || kv_rows <= 0) return -1;
+    if (ldq < heads * 64 || ldkv < heads / group * 64) return -1;
     if ((((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)O) & 15) || (ldq | ldkv | ldo | ext_ld) % 8) return -1;
     FaTcArgs t;
     t.Q = Q;
@@ -751,7 +805,7 @@ extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, con
     if (!err_addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&err_addr[dev & 63]), g_fa_err) != cudaSuccess)
         return -1;
     t.err = err_addr[dev & 63];
-    return launch_fa_tc(t, n_work, heads, st);
+    return launch_fa_tc(t, n_work, heads, q_rows, kv_rows, st);
 }
 
 extern "C" int d1_flash_attn_error(void) {

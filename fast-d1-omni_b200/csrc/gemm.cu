@@ -55,6 +55,7 @@ struct GemmArgs {
     int num_m, num_n;     // tile grid
     int num_tiles, num_kb;
     int num_units, kb_per; // split-K: work unit u = (tile u % num_tiles, K blocks [(u / num_tiles) * kb_per, +kb_per))
+    int sk, sk_full;       // sk = 1: stream-K schedule (unit_of), whole tiles below sk_full
     void* Y;
     int ldy;
     int y_f32;
@@ -65,6 +66,36 @@ struct GemmArgs {
     int n_fast;           // tile order: 1 walks N fastest (A, the larger operand, is read from DRAM once)
     int* err;
 };
+
+// The i-th work unit of worker p of P (a CTA, or a CTA pair): output tile and K-block range [kb0, kb1).
+// Uniform schedule (sk = 0): units p, p + P, ... of the split grid. Stream-K schedule (sk = 1, reduce-add epilogue
+// only): worker p first takes the whole tiles p, p + P, ... below sk_full (a multiple of P), then an equal,
+// contiguous share of the remaining tiles' K blocks (flattened tile by tile), one unit per tile its share touches;
+// the partial tiles meet in Y through the reduce-add. Every role of a worker walks the same sequence.
+__device__ __forceinline__ bool unit_of(const GemmArgs& a, int p, int P, int i, int& tile, int& kb0, int& kb1) {
+    if (!a.sk) {
+        const int u = p + i * P;
+        if (u >= a.num_units) return false;
+        tile = u % a.num_tiles;
+        kb0 = (u / a.num_tiles) * a.kb_per;
+        kb1 = min(a.num_kb, kb0 + a.kb_per);
+        return true;
+    }
+    const int nfull = a.sk_full / P;
+    if (i < nfull) {
+        tile = p + i * P;
+        kb0 = 0;
+        kb1 = a.num_kb;
+        return true;
+    }
+    const int rem = (a.num_tiles - a.sk_full) * a.num_kb;
+    const int s = (int)((long long)p * rem / P), e = (int)((long long)(p + 1) * rem / P);
+    const int t = s / a.num_kb + (i - nfull);
+    kb0 = i == nfull ? s - t * a.num_kb : 0;
+    kb1 = min(a.num_kb, e - t * a.num_kb);
+    tile = a.sk_full + t;
+    return kb1 > kb0;
+}
 
 // Tile index -> (row block, column block). The CTAs running at the same time share the operand that the order
 // repeats, so the larger operand is walked slowest: it streams from DRAM once while the smaller stays in L2.
@@ -265,9 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
-            for (int u = blockIdx.x; u < a.num_units && !aborted; u += gridDim.x) {
-                const int tile = u % a.num_tiles, kb0 = (u / a.num_tiles) * a.kb_per;
-                const int kb1 = min(a.num_kb, kb0 + a.kb_per);
+            int tile, kb0, kb1;
+            for (int i = 0; !aborted && unit_of(a, blockIdx.x, gridDim.x, i, tile, kb0, kb1); i++) {
                 int m_blk, n_blk;
                 tile_coords(a, tile, m_blk, n_blk);
                 for (int kb = kb0; kb < kb1; kb++) {
@@ -304,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0, it = 0;
             uint32_t phase = 0;
             bool aborted = false;
-            for (int u = blockIdx.x; u < a.num_units && !aborted; u += gridDim.x, it++) {
-                const int kb0 = (u / a.num_tiles) * a.kb_per, kb1 = min(a.num_kb, kb0 + a.kb_per);
+            int tile, kb0, kb1;
+            for (; !aborted && unit_of(a, blockIdx.x, gridDim.x, it, tile, kb0, kb1); it++) {
                 const int acc = it & 1;
                 const uint32_t acc_par = (it >> 1) & 1;
                 if (!mbar_wait(acce_bar(acc), acc_par ^ 1, abort_flag)) {
@@ -345,8 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sub = warp & 3;  // TMEM lane quarter (rows sub*32 .. +31) this warp may access
         uint8_t* stage0 = epi_smem + sub * 2 * EPI_BUF;
         int buf = 0, it = 0;
-        for (int u = blockIdx.x; u < a.num_units; u += gridDim.x, it++) {
-            const int tile = u % a.num_tiles;
+        int tile, kb0, kb1;
+        for (; unit_of(a, blockIdx.x, gridDim.x, it, tile, kb0, kb1); it++) {
             const int acc = it & 1;
             const uint32_t acc_par = (it >> 1) & 1;
             const bool ok = __all_sync(D1_FULL_MASK, mbar_wait(accf_bar(acc), acc_par, abort_flag));
@@ -511,9 +541,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int stage = 0;
             uint32_t phase = 0, issued = 0, issued_par = 0;
             bool aborted = false;
-            for (int u = pair; u < a.num_units && !aborted; u += npairs) {
-                const int tile = u % a.num_tiles, kb0 = (u / a.num_tiles) * a.kb_per;
-                const int kb1 = min(a.num_kb, kb0 + a.kb_per);
+            int tile, kb0, kb1;
+            for (int i = 0; !aborted && unit_of(a, pair, npairs, i, tile, kb0, kb1); i++) {
                 int m_blk, n_blk;
                 tile_coords(a, tile, m_blk, n_blk);
                 const int arow = m_blk * 2 * BM + (int)rank * BM;
@@ -549,8 +578,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int stage = 0, it = 0;
             uint32_t phase = 0;
             bool aborted = false;
-            for (int u = pair; u < a.num_units && !aborted; u += npairs, it++) {
-                const int kb0 = (u / a.num_tiles) * a.kb_per, kb1 = min(a.num_kb, kb0 + a.kb_per);
+            int tile, kb0, kb1;
+            for (; !aborted && unit_of(a, pair, npairs, it, tile, kb0, kb1); it++) {
                 const int acc = it & 1;
                 const uint32_t acc_par = (it >> 1) & 1;
                 if (!mbar_wait_cluster(acce_bar(acc), acc_par ^ 1, abort_flag)) {
@@ -592,8 +621,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         uint8_t* sbuf0 = epi_smem + ew * EPI_BUF;
         const uint32_t acce_leader0 = mapa_shared(acce_bar(0), 0), acce_leader1 = mapa_shared(acce_bar(1), 0);
         int sb = 0, it = 0;
-        for (int u = pair; u < a.num_units; u += npairs, it++) {
-            const int tile = u % a.num_tiles;
+        int tile, kb0, kb1;
+        for (; unit_of(a, pair, npairs, it, tile, kb0, kb1); it++) {
             const int acc = it & 1;
             const uint32_t acc_par = (it >> 1) & 1;
             const bool ok = __all_sync(D1_FULL_MASK, mbar_wait(accf_bar(acc), acc_par, abort_flag));
@@ -729,23 +758,6 @@ __global__ void k_fill_pattern(__half* p, size_t n, uint32_t seed) {
 
 // ---------------------------------------------------------------------------------------------- host side
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
 struct TmapKey {
     uintptr_t ptr;
     uint64_t inner, outer, stride;
@@ -831,6 +843,19 @@ bool get_tmap(Ctx* c, CUtensorMap* out, const void* base, uint64_t inner, uint64
     return true;
 }
 
+// Stream-K (reduce-add epilogue, no split requested): when whole tiles would leave the last wave of P workers
+// partly idle, every worker takes the same number of whole tiles and an equal share of the rest's K blocks.
+// Returns the number of workers to launch.
+int set_stream_k(GemmArgs& a, int P, int workers) {
+    a.sk = 0;
+    if (a.kb_per < a.num_kb || a.num_tiles % P == 0) return workers;
+    const int full = a.num_tiles / P * P;
+    if ((a.num_tiles - full) * a.num_kb < 4 * P) return workers;  // shares of under 4 K blocks: not worth it
+    a.sk = 1;
+    a.sk_full = full;
+    return P;
+}
+
 // Split-K: a.kb_per holds the requested split on entry; every split gets a non-empty K range.
 void set_split(GemmArgs& a) {
     int ks = a.kb_per < 1 ? 1 : a.kb_per;
@@ -876,7 +901,8 @@ int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, i
     set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    const int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
+    int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
+    if (EPI == EPI_ADD) grid = set_stream_k(a, c->num_sms, grid);
     launch_pdl(kern, grid, kThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
@@ -916,7 +942,8 @@ int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, 
     set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    const int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
+    int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
+    if (EPI == EPI_ADD) pairs = set_stream_k(a, c->pair_slots, pairs);
     launch_pdl(kern, 2 * pairs, kPairThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }

@@ -68,17 +68,23 @@ struct Kt {
     int (*gemm_bias_act)(void*, int, int, int, const d1_half*, int, const d1_half*, int, const float*, int, d1_half*,
                          int, cudaStream_t) = nullptr;
     int (*flash_attn_tc)(const d1_half*, int, const d1_half*, const d1_half*, int, int, d1_half*, int, const AttnSeq*,
-                         const int*, int, int, int, float, cudaStream_t) = nullptr;
+                         const int*, int, int, int, float, int, int, cudaStream_t) = nullptr;
     void (*lt_destroy)(void*) = nullptr;
 
     // Bidirectional attention over a complete work list (every 64-row tile of every sequence, as the runners
     // build it): the tcgen05 kernel when the library has it, fused forms are on and there are no biases to add
-    // on load; d1_flash_attn otherwise.
+    // on load; d1_flash_attn otherwise. q_rows / kv_rows bound the rows of Q and of K/V. The work list is the
+    // one work_items(spans, attn_step(fused)) builds.
+    int attn_step(bool fused) const { return fused && flash_attn_tc ? 256 : 64; }
     int attention(bool fused, const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
                   const float* bq, const float* bk, const float* bv, d1_half* O, int ldo, const AttnSeq* seqs,
-                  const int* work, int n_work, int heads, int group, float scale, cudaStream_t st) const {
-        if (fused && flash_attn_tc && !bq && !bk && !bv)
-            return flash_attn_tc(Q, ldq, K, V, ldkv, ext_ld, O, ldo, seqs, work, n_work, heads, group, scale, st);
+                  const int* work, int n_work, int heads, int group, float scale, int q_rows, int kv_rows,
+                  cudaStream_t st) const {
+        if (attn_step(fused) == 256) {
+            if (bq || bk || bv) return -1;  // fused runs fold the q/k/v biases into the QKV GEMM
+            return flash_attn_tc(Q, ldq, K, V, ldkv, ext_ld, O, ldo, seqs, work, n_work, heads, group, scale, q_rows,
+                                 kv_rows, st);
+        }
         return flash_attn(Q, ldq, K, V, ldkv, ext_ld, bq, bk, bv, O, ldo, seqs, work, n_work, heads, group, scale, st);
     }
 
@@ -279,14 +285,15 @@ struct MetaWriter {
 };
 
 // (seq index, query-tile start) for every 64-row query tile (src/model.rs:328-339), longest sequences first so
-// the long tiles start in the first wave.
-std::vector<int> work_items(const std::vector<std::pair<int, int>>& spans) {
+// the long tiles start in the first wave. step 256: one item per 256-row block, the list the tcgen05 attention
+// takes without scanning past the items it skips.
+std::vector<int> work_items(const std::vector<std::pair<int, int>>& spans, int step = 64) {
     std::vector<int> order(spans.size());
     for (size_t i = 0; i < order.size(); i++) order[i] = (int)i;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return spans[a].second > spans[b].second; });
     std::vector<int> w;
     for (int i : order)
-        for (int q = 0; q < spans[i].second; q += 64) {
+        for (int q = 0; q < spans[i].second; q += step) {
             w.push_back(i);
             w.push_back(q);
         }
@@ -338,7 +345,7 @@ int trunk(D1Model* m, D1Workspace* ws, int t, const int* tok_seq, const SeqInfo*
             m->launches += 2;
             CK(k.qk_norm_rope(big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq, seqs, idx, t, m->w.eps, st));
             CK(k.attention(m->fused, big, ld, big + D, big + D + KV_DIM, ld, KV_DIM, nullptr, nullptr, nullptr, act, D,
-                           attn[idx], work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, st));
+                           attn[idx], work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, t, t, st));
             if (prefix_pass && last) return 0;
             CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
         }
@@ -535,7 +542,7 @@ int d1h_launch_prefix(D1Model* m, D1Workspace* ws, int slot, const D1PrefixSeq* 
         for (auto& sp : spans) a.push_back(AttnSeq{sp.first, sp.second, sp.first, sp.second, 0, 0, nullptr, nullptr});
         attn.push_back(w.put(a));
     }
-    std::vector<int> work = work_items(spans);
+    std::vector<int> work = work_items(spans, m->k.attn_step(m->fused));
     const int* d_work = w.put(work);
     if (w.overflow) return fail("batch metadata exceeds 8 MB");
     if (cudaMemcpyAsync(ws->meta, ws->host_meta[slot], w.off, cudaMemcpyHostToDevice, st) != cudaSuccess)
@@ -618,7 +625,8 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
     }
     const AttnSeq* d_head_attn = w.put(head_attn);
     const AttnSeq* d_last_attn = w.put(last_attn);
-    std::vector<int> work = work_items(spans), mwork = work_items(mspans);
+    const int step = m->k.attn_step(m->fused);
+    std::vector<int> work = work_items(spans, step), mwork = work_items(mspans, step);
     const int* d_work = w.put(work);
     const int* d_mwork = w.put(mwork);
     const int* d_mrows = w.put(marker_rows);
@@ -659,7 +667,7 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
         if (li + 1 < nh) {
             m->launches++;
             CK(k.attention(m->fused, big, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, act, D, d_head_attn,
-                           d_work, n_work, HEADS, 1, 0.125f, st));
+                           d_work, n_work, HEADS, 1, 0.125f, t, t, st));
             CK(m->gemm(t, D, D, act, D, l.out, D, h, D, 1, 1.f, 1.f, st));
             m->launches++;
             CK(k.layernorm(h, l.out_b, 1.f, l.n2_w, l.n2_b, xn, nullptr, t, D, 1e-5f, st));
@@ -675,7 +683,7 @@ int d1h_launch_text(D1Model* m, D1Workspace* ws, int slot, const D1TextSeq* seqs
                 CK(k.gather_rows(big, ws->mq, d_mrows, nm, qkv_ld * 2, st));
                 CK(k.gather_rows(h, ws->mh, d_mrows, nm, D * 4, st));
                 CK(k.attention(m->fused, ws->mq, qkv_ld, big + D, big + 2 * D, qkv_ld, 0, bq, bk, bv, ws->mo, D,
-                               d_last_attn, d_mwork, n_mwork, HEADS, 1, 0.125f, st));
+                               d_last_attn, d_mwork, n_mwork, HEADS, 1, 0.125f, nm, t, st));
                 CK(m->gemm(nm, D, D, ws->mo, D, l.out, D, ws->mh, D, 1, 1.f, 1.f, st));
                 m->launches++;
                 CK(k.layernorm(ws->mh, l.out_b, 1.f, l.n2_w, l.n2_b, ws->mx, nullptr, nm, D, 1e-5f, st));
@@ -961,7 +969,7 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
         spans.push_back({off, n});
         off += n;
     }
-    std::vector<int> work = work_items(spans);
+    std::vector<int> work = work_items(spans, v->k.attn_step(v->fused));
     MetaWriter mw{v->host_meta, v->meta};
     const AttnSeq* d_seqs = mw.put(seqs);
     const int* d_work = mw.put(work);
@@ -1033,7 +1041,7 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
         L++;
         CK(k.attention(v->fused, big, 3 * VD, big + VD, big + 2 * VD, 3 * VD, 0, fold ? nullptr : l.qkv_b,
                        fold ? nullptr : l.qkv_b + VD, fold ? nullptr : l.qkv_b + 2 * VD, act, VD, d_seqs, d_work,
-                       n_work, VHEADS, 1, 0.125f, st));
+                       n_work, VHEADS, 1, 0.125f, ti, ti, st));
         CK(kt_gemm(k, v->lt, L, ti, VD, VD, act, VD, l.out, VD, h, VD, 1, 1.f, 1.f, st));
         L++;
         CK(k.layernorm(h, l.out_b, 1.f, l.ln2_w, l.ln2_b, xn, nullptr, ti, VD, eps, st));
@@ -1439,5 +1447,7 @@ int d1h_model_layers(const D1Model* m, int is_attn) {
     for (const auto& l : m->layers) n += (l.is_attn != 0) == (is_attn != 0);
     return n;
 }
+
+void* d1h_gemm_ctx(D1Model* m) { return m ? m->lt : nullptr; }
 
 }  // extern "C"

@@ -149,6 +149,18 @@ class TextModel:
             raise RuntimeError(f"d1h_tune failed: {self.L.d1h_last_error().decode()}")
         return n
 
+    def save_plans(self, path: str) -> None:
+        """Writes the tuned GEMM plans (d1_lt_save on the model's GEMM context)."""
+        if self.L.d1_lt_save(self.L.d1h_gemm_ctx(self.m), path.encode()) != 0:
+            raise RuntimeError(f"d1_lt_save failed for {path}")
+
+    def load_plans(self, path: str) -> int:
+        """Reads GEMM plans written by save_plans for this build; returns how many were loaded."""
+        n = self.L.d1_lt_load(self.L.d1h_gemm_ctx(self.m), path.encode())
+        if n < 0:
+            raise RuntimeError(f"d1_lt_load failed for {path} ({n}: missing file or another build)")
+        return n
+
     @property
     def launches(self) -> int:
         return int(self.L.d1h_launch_count(self.m))

@@ -280,6 +280,9 @@ int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const fl
 int d1h_vision_capacity(const D1Vision* v);
 /* Number of attention (is_attn = 1) or conv (is_attn = 0) trunk layers of the model. */
 int d1h_model_layers(const D1Model* m, int is_attn);
+/* The model's GEMM context (the ctx of d1_lt_*): d1_lt_save / d1_lt_load keep its tuned plans across runs, as the
+ * reference's engine keeps its cuBLASLt plans (src/engine.rs:528-616). */
+void* d1h_gemm_ctx(D1Model* m);
 
 /* ------------------------------------------------------------------------------------------------ engine
  * Continuous batching over one device's runners (src/engine.rs:149-525): requests (jobs) of question rows and

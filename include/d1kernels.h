@@ -214,12 +214,16 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
 int d1_lt_error(void* ctx);
 
 /* extension — d1_flash_attn without biases on tcgen05 tensor cores (S and O in TMEM); same arguments and result
- * as d1_flash_attn with bq = bk = bv = NULL, for a work list that covers every 64-row tile of every sequence (as
- * src/model.rs builds it): the kernel works in 256-row blocks, each starting at an item whose q0 is a multiple of
- * 256. Pointers 16-byte aligned, leading dimensions multiples of 8. */
+ * as d1_flash_attn with bq = bk = bv = NULL. The kernel works in 256-row blocks, each starting at a work item whose
+ * q0 is a multiple of 256 (other items are ignored): the work list must hold such an item for every 256-row block
+ * of every sequence — a list of every 64-row tile (as src/model.rs builds it) does, and a list of only the
+ * 256-row block starts is the cheaper form. Pointers 16-byte aligned, leading dimensions multiples of 8. q_rows / kv_rows: rows of Q / of K and V that
+ * may be read (every sequence's q_start + q_len <= q_rows, kv_start + kv_len <= kv_rows); query and local key
+ * tiles are fetched by TMA, which reads whole 128-row / 64-row tiles within those bounds (rows of other sequences
+ * are read but never used; rows of K and V inside the bounds must hold finite values). */
 int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld, d1_half* O,
                      int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads, int group, float scale,
-                     cudaStream_t stream);
+                     int q_rows, int kv_rows, cudaStream_t stream);
 
 /* extension — reads and clears the attention kernels' device error word (nonzero: a kernel gave up on a bounded
  * wait and returned early; its output is undefined). */

@@ -19,8 +19,9 @@ def P(t):
     return C.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def attn_meta(pkg, seqs, ext=None):
-    """seqs: [(q_start, q_len, kv_start, kv_len)]; ext: per seq None or (k tensor, v tensor) [ext_len, ext_ld]."""
+def attn_meta(pkg, seqs, ext=None, step=64):
+    """seqs: [(q_start, q_len, kv_start, kv_len)]; ext: per seq None or (k tensor, v tensor) [ext_len, ext_ld];
+    step: rows per work item (64: every tile, as the reference builds the list; 256: the tcgen05 kernel's blocks)."""
     arr = (pkg.abi.AttnSeq * len(seqs))()
     for i, (qs, ql, ks, kl) in enumerate(seqs):
         arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = qs, ql, ks, kl
@@ -30,13 +31,14 @@ def attn_meta(pkg, seqs, ext=None):
     meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
     work = []
     for i, (qs, ql, ks, kl) in enumerate(seqs):
-        work += [(i, q) for q in range(0, ql, 64)]
+        work += [(i, q) for q in range(0, ql, step)]
     w = torch.tensor(np.asarray(work, np.int32).reshape(-1), device="cuda")
     return meta, w, len(work)
 
 
-def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, ext_ld=0, q_rows=None, tc=False):
-    meta, work, n_work = attn_meta(pkg, seqs, ext)
+def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, ext_ld=0, q_rows=None, tc=False,
+        step=64):
+    meta, work, n_work = attn_meta(pkg, seqs, ext, step)
     rows = q_rows if q_rows is not None else Q.shape[0]
     O_ = torch.zeros(rows, heads * 64, dtype=torch.float16, device="cuda")
     bq, bk, bv = bias if bias is not None else (None, None, None)
@@ -44,7 +46,7 @@ def run(lib, pkg, Q, ldq, K, V, ldkv, seqs, heads, group, bias=None, ext=None, e
     if tc:  # the tcgen05 form (extension), bias-free only
         assert bias is None
         r = lib.d1_flash_attn_tc(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(O_), heads * 64, P(meta), P(work), n_work,
-                                 heads, group, 0.125, st)
+                                 heads, group, 0.125, Q.shape[0], K.shape[0], st)
     else:
         r = lib.d1_flash_attn(P(Q), ldq, P(K), P(V), ldkv, ext_ld, P(bq), P(bk), P(bv), P(O_), heads * 64, P(meta),
                               P(work), n_work, heads, group, 0.125, st)
@@ -103,11 +105,13 @@ def test_edge_lengths_mha_bias(pkg, gpu_lib, ref_lib, lens):
     assert np.abs(got - ref_k).max() <= 4e-3
 
 
+@pytest.mark.parametrize("step", [64, 256])
 @pytest.mark.parametrize("group", [1, 2])
 @pytest.mark.parametrize("lens", [[1], [63, 64, 65], [127, 128, 129, 255, 256, 257], [300, 1, 513, 2]])
-def test_tc_edge_lengths(pkg, gpu_lib, lens, group):
+def test_tc_edge_lengths(pkg, gpu_lib, lens, group, step):
     """d1_flash_attn_tc on ragged lengths around its 128-row tiles and 256-row units (units whose second tile is
-    empty, single-tile units, partial key tiles), MHA and GQA, against the oracle and the mma.sync kernel."""
+    empty, single-tile units, partial key tiles), MHA and GQA, with the reference's 64-row work list and the
+    256-row one, against the oracle and the mma.sync kernel."""
     rng = np.random.default_rng(sum(lens) + group)
     T = sum(lens)
     ld = 1024 + 2 * 1024 // group
@@ -119,7 +123,7 @@ def test_tc_edge_lengths(pkg, gpu_lib, lens, group):
     d = torch.from_numpy(qkv).cuda()
     kvw = 1024 // group
     K, V = d[:, 1024:], d[:, 1024 + kvw:]
-    got_tc = run(gpu_lib, pkg, d, ld, K, V, ld, spans, 16, group, tc=True)
+    got_tc = run(gpu_lib, pkg, d, ld, K, V, ld, spans, 16, group, tc=True, step=step)
     got = run(gpu_lib, pkg, d, ld, K, V, ld, spans, 16, group)
     q = qkv.astype(np.float32)
     want = O.attention(q[:, :1024], q[:, 1024:1024 + kvw], q[:, 1024 + kvw:], spans, 16, group, 0.125)
@@ -172,10 +176,13 @@ def test_marker_queries(pkg, gpu_lib, ref_lib):
     assert np.abs(got - ref_k).max() <= 4e-3
 
 
-def test_prefix_keys(pkg, gpu_lib, ref_lib):
-    """Text after a media prefix: the prefix's cached K/V ([ext_len][512]) come before the local keys."""
-    rng = np.random.default_rng(12)
-    lens, ext_lens = [70, 5], [129, 64]
+@pytest.mark.parametrize("lens", [[70, 5], [300, 200]])
+def test_prefix_keys(pkg, gpu_lib, ref_lib, lens):
+    """Text after a media prefix: the prefix's cached K/V ([ext_len][512]) come before the local keys. The longer
+    case gives the tcgen05 kernel every kind of key tile: prefix only, prefix + local, whole local tiles (TMA) and a
+    partial last tile."""
+    rng = np.random.default_rng(12 + lens[0])
+    ext_lens = [129, 64]
     T = sum(lens)
     qkv = rng.standard_normal((T, 2048)).astype(np.float16)
     ext_np = [(rng.standard_normal((e, 512)).astype(np.float16), rng.standard_normal((e, 512)).astype(np.float16))
