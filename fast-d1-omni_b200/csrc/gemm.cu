@@ -55,7 +55,6 @@ struct GemmArgs {
     int num_m, num_n;     // tile grid
     int num_tiles, num_kb;
     int num_units, kb_per; // split-K: work unit u = (tile u % num_tiles, K blocks [(u / num_tiles) * kb_per, +kb_per))
-    int sk, sk_full;       // sk = 1: stream-K schedule (unit_of), whole tiles below sk_full
     void* Y;
     int ldy;
     int y_f32;
@@ -67,34 +66,17 @@ struct GemmArgs {
     int* err;
 };
 
-// The i-th work unit of worker p of P (a CTA, or a CTA pair): output tile and K-block range [kb0, kb1).
-// Uniform schedule (sk = 0): units p, p + P, ... of the split grid. Stream-K schedule (sk = 1, reduce-add epilogue
-// only): worker p first takes the whole tiles p, p + P, ... below sk_full (a multiple of P), then an equal,
-// contiguous share of the remaining tiles' K blocks (flattened tile by tile), one unit per tile its share touches;
-// the partial tiles meet in Y through the reduce-add. Every role of a worker walks the same sequence.
+// The i-th work unit of worker p of P (a CTA, or a CTA pair): units p, p + P, ... of the split grid, each an output
+// tile and its K-block range [kb0, kb1). Every role of a worker walks the same sequence. (A stream-K schedule,
+// whole tiles plus equal shares of the last wave's K blocks meeting in Y through the reduce-add, measured 2% slower
+// on the forward than this one: its extra reduce-add traffic costs more than the idle part of the last wave.)
 __device__ __forceinline__ bool unit_of(const GemmArgs& a, int p, int P, int i, int& tile, int& kb0, int& kb1) {
-    if (!a.sk) {
-        const int u = p + i * P;
-        if (u >= a.num_units) return false;
-        tile = u % a.num_tiles;
-        kb0 = (u / a.num_tiles) * a.kb_per;
-        kb1 = min(a.num_kb, kb0 + a.kb_per);
-        return true;
-    }
-    const int nfull = a.sk_full / P;
-    if (i < nfull) {
-        tile = p + i * P;
-        kb0 = 0;
-        kb1 = a.num_kb;
-        return true;
-    }
-    const int rem = (a.num_tiles - a.sk_full) * a.num_kb;
-    const int s = (int)((long long)p * rem / P), e = (int)((long long)(p + 1) * rem / P);
-    const int t = s / a.num_kb + (i - nfull);
-    kb0 = i == nfull ? s - t * a.num_kb : 0;
-    kb1 = min(a.num_kb, e - t * a.num_kb);
-    tile = a.sk_full + t;
-    return kb1 > kb0;
+    const int u = p + i * P;
+    if (u >= a.num_units) return false;
+    tile = u % a.num_tiles;
+    kb0 = (u / a.num_tiles) * a.kb_per;
+    kb1 = min(a.num_kb, kb0 + a.kb_per);
+    return true;
 }
 
 // Tile index -> (row block, column block). The CTAs running at the same time share the operand that the order
@@ -843,19 +825,6 @@ bool get_tmap(Ctx* c, CUtensorMap* out, const void* base, uint64_t inner, uint64
     return true;
 }
 
-// Stream-K (reduce-add epilogue, no split requested): when whole tiles would leave the last wave of P workers
-// partly idle, every worker takes the same number of whole tiles and an equal share of the rest's K blocks.
-// Returns the number of workers to launch.
-int set_stream_k(GemmArgs& a, int P, int workers) {
-    a.sk = 0;
-    if (a.kb_per < a.num_kb || a.num_tiles % P == 0) return workers;
-    const int full = a.num_tiles / P * P;
-    if ((a.num_tiles - full) * a.num_kb < 4 * P) return workers;  // shares of under 4 K blocks: not worth it
-    a.sk = 1;
-    a.sk_full = full;
-    return P;
-}
-
 // Split-K: a.kb_per holds the requested split on entry; every split gets a non-empty K range.
 void set_split(GemmArgs& a) {
     int ks = a.kb_per < 1 ? 1 : a.kb_per;
@@ -901,8 +870,7 @@ int launch_tc(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, i
     set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
-    if (EPI == EPI_ADD) grid = set_stream_k(a, c->num_sms, grid);
+    const int grid = a.num_units < c->num_sms ? a.num_units : c->num_sms;
     launch_pdl(kern, grid, kThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
@@ -942,8 +910,7 @@ int launch_tc2(Ctx* c, int bit, const void* X, int ldx, const void* W, int ldw, 
     set_split(a);
     a.n_fast = a.M > w_rows;
     a.err = c->d_err;
-    int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
-    if (EPI == EPI_ADD) pairs = set_stream_k(a, c->pair_slots, pairs);
+    const int pairs = a.num_units < c->pair_slots ? a.num_units : c->pair_slots;
     launch_pdl(kern, 2 * pairs, kPairThreads, S::BYTES, st, ta, tb, ty, a);
     return (int)cudaGetLastError();
 }
