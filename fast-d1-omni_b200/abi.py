@@ -142,6 +142,7 @@ KERNELS = {
 EXTENSIONS = {
     "d1_gemm_swiglu": (i32, [p, i32, i32, i32, p, i32, p, i32, p, i32, p]),
     "d1_gemm_bias_act": (i32, [p, i32, i32, i32, p, i32, p, i32, p, i32, p, i32, p]),
+    "d1_gemm_qk_norm_rope": (i32, [p, i32, i32, p, i32, p, i32, p, i32, i32, i32, p, p, p, p, p, f32, p]),
     "d1_lt_error": (i32, [p]),
     "d1_flash_attn_error": (i32, []),
     "d1_flash_attn_tc": (i32, [p, i32, p, p, i32, i32, p, i32, p, p, i32, i32, i32, f32, i32, i32, p]),

@@ -48,6 +48,7 @@ enum Epi : int {
     EPI_SWIGLU = 2,    // out = silu(half(g)) * half(u), fp16
     EPI_BIAS_ACT = 3,  // Y = act(half(acc) + bias), fp16
     EPI_DIRECT = 4,    // any alpha/beta, direct stores (strides or alignment the tensor maps cannot take)
+    EPI_QKROPE = 5,    // fp16 Y = [q | k | v] heads, q and k heads RMS-normed and rotated (d1_qk_norm_rope)
 };
 
 struct GemmArgs {
@@ -64,6 +65,14 @@ struct GemmArgs {
     int F;                // SwiGLU: output columns (rows [0,F) of W are gate, [F,2F) up)
     int n_fast;           // tile order: 1 walks N fastest (A, the larger operand, is read from DRAM once)
     int* err;
+    // EPI_QKROPE: columns [0, q_cols) are query heads, [q_cols, qk_cols) key heads, the rest value heads
+    int q_cols, qk_cols;
+    float eps;
+    const float* qn;
+    const float* kn;
+    const float* rope;     // (cos, sin) [pos][32]
+    const int* tok_seq;
+    const SeqInfo* seqs;
 };
 
 // The i-th work unit of worker p of P (a CTA, or a CTA pair): units p, p + P, ... of the split grid, each an output
@@ -155,6 +164,67 @@ __device__ __forceinline__ void stage_f(uint8_t* buf, int t, const float* v) {
     for (int j = 0; j < 8; j++)
         *reinterpret_cast<float4*>(buf + t * 128 + ((j ^ (t & 7)) << 4)) =
             make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// RoPE position of output row `row` (EPI_QKROPE): its place in its sequence plus the sequence's position offset.
+__device__ __forceinline__ int qkrope_pos(const GemmArgs& a, int row) {
+    if (row >= a.M) return 0;
+    const SeqInfo& s = a.seqs[__ldg(a.tok_seq + row)];
+    return row - s.start + s.pos_off;
+}
+
+// One 64-column head of the row this thread owns (TMEM lane), from the fp32 accumulator: the GEMM output rounded to
+// fp16, as the unfused path stores it, then for query and key heads the arithmetic of k_qk_norm_rope8 term for term
+// (cuda/kernels.cu:263-303): RMS over the head's 64 values (eight 8-value chains, then a pairwise tree), the q/k
+// norm weight, rotate-half RoPE at `pos` (pairs l, l + 32). Value heads are only rounded.
+__device__ __forceinline__ void qkrope_head(const GemmArgs& a, uint32_t taddr, int col, int pos, float (&o)[64]) {
+    {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(taddr, r0);
+        tmem_ld32(taddr + 32, r1);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            o[i] = round_h(__uint_as_float(r0[i]));
+            o[32 + i] = round_h(__uint_as_float(r1[i]));
+        }
+    }
+    if (col >= a.qk_cols) return;
+    float c[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) s += o[8 * k + i] * o[8 * k + i];
+        c[k] = s;
+    }
+    const float ss = ((c[0] + c[1]) + (c[2] + c[3])) + ((c[4] + c[5]) + (c[6] + c[7]));
+    const float r = rsqrtf(ss / 64.f + a.eps);
+    // weights and (cos, sin) are loaded four float4 at a time (the empty asm statements keep the compiler from
+    // hoisting all 32 loads at once, which would not fit the pair kernel's registers)
+    const float4* w4 = reinterpret_cast<const float4*>(col < a.q_cols ? a.qn : a.kn);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        if ((i & 3) == 0) asm volatile("" ::: "memory");
+        const float4 w = __ldg(w4 + i);
+        o[4 * i] = o[4 * i] * r * w.x;
+        o[4 * i + 1] = o[4 * i + 1] * r * w.y;
+        o[4 * i + 2] = o[4 * i + 2] * r * w.z;
+        o[4 * i + 3] = o[4 * i + 3] * r * w.w;
+    }
+    const float4* cs4 = reinterpret_cast<const float4*>(a.rope + (size_t)pos * 64);
+#pragma unroll
+    for (int p2 = 0; p2 < 16; p2++) {
+        if ((p2 & 3) == 0) asm volatile("" ::: "memory");
+        const float4 t = __ldg(cs4 + p2);  // (cos, sin) of pairs 2 p2 and 2 p2 + 1
+        float y0 = o[2 * p2], y1 = o[2 * p2 + 32];
+        o[2 * p2] = y0 * t.x - y1 * t.y;
+        o[2 * p2 + 32] = y1 * t.x + y0 * t.y;
+        y0 = o[2 * p2 + 1];
+        y1 = o[2 * p2 + 33];
+        o[2 * p2 + 1] = y0 * t.z - y1 * t.w;
+        o[2 * p2 + 33] = y1 * t.z + y0 * t.w;
+    }
 }
 
 // v = act(half(acc) + bias) for one 32-column chunk: bias read as float4 when aligned, the activation chosen once
@@ -372,55 +442,82 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = m_blk * BM + sub * 32;
             const int col_base = n_blk * OUT_COLS;
             const uint32_t tbase = tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(acc * BN);
+            if constexpr (EPI == EPI_QKROPE) {  // one 64-column head at a time: two 32x32 fp16 blocks per buffer
+                const int pos = qkrope_pos(a, row0 + lane);
 #pragma unroll 1
-            for (int c0 = 0; c0 < OUT_COLS; c0 += 32) {
-                float v[32];
-                {
-                    uint32_t r[32];
-                    tmem_ld32(tbase + c0, r);
-                    if (EPI == EPI_SWIGLU) {
-                        uint32_t u[32];
-                        tmem_ld32(tbase + BN / 2 + c0, u);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; i++)
-                            v[i] = silu(round_h(__uint_as_float(r[i]))) * round_h(__uint_as_float(u[i]));
-                    } else {
-                        tc_wait_ld();
-                        if (EPI == EPI_BIAS_ACT) {
-                            bias_act32(a, col_base + c0, r, v);
+                for (int h0 = 0; h0 < OUT_COLS; h0 += 64) {
+                    float o[64];
+                    qkrope_head(a, tbase + h0, col_base + h0, pos, o);
+                    if (h0 + 64 >= OUT_COLS) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(acce_bar(acc));
+                    }
+                    uint8_t* sbuf = stage0 + buf * EPI_BUF;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                    stage_h(sbuf, lane, o);
+                    stage_h(sbuf + EPI_BUF / 2, lane, o + 32);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmY, smem_u32(sbuf), col_base + h0, row0);
+                        tma_store_2d(&tmY, smem_u32(sbuf) + EPI_BUF / 2, col_base + h0 + 32, row0);
+                        bulk_commit();
+                    }
+                    buf ^= 1;
+                }
+            } else {
+    #pragma unroll 1
+                for (int c0 = 0; c0 < OUT_COLS; c0 += 32) {
+                    float v[32];
+                    {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c0, r);
+                        if (EPI == EPI_SWIGLU) {
+                            uint32_t u[32];
+                            tmem_ld32(tbase + BN / 2 + c0, u);
+                            tc_wait_ld();
+    #pragma unroll
+                            for (int i = 0; i < 32; i++)
+                                v[i] = silu(round_h(__uint_as_float(r[i]))) * round_h(__uint_as_float(u[i]));
                         } else {
-#pragma unroll
-                            for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
+                            tc_wait_ld();
+                            if (EPI == EPI_BIAS_ACT) {
+                                bias_act32(a, col_base + c0, r, v);
+                            } else {
+    #pragma unroll
+                                for (int i = 0; i < 32; i++) v[i] = a.alpha * __uint_as_float(r[i]);
+                            }
                         }
                     }
-                }
-                if (c0 + 32 >= OUT_COLS) {  // last TMEM read of this tile: hand the accumulator back to the MMA
-                    tc_fence_before();
+                    if (c0 + 32 >= OUT_COLS) {  // last TMEM read of this tile: hand the accumulator back to the MMA
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(acce_bar(acc));
+                    }
+                    if (EPI == EPI_DIRECT) {
+                        direct_store(a, row0 + lane, col_base + c0, v);
+                        continue;
+                    }
+                    uint8_t* sbuf = stage0 + buf * EPI_BUF;
+                    if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(acce_bar(acc));
-                }
-                if (EPI == EPI_DIRECT) {
-                    direct_store(a, row0 + lane, col_base + c0, v);
-                    continue;
-                }
-                uint8_t* sbuf = stage0 + buf * EPI_BUF;
-                if (lane == 0) bulk_wait_read<1>();  // the store that last read this buffer is done with it
-                __syncwarp();
-                if (OUT32)
-                    stage_f(sbuf, lane, v);
-                else
-                    stage_h(sbuf, lane, v);
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (EPI == EPI_ADD)
-                        tma_add_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                    if (OUT32)
+                        stage_f(sbuf, lane, v);
                     else
-                        tma_store_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
-                    bulk_commit();
+                        stage_h(sbuf, lane, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (EPI == EPI_ADD)
+                            tma_add_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                        else
+                            tma_store_2d(&tmY, smem_u32(sbuf), col_base + c0, row0);
+                        bulk_commit();
+                    }
+                    buf ^= 1;
                 }
-                buf ^= 1;
             }
         }
         if (lane == 0) bulk_wait_read<0>();
@@ -467,7 +564,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     constexpr int SUBTILES = OUT32 ? 1 : 2;  // 32x32 output blocks per 4 KB staging buffer
     constexpr int SUB_BYTES = EPI_BUF / SUBTILES;
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair MMA: M=256 needs N % 16 == 0, 16..256");
-    static_assert(EPI != EPI_DIRECT, "the pair kernel only takes the TMA epilogues");
+    static_assert(EPI != EPI_DIRECT && EPI != EPI_QKROPE, "the pair kernel takes the TMA epilogues but QK-rope");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1142,6 +1239,44 @@ int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, 
         case CFG_1SM_128: return launch_tc<128, 6, EPI_BIAS_ACT, false>(c, 9, X, ldx, W, ldw, N, a, st) ? -1 : 0;
         case CFG_1SM_64: return launch_tc<64, 8, EPI_BIAS_ACT, false>(c, 23, X, ldx, W, ldw, N, a, st) ? -1 : 0;
         default: return launch_tc<256, 4, EPI_BIAS_ACT, false>(c, 10, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+    }
+}
+
+int d1_gemm_qk_norm_rope(void* ctx, int M, int K, const d1_half* X, int ldx, const d1_half* W, int ldw, d1_half* Y,
+                         int ldy, int H, int KVH, const float* qn, const float* kn, const float* rope,
+                         const int* tok_seq, const SeqInfo* seqs, float eps, cudaStream_t st) {
+    Ctx* c = (Ctx*)ctx;
+    if (!c || M < 0 || K <= 0 || H <= 0 || KVH <= 0 || !qn || !kn || !rope || !tok_seq || !seqs) return -1;
+    if ((reinterpret_cast<uintptr_t>(rope) | reinterpret_cast<uintptr_t>(qn) | reinterpret_cast<uintptr_t>(kn)) & 15)
+        return -1;  // read as float4
+    std::lock_guard<std::mutex> lock(c->mu);
+    const int N = (H + 2 * KVH) * 64;
+    if (M == 0) return 0;
+    if (!tc_ok(X, ldx, W, ldw, 0, K) || !tma_out_ok(Y, ldy, 0) || ldy < N) return -1;
+    GemmArgs a{};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.alpha = 1.f;
+    a.q_cols = H * 64;
+    a.qk_cols = (H + KVH) * 64;
+    a.eps = eps;
+    a.qn = qn;
+    a.kn = kn;
+    a.rope = rope;
+    a.tok_seq = tok_seq;
+    a.seqs = seqs;
+    // single-SM tiles only: the epilogue's 64-value heads fit the 1-SM kernel's registers (on par with the CTA pair
+    // for this shape on B200)
+    int cfg = default_cfg(c, M, N);
+    if (cfg == CFG_PAIR_256) cfg = CFG_1SM_256;
+    if (cfg == CFG_PAIR_128) cfg = CFG_1SM_128;
+    switch (cfg) {
+        case CFG_1SM_128: return launch_tc<128, 6, EPI_QKROPE, false>(c, 24, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        case CFG_1SM_64: return launch_tc<64, 8, EPI_QKROPE, false>(c, 25, X, ldx, W, ldw, N, a, st) ? -1 : 0;
+        default: return launch_tc<256, 4, EPI_QKROPE, false>(c, 26, X, ldx, W, ldw, N, a, st) ? -1 : 0;
     }
 }
 

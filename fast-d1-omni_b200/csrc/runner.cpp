@@ -69,6 +69,9 @@ struct Kt {
                          int, cudaStream_t) = nullptr;
     int (*flash_attn_tc)(const d1_half*, int, const d1_half*, const d1_half*, int, int, d1_half*, int, const AttnSeq*,
                          const int*, int, int, int, float, int, int, cudaStream_t) = nullptr;
+    int (*gemm_qk_rope)(void*, int, int, const d1_half*, int, const d1_half*, int, d1_half*, int, int, int,
+                        const float*, const float*, const float*, const int*, const SeqInfo*, float,
+                        cudaStream_t) = nullptr;
     void (*lt_destroy)(void*) = nullptr;
 
     // Bidirectional attention over a complete work list (every 64-row tile of every sequence, as the runners
@@ -110,6 +113,7 @@ struct Kt {
         gemm_swiglu = d1_gemm_swiglu;
         gemm_bias_act = d1_gemm_bias_act;
         flash_attn_tc = d1_flash_attn_tc;
+        gemm_qk_rope = d1_gemm_qk_norm_rope;
         lt_destroy = d1_lt_destroy;
         return true;
     }
@@ -139,6 +143,7 @@ struct Kt {
                sym(lt_tune, "d1_lt_tune") && sym(lt_bucket, "d1_lt_bucket") &&
                sym(lt_free_scratch, "d1_lt_free_scratch") && sym(gemm_swiglu, "d1_gemm_swiglu", false) &&
                sym(gemm_bias_act, "d1_gemm_bias_act", false) && sym(flash_attn_tc, "d1_flash_attn_tc", false) &&
+               sym(gemm_qk_rope, "d1_gemm_qk_norm_rope", false) &&
                sym(lt_destroy, "d1_lt_destroy", false);
     }
 };
@@ -341,9 +346,15 @@ int trunk(D1Model* m, D1Workspace* ws, int t, const int* tok_seq, const SeqInfo*
             CK(m->gemm(t, D, D, act, D, l.out_proj, D, h, D, 1, 1.f, 1.f, st));
         } else {
             const int ld = D + 2 * KV_DIM;
-            CK(m->gemm(t, ld, D, xn, D, l.qkv, D, big, ld, 0, 1.f, 0.f, st));
-            m->launches += 2;
-            CK(k.qk_norm_rope(big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq, seqs, idx, t, m->w.eps, st));
+            if (m->fused && k.gemm_qk_rope && !prefix_pass) {  // prefix passes also store K/V to the cache
+                m->launches += 2;
+                CK(k.gemm_qk_rope(m->lt, t, D, xn, D, l.qkv, D, big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq,
+                                  seqs, m->w.eps, st));
+            } else {
+                CK(m->gemm(t, ld, D, xn, D, l.qkv, D, big, ld, 0, 1.f, 0.f, st));
+                m->launches += 2;
+                CK(k.qk_norm_rope(big, ld, HEADS, KV_HEADS, l.qn, l.kn, m->rope, tok_seq, seqs, idx, t, m->w.eps, st));
+            }
             CK(k.attention(m->fused, big, ld, big + D, big + D + KV_DIM, ld, KV_DIM, nullptr, nullptr, nullptr, act, D,
                            attn[idx], work, n_work, HEADS, HEADS / KV_HEADS, 0.125f, t, t, st));
             if (prefix_pass && last) return 0;

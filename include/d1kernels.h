@@ -209,6 +209,15 @@ int d1_gemm_swiglu(void* ctx, int M, int F, int K, const d1_half* X, int ldx, co
 int d1_gemm_bias_act(void* ctx, int M, int N, int K, const d1_half* X, int ldx, const d1_half* W, int ldw,
                      const float* bias, int act, d1_half* Y, int ldy, cudaStream_t stream);
 
+/* extension — the attention layers' QKV projection with QK-norm + RoPE in the epilogue: Y = [q | k | v] (fp16,
+ * H + 2 KVH heads of 64 columns) = X . W^T, then q and k heads as d1_qk_norm_rope gives them (same arithmetic on the
+ * fp16-rounded GEMM output). Equal to d1_lt_gemm (fp16 out) followed by d1_qk_norm_rope (src/model.rs:376-381),
+ * except that seqs[].save_k / save_v are not written: prefix passes use the two calls. rope, qn and kn 16-byte
+ * aligned. */
+int d1_gemm_qk_norm_rope(void* ctx, int M, int K, const d1_half* X, int ldx, const d1_half* W, int ldw, d1_half* Y,
+                         int ldy, int H, int KVH, const float* qn, const float* kn, const float* rope,
+                         const int* tok_seq, const SeqInfo* seqs, float eps, cudaStream_t stream);
+
 /* extension — reads and clears the context's device error word: nonzero when a kernel of this library gave up
  * on a bounded wait (the kernel returns early instead of hanging; its output is then undefined). */
 int d1_lt_error(void* ctx);
@@ -217,10 +226,11 @@ int d1_lt_error(void* ctx);
  * as d1_flash_attn with bq = bk = bv = NULL. The kernel works in 256-row blocks, each starting at a work item whose
  * q0 is a multiple of 256 (other items are ignored): the work list must hold such an item for every 256-row block
  * of every sequence — a list of every 64-row tile (as src/model.rs builds it) does, and a list of only the
- * 256-row block starts is the cheaper form. Pointers 16-byte aligned, leading dimensions multiples of 8. q_rows / kv_rows: rows of Q / of K and V that
- * may be read (every sequence's q_start + q_len <= q_rows, kv_start + kv_len <= kv_rows); query and local key
- * tiles are fetched by TMA, which reads whole 128-row / 64-row tiles within those bounds (rows of other sequences
- * are read but never used; rows of K and V inside the bounds must hold finite values). */
+ * 256-row block starts is the cheaper form. Pointers 16-byte aligned, leading dimensions multiples of 8.
+ * q_rows / kv_rows: rows of Q / of K and V that may be read (every sequence's q_start + q_len <= q_rows,
+ * kv_start + kv_len <= kv_rows); query and local key tiles are fetched by TMA, which reads whole 128-row / 64-row
+ * tiles within those bounds (rows of other sequences are read but never used; rows of K and V inside the bounds
+ * must hold finite values). */
 int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld, d1_half* O,
                      int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads, int group, float scale,
                      int q_rows, int kv_rows, cudaStream_t stream);

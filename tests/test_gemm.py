@@ -206,3 +206,50 @@ def test_tune_save_load(gpu_lib, ctx, tmp_path):
     c2 = gpu_lib.d1_lt_init(0)
     assert gpu_lib.d1_lt_load(c2, path) >= 1
     gpu_lib.d1_lt_destroy(c2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [300, 8192])
+def test_qk_norm_rope_fused(pkg, gpu_lib, ctx, M):
+    """d1_gemm_qk_norm_rope == d1_lt_gemm(fp16) + d1_qk_norm_rope (src/model.rs:376-381) on ragged sequences with
+    position offsets (text after a media prefix); M 300 runs the small-tile kernel, M 8192 the 256-column one. The
+    epilogue repeats the kernel's arithmetic on the same fp16-rounded GEMM output, so the two agree to within one
+    fp16 rounding (different instruction scheduling may contract one multiply-add differently); both against the
+    oracle's fp32 QK-norm + RoPE of that output."""
+    from oracle import d1_oracle as O
+    rng = np.random.default_rng(20 + M)
+    H, KVH, K = 16, 8, 1024
+    N = (H + 2 * KVH) * 64
+    lens = [M // 3, M // 3 + 5, M - 2 * (M // 3) - 5]
+    pos_off = [0, 77, 4000]
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16)).cuda()
+    w = torch.from_numpy((rng.standard_normal((N, K)) * 0.03).astype(np.float16)).cuda()
+    qn = torch.from_numpy(rng.uniform(0.5, 1.5, 64).astype(np.float32)).cuda()
+    kn = torch.from_numpy(rng.uniform(0.5, 1.5, 64).astype(np.float32)).cuda()
+    rope_np = O.rope_table(1e6)
+    rope = torch.from_numpy(np.ascontiguousarray(rope_np, np.float32)).cuda()
+    arr = (pkg.abi.SeqInfo * len(lens))()
+    s = 0
+    for i, n in enumerate(lens):
+        arr[i].start, arr[i].len, arr[i].pos_off = s, n, pos_off[i]
+        s += n
+    seqs = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    tok = torch.from_numpy(np.concatenate([np.full(n, i, np.int32) for i, n in enumerate(lens)])).cuda()
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    assert gpu_lib.d1_gemm_qk_norm_rope(ctx, M, K, _p(x), K, _p(w), K, _p(y), N, H, KVH, _p(qn), _p(kn), _p(rope),
+                                        _p(tok), _p(seqs), 1e-5, st) == 0
+    y2 = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    run_gemm(gpu_lib, ctx, x, w, y2)
+    raw = y2.float().cpu().numpy()
+    assert gpu_lib.d1_qk_norm_rope(_p(y2), N, H, KVH, _p(qn), _p(kn), _p(rope), _p(tok), _p(seqs), 0, M, 1e-5,
+                                   st) == 0
+    torch.cuda.synchronize()
+    assert gpu_lib.d1_lt_error(ctx) == 0
+    a, b = y.float().cpu().numpy(), y2.float().cpu().numpy()
+    assert np.abs(a - b).max() <= 2.0 ** -10 * np.abs(b).max() + 1e-6 or \
+        (np.abs(a - b) <= np.abs(b) * 2.0 ** -10 + 1e-4).all()
+    assert np.array_equal(a[:, (H + KVH) * 64:], raw[:, (H + KVH) * 64:])  # value heads: the GEMM output
+    pos = np.concatenate([np.arange(n) + po for n, po in zip(lens, pos_off)])
+    want = O.qk_norm_rope(raw, H, KVH, qn.cpu().numpy(), kn.cpu().numpy(), rope_np, pos, 1e-5)
+    assert (np.abs(a - want) <= np.abs(want) * 2.0 ** -10 + 2e-4).all()
