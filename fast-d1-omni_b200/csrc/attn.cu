@@ -290,7 +290,9 @@ enum : int {
     B_ODONE = B_PFULL + 4,             // [w][b]: the P.V that read P[w][b]
     B_OFREE = B_ODONE + 4,             // [w]
     B_DRAIN = B_OFREE + 2,
-    T_NBARS = B_DRAIN + 1
+    B_OSTAGED = B_DRAIN + 1,           // [w]: the warpgroup's O tile is in shared memory (4 warp arrivals)
+    B_OREAD = B_OSTAGED + 2,           // [w]: its bulk store has read it (the issuing thread)
+    T_NBARS = B_OREAD + 2
 };
 constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 4 * T_P_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
@@ -313,6 +315,16 @@ struct FaTcArgs {
 };
 
 __device__ __forceinline__ void fence_async_smem_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Bulk tensor store of a staged O tile and its completion waits (issued and awaited by one thread).
+__device__ __forceinline__ void o_tile_store(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)map),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void o_store_read_done() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void o_store_done() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void record_err(int* err, volatile int* abort_flag, int code) {
     *abort_flag = 1;
@@ -364,7 +376,8 @@ constexpr int T_THREADS = 384;
 
 __global__ void __launch_bounds__(T_THREADS, 1)
     k_flash_attn_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const FaTcArgs a) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -399,6 +412,10 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         mbar_init(bar(B_OFREE + 0), 4);
         mbar_init(bar(B_OFREE + 1), 4);
         mbar_init(bar(B_DRAIN), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(B_OSTAGED + i), 4);
+            mbar_init(bar(B_OREAD + i), 1);
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -406,6 +423,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         prefetch_tmap(&tmQ);
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
+        prefetch_tmap(&tmO);
     }
     if (warp == 9) {
         tmem_alloc(smem_u32(tmem_slot), T_TMEM_COLS);
@@ -595,6 +613,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
         int cnt = 0;
+        int staged = -1;  // P buffer holding an O tile whose bulk store may still be reading it
+        int nst = 0;      // O tiles this warpgroup has staged
         bool ok = true;
         Unit un;
         for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
@@ -659,6 +679,15 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     }
                     tc_wait_st();
                 }
+                if (b == staged) {  // the previous unit's O tile was staged here: wait until its store has read it
+                    if (row == 0) {
+                        o_store_read_done();
+                        mbar_arrive(bar(B_OREAD + w));
+                    }
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_OREAD + w), (nst - 1) & 1, abort_flag))))
+                        break;
+                    staged = -1;
+                }
                 float rs8[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) rs8[e] = 0.f;
@@ -690,26 +719,49 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;
-            const int q = un.q0 + w * TQ + row;
-            __half* orow = a.O + (size_t)(un.s.q_start + (q < un.s.q_len ? q : 0)) * a.ldo + un.h * 64;
-#pragma unroll 1
-            for (int c2 = 0; c2 < 2; c2++) {  // O in two 32-column pieces
-                uint32_t o[32];
-                tmem_ld32(tO + c2 * 32, o);
-                tc_wait_ld();
-                if (q < un.s.q_len)
-#pragma unroll
-                    for (int k8 = 0; k8 < 4; k8++)
-                        *reinterpret_cast<uint4*>(orow + c2 * 32 + k8 * 8) = make_uint4(
-                            pack_h2(__uint_as_float(o[8 * k8]) * il, __uint_as_float(o[8 * k8 + 1]) * il),
-                            pack_h2(__uint_as_float(o[8 * k8 + 2]) * il, __uint_as_float(o[8 * k8 + 3]) * il),
-                            pack_h2(__uint_as_float(o[8 * k8 + 4]) * il, __uint_as_float(o[8 * k8 + 5]) * il),
-                            pack_h2(__uint_as_float(o[8 * k8 + 6]) * il, __uint_as_float(o[8 * k8 + 7]) * il));
-            }
+            uint32_t o[64];
+            tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
+            tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
+            tc_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_OFREE + w));  // the next unit's first P.V may overwrite O
+            if (lane == 0) mbar_arrive(bar(B_OFREE + w));  // O is read: the next unit's first P.V may overwrite it
+            const int q0w = un.q0 + w * TQ, q = q0w + row;
+            if (q0w + TQ <= un.s.q_len) {
+                // a whole 128-row tile: staged in the P buffer the next unit writes second (both are free: every
+                // P.V of this unit is done), then one bulk tensor store of 16 KB
+                const int sb = (cnt + 1) & 1;
+                uint8_t* stile = sP + (2 * w + sb) * T_P_BYTES;
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++)
+                    *reinterpret_cast<uint4*>(stile + row * 128 + ((ch ^ (row & 7)) << 4)) = make_uint4(
+                        pack_h2(__uint_as_float(o[8 * ch]) * il, __uint_as_float(o[8 * ch + 1]) * il),
+                        pack_h2(__uint_as_float(o[8 * ch + 2]) * il, __uint_as_float(o[8 * ch + 3]) * il),
+                        pack_h2(__uint_as_float(o[8 * ch + 4]) * il, __uint_as_float(o[8 * ch + 5]) * il),
+                        pack_h2(__uint_as_float(o[8 * ch + 6]) * il, __uint_as_float(o[8 * ch + 7]) * il));
+                fence_async_smem_cta();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_OSTAGED + w));
+                bool staged_ok = true;
+                if (row == 0) {
+                    staged_ok = mbar_wait(bar(B_OSTAGED + w), nst & 1, abort_flag);
+                    if (staged_ok) o_tile_store(&tmO, smem_u32(stile), un.h * 64, un.s.q_start + q0w);
+                }
+                staged = sb;
+                nst++;
+                if (!(ok = __all_sync(D1_FULL_MASK, staged_ok))) break;
+            } else if (q < un.s.q_len) {  // a partial tile: this row's 128 bytes directly
+                __half* orow = a.O + (size_t)(un.s.q_start + q) * a.ldo + un.h * 64;
+#pragma unroll
+                for (int k8 = 0; k8 < 8; k8++)
+                    *reinterpret_cast<uint4*>(orow + k8 * 8) = make_uint4(
+                        pack_h2(__uint_as_float(o[8 * k8]) * il, __uint_as_float(o[8 * k8 + 1]) * il),
+                        pack_h2(__uint_as_float(o[8 * k8 + 2]) * il, __uint_as_float(o[8 * k8 + 3]) * il),
+                        pack_h2(__uint_as_float(o[8 * k8 + 4]) * il, __uint_as_float(o[8 * k8 + 5]) * il),
+                        pack_h2(__uint_as_float(o[8 * k8 + 6]) * il, __uint_as_float(o[8 * k8 + 7]) * il));
+            }
         }
+        if (row == 0) o_store_done();  // no O store still reads this CTA's shared memory when it exits
         if (!ok && lane == 0) record_err(a.err, abort_flag, kErrWaitAccFull);
     }
     tc_fence_before();
@@ -748,13 +800,13 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, int q_rows, int kv_rows, cu
     }
     a.n_units = n_work * heads;
     a.heads = heads;
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tq, tk, tv, to;
     const int kv_cols = heads / a.group * 64;
     if (!attn_tmap(&tq, a.Q, heads * 64, q_rows, a.ldq, TQ) || !attn_tmap(&tk, a.K, kv_cols, kv_rows, a.ldkv, TKV) ||
-        !attn_tmap(&tv, a.V, kv_cols, kv_rows, a.ldkv, TKV))
+        !attn_tmap(&tv, a.V, kv_cols, kv_rows, a.ldkv, TKV) || !attn_tmap(&to, a.O, heads * 64, q_rows, a.ldo, TQ))
         return -1;
     const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
-    launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, tq, tk, tv, a);
+    launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, tq, tk, tv, to, a);
     return (int)cudaGetLastError();
 }
 
@@ -784,7 +836,7 @@ extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, con
                                 int group, float scale, int q_rows, int kv_rows, cudaStream_t st) {
     if (n_work <= 0) return n_work == 0 ? 0 : -1;
     if (heads <= 0 || group <= 0 || heads % group || q_rows <= 0 || kv_rows <= 0) return -1;
-    if (ldq < heads * 64 || ldkv < heads / group * 64) return -1;
+    if (ldq < heads * 64 || ldo < heads * 64 || ldkv < heads / group * 64) return -1;
     if ((((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)O) & 15) || (ldq | ldkv | ldo | ext_ld) % 8) return -1;
     FaTcArgs t;
     t.Q = Q;
