@@ -227,7 +227,7 @@ int d1_lt_error(void* ctx);
  * q0 is a multiple of 256 (other items are ignored): the work list must hold such an item for every 256-row block
  * of every sequence — a list of every 64-row tile (as src/model.rs builds it) does, and a list of only the
  * 256-row block starts is the cheaper form. Pointers 16-byte aligned, leading dimensions multiples of 8.
- * q_rows / kv_rows: rows of Q / of K and V that may be read (every sequence's q_start + q_len <= q_rows,
+ * q_rows / kv_rows: rows of Q and O / of K and V that may be accessed (every sequence's q_start + q_len <= q_rows,
  * kv_start + kv_len <= kv_rows); query and local key tiles are fetched by TMA, which reads whole 128-row / 64-row
  * tiles within those bounds (rows of other sequences are read but never used; rows of K and V inside the bounds
  * must hold finite values). */
