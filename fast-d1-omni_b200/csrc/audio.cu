@@ -538,48 +538,58 @@ __global__ void __launch_bounds__(256) k_mel_frames(const float* __restrict__ x,
     }
 }
 
-// Per-channel normalisation over the valid frames: 1024 threads, thread (part, channel) sums the frames
-// f = part (mod 8) in f64, the 8 partial sums are combined in part order (the reference sums frames sequentially in
-// f64; the orders differ by f64 rounding only, ~1e-16 relative), then every element is normalised in parallel.
+// Per-channel normalisation over the valid frames. CTA g owns channels [8g, 8g + 8): thread (part, channel) of its
+// first 64 sums the frames f = part (mod 8) in f64 and the 8 partial sums are combined in part order (the reference
+// sums frames sequentially in f64; the orders differ by f64 rounding only, ~1e-16 relative), then all 256 threads
+// normalise the CTA's channels over every frame. 16 CTAs instead of one: the f64 divides and the 3 passes over the
+// features spread over 16 SMs.
 constexpr int MEL_PARTS = 8;
+constexpr int MEL_CH = 8;  // channels per CTA
 
-__global__ void __launch_bounds__(MEL_N * MEL_PARTS) k_mel_norm(float* __restrict__ mel, int frames, int valid) {
-    __shared__ double part_sum[MEL_PARTS][MEL_N];
-    __shared__ double stat[2][MEL_N];  // mean, 1 / (std + 1e-5)
-    const int m = threadIdx.x % MEL_N, part = threadIdx.x / MEL_N;
+__global__ void __launch_bounds__(256) k_mel_norm(float* __restrict__ mel, int frames, int valid) {
+    __shared__ double part_sum[MEL_PARTS][MEL_CH];
+    __shared__ double stat[2][MEL_CH];  // mean, std + 1e-5
+    const int c0 = blockIdx.x * MEL_CH;
+    const int lc = threadIdx.x % MEL_CH, part = threadIdx.x / MEL_CH;  // stats: threads 0 .. 63
+    const bool stats = threadIdx.x < MEL_CH * MEL_PARTS;
     double acc = 0.0;
+    if (stats) {
 #pragma unroll 4
-    for (int f = part; f < valid; f += MEL_PARTS) acc = __dadd_rn(acc, (double)mel[(size_t)f * MEL_N + m]);
-    part_sum[part][m] = acc;
-    __syncthreads();
-    if (part == 0) {
-        double t = 0.0;
-        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][m]);
-        stat[0][m] = __ddiv_rn(t, (double)valid);
+        for (int f = part; f < valid; f += MEL_PARTS) acc = __dadd_rn(acc, (double)mel[(size_t)f * MEL_N + c0 + lc]);
+        part_sum[part][lc] = acc;
     }
     __syncthreads();
-    const double mean = stat[0][m];
-    acc = 0.0;
-#pragma unroll 4
-    for (int f = part; f < valid; f += MEL_PARTS) {
-        const double d = __dsub_rn((double)mel[(size_t)f * MEL_N + m], mean);
-        acc = __dadd_rn(acc, __dmul_rn(d, d));
+    if (threadIdx.x < MEL_CH) {
+        double t = 0.0;
+        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][lc]);
+        stat[0][lc] = __ddiv_rn(t, (double)valid);
     }
     __syncthreads();
-    part_sum[part][m] = acc;
+    if (stats) {
+        const double mean = stat[0][lc];
+        acc = 0.0;
+#pragma unroll 4
+        for (int f = part; f < valid; f += MEL_PARTS) {
+            const double d = __dsub_rn((double)mel[(size_t)f * MEL_N + c0 + lc], mean);
+            acc = __dadd_rn(acc, __dmul_rn(d, d));
+        }
+    }
     __syncthreads();
-    if (part == 0) {
+    if (stats) part_sum[part][lc] = acc;
+    __syncthreads();
+    if (threadIdx.x < MEL_CH) {
         double t = 0.0;
-        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][m]);
+        for (int q = 0; q < MEL_PARTS; q++) t = __dadd_rn(t, part_sum[q][lc]);
         double sd = sqrt(__ddiv_rn(t, __dsub_rn((double)valid, 1.0)));
         if (isnan(sd)) sd = 0.0;
-        stat[1][m] = __dadd_rn(sd, 1e-5);
+        stat[1][lc] = __dadd_rn(sd, 1e-5);
     }
     __syncthreads();
-    for (size_t i = threadIdx.x; i < (size_t)frames * MEL_N; i += MEL_N * MEL_PARTS) {
-        const int c = (int)(i % MEL_N);
-        const int f = (int)(i / MEL_N);
-        mel[i] = f < valid ? __double2float_rn(__ddiv_rn(__dsub_rn((double)mel[i], stat[0][c]), stat[1][c])) : 0.f;
+    for (size_t i = threadIdx.x; i < (size_t)frames * MEL_CH; i += blockDim.x) {
+        const int c = (int)(i % MEL_CH);
+        const int f = (int)(i / MEL_CH);
+        float* p = mel + (size_t)f * MEL_N + c0 + c;
+        *p = f < valid ? __double2float_rn(__ddiv_rn(__dsub_rn((double)*p, stat[0][c]), stat[1][c])) : 0.f;
     }
 }
 
@@ -649,6 +659,6 @@ extern "C" int d1_log_mel(const float* x, int n, float* mel, cudaStream_t st) {
     if (mel_tables_ready()) return -1;
     const int frames = 1 + n / MEL_HOP, valid = n / MEL_HOP;
     k_mel_frames<<<frames, 256, 0, st>>>(x, n, mel);
-    k_mel_norm<<<1, MEL_N * MEL_PARTS, 0, st>>>(mel, frames, valid);
+    k_mel_norm<<<MEL_N / MEL_CH, 256, 0, st>>>(mel, frames, valid);
     return (int)cudaGetLastError();
 }
