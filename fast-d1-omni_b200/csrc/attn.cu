@@ -613,8 +613,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
         int cnt = 0;
-        int staged = -1;  // P buffer holding an O tile whose bulk store may still be reading it
-        int nst = 0;      // O tiles this warpgroup has staged
+        unsigned pend = 0;  // P buffers (bit b) holding an O tile whose bulk store may still be reading it
+        int nst = 0;        // O tiles this warpgroup has staged
+        int nread = 0;      // times it has waited for its stores to finish reading
         bool ok = true;
         Unit un;
         for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
@@ -679,14 +680,14 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     }
                     tc_wait_st();
                 }
-                if (b == staged) {  // the previous unit's O tile was staged here: wait until its store has read it
+                if ((pend >> b) & 1) {  // an earlier O tile was staged here: wait until every store has read its tile
                     if (row == 0) {
                         o_store_read_done();
                         mbar_arrive(bar(B_OREAD + w));
                     }
-                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_OREAD + w), (nst - 1) & 1, abort_flag))))
-                        break;
-                    staged = -1;
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_OREAD + w), nread & 1, abort_flag)))) break;
+                    nread++;
+                    pend = 0;
                 }
                 float rs8[8];
 #pragma unroll
@@ -747,7 +748,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     staged_ok = mbar_wait(bar(B_OSTAGED + w), nst & 1, abort_flag);
                     if (staged_ok) o_tile_store(&tmO, smem_u32(stile), un.h * 64, un.s.q_start + q0w);
                 }
-                staged = sb;
+                pend |= 1u << sb;
                 nst++;
                 if (!(ok = __all_sync(D1_FULL_MASK, staged_ok))) break;
             } else if (q < un.s.q_len) {  // a partial tile: this row's 128 bytes directly
