@@ -129,10 +129,15 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 // ---------------------------------------------------------------------------------------------- bulk stores
 
+// Output tiles are written with an L2 evict-last hint: the next kernel of the forward reads them straight away.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)map),
-                 "r"(src), "r"(x), "r"(y)
-                 : "memory");
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+            (uint64_t)map),
+        "r"(src), "r"(x), "r"(y), "l"(policy)
+        : "memory");
 }
 // Reduce-add into the fp32 residual with an L2 evict-last hint: the residual stream is read again by the next
 // RMSNorm right after this GEMM, so its lines are kept in L2 ahead of the operand tiles streaming through.
