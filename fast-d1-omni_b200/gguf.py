@@ -104,6 +104,8 @@ class Gguf:
         if nbytes is None:
             raise ValueError(f"{name}: unsupported ggml type {ty}")
         start = self.data_start + off
+        if start + nbytes > len(self.buf):
+            raise ValueError(f"{self.path}: tensor {name} runs past the end of the file (truncated)")
         return ty, n, self.buf[start:start + nbytes]
 
     def f32(self, name):

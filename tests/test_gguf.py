@@ -328,6 +328,10 @@ def test_errors(tmp_path):
         g.f32("nope")
     with pytest.raises(ValueError, match="unsupported ggml type 2"):
         g.f32("q4")
+    p2 = tmp_path / "short.gguf"  # the data of "x" (512 bytes, then "q4"'s 32) cut 64 bytes short
+    p2.write_bytes((tmp_path / "e.gguf").read_bytes()[:-64])
+    with pytest.raises(ValueError, match="past the end"):
+        G.Gguf(str(p2)).f32("x")
     t = Writer().kv("general.architecture", 8, "llama").write(str(tmp_path / "arch.gguf"))
     with pytest.raises(ValueError, match="want lfm2"):
         G.load_text(t)
