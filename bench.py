@@ -72,17 +72,58 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """SM clock and throttle-reason sampling during the timed region (read-only). NVML from a background thread every
+    10 ms, so even a ~0.1 s region gets ~10 samples; nvidia-smi at 200 ms when NVML is unavailable. The GPU is found
+    by the UUID torch reports for the CUDA device (CUDA_VISIBLE_DEVICES-safe)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): sw power cap 0x4, hw slowdown 0x8, sw thermal 0x20, hw thermal 0x40
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.samples = []  # (sm MHz, reason bits)
+        self.max_mhz = None
+        self.lines = []
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+        try:
+            import pynvml
+            h = self._nvml_handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.stop = threading.Event()
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                             int(reasons(h))))
+                    except Exception:
+                        return
+                    self.stop.wait(0.01)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -92,7 +133,9 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,9 +146,12 @@ class Clocks:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons = [], self.max_mhz, set()
+        for mhz, bits in self.samples:
+            sm.append(mhz)
+            reasons.update(n for n, b in self.BITS.items() if bits & b)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
+        for l in self.lines:
             f = [x.strip() for x in l.split(",")]
             if len(f) < 9:
                 continue
@@ -119,7 +165,8 @@ class Clocks:
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 def cpu_sample(n_seqs: int, seed: int = 3):
