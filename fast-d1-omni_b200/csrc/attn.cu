@@ -14,10 +14,10 @@
 // takes any work list, as the reference's kernel does, and adds biases on load.
 //
 // d1_flash_attn_tc (extension) is the same computation for the bias-free forms on tcgen05 (k_flash_attn_tc below:
-// S and O in TMEM, the score tiles issued two steps ahead of a ping-pong pair of softmax warpgroups). Measured on
-// B200 (CUDA events, 16 heads, GQA 2): on par with the mma.sync kernel at 32 x 256 tokens (42 vs 44 us) and
-// 1.3-1.5x faster on long sequences (4 x 2048 tokens: 175 vs 263 us, 394 TF/s). The runners use it whenever the
-// attention has no biases to add on load (their work lists cover every tile).
+// S and O in TMEM, the score tiles issued two steps ahead of a ping-pong pair of softmax warpgroups, TMA loads and
+// stores). Measured on B200 (CUDA events, 16 heads, GQA 2): 29.5-31 us at 32 x 256 tokens (44 us for the mma.sync
+// kernel) and 165 us at 4 x 2048 tokens (417 TF/s; 263 us). The runners use it whenever the attention has no biases
+// to add on load (their work lists cover every 256-row block).
 #include "common.cuh"
 #include "warp_mma.cuh"
 
@@ -265,10 +265,11 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 //        (128-byte swizzle: the A operand of P.V) and accumulates the row sum. O is rescaled in TMEM only when the
 //        row max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well
 //        inside fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory.
-//   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring, K/V tiles of 64 keys ([ext prefix keys | local
-//        keys]) into a 6-stage ring, with cp.async into the swizzled layouts (V is the MN-major B operand of P.V:
-//        same bytes); each lane's copies complete the slot's barrier when they land (cp.async.mbarrier.arrive), and
-//        the next unit's loads overlap the current unit's math.
+//   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring and K/V tiles of 64 keys ([ext prefix keys |
+//        local keys]) into a 6-stage ring, in the swizzled layouts (V is the MN-major B operand of P.V: same bytes):
+//        Q and whole local K/V tiles by TMA from one thread, prefix and partial tiles by cp.async from all three
+//        warps (each lane's copies complete the slot's barrier when they land); the next unit's loads overlap the
+//        current unit's math.
 //   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64) and
 //        O_w += P_w(j).V_j (M=128, N=64, K=64).
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
