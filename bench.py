@@ -18,9 +18,13 @@ peak. One step = one Runner::launch_text (src/model.rs:470-599) of an 8192-token
 only; its fp32 PyTorch path needs remote code and weights that are not available offline), so this arm times the
 oracle port (fp32 numpy restatement of the reference's arithmetic) on all host threads, on bounded samples. When a
 GPU and oracle/_ref/libd1ref.so (the reference's cuda/*.cu built unchanged) are present, the line also carries
-`reference_gpu_engine`: the reference's own F16 engine (its kernels + cuBLASLt) timed on the same batches.
+`reference_gpu_engine`: the reference's own F16 engine (its kernels + cuBLASLt, plans tuned at the effort its engine
+uses) timed on the same batches, in a child process that runs the cuBLASLt the reference was compiled against.
 
---gemm-sweep: BASELINE config 1, every projection GEMM shape, one JSON line per shape.
+--gemm-sweep: BASELINE config 1, every projection GEMM shape, one JSON line per shape, with the reference's
+cuBLASLt GEMM (d1_lt_tune at effort 1, then d1_lt_gemm of oracle/_ref/libd1ref.so) timed beside each form.
+--attn-config2: BASELINE config 2 (packed varlen GQA attention, log-normal lengths) at 2048 / 8192 / 16384 tokens:
+the tcgen05 kernel, this library's mma.sync kernel and the reference's k_flash_attn, one JSON line per size.
 --workload mixed: BASELINE config 4 — the mixed text / image / audio request stream through the continuous-batching
 engine, one replica per GPU (torchrun for N > 1).
 
@@ -47,7 +51,12 @@ N_SEQS = 32
 TOKENS = SEQ_LEN * N_SEQS
 GEMM_FLOP_PER_TOKEN = 574_619_648          # trunk projection GEMMs (2 x 287,309,824 linear params)
 SWIGLU_FLOP_PER_TOKEN = 2 * 9216 * 1024    # w1|w3, fused SwiGLU epilogue
-SWIGLU_TRAFFIC_PER_LAUNCH = 69.6e6          # ncu dram read+write per launch at this shape (profiles/gemm_swiglu_pair_m8192.md)
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one d1_gemm_swiglu launch at M=8192 (the capture of
+# profiles/gemm_swiglu_pair_m8192.md, taken 2026-12-01 on one B200). It is below the launch's 111 MB of
+# algorithmic bytes (A 16.8 MB + W 18.9 MB read, 75.5 MB written) because most of the output is still dirty in the
+# 126 MB L2 when the kernel ends: ncu counts DRAM writes of the launch only.
+SWIGLU_NCU_DRAM_BYTES_M8192 = 69.6e6
+SUSTAINED_STEPS = 440  # second timed region: >= 2 s of back-to-back steps (clocks settle at the power cap)
 
 
 def load_package():
@@ -169,8 +178,26 @@ class Clocks:
                 "source": "nvml" if self.samples else "nvidia-smi"}
 
 
+def use_all_cores() -> int:
+    """Lets the oracle port use every host thread this process may run on, whatever OMP_NUM_THREADS the launcher
+    set (torchrun sets 1): the BLAS pools through threadpoolctl, torch's intra-op pool through set_num_threads.
+    Returns the thread count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        import numpy  # noqa: F401  (load the BLAS before limiting it)
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    if "torch" in sys.modules:
+        sys.modules["torch"].set_num_threads(n)
+    return n
+
+
 def cpu_sample(n_seqs: int, seed: int = 3):
     """Time the oracle port (fp32 numpy) on a bounded sample: n_seqs x 256-token sequences of the workload."""
+    use_all_cores()
     from oracle import d1_oracle as O
     pkg = load_package()
     from fast_d1_omni_b200.weights import text_batch, text_weights
@@ -195,6 +222,7 @@ def run_reference(args, rank, world):
     """--impl reference: the oracle port on the host cores, rank 0 only."""
     if rank != 0:
         return
+    use_all_cores()
     from oracle import d1_oracle as O
     load_package()
     from fast_d1_omni_b200.weights import text_batch, text_weights
@@ -217,7 +245,7 @@ def run_reference(args, rank, world):
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": f"{n_sample} sequences x {SEQ_LEN} tokens per step, oracle/d1_oracle.py fp32"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    gpu = reference_gpu_engine(w, args.steps, args.warmup)
+    gpu = reference_gpu_engine_child(args.steps, args.warmup)
     if gpu is not None:
         line["reference_gpu_engine"] = gpu
     print(json.dumps(line), flush=True)
@@ -226,35 +254,80 @@ def run_reference(args, rank, world):
 REF_LIB = ROOT / "oracle" / "_ref" / "libd1ref.so"
 
 
-def reference_gpu_engine(w, steps, warmup):
+def preload_reference_cublaslt():
+    """Loads the CUDA toolkit's cuBLASLt / cuBLAS (the libraries oracle/_ref/libd1ref.so was compiled and linked
+    against) into the process before torch, whose wheels bundle an older cuBLASLt under the same soname
+    (libcublasLt.so.12): without this, libd1ref.so binds to whichever copy torch loaded first. Returns the loaded
+    cuBLASLt version, or None when the toolkit copy is not found (torch's is then used)."""
+    import ctypes as C
+    cuda_home = os.environ.get("CUDA_HOME") or os.environ.get("CUDA_PATH") or "/usr/local/cuda"
+    lt = Path(cuda_home) / "lib64" / "libcublasLt.so.12"
+    if "torch" in sys.modules or not lt.exists():
+        return None
+    h = C.CDLL(str(lt), mode=C.RTLD_GLOBAL)
+    blas = lt.with_name("libcublas.so.12")
+    if blas.exists():
+        C.CDLL(str(blas), mode=C.RTLD_GLOBAL)
+    h.cublasLtGetVersion.restype = C.c_size_t
+    return int(h.cublasLtGetVersion())
+
+
+def reference_gpu_engine_child(steps, warmup):
+    """Runs reference_gpu_engine in a child process at the reference engine's tuning effort (1, src/engine.rs:593);
+    if that child does not finish cleanly, once more at effort 0, and says why. None when there is no reference
+    library or no GPU."""
+    if not REF_LIB.exists():
+        return None
+    out = {}
+    for effort in (1, 0):
+        cmd = [sys.executable, str(Path(__file__).resolve()), "--ref-engine-child", str(effort),
+               "--steps", str(steps), "--warmup", str(warmup)]
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=420 if effort else 300)
+        except subprocess.TimeoutExpired:
+            out[f"effort{effort}_failure"] = "timed out"
+            continue
+        sys.stderr.write(r.stderr[-2000:])
+        lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+        if r.returncode == 0 and lines:
+            res = json.loads(lines[-1])
+            if res.get("unavailable"):
+                return None
+            res.update(out)
+            return res
+        out[f"effort{effort}_failure"] = (f"exit {r.returncode}" if r.returncode >= 0 else
+                                          f"killed by signal {-r.returncode}")
+    return out or None
+
+
+def reference_gpu_engine(steps, warmup, effort):
     """The reference's own F16 CUDA engine on this GPU: cuda/kernels.cu + cuda/gemm.cu (cuBLASLt autotuner) built
     unchanged into oracle/_ref/libd1ref.so, driven by the same host runner (src/model.rs restated), on the same
-    8192-token batches as this library's arm. Its GEMM plans come from d1_lt_tune at effort 0 (cuBLASLt heuristic
-    candidates, each timed) on first use of each shape during the warm-up steps: the effort-1 search of
-    src/engine.rs:593 (every cuBLASLt algorithm x tile) crashed the process with SIGSEGV on B200 and is not run.
-    Device time over `steps` back-to-back launch_text steps (CUDA events). None when there is no GPU or the
-    reference library was not built."""
-    try:
-        import torch
-        if not torch.cuda.is_available() or not REF_LIB.exists():
-            return None
-    except Exception:
-        return None
+    8192-token batches as this library's arm. Its GEMM plans come from d1_lt_tune at `effort` on the first use of
+    each shape during the warm-up steps (the buckets these batches touch; the reference's engine tunes every bucket
+    at startup with effort 1). Device time over `steps` back-to-back launch_text steps (CUDA events)."""
+    lt_version = preload_reference_cublaslt()
+    import torch
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
     load_package()
     from fast_d1_omni_b200.model import TextModel
-    from fast_d1_omni_b200.weights import text_batch
+    from fast_d1_omni_b200.weights import text_batch, text_weights
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    print("reference GPU engine: loading", file=sys.stderr, flush=True)
-    model = TextModel(w, device=0, kernel_lib=str(REF_LIB), fused=False, cap_tokens=TOKENS)
+    print(f"reference GPU engine: loading (cuBLASLt {lt_version})", file=sys.stderr, flush=True)
+    model = TextModel(text_weights(0), device=0, kernel_lib=str(REF_LIB), fused=False, cap_tokens=TOKENS)
+    model.set_tune_effort(effort)
     try:
-        print("reference GPU engine: warm-up (effort-0 plans on first use)", file=sys.stderr, flush=True)
+        print(f"reference GPU engine: warm-up (effort-{effort} plans on first use)", file=sys.stderr, flush=True)
         batches = [text_batch(i, N_SEQS, SEQ_LEN) for i in range(4)]
         stream = torch.cuda.Stream(dev)
+        t_tune = time.perf_counter()
         with torch.cuda.stream(stream):
             for i in range(warmup):
                 model.launch(batches[i % 4], i % 2, stream)
             torch.cuda.synchronize(dev)
+            t_tune = time.perf_counter() - t_tune
             model._pending.clear()
             print("reference GPU engine: timing", file=sys.stderr, flush=True)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -267,9 +340,11 @@ def reference_gpu_engine(w, steps, warmup):
         ms = e0.elapsed_time(e1)
         return {"value": TOKENS * steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms / steps,
                 "device": torch.cuda.get_device_name(dev),
-                "gemm_plans": "d1_lt_tune effort 0 on first use (cuBLASLt heuristic candidates, timed)",
+                "gemm_plans": f"d1_lt_tune effort {effort} on first use of each shape and bucket",
+                "warmup_with_tuning_s": round(t_tune, 1), "cublaslt_version": lt_version,
                 "source": "oracle/_ref/libd1ref.so: the reference's cuda/kernels.cu + cuda/gemm.cu (cuBLASLt) built "
-                          "unchanged, through this repository's restatement of src/model.rs"}
+                          "unchanged, driven through this repository's C++ restatement of src/model.rs (the "
+                          "reference's Rust host needs cargo, which this image lacks)"}
     finally:
         model.close()
 
@@ -310,48 +385,80 @@ SWEEP_NK = ((3072, 1024, "conv in_proj"), (2048, 1024, "fused QKV"), (1024, 1024
 def gemm_sweep(pkg, dev, stream, reps=20):
     """C = A.W^T for every M x (N, K), fp16 in, fp32 accumulate, after d1_lt_tune (effort 1).
     Per shape: the plain fp16-store GEMM and the trunk's own form of that projection (residual add into the fp32
-    stream for out_proj / w2, the fused SwiGLU for w1|w3). One JSON line per shape; CUDA-event averages over
-    `reps` launches of inputs larger than L2 at M >= 8192 (the smaller shapes are L2-resident by nature)."""
+    stream for out_proj / w2, the fused SwiGLU for w1|w3). Beside each form, the reference's own path for it
+    (oracle/_ref/libd1ref.so, the reference's cuda/gemm.cu + cuda/kernels.cu built unchanged): d1_lt_tune at
+    effort 1 (the reference engine's effort; cuda/gemm.cu searches only up to M 8192 and takes the heuristic
+    candidates above), then d1_lt_gemm; for w1|w3 its GEMM into [g|u] plus its k_swiglu. One JSON line per shape;
+    CUDA-event averages over `reps` launches of inputs larger than L2 at M >= 8192 (the smaller shapes are
+    L2-resident by nature)."""
     import ctypes as C
     import torch
     lib = pkg.lib()
     ctx = lib.d1_lt_init(0)
+    ref = None
+    if REF_LIB.exists():
+        ref = C.CDLL(str(REF_LIB))
+        pkg.abi.bind(ref, (pkg.abi.KERNELS,))
+        rctx = ref.d1_lt_init(32 << 20)
     st = C.c_void_p(stream.cuda_stream)
     P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
     _, tflops, kind = peaks()
     g = torch.Generator(device=dev).manual_seed(1)
     out = []
+
+    def timed(fn):
+        for _ in range(3):
+            assert fn() == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps * 1e3
+
     for (N, K, name) in SWEEP_NK:
         wt = (torch.randn(N, K, device=dev, generator=g) * 0.02).half()
         for M in SWEEP_M:
             x = torch.randn(M, K, device=dev, generator=g).half()
             y16 = torch.empty(M, N, device=dev, dtype=torch.float16)
-            forms = {"store_f16": lambda: lib.d1_lt_gemm(ctx, M, N, K, P(x), K, P(wt), K, 0, P(y16), N, 0, 0, 1.0,
-                                                         0.0, st)}
+            forms = {"store_f16": lambda lb, c: lb.d1_lt_gemm(c, M, N, K, P(x), K, P(wt), K, 0, P(y16), N, 0, 0, 1.0,
+                                                               0.0, st)}
+            tunes = [(0,)]
             if N == 1024:
                 y32 = torch.zeros(M, N, device=dev)
-                forms["trunk_residual_f32"] = lambda: lib.d1_lt_gemm(ctx, M, N, K, P(x), K, P(wt), K, 0, P(y32), N, 1,
-                                                                     0, 1.0, 1.0, st)
-                lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, 1, 0, 1, st)
+                forms["trunk_residual_f32"] = lambda lb, c: lb.d1_lt_gemm(c, M, N, K, P(x), K, P(wt), K, 0, P(y32),
+                                                                           N, 1, 0, 1.0, 1.0, st)
+                tunes.append((1,))
             if N == 9216:
                 act = torch.empty(M, N // 2, device=dev, dtype=torch.float16)
-                forms["trunk_swiglu"] = lambda: lib.d1_gemm_swiglu(ctx, M, N // 2, K, P(x), K, P(wt), K, P(act),
-                                                                   N // 2, st)
-            lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, 0, 0, 1, st)
+
+                def swiglu(lb, c):
+                    if lb is lib:
+                        return lb.d1_gemm_swiglu(c, M, N // 2, K, P(x), K, P(wt), K, P(act), N // 2, st)
+                    e = lb.d1_lt_gemm(c, M, N, K, P(x), K, P(wt), K, 0, P(y16), N, 0, 0, 1.0, 0.0, st)
+                    return e or lb.d1_swiglu(P(y16), P(act), M, N // 2, st)
+                forms["trunk_swiglu"] = swiglu
+            for (y_f32,) in tunes:
+                lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, y_f32, 0, 1, st)
+                if ref is not None:
+                    assert ref.d1_lt_tune(rctx, M, N, K, K, K, 0, N, y_f32, 0, 1, st) > 0
+            if ref is not None:
+                ref.d1_lt_free_scratch(rctx)
             rec = {"sweep": "config1", "shape": name, "M": M, "N": N, "K": K}
             for fname, fn in forms.items():
-                for _ in range(3):
-                    assert fn() == 0
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                for _ in range(reps):
-                    fn()
-                e1.record(stream)
-                torch.cuda.synchronize(dev)
-                us = e0.elapsed_time(e1) / reps * 1e3
+                us = timed(lambda: fn(lib, ctx))
                 tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
                 rec[fname] = {"us": round(us, 2), "tflops": round(tf, 1), "frac_of_peak": round(tf / tflops, 3)}
+                if ref is not None:
+                    rus = timed(lambda: fn(ref, rctx))
+                    rtf = 2.0 * M * N * K / (rus * 1e-6) / 1e12
+                    rec[fname]["reference"] = {"us": round(rus, 2), "tflops": round(rtf, 1),
+                                               "frac_of_peak": round(rtf / tflops, 3)}
+                    rec[fname]["speedup_vs_reference"] = round(rus / us, 3)
             rec["peak"] = f"{tflops} TFLOP/s ({kind}, bf16 cuBLAS burst)"
+            if ref is not None:
+                rec["reference_plans"] = "d1_lt_tune effort 1 (cuBLASLt search up to M 8192, heuristics above)"
             out.append(rec)
             print(json.dumps(rec), flush=True)
     err = lib.d1_lt_error(ctx)
@@ -359,6 +466,70 @@ def gemm_sweep(pkg, dev, stream, reps=20):
     if err:
         raise RuntimeError(f"GEMM kernel reported error {err}")
     return out
+
+
+def attn_config2(pkg, dev, reps=20, warm=3):
+    """packed varlen bidirectional GQA attention (16 query heads, 8 KV heads, head dim 64,
+    Q/K/V N(0,1) fp16, seed 2), lengths log-normal (median 384, sigma 1) clipped to 32..16384, at 2048, 8192 and
+    16384 packed tokens. Times this library's tcgen05 kernel (d1_flash_attn_tc, 256-row work items), its mma.sync
+    kernel (d1_flash_attn, 64-row items as the reference builds them) and the reference's own k_flash_attn
+    (d1_flash_attn of oracle/_ref/libd1ref.so) on the same inputs; FLOPs = sum over sequences of 4 L^2 64 x 16."""
+    import ctypes as C
+    import torch
+    from fast_d1_omni_b200.weights import lognormal_lengths
+    lib = pkg.lib()
+    ref = None
+    if REF_LIB.exists():
+        ref = C.CDLL(str(REF_LIB))
+        pkg.abi.bind(ref, (pkg.abi.KERNELS,))
+    _, tflops, kind = peaks()
+    st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    for total in (2048, 8192, 16384):
+        lens = lognormal_lengths(2, total)
+        arr = (pkg.abi.AttnSeq * len(lens))()
+        s = 0
+        for i, n in enumerate(lens):
+            arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = s, n, s, n
+            s += n
+        meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
+
+        def work(step):
+            w = [(i, q) for i, n in enumerate(lens) for q in range(0, n, step)]
+            return torch.tensor(np.asarray(w, np.int32).reshape(-1), device=dev), len(w)
+        w64, n64 = work(64)
+        w256, n256 = work(256)
+        g = torch.Generator(device=dev).manual_seed(2)
+        qkv = torch.randn(total, 2048, device=dev, generator=g).half()
+        out = torch.empty(total, 1024, device=dev, dtype=torch.float16)
+        Q, K, V = qkv, qkv[:, 1024:], qkv[:, 1536:]
+        runs = {"tcgen05": lambda: lib.d1_flash_attn_tc(P(Q), 2048, P(K), P(V), 2048, 512, P(out), 1024, P(meta),
+                                                        P(w256), n256, 16, 2, 0.125, total, total, st),
+                "mma_sync": lambda: lib.d1_flash_attn(P(Q), 2048, P(K), P(V), 2048, 512, None, None, None, P(out),
+                                                      1024, P(meta), P(w64), n64, 16, 2, 0.125, st)}
+        if ref is not None:
+            runs["reference"] = lambda: ref.d1_flash_attn(P(Q), 2048, P(K), P(V), 2048, 512, None, None, None,
+                                                          P(out), 1024, P(meta), P(w64), n64, 16, 2, 0.125, st)
+        flops = sum(4.0 * n * n * 64 * 16 for n in lens)
+        rec = {"sweep": "config2", "tokens": total, "sequences": len(lens), "gflop": round(flops / 1e9, 2)}
+        for name, fn in runs.items():
+            for _ in range(warm):
+                assert fn() == 0
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) / reps * 1e3
+            tf = flops / (us * 1e-6) / 1e12
+            rec[name] = {"us": round(us, 2), "tflops": round(tf, 1), "frac_of_peak": round(tf / tflops, 3)}
+        if lib.d1_flash_attn_error():
+            raise RuntimeError("attention kernel reported a wait that gave up")
+        if "reference" in rec:
+            rec["tcgen05_speedup_vs_reference"] = round(rec["reference"]["us"] / rec["tcgen05"]["us"], 3)
+        rec["peak"] = f"{tflops} TFLOP/s ({kind}, bf16 cuBLAS burst)"
+        print(json.dumps(rec), flush=True)
 
 
 MIXED_PER_GPU = 48  # config-4 requests per GPU (weak scaling): ~90K trunk tokens, ~11 batches of 8192
@@ -498,8 +669,20 @@ def main():
                     help="run only the runners' attention kernel on 8192/L sequences of L tokens (an ncu case)")
     ap.add_argument("--only-roofline", action="store_true",
                     help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
+    ap.add_argument("--attn-config2", action="store_true",
+                    help="BASELINE config 2: attention at 2048/8192/16384 packed tokens, this library and the reference")
+    ap.add_argument("--ref-engine-child", type=int, default=-1, metavar="EFFORT", help=argparse.SUPPRESS)
+    ap.add_argument("--sustained-steps", type=int, default=SUSTAINED_STEPS,
+                    help="steps of the second (>= 2 s) timed region; 0 skips it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+
+    if args.ref_engine_child >= 0:  # the reference engine in its own process (see reference_gpu_engine_child)
+        res = reference_gpu_engine(args.steps, args.warmup, args.ref_engine_child)
+        print(json.dumps(res), flush=True)
+        return
+    if args.gemm_sweep:  # the reference's cuBLASLt beside this library's GEMMs: load its cuBLASLt before torch
+        preload_reference_cublaslt()
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -526,6 +709,10 @@ def main():
     if args.gemm_sweep:
         if rank == 0:
             gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
+        return
+    if args.attn_config2:
+        if rank == 0:
+            attn_config2(pkg, dev, reps=args.steps, warm=args.warmup)
         return
     if args.only_attention:
         us, tf = attention_launches(pkg, dev, args.only_attention, reps=args.steps, warm=args.warmup)
@@ -594,14 +781,32 @@ def main():
         d2h = int(model.L.d1h_d2h_bytes(model.ws, 0))
         barrier()
 
+        # ---------------------------------------------------------------- sustained: >= 2 s of steps (value_sustained)
+        sus_ms, sus_clk = 0.0, None
+        if args.sustained_steps > 0:
+            torch.cuda.synchronize(dev)
+            barrier()
+            torch.cuda.synchronize(dev)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with Clocks(local) as sus_clk:
+                s0.record(stream)
+                for i in range(args.sustained_steps):
+                    model.launch(batches[i % 4], i % 2, stream)
+                s1.record(stream)
+                torch.cuda.synchronize(dev)
+            for s in (0, 1):
+                model._pending.pop(s, None)
+            sus_ms = s0.elapsed_time(s1)
+            barrier()
+
     # ---------------------------------------------------------------- roofline: the fused SwiGLU GEMM alone
     gemm_ms = swiglu_gemm_ms(pkg, dev, stream)
 
     # ---------------------------------------------------------------- aggregate over ranks
-    t = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device=dev)
+    t = torch.tensor([dev_ms, e2e_s, sus_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms_max, e2e_max = float(t[0]), float(t[1])
+    dev_ms_max, e2e_max, sus_ms_max = float(t[0]), float(t[1]), float(t[2])
     total_tokens = TOKENS * args.steps * world
     value = total_tokens / (dev_ms_max / 1e3)
     e2e_value = total_tokens / e2e_max
@@ -623,11 +828,22 @@ def main():
             "gemm_tflops_trunk_equiv": GEMM_FLOP_PER_TOKEN * value / world / 1e12,
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc2<256,6,EPI_SWIGLU> (w1|w3 + SwiGLU, CTA pair), M=8192",
                          "achieved": achieved, "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
-                         "peak_kind": f"{kind} (bf16 cuBLAS burst)", "traffic": SWIGLU_TRAFFIC_PER_LAUNCH,
+                         "peak_kind": f"{kind} (bf16 cuBLAS burst)", "traffic": SWIGLU_NCU_DRAM_BYTES_M8192,
+                         "traffic_note": "ncu DRAM read+write of one launch at this shape (2026-12-01 capture); below "
+                                         "the 111 MB algorithmic bytes because the output is still dirty in L2 when "
+                                         "the kernel ends",
                          "gemm_ms": gemm_ms},
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
+        if sus_ms_max > 0:
+            sus_tokens = TOKENS * args.sustained_steps * world
+            line["value_sustained"] = {"value": sus_tokens / (sus_ms_max / 1e3), "unit": "tokens/s",
+                                       "steps": args.sustained_steps, "seconds": sus_ms_max / 1e3,
+                                       "ms_per_step": sus_ms_max / args.sustained_steps,
+                                       "clocks": sus_clk.summary() if sus_clk else None,
+                                       "note": "the same steps back to back for >= 2 s, after the burst region; "
+                                               "clocks settle at the 1 kW power cap"}
         if not args.no_cpu_baseline:
             v, dt = cpu_sample(2)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",

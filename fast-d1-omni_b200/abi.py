@@ -152,6 +152,7 @@ EXTENSIONS = {
     "d1_log_mel": (i32, [p, i32, p, p]),
     "d1_vision_pos": (i32, [p, p, p, p, i32, i32, i32, i32, p, p]),
     "d1_gemm_noalloc": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, i32, p]),
+    "d1_gemm_noalloc_error": (i32, []),
     "d1_lt_destroy": (None, [p]),
     "d1_build_id": (C.c_char_p, []),
 }
@@ -181,6 +182,7 @@ RUNNER = {
     "d1h_vision_capacity": (i32, [p]),
     "d1h_model_layers": (i32, [p, i32]),
     "d1h_gemm_ctx": (p, [p]),
+    "d1h_set_tune_effort": (i32, [p, i32]),
     "d1e_create": (p, [p, p, p, C.POINTER(EngineConfig), p]),
     "d1e_destroy": (None, [p]),
     "d1e_submit": (C.c_longlong, [p, C.POINTER(Job)]),

@@ -1479,7 +1479,7 @@ extern "C" int d1_gemm_noalloc(int M, int N, int K, const d1_half* X, int ldx, c
     if (M < 0 || N < 0 || K < 0 || split < 1 || split > 64) return -1;
     if (M == 0 || N == 0) return 0;
     if ((size_t)M * (size_t)N > kNoallocMaxElems) return -1;  // beyond the static accumulator
-    if (!Y || ldy < N || N % 4 || !tc_ok(X, ldx, W, ldw, 0, K)) return -1;
+    if (!X || !W || !Y || ldy < N || N % 4 || !tc_ok(X, ldx, W, ldw, 0, K)) return -1;
     NoallocDev d;
     if (!noalloc_setup(d)) return -1;
     float* acc = d.scratch;
@@ -1516,5 +1516,18 @@ extern "C" int d1_gemm_noalloc(int M, int N, int K, const d1_half* X, int ldx, c
     const size_t total = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)d.num_sms * 8);
     k_noalloc_to_f16<<<blocks, 256, 0, st>>>(acc, M, N, reinterpret_cast<__half*>(Y), ldy);
-    return (int)cudaGetLastError();
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Reads and clears the error word the last d1_gemm_noalloc call on the current device left in the static buffer
+// (a bounded wait of the GEMM kernel that ran out; Y is then not the product). Synchronous: it waits for the
+// device's work, so the word is the one the last issued call wrote.
+extern "C" int d1_gemm_noalloc_error(void) {
+    NoallocDev d;
+    if (!noalloc_setup(d)) return -1;
+    int* err = reinterpret_cast<int*>(d.scratch + kNoallocErrOff);
+    int e = 0;
+    if (cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (e && cudaMemset(err, 0, sizeof(int)) != cudaSuccess) return -1;
+    return e;
 }

@@ -206,6 +206,7 @@ struct D1Model {
     bool fused = false;
     std::atomic<long long> launches{0};  // engines of one device may share the model
     int dev = 0;
+    int tune_effort = 0;  // d1_lt_tune effort of the plans tuned on first use
 
     // Blas::gemm (src/cuda.rs:433-490): Y = alpha X W^T + beta Y. A library without a plan for the shape
     // (d1_lt_gemm == -2) gets a heuristic plan tuned on the spot instead of a cuBLAS fallback.
@@ -215,7 +216,7 @@ struct D1Model {
         launches++;
         int e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
         if (e == -2) {
-            if (k.lt_tune(lt, m, n, kk, ldx, ldw, 0, ldy, y_f32, 0, 0, st) < 0.f)
+            if (k.lt_tune(lt, m, n, kk, ldx, ldw, 0, ldy, y_f32, 0, tune_effort, st) < 0.f)
                 return fail("GEMM tuning failed for m=" + std::to_string(m) + " n=" + std::to_string(n));
             e = k.lt_gemm(lt, m, n, kk, x, ldx, wt, ldw, 0, y, ldy, y_f32, 0, alpha, beta, st);
         }
@@ -1460,5 +1461,11 @@ int d1h_model_layers(const D1Model* m, int is_attn) {
 }
 
 void* d1h_gemm_ctx(D1Model* m) { return m ? m->lt : nullptr; }
+
+int d1h_set_tune_effort(D1Model* m, int effort) {
+    if (!m || effort < 0 || effort > 2) return -1;
+    m->tune_effort = effort;
+    return 0;
+}
 
 }  // extern "C"

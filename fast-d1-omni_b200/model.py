@@ -149,6 +149,11 @@ class TextModel:
             raise RuntimeError(f"d1h_tune failed: {self.L.d1h_last_error().decode()}")
         return n
 
+    def set_tune_effort(self, effort: int) -> None:
+        """Effort of the GEMM plans tuned on the first use of a shape and M bucket (d1h_set_tune_effort)."""
+        if self.L.d1h_set_tune_effort(self.m, int(effort)) != 0:
+            raise ValueError(f"tune effort {effort} outside 0..2")
+
     def save_plans(self, path: str) -> None:
         """Writes the tuned GEMM plans (d1_lt_save on the model's GEMM context)."""
         if self.L.d1_lt_save(self.L.d1h_gemm_ctx(self.m), path.encode()) != 0:

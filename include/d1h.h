@@ -283,6 +283,11 @@ int d1h_model_layers(const D1Model* m, int is_attn);
 /* The model's GEMM context (the ctx of d1_lt_*): d1_lt_save / d1_lt_load keep its tuned plans across runs, as the
  * reference's engine keeps its cuBLASLt plans (src/engine.rs:528-616). */
 void* d1h_gemm_ctx(D1Model* m);
+/* Effort (the d1_lt_tune argument: 0 heuristics, 1 pruned search, 2 exhaustive) of the plans the model tunes on
+ * the first use of a GEMM shape and M bucket that has none (default 0). The reference's engine tunes its startup
+ * plans at effort 1 (src/engine.rs:593); with effort 1 here, the buckets a workload touches get the same plans
+ * without tuning the ones it never uses. Returns 0, or -1 for a null model or an effort outside 0..2. */
+int d1h_set_tune_effort(D1Model* m, int effort);
 
 /* ------------------------------------------------------------------------------------------------ engine
  * Continuous batching over one device's runners (src/engine.rs:149-525): requests (jobs) of question rows and

@@ -284,10 +284,17 @@ int d1_relpos_attn_error(void);
  * (W nn.Linear, fp32 accumulation), the K range of every 128x128 output tile split across up to `split` CTAs
  * (1 .. 64). Needs no context: its scratch — the fp32 partial sums and the kernels' error word — is a file-scope
  * static device buffer of 2^20 floats (4 MiB), cleared at the start of every call; M*N above 2^20 is rejected
- * (-1), as are N not a multiple of 4 and X/W rows that are not 16-byte aligned. Calls that overlap on one device
- * (other streams or threads) race on that buffer and must not be issued. Returns 0 or an error status. */
+ * (-1), as are null pointers, N not a multiple of 4 and X/W rows that are not 16-byte aligned. Calls that overlap
+ * on one device (other streams or threads) race on that buffer and must not be issued. Returns 0 when both
+ * launches were issued, -1 otherwise (bad argument, set-up failure or launch error); a kernel that gave up on a
+ * bounded wait shows only in d1_gemm_noalloc_error(). */
 int d1_gemm_noalloc(int M, int N, int K, const d1_half* X, int ldx, const d1_half* W, int ldw, d1_half* Y, int ldy,
                     int split, cudaStream_t stream);
+
+/* extension, no reference counterpart — reads and clears the error word of d1_gemm_noalloc on the current device
+ * (0: the last call's GEMM completed; nonzero: one of its bounded waits ran out and Y is not the product; -1: the
+ * word could not be read). Waits for the device's outstanding work. */
+int d1_gemm_noalloc_error(void);
 
 /* extension — releases a context made by d1_lt_init (the reference never frees it). */
 void d1_lt_destroy(void* ctx);

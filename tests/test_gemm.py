@@ -52,9 +52,14 @@ def run_gemm(lib, ctx, x, w, y, alpha=1.0, beta=0.0):
     assert lib.d1_lt_error(ctx) == 0
 
 
+CONFIG1_M = [256, 1024, 4096, 8192, 16384]
+# tile configurations a plan can name (csrc/gemm.cu Cfg): 1-SM 128/256/64-column tiles, CTA pair 256x256 / 256x128
+CFGS = {0: "1sm_128", 1: "1sm_256", 2: "pair_256", 3: "pair_128", 4: "1sm_64"}
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("N,K", CONFIG1_NK)
-@pytest.mark.parametrize("M", [256, 1024, 8192])
+@pytest.mark.parametrize("M", CONFIG1_M)
 def test_config1_f16_out(gpu_lib, ctx, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(M, K, device="cuda", generator=g).half()
@@ -64,9 +69,57 @@ def test_config1_f16_out(gpu_lib, ctx, M, N, K):
     check_f16(y, ref_gemm(x, w))
 
 
+def _forced_ctx(lib, tmp_path, M, N, K, ldy, y_f32, cfg, split):
+    """A fresh context whose only plan runs (N, K) at M's bucket with tile configuration `cfg` and split-K `split`
+    (written in d1_lt_save's format and read back by d1_lt_load)."""
+    c = lib.d1_lt_init(0)
+    assert c
+    path = tmp_path / f"plan_{cfg}_{split}_{y_f32}.txt"
+    path.write_text(f"d1b200-gemm-plans v1 {lib.d1_build_id().decode()}\n"
+                    f"{N} {K} {K} {K} {ldy} 0 {y_f32} 0 {lib.d1_lt_bucket(M)} {cfg} {split} 1.0\n")
+    assert lib.d1_lt_load(c, str(path).encode()) == 1
+    return c
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,K", CONFIG1_NK)
+@pytest.mark.parametrize("M", CONFIG1_M)
+def test_config1_every_plan(gpu_lib, tmp_path, M, N, K):
+    """BASELINE config 1 under every tile configuration the tuner can pick (the tuned plan of a shape depends on
+    the timing of the GPU it runs on): the fp16 store form, and for the residual projections (N = 1024) the trunk's
+    fp32 reduce-add form Y += X.W^T with split-K 1, 2 and 4."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    ref = ref_gemm(x, w)
+    y0 = torch.randn(M, N, device="cuda", generator=g) if N == 1024 else None
+    for cfg in CFGS:
+        c = _forced_ctx(gpu_lib, tmp_path, M, N, K, N, 0, cfg, 1)
+        try:
+            y = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float16)
+            run_gemm(gpu_lib, c, x, w, y)
+            assert gpu_lib.d1_lt_error(c) == 0
+            check_f16(y, ref)
+        finally:
+            gpu_lib.d1_lt_destroy(c)
+        if y0 is None:
+            continue
+        for split in (1, 2, 4):
+            c = _forced_ctx(gpu_lib, tmp_path, M, N, K, N, 1, cfg, split)
+            try:
+                y = y0.clone()
+                run_gemm(gpu_lib, c, x, w, y, 1.0, 1.0)
+                assert gpu_lib.d1_lt_error(c) == 0
+                want = ref + y0.double()
+                err = (y.double() - want).abs().max().item()
+                assert err <= 1e-4 * want.abs().max().item(), (CFGS[cfg], split, err)
+            finally:
+                gpu_lib.d1_lt_destroy(c)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("N,K", [(1024, 1024), (1024, 4608)])
-@pytest.mark.parametrize("M", [1, 3, 127, 129, 512, 1000, 4096])
+@pytest.mark.parametrize("M", [1, 3, 127, 129, 512, 1000, 4096, 16384])
 def test_residual_f32(gpu_lib, ctx, M, N, K):
     """The trunk's residual projections: Y32 = X.W^T + Y32 (beta = 1, src/model.rs:373,390,396)."""
     g = torch.Generator(device="cuda").manual_seed(2)
@@ -141,7 +194,7 @@ def test_wkn_layout(gpu_lib, ctx):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M", [1, 200, 8192])
+@pytest.mark.parametrize("M", [1, 200, 256, 1024, 4096, 8192, 16384])
 def test_swiglu_fused(gpu_lib, ctx, M):
     """d1_gemm_swiglu == d1_lt_gemm(N = 2F) + d1_swiglu (src/model.rs:394-395)."""
     g = torch.Generator(device="cuda").manual_seed(7)

@@ -37,6 +37,7 @@ def test_noalloc_gemm_two_calls(gpu_lib):
         free0 = torch.cuda.mem_get_info()[0]
         assert gpu_lib.d1_gemm_noalloc(M, N, K, P(xd), K, P(wd), K, P(y), N, split, ST()) == 0
         torch.cuda.synchronize()
+        assert gpu_lib.d1_gemm_noalloc_error() == 0  # every bounded wait of the GEMM completed
         if i > 0:  # the second call in a row leaves the device's free memory untouched
             assert torch.cuda.mem_get_info()[0] == free0
         got = y.cpu().numpy().astype(np.float64)
@@ -51,6 +52,7 @@ def test_noalloc_gemm_two_calls(gpu_lib):
     y = torch.empty((M, N), dtype=torch.float16, device="cuda")
     assert gpu_lib.d1_gemm_noalloc(M, N, K, P(torch.from_numpy(x).cuda()), K, P(torch.from_numpy(w).cuda()), K, P(y),
                                    N, split, ST()) == 0
+    assert gpu_lib.d1_gemm_noalloc_error() == 0
     assert half_ulp_close(y.cpu().numpy().astype(np.float64), outs[0], 2.0 ** -10, 2e-4).all()
 
 
@@ -59,3 +61,6 @@ def test_noalloc_gemm_rejects_oversize(gpu_lib):
     y = torch.zeros(1025, 1024, dtype=torch.float16, device="cuda")
     assert gpu_lib.d1_gemm_noalloc(1025, 1024, 1024, P(x), 1024, P(x), 1024, P(y), 1024, 2, ST()) == -1  # M*N > 2^20
     assert gpu_lib.d1_gemm_noalloc(8, 1022, 1024, P(x), 1024, P(x), 1024, P(y), 1024, 2, ST()) == -1     # N % 4
+    assert gpu_lib.d1_gemm_noalloc(8, 1024, 1024, None, 1024, P(x), 1024, P(y), 1024, 2, ST()) == -1      # null X
+    assert gpu_lib.d1_gemm_noalloc(8, 1024, 1024, P(x), 1024, None, 1024, P(y), 1024, 2, ST()) == -1      # null W
+    assert gpu_lib.d1_gemm_noalloc_error() == 0
