@@ -56,6 +56,7 @@ SWIGLU_FLOP_PER_TOKEN = 2 * 9216 * 1024    # w1|w3, fused SwiGLU epilogue
 # algorithmic bytes (A 16.8 MB + W 18.9 MB read, 75.5 MB written) because most of the output is still dirty in the
 # 126 MB L2 when the kernel ends: ncu counts DRAM writes of the launch only.
 SWIGLU_NCU_DRAM_BYTES_M8192 = 69.6e6
+REF_SWEEP_EFFORT = 0   # the reference's d1_lt_tune effort in --gemm-sweep (effort 1 crashes on B200)
 SUSTAINED_STEPS = 440  # second timed region: >= 2 s of back-to-back steps (clocks settle at the power cap)
 
 
@@ -387,8 +388,8 @@ def gemm_sweep(pkg, dev, stream, reps=20):
     Per shape: the plain fp16-store GEMM and the trunk's own form of that projection (residual add into the fp32
     stream for out_proj / w2, the fused SwiGLU for w1|w3). Beside each form, the reference's own path for it
     (oracle/_ref/libd1ref.so, the reference's cuda/gemm.cu + cuda/kernels.cu built unchanged): d1_lt_tune at
-    effort 1 (the reference engine's effort; cuda/gemm.cu searches only up to M 8192 and takes the heuristic
-    candidates above), then d1_lt_gemm; for w1|w3 its GEMM into [g|u] plus its k_swiglu. One JSON line per shape;
+    effort 0 (the cuBLASLt heuristic candidates, each timed; the reference engine's effort-1 search ends the process
+    with SIGSEGV on B200), then d1_lt_gemm; for w1|w3 its GEMM into [g|u] plus its k_swiglu. One JSON line per shape;
     CUDA-event averages over `reps` launches of inputs larger than L2 at M >= 8192 (the smaller shapes are
     L2-resident by nature)."""
     import ctypes as C
@@ -442,7 +443,7 @@ def gemm_sweep(pkg, dev, stream, reps=20):
             for (y_f32,) in tunes:
                 lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, y_f32, 0, 1, st)
                 if ref is not None:
-                    assert ref.d1_lt_tune(rctx, M, N, K, K, K, 0, N, y_f32, 0, 1, st) > 0
+                    assert ref.d1_lt_tune(rctx, M, N, K, K, K, 0, N, y_f32, 0, REF_SWEEP_EFFORT, st) > 0
             if ref is not None:
                 ref.d1_lt_free_scratch(rctx)
             rec = {"sweep": "config1", "shape": name, "M": M, "N": N, "K": K}
@@ -458,7 +459,8 @@ def gemm_sweep(pkg, dev, stream, reps=20):
                     rec[fname]["speedup_vs_reference"] = round(rus / us, 3)
             rec["peak"] = f"{tflops} TFLOP/s ({kind}, bf16 cuBLAS burst)"
             if ref is not None:
-                rec["reference_plans"] = "d1_lt_tune effort 1 (cuBLASLt search up to M 8192, heuristics above)"
+                rec["reference_plans"] = (f"d1_lt_tune effort {REF_SWEEP_EFFORT}: the cuBLASLt heuristic candidates, "
+                                          "each timed (its effort-1 search ends the process with SIGSEGV on B200)")
             out.append(rec)
             print(json.dumps(rec), flush=True)
     err = lib.d1_lt_error(ctx)
@@ -766,6 +768,10 @@ def main():
         dev_ms = e0.elapsed_time(e1)
         barrier()
 
+        # ---------------------------------------------------------------- roofline: the fused SwiGLU GEMM alone
+        gemm_ms = swiglu_gemm_ms(pkg, dev, stream)
+        barrier()
+
         # ---------------------------------------------------------------- end to end through the API (e2e)
         torch.cuda.synchronize(dev)
         barrier()
@@ -798,9 +804,6 @@ def main():
                 model._pending.pop(s, None)
             sus_ms = s0.elapsed_time(s1)
             barrier()
-
-    # ---------------------------------------------------------------- roofline: the fused SwiGLU GEMM alone
-    gemm_ms = swiglu_gemm_ms(pkg, dev, stream)
 
     # ---------------------------------------------------------------- aggregate over ranks
     t = torch.tensor([dev_ms, e2e_s, sus_ms], dtype=torch.float64, device=dev)

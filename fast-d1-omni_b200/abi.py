@@ -151,6 +151,9 @@ EXTENSIONS = {
     "d1_relpos_attn_error": (i32, []),
     "d1_log_mel": (i32, [p, i32, p, p]),
     "d1_vision_pos": (i32, [p, p, p, p, i32, i32, i32, i32, p, p]),
+    "d1_layernorm_rows": (i32, [p, p, f32, p, p, p, p, i32, i32, f32, p]),
+    "d1_sub_conv01": (i32, [p, i32, i32, p, p, p, p, p, i32, i32, p]),
+    "d1_conformer_dw_clips": (i32, [p, p, p, p, p, p, p, p, i32, i32, i32, i32, p]),
     "d1_gemm_noalloc": (i32, [i32, i32, i32, p, i32, p, i32, p, i32, i32, p]),
     "d1_gemm_noalloc_error": (i32, []),
     "d1_lt_destroy": (None, [p]),

@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, co
 template <int NV>
 __global__ void __launch_bounds__(256) k_layernorm(float* x, const float* __restrict__ pend, float pend_scale,
                                                    const float* __restrict__ w, const float* __restrict__ b,
-                                                   __half* __restrict__ y, float* yf, int rows, float eps) {
+                                                   __half* __restrict__ y, float* yf,
+                                                   const int* __restrict__ y_rows, int rows, float eps) {
     pdl_entry();
     constexpr int D = NV * 128;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -108,7 +109,10 @@ __global__ void __launch_bounds__(256) k_layernorm(float* x, const float* __rest
         o.y = (v[i].y - mean) * r * g.y + bb.y;
         o.z = (v[i].z - mean) * r * g.z + bb.z;
         o.w = (v[i].w - mean) * r * g.w + bb.w;
-        if (y) reinterpret_cast<uint2*>(y + (size_t)row * D)[lane + 32 * i] = make_uint2(h2u(o.x, o.y), h2u(o.z, o.w));
+        if (y) {
+            const size_t yr = y_rows ? (size_t)__ldg(y_rows + row) : (size_t)row;
+            reinterpret_cast<uint2*>(y + yr * D)[lane + 32 * i] = make_uint2(h2u(o.x, o.y), h2u(o.z, o.w));
+        }
         if (yf) reinterpret_cast<float4*>(yf + (size_t)row * D)[lane + 32 * i] = o;
     }
 }
@@ -530,53 +534,158 @@ __global__ void __launch_bounds__(256) k_vision_pos(const float* __restrict__ gr
     }
 }
 
-__global__ void k_unshuffle(const __half* __restrict__ x, __half* __restrict__ out, int ph, int pw, int C) {
+// 2x2 pixel unshuffle (cuda/kernels.cu:517-525) as a row permutation: viewed as [ph*pw][C], row 4*o + q of
+// out [(ph/2)*(pw/2)][4C] is input row (2*(o / (pw/2)) + (q >> 1)) * pw + 2*(o % (pw/2)) + (q & 1). A flat grid
+// over the 16-byte vectors of out, each thread computing its source vector: every load and store is a whole
+// 16-byte vector and consecutive threads touch consecutive output bytes. (The runners fold the permutation into
+// the post-LayerNorm's stores instead: d1_layernorm_rows.)
+__global__ void __launch_bounds__(256) k_unshuffle16(const uint4* __restrict__ x, uint4* __restrict__ out, int pw,
+                                                     int vpr, long long total) {
     pdl_entry();
-    const int o = blockIdx.x;
-    const int i = o / (pw / 2), jj = o % (pw / 2);
-    for (int k = threadIdx.x * 8; k < 4 * C; k += blockDim.x * 8) {
-        const int q = k / C, c = k % C;
-        const int yy = 2 * i + (q >> 1), xx = 2 * jj + (q & 1);
-        *reinterpret_cast<uint4*>(out + (size_t)o * 4 * C + k) =
-            __ldg(reinterpret_cast<const uint4*>(x + ((size_t)yy * pw + xx) * C + c));
+    const int hw = pw >> 1;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / vpr;
+        const int v = (int)(i - r * vpr), o = (int)(r >> 2), q = (int)(r & 3);
+        const long long src = (long long)(2 * (o / hw) + (q >> 1)) * pw + 2 * (o % hw) + (q & 1);
+        out[i] = __ldg(x + src * vpr + v);
     }
 }
 
 // ------------------------------------------------------------------------------------------------ audio
-// First subsampling conv: mel [Tin][F] -> [Tout][Fout][256], 3x3 stride 2, pad 1, ReLU (cuda/kernels.cu:529-545).
-__global__ void __launch_bounds__(256) k_sub_conv0(const float* __restrict__ mel, int tin_valid, int F,
-                                                   const float* __restrict__ w, const float* __restrict__ b,
-                                                   float* __restrict__ out, int Tout, int Fout) {
+// The FastConformer subsampling (src/audio.rs:514-525): conv0 = 3x3 stride-2 conv 1 -> 256 channels + ReLU over the
+// mel frames (cuda/kernels.cu:529-545), then 3x3 stride-2 depthwise convs (:548-564). Per output element both sum
+// bias + w.x over the taps in (dt, df) order as fused multiply-adds, skipping taps outside the valid input — the
+// reference's arithmetic, so the results are bit-identical. The data movement is this file's own:
+//   k_sub_conv0_rows   one CTA per output time row, a thread per channel keeping its 9 weights in registers; the
+//                      three mel rows it reads are staged once in shared memory and broadcast to all channels.
+//   k_sub_conv01       conv0 and the first depthwise conv fused: a CTA per (output row of the depthwise conv,
+//                      32-channel group) computes the three conv0 rows it needs into shared memory (never written
+//                      to HBM) and convolves them there.
+//   k_dw3s2_v4         the depthwise conv alone: a thread per (output position, 4 channels), 16-byte loads and
+//                      stores, the 36 weights of its channels in registers.
+constexpr int kSubC = 256;
+
+__global__ void __launch_bounds__(256) k_sub_conv0_rows(const float* __restrict__ mel, int tin_valid, int F,
+                                                        const float* __restrict__ w, const float* __restrict__ b,
+                                                        float* __restrict__ out, int Fout) {
+    extern __shared__ float rows3[];  // [3][F]
     pdl_entry();
-    const int t = blockIdx.x, f = blockIdx.y, c = threadIdx.x;
-    __shared__ float patch[9];
-    if (threadIdx.x < 9) {
-        const int ti = 2 * t - 1 + threadIdx.x / 3, fi = 2 * f - 1 + threadIdx.x % 3;
-        patch[threadIdx.x] = (ti >= 0 && ti < tin_valid && fi >= 0 && fi < F) ? mel[(size_t)ti * F + fi] : 0.f;
+    const int t = blockIdx.x, c = threadIdx.x;
+    for (int i = threadIdx.x; i < 3 * F; i += blockDim.x) {
+        const int ti = 2 * t - 1 + i / F;
+        rows3[i] = (ti >= 0 && ti < tin_valid) ? mel[(size_t)ti * F + i % F] : 0.f;
     }
+    float wc[9];
+#pragma unroll
+    for (int k = 0; k < 9; k++) wc[k] = __ldg(w + c * 9 + k);
+    const float bc = __ldg(b + c);
+    bool rv[3];
+#pragma unroll
+    for (int dt = 0; dt < 3; dt++) rv[dt] = 2 * t - 1 + dt >= 0 && 2 * t - 1 + dt < tin_valid;
     __syncthreads();
-    float acc = b[c];
+    for (int f = 0; f < Fout; f++) {
+        float acc = bc;
 #pragma unroll
-    for (int dt = 0; dt < 3; dt++) {
-        const int ti = 2 * t - 1 + dt;
-        if (ti < 0 || ti >= tin_valid) continue;
+        for (int dt = 0; dt < 3; dt++) {
+            if (!rv[dt]) continue;
 #pragma unroll
-        for (int df = 0; df < 3; df++) {
-            const int fi = 2 * f - 1 + df;
-            if (fi < 0 || fi >= F) continue;
-            acc += w[c * 9 + dt * 3 + df] * patch[dt * 3 + df];
+            for (int df = 0; df < 3; df++) {
+                const int fi = 2 * f - 1 + df;
+                if (fi >= 0 && fi < F) acc = __fmaf_rn(wc[dt * 3 + df], rows3[dt * F + fi], acc);
+            }
         }
+        out[((size_t)t * Fout + f) * kSubC + c] = fmaxf(acc, 0.f);
     }
-    out[((size_t)t * Fout + f) * 256 + c] = fmaxf(acc, 0.f);
 }
 
-// Depthwise 3x3 stride-2 conv on [Tin][Fin][256] (cuda/kernels.cu:548-564).
-__global__ void __launch_bounds__(256) k_sub_dwconv(const float* __restrict__ x, int tin_valid, int Fin,
-                                                    const float* __restrict__ w, const float* __restrict__ b,
-                                                    float* __restrict__ out, int Fout) {
+constexpr int kSubGroup = 32;   // channels per CTA of the fused kernel
+constexpr int kSubMaxF = 128;   // mel bins the fused kernel stages (the encoder's 128)
+constexpr int kSubMaxF1 = 64;   // conv0 output bins: (kSubMaxF - 1) / 2 + 1
+
+__global__ void __launch_bounds__(256) k_sub_conv01(const float* __restrict__ mel, int tin_valid, int F,
+                                                    const float* __restrict__ w0, const float* __restrict__ b0,
+                                                    const float* __restrict__ w1, const float* __restrict__ b1,
+                                                    float* __restrict__ out, int l1, int F1, int F2) {
+    __shared__ float m7[7][kSubMaxF];                  // mel rows 4*t2-3 .. 4*t2+3
+    __shared__ float s1[3][kSubMaxF1][kSubGroup];      // conv0 rows 2*t2-1 .. 2*t2+1, this CTA's channels
     pdl_entry();
-    const int t = blockIdx.x, f = blockIdx.y, c = threadIdx.x;
-    float acc = b[c];
+    const int t2 = blockIdx.x, c0 = blockIdx.y * kSubGroup;
+    const int c = threadIdx.x & (kSubGroup - 1), g = threadIdx.x / kSubGroup, ng = blockDim.x / kSubGroup;
+    for (int i = threadIdx.x; i < 7 * F; i += blockDim.x) {
+        const int ti = 4 * t2 - 3 + i / F;
+        m7[i / F][i % F] = (ti >= 0 && ti < tin_valid) ? mel[(size_t)ti * F + i % F] : 0.f;
+    }
+    float wa[9], wb[9];
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+        wa[k] = __ldg(w0 + (c0 + c) * 9 + k);
+        wb[k] = __ldg(w1 + (c0 + c) * 9 + k);
+    }
+    const float ba = __ldg(b0 + c0 + c), bb = __ldg(b1 + c0 + c);
+    __syncthreads();
+    // conv0 rows r = 2*t2 - 1 + j (those inside [0, l1)), mel row of tap dt: 2r - 1 + dt = 4*t2 - 3 + 2j + dt
+    for (int j = 0; j < 3; j++) {
+        const int r = 2 * t2 - 1 + j;
+        if (r < 0 || r >= l1) continue;
+        bool rv[3];
+#pragma unroll
+        for (int dt = 0; dt < 3; dt++) rv[dt] = 2 * r - 1 + dt >= 0 && 2 * r - 1 + dt < tin_valid;
+        for (int f = g; f < F1; f += ng) {
+            float acc = ba;
+#pragma unroll
+            for (int dt = 0; dt < 3; dt++) {
+                if (!rv[dt]) continue;
+#pragma unroll
+                for (int df = 0; df < 3; df++) {
+                    const int fi = 2 * f - 1 + df;
+                    if (fi >= 0 && fi < F) acc = __fmaf_rn(wa[dt * 3 + df], m7[2 * j + dt][fi], acc);
+                }
+            }
+            s1[j][f][c] = fmaxf(acc, 0.f);
+        }
+    }
+    __syncthreads();
+    bool rv[3];
+#pragma unroll
+    for (int dt = 0; dt < 3; dt++) rv[dt] = 2 * t2 - 1 + dt >= 0 && 2 * t2 - 1 + dt < l1;
+    for (int f2 = g; f2 < F2; f2 += ng) {
+        float acc = bb;
+#pragma unroll
+        for (int dt = 0; dt < 3; dt++) {
+            if (!rv[dt]) continue;
+#pragma unroll
+            for (int df = 0; df < 3; df++) {
+                const int fi = 2 * f2 - 1 + df;
+                if (fi >= 0 && fi < F1) acc = __fmaf_rn(wb[dt * 3 + df], s1[dt][fi][c], acc);
+            }
+        }
+        out[((size_t)t2 * F2 + f2) * kSubC + c0 + c] = acc;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_dw3s2_v4(const float4* __restrict__ x, int tin_valid, int Fin,
+                                                  const float* __restrict__ w, const float* __restrict__ b,
+                                                  float4* __restrict__ out, int Tout, int Fout) {
+    pdl_entry();
+    constexpr int V = kSubC / 4;  // float4 vectors per position
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)Tout * Fout * V) return;
+    const int v = (int)(i % V);
+    const long long pos = i / V;
+    const int f = (int)(pos % Fout), t = (int)(pos / Fout);
+    // weights of channels 4v .. 4v+3: 36 consecutive floats, tap-major per channel
+    float wr[36];
+    const float4* w4 = reinterpret_cast<const float4*>(w + (size_t)v * 36);
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+        const float4 q = __ldg(w4 + k);
+        wr[4 * k] = q.x;
+        wr[4 * k + 1] = q.y;
+        wr[4 * k + 2] = q.z;
+        wr[4 * k + 3] = q.w;
+    }
+    float4 acc = __ldg(reinterpret_cast<const float4*>(b) + v);
 #pragma unroll
     for (int dt = 0; dt < 3; dt++) {
         const int ti = 2 * t - 1 + dt;
@@ -585,84 +694,176 @@ __global__ void __launch_bounds__(256) k_sub_dwconv(const float* __restrict__ x,
         for (int df = 0; df < 3; df++) {
             const int fi = 2 * f - 1 + df;
             if (fi < 0 || fi >= Fin) continue;
-            acc += w[c * 9 + dt * 3 + df] * x[((size_t)ti * Fin + fi) * 256 + c];
+            const float4 xv = __ldg(x + ((size_t)ti * Fin + fi) * V + v);
+            const int k = dt * 3 + df;
+            acc.x = __fmaf_rn(wr[k], xv.x, acc.x);
+            acc.y = __fmaf_rn(wr[9 + k], xv.y, acc.y);
+            acc.z = __fmaf_rn(wr[18 + k], xv.z, acc.z);
+            acc.w = __fmaf_rn(wr[27 + k], xv.w, acc.w);
         }
     }
-    out[((size_t)t * Fout + f) * 256 + c] = acc;
+    out[i] = acc;
 }
 
-// qkv [T][3Dm] -> qu = q+bq+u, qv = q+bq+v, k+bk, v+bv (cuda/kernels.cu:566-580).
-__global__ void k_relpos_prep(const __half* __restrict__ qkv, const float* __restrict__ bq,
-                              const float* __restrict__ bk, const float* __restrict__ bv, const float* __restrict__ pu,
-                              const float* __restrict__ pv, __half* __restrict__ qu, __half* __restrict__ qvv,
-                              __half* __restrict__ k, __half* __restrict__ v, int T, int Dm) {
+// Rel-pos attention inputs (cuda/kernels.cu:566-580): qu = half(q + bq + u), qv = half(q + bq + v),
+// k = half(k + bk), v = half(v + bv) from qkv [T][3Dm] (fp32 sums in that order). A flat grid over 8-column groups
+// of all rows: one 16-byte load of each of q, k, v and four 16-byte stores per thread (VEC 8), or one column per
+// thread when Dm or the pointers do not allow 16-byte vectors (VEC 1).
+template <int VEC>
+__global__ void __launch_bounds__(256) k_relpos_prep_v(const __half* __restrict__ qkv, const float* __restrict__ bq,
+                                                       const float* __restrict__ bk, const float* __restrict__ bv,
+                                                       const float* __restrict__ pu, const float* __restrict__ pv,
+                                                       __half* __restrict__ qu, __half* __restrict__ qvv,
+                                                       __half* __restrict__ ko, __half* __restrict__ vo, int T,
+                                                       int Dm) {
     pdl_entry();
-    const int t = blockIdx.x;
-    const __half* r = qkv + (size_t)t * 3 * Dm;
-    for (int c = threadIdx.x; c < Dm; c += blockDim.x) {
-        const float q = __half2float(r[c]) + bq[c];
-        qu[(size_t)t * Dm + c] = __float2half(q + pu[c]);
-        qvv[(size_t)t * Dm + c] = __float2half(q + pv[c]);
-        k[(size_t)t * Dm + c] = __float2half(__half2float(r[Dm + c]) + bk[c]);
-        v[(size_t)t * Dm + c] = __float2half(__half2float(r[2 * Dm + c]) + bv[c]);
+    const int gpr = Dm / VEC;
+    const long long n = (long long)T * gpr;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / gpr), c = (int)(i - (long long)t * gpr) * VEC;
+        const __half* r = qkv + (size_t)t * 3 * Dm;
+        float q[VEC], k[VEC], v[VEC];
+        if constexpr (VEC == 8) {
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(r + c)), q);
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(r + Dm + c)), k);
+            h8_to_f(__ldg(reinterpret_cast<const uint4*>(r + 2 * Dm + c)), v);
+        } else {
+            q[0] = __half2float(r[c]);
+            k[0] = __half2float(r[Dm + c]);
+            v[0] = __half2float(r[2 * Dm + c]);
+        }
+        float a[VEC], bq2[VEC], kk[VEC], vv[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; e++) {
+            const float qb = q[e] + __ldg(bq + c + e);
+            a[e] = qb + __ldg(pu + c + e);
+            bq2[e] = qb + __ldg(pv + c + e);
+            kk[e] = k[e] + __ldg(bk + c + e);
+            vv[e] = v[e] + __ldg(bv + c + e);
+        }
+        const size_t o = (size_t)t * Dm + c;
+        if constexpr (VEC == 8) {
+            *reinterpret_cast<uint4*>(qu + o) = f_to_h8(a);
+            *reinterpret_cast<uint4*>(qvv + o) = f_to_h8(bq2);
+            *reinterpret_cast<uint4*>(ko + o) = f_to_h8(kk);
+            *reinterpret_cast<uint4*>(vo + o) = f_to_h8(vv);
+        } else {
+            qu[o] = __float2half(a[0]);
+            qvv[o] = __float2half(bq2[0]);
+            ko[o] = __float2half(kk[0]);
+            vo[o] = __float2half(vv[0]);
+        }
     }
 }
 
-// p[h][i][j] = softmax_j((ac[h][i][j] + bd[h][i][j + T-1-i]) * scale) (cuda/kernels.cu:582-616).
-__global__ void __launch_bounds__(256) k_relpos_softmax(const float* __restrict__ ac, const float* __restrict__ bd,
-                                                        __half* __restrict__ p, int T, float scale) {
+// p[h][i][j] = softmax_j((ac[h][i][j] + bd[h][i][j + T-1-i]) * scale) (cuda/kernels.cu:582-616: the same formulas
+// — row max, sum of expf(z - max), expf(z - max) * (1 / sum)). One warp per row; each lane keeps its K scores of
+// the row in registers (rows of up to 32*K columns), so ac and bd are read once instead of once per pass.
+// K == 0: longer rows, re-read per pass.
+template <int K>
+__global__ void __launch_bounds__(256) k_relpos_softmax_warp(const float* __restrict__ ac, const float* __restrict__ bd,
+                                                             __half* __restrict__ p, int T, int H, float scale) {
     pdl_entry();
-    const int h = blockIdx.y, i = blockIdx.x;
-    const float* a = ac + ((size_t)h * T + i) * T;
-    const float* b = bd + ((size_t)h * T + i) * (2 * T - 1) + (T - 1 - i);
-    __shared__ float red[32];
+    const int lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= (long long)H * T) return;
+    const int i = (int)(row % T);
+    const float* a = ac + row * T;
+    const float* b = bd + row * (2 * T - 1) + (T - 1 - i);
+    __half* pr = p + row * T;
     float mx = -INFINITY;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) mx = fmaxf(mx, (a[j] + b[j]) * scale);
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -INFINITY;
-        v = warp_max(v);
-        if (threadIdx.x == 0) red[0] = v;
+    if constexpr (K > 0) {
+        float z[K];
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int j = lane + 32 * k;
+            z[k] = j < T ? (__ldg(a + j) + __ldg(b + j)) * scale : -INFINITY;
+            mx = fmaxf(mx, z[k]);
+        }
+        mx = warp_max(mx);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            z[k] = expf(z[k] - mx);  // exp(-inf) = 0 for the padding lanes
+            s += z[k];
+        }
+        const float inv = 1.f / warp_sum(s);
+#pragma unroll
+        for (int k = 0; k < K; k++)
+            if (lane + 32 * k < T) pr[lane + 32 * k] = __float2half(z[k] * inv);
+    } else {
+        for (int j = lane; j < T; j += 32) mx = fmaxf(mx, (__ldg(a + j) + __ldg(b + j)) * scale);
+        mx = warp_max(mx);
+        float s = 0.f;
+        for (int j = lane; j < T; j += 32) s += expf((__ldg(a + j) + __ldg(b + j)) * scale - mx);
+        const float inv = 1.f / warp_sum(s);
+        for (int j = lane; j < T; j += 32) pr[j] = __float2half(expf((__ldg(a + j) + __ldg(b + j)) * scale - mx) * inv);
     }
-    __syncthreads();
-    mx = red[0];
-    __syncthreads();
-    float sum = 0.f;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) sum += expf((a[j] + b[j]) * scale - mx);
-    sum = warp_sum(sum);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    const float inv = 1.f / red[0];
-    __half* pr = p + ((size_t)h * T + i) * T;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) pr[j] = __float2half(expf((a[j] + b[j]) * scale - mx) * inv);
 }
 
-// Conformer conv module middle: GLU -> depthwise k (zero pad) + bias -> BN affine -> SiLU (cuda/kernels.cu:618-637).
-__global__ void k_conformer_dw(const __half* __restrict__ a, const float* __restrict__ b1, const float* __restrict__ dw,
-                               const float* __restrict__ dwb, const float* __restrict__ bn_s,
-                               const float* __restrict__ bn_b, __half* __restrict__ out, int T, int C, int ksize) {
+// Conformer conv module middle (cuda/kernels.cu:618-637): GLU (x + b1) * sigmoid(gate + b1'), depthwise conv of
+// `ksize` taps zero-padded at each clip's edges + bias, BN affine, SiLU, fp16 out; the reference's arithmetic per
+// element (GLU values, then fused multiply-adds over the taps in order, then the affine). Data movement: a CTA per
+// (32-row time window, 64-channel group) over the packed rows of all clips. The GLU of every input row the window
+// reads (window + halo) is computed once into shared memory — not once per tap — and the taps are summed from
+// there; each output row finds its clip's bounds in `offs` (null: one clip of all rows).
+constexpr int kCdwRows = 32, kCdwCh = 64, kCdwMaxK = 31;
+
+__global__ void __launch_bounds__(256) k_conformer_glu_dw(const __half* __restrict__ a, const float* __restrict__ b1,
+                                                          const float* __restrict__ dw, const float* __restrict__ dwb,
+                                                          const float* __restrict__ bn_s,
+                                                          const float* __restrict__ bn_b, __half* __restrict__ out,
+                                                          const int* __restrict__ offs, int n_clips, int R, int C,
+                                                          int ksize) {
+    __shared__ float glu[kCdwRows + kCdwMaxK - 1][kCdwCh];
+    __shared__ int clip_lo[kCdwRows], clip_hi[kCdwRows];
     pdl_entry();
-    const int t = blockIdx.x;
-    const int pad = (ksize - 1) / 2;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float acc = dwb[c];
-        for (int kk = 0; kk < ksize; kk++) {
-            const int ti = t + kk - pad;
-            if (ti < 0 || ti >= T) continue;
-            const float x = __half2float(a[(size_t)ti * 2 * C + c]) + b1[c];
-            const float gt = __half2float(a[(size_t)ti * 2 * C + C + c]) + b1[C + c];
-            acc += dw[c * ksize + kk] * (x / (1.f + expf(-gt)));
+    const int r0 = blockIdx.x * kCdwRows, c0 = blockIdx.y * kCdwCh;
+    const int pad = (ksize - 1) / 2, span = kCdwRows + ksize - 1;
+    const int cl = threadIdx.x % kCdwCh, rg = threadIdx.x / kCdwCh, nrg = blockDim.x / kCdwCh;
+    const int c = c0 + cl;
+    if (threadIdx.x < kCdwRows) {
+        const int r = r0 + threadIdx.x;
+        int lo = 0, hi = R;
+        if (offs && r < R) {  // the clip holding row r: offs[k] <= r < offs[k + 1]
+            int l = 0, h = n_clips;
+            while (h - l > 1) {
+                const int m = (l + h) >> 1;
+                if (__ldg(offs + m) <= r) l = m; else h = m;
+            }
+            lo = __ldg(offs + l);
+            hi = __ldg(offs + l + 1);
         }
-        acc = acc * bn_s[c] + bn_b[c];
-        out[(size_t)t * C + c] = __float2half(silu(acc));
+        clip_lo[threadIdx.x] = lo;
+        clip_hi[threadIdx.x] = hi;
+    }
+    if (c < C) {
+        const float bx = __ldg(b1 + c), bg = __ldg(b1 + C + c);
+        for (int j = rg; j < span; j += nrg) {
+            const int ti = r0 - pad + j;
+            float gv = 0.f;
+            if (ti >= 0 && ti < R) {
+                const float x = __half2float(a[(size_t)ti * 2 * C + c]) + bx;
+                const float gt = __half2float(a[(size_t)ti * 2 * C + C + c]) + bg;
+                gv = x / (1.f + expf(-gt));
+            }
+            glu[j][cl] = gv;
+        }
+    }
+    __syncthreads();
+    if (c >= C) return;
+    const float bias = __ldg(dwb + c), s = __ldg(bn_s + c), sh = __ldg(bn_b + c);
+    for (int i = rg; i < kCdwRows; i += nrg) {
+        const int r = r0 + i;
+        if (r >= R) break;
+        const int lo = clip_lo[i], hi = clip_hi[i];
+        float acc = bias;
+        for (int kk = 0; kk < ksize; kk++) {
+            const int ti = r + kk - pad;
+            if (ti >= lo && ti < hi) acc = __fmaf_rn(__ldg(dw + (size_t)c * ksize + kk), glu[i + kk][cl], acc);
+        }
+        acc = __fmaf_rn(acc, s, sh);
+        out[(size_t)r * C + c] = __float2half(silu(acc));
     }
 }
 
@@ -693,9 +894,9 @@ int d1_layernorm(float* x, const float* pend_bias, float pend_scale, const float
         return -1;
     const int grid = nblk(rows, 8);
     switch (D) {
-        case 1024: launch_pdl(k_layernorm<8>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
-        case 768: launch_pdl(k_layernorm<6>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
-        case 512: launch_pdl(k_layernorm<4>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, rows, eps); break;
+        case 1024: launch_pdl(k_layernorm<8>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, nullptr, rows, eps); break;
+        case 768: launch_pdl(k_layernorm<6>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, nullptr, rows, eps); break;
+        case 512: launch_pdl(k_layernorm<4>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, yf, nullptr, rows, eps); break;
         default: return -1;
     }
     return (int)cudaGetLastError();
@@ -802,45 +1003,95 @@ int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, con
 
 int d1_unshuffle(const d1_half* x, d1_half* out, int ph, int pw, int C, cudaStream_t st) {
     if (ph <= 0 || pw <= 0) return 0;
-    if (C % 8 || !al16(x) || !al16(out)) return -1;
-    launch_pdl(k_unshuffle, (ph / 2) * (pw / 2), 128, 0, st, x, out, ph, pw, C);
+    if ((ph & 1) || (pw & 1) || C % 8 || !al16(x) || !al16(out)) return -1;
+    const long long total = (long long)ph * pw * (C / 8);
+    launch_pdl(k_unshuffle16, egrid((size_t)total, 256), 256, 0, st, reinterpret_cast<const uint4*>(x),
+               reinterpret_cast<uint4*>(out), pw, C / 8, total);
     return (int)cudaGetLastError();
 }
 
 int d1_sub_conv0(const float* mel, int tin_valid, int F, const float* w, const float* b, float* out, int Tout, int Fout,
                  cudaStream_t st) {
     if (Tout <= 0 || Fout <= 0) return 0;
-    dim3 grid(Tout, Fout);
-    launch_pdl(k_sub_conv0, grid, 256, 0, st, mel, tin_valid, F, w, b, out, Tout, Fout);
+    if (!mel || !w || !b || !out || F <= 0 || F > 4096 || tin_valid < 0) return -1;
+    launch_pdl(k_sub_conv0_rows, Tout, kSubC, (size_t)3 * F * sizeof(float), st, mel, tin_valid, F, w, b, out, Fout);
     return (int)cudaGetLastError();
 }
 
 int d1_sub_dwconv(const float* x, int tin_valid, int Fin, const float* w, const float* b, float* out, int Tout,
                   int Fout, cudaStream_t st) {
     if (Tout <= 0 || Fout <= 0) return 0;
-    dim3 grid(Tout, Fout);
-    launch_pdl(k_sub_dwconv, grid, 256, 0, st, x, tin_valid, Fin, w, b, out, Fout);
+    if (!al16(x) || !al16(w) || !al16(b) || !al16(out) || Fin <= 0 || tin_valid < 0) return -1;
+    const long long n = (long long)Tout * Fout * (kSubC / 4);
+    launch_pdl(k_dw3s2_v4, nblk((size_t)n, 256), 256, 0, st, reinterpret_cast<const float4*>(x), tin_valid, Fin, w, b,
+               reinterpret_cast<float4*>(out), Tout, Fout);
     return (int)cudaGetLastError();
 }
 
 int d1_relpos_prep(const d1_half* qkv, const float* bq, const float* bk, const float* bv, const float* pu,
                    const float* pv, d1_half* qu, d1_half* qv, d1_half* k, d1_half* v, int T, int Dm, cudaStream_t st) {
-    if (T <= 0) return 0;
-    launch_pdl(k_relpos_prep, T, 256, 0, st, qkv, bq, bk, bv, pu, pv, qu, qv, k, v, T, Dm);
+    if (T <= 0 || Dm <= 0) return T == 0 ? 0 : -1;
+    if (Dm % 8 == 0 && al16(qkv) && al16(qu) && al16(qv) && al16(k) && al16(v))
+        launch_pdl(k_relpos_prep_v<8>, egrid((size_t)T * Dm / 8, 256), 256, 0, st, qkv, bq, bk, bv, pu, pv, qu, qv, k, v,
+                   T, Dm);
+    else
+        launch_pdl(k_relpos_prep_v<1>, egrid((size_t)T * Dm, 256), 256, 0, st, qkv, bq, bk, bv, pu, pv, qu, qv, k, v,
+                   T, Dm);
     return (int)cudaGetLastError();
 }
 
 int d1_relpos_softmax(const float* ac, const float* bd, d1_half* p, int T, int H, float scale, cudaStream_t st) {
     if (T <= 0 || H <= 0) return 0;
-    dim3 grid(T, H);
-    launch_pdl(k_relpos_softmax, grid, 256, 0, st, ac, bd, p, T, scale);
+    const int grid = nblk((size_t)T * H, 8);  // a warp per row, 8 rows per CTA
+    if (T <= 128)
+        launch_pdl(k_relpos_softmax_warp<4>, grid, 256, 0, st, ac, bd, p, T, H, scale);
+    else if (T <= 256)
+        launch_pdl(k_relpos_softmax_warp<8>, grid, 256, 0, st, ac, bd, p, T, H, scale);
+    else if (T <= 512)
+        launch_pdl(k_relpos_softmax_warp<16>, grid, 256, 0, st, ac, bd, p, T, H, scale);
+    else
+        launch_pdl(k_relpos_softmax_warp<0>, grid, 256, 0, st, ac, bd, p, T, H, scale);
     return (int)cudaGetLastError();
 }
 
 int d1_conformer_dw(const d1_half* a, const float* b1, const float* dw, const float* dwb, const float* bn_s,
                     const float* bn_b, d1_half* out, int T, int C, int ksize, cudaStream_t st) {
-    if (T <= 0) return 0;
-    launch_pdl(k_conformer_dw, T, 256, 0, st, a, b1, dw, dwb, bn_s, bn_b, out, T, C, ksize);
+    return d1_conformer_dw_clips(a, b1, dw, dwb, bn_s, bn_b, out, nullptr, 1, T, C, ksize, st);
+}
+
+int d1_conformer_dw_clips(const d1_half* a, const float* b1, const float* dw, const float* dwb, const float* bn_s,
+                          const float* bn_b, d1_half* out, const int* offs, int n_clips, int rows, int C, int ksize,
+                          cudaStream_t st) {
+    if (rows <= 0) return rows == 0 ? 0 : -1;
+    if (C <= 0 || ksize < 1 || ksize > kCdwMaxK || n_clips < 1 || !a || !b1 || !dw || !dwb || !bn_s || !bn_b || !out)
+        return -1;
+    dim3 grid(nblk(rows, kCdwRows), nblk(C, kCdwCh));
+    launch_pdl(k_conformer_glu_dw, grid, 256, 0, st, a, b1, dw, dwb, bn_s, bn_b, out, offs, n_clips, rows, C, ksize);
+    return (int)cudaGetLastError();
+}
+
+int d1_sub_conv01(const float* mel, int tin_valid, int F, const float* w0, const float* b0, const float* w1,
+                  const float* b1, float* out, int l1, int l2, cudaStream_t st) {
+    if (l2 <= 0) return l2 == 0 ? 0 : -1;
+    const int F1 = (F - 1) / 2 + 1, F2 = (F1 - 1) / 2 + 1;
+    if (!mel || !w0 || !b0 || !w1 || !b1 || !out || F <= 0 || F > kSubMaxF || l1 <= 0 || tin_valid < 0) return -1;
+    dim3 grid(l2, kSubC / kSubGroup);
+    launch_pdl(k_sub_conv01, grid, 256, 0, st, mel, tin_valid, F, w0, b0, w1, b1, out, l1, F1, F2);
+    return (int)cudaGetLastError();
+}
+
+int d1_layernorm_rows(float* x, const float* pend_bias, float pend_scale, const float* w, const float* b, d1_half* y,
+                      const int* y_rows, int rows, int D, float eps, cudaStream_t st) {
+    if (rows <= 0) return rows == 0 ? 0 : -1;
+    if (!y || !y_rows || !al16(x) || !al16(w) || !al16(b) || (pend_bias && !al16(pend_bias)) || ((uintptr_t)y & 7))
+        return -1;
+    const int grid = nblk(rows, 8);
+    switch (D) {
+        case 1024: launch_pdl(k_layernorm<8>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, nullptr, y_rows, rows, eps); break;
+        case 768: launch_pdl(k_layernorm<6>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, nullptr, y_rows, rows, eps); break;
+        case 512: launch_pdl(k_layernorm<4>, grid, 256, 0, st, x, pend_bias, pend_scale, w, b, y, nullptr, y_rows, rows, eps); break;
+        default: return -1;
+    }
     return (int)cudaGetLastError();
 }
 

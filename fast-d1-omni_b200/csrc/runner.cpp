@@ -1010,6 +1010,21 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
             pos_taps[i] = (int)taps;
         }
     }
+    // fused: the unshuffle (src/vision.rs:372-376) as the output rows of the post-LayerNorm, which then writes the
+    // projector input directly (row y*pw + x of a crop -> row 4*((y/2)*(pw/2) + x/2) + 2*(y%2) + x%2 of big)
+    const int* d_unshuffle = nullptr;
+    if (v->fused && v->builtin) {
+        std::vector<int> yr((size_t)t);
+        size_t src = 0, dst = 0;
+        for (int i = 0; i < n_crops; i++) {
+            const int hw = pw[i] / 2;
+            for (int y = 0; y < ph[i]; y++)
+                for (int x = 0; x < pw[i]; x++)
+                    yr[src++] = (int)(4 * (dst + (size_t)(y / 2) * hw + x / 2) + 2 * (y % 2) + x % 2);
+            dst += (size_t)ph[i] * pw[i] / 4;
+        }
+        d_unshuffle = mw.put(yr);
+    }
     if (mw.overflow || mw.off > VMETA) return fail("vision metadata too large");
     memcpy(v->host_pix, pixels, (size_t)t * VD * 2);
     if (cudaMemcpyAsync(v->meta, v->host_meta, mw.off, cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -1069,14 +1084,19 @@ int d1h_vision_encode(D1Vision* v, int n_crops, const int* ph, const int* pw, co
         pend = l.fc2_b;
     }
     L++;
-    CK(k.layernorm(h, pend, 1.f, v->w.post_w, v->w.post_b, xn, nullptr, ti, VD, eps, st));
-    // projector: unshuffle each crop -> big [P, 3072] -> linear_1 + GELU -> linear_2 (+bias) -> out
     int src = 0, dst = 0;
-    for (int i = 0; i < n_crops; i++) {
-        L++;
-        CK(k.unshuffle(xn + (size_t)src * VD, big + (size_t)dst * 4 * VD, ph[i], pw[i], VD, st));
-        src += ph[i] * pw[i];
-        dst += ph[i] * pw[i] / 4;
+    if (d_unshuffle) {
+        CK(d1_layernorm_rows(h, pend, 1.f, v->w.post_w, v->w.post_b, big, d_unshuffle, ti, VD, eps, st));
+        dst = ti / 4;
+    } else {
+        CK(k.layernorm(h, pend, 1.f, v->w.post_w, v->w.post_b, xn, nullptr, ti, VD, eps, st));
+        // projector: unshuffle each crop -> big [P, 3072] -> linear_1 + GELU -> linear_2 (+bias) -> out
+        for (int i = 0; i < n_crops; i++) {
+            L++;
+            CK(k.unshuffle(xn + (size_t)src * VD, big + (size_t)dst * 4 * VD, ph[i], pw[i], VD, st));
+            src += ph[i] * pw[i];
+            dst += ph[i] * pw[i] / 4;
+        }
     }
     const int p = dst;
     if (v->fused && k.gemm_bias_act) {
@@ -1365,9 +1385,14 @@ int audio_encode_core(D1Audio* a, int n_clips, const int* valid, const float* co
     // ---- subsampling per clip (src/audio.rs:511-525) into rows offs[c] .. of x
     for (int c = 0; c < n_clips; c++) {
         const int v = valid[c], l1 = (v - 1) / 2 + 1, l2 = (l1 - 1) / 2 + 1, t = audio_out_len(v);
-        L += 3;
-        CK(d1_sub_conv0(melc_dev[c], v, N_MELS, w.c0_w, w.c0_b, a->s1, l1, 64, st));
-        CK(d1_sub_dwconv(a->s1, l1, 64, w.c2_w, w.c2_b, a->s2, l2, 32, st));
+        if (fz) {  // conv0 + the first depthwise conv in one kernel, the conv0 rows kept on chip
+            L += 2;
+            CK(d1_sub_conv01(melc_dev[c], v, N_MELS, w.c0_w, w.c0_b, w.c2_w, w.c2_b, a->s2, l1, l2, st));
+        } else {
+            L += 3;
+            CK(d1_sub_conv0(melc_dev[c], v, N_MELS, w.c0_w, w.c0_b, a->s1, l1, 64, st));
+            CK(d1_sub_dwconv(a->s1, l1, 64, w.c2_w, w.c2_b, a->s2, l2, 32, st));
+        }
         CK(sgemm_ba(l2 * 32, SUB_C, SUB_C, a->s2, w.c3_w, a->s3, w.c3_b, 1));
         CK(d1_sub_dwconv(a->s3, l2, 32, w.c5_w, w.c5_b, a->s2, t, 16, st));
         CK(sgemm_ba(t * 16, SUB_C, SUB_C, a->s2, w.c6_w, a->s1, w.c6_b, 1));
@@ -1417,11 +1442,16 @@ int audio_encode_core(D1Audio* a, int n_clips, const int* valid, const float* co
         // conv module: pw1 -> GLU / depthwise 9 / BN / SiLU (per clip: zero padding at the clip's edges) -> pw2
         CK(ln(x, l.out_b, 1.f, l.conv_n_w, l.conv_n_b, xn, nullptr, AD));
         CK(gemm_h(2 * AD, AD, xn, l.pw1, big, nullptr, 0));
-        for (int c = 0; c < n_clips; c++) {
-            const int s = a->host_offs[c], t = a->host_offs[c + 1] - s;
+        if (fz) {  // every clip in one launch, each zero-padded at its own edges
             L++;
-            CK(d1_conformer_dw(big + (size_t)s * 2 * AD, l.pw1_b, l.dw, l.dw_b, l.bn_s, l.bn_b, o + (size_t)s * AD, t,
-                               AD, 9, st));
+            CK(d1_conformer_dw_clips(big, l.pw1_b, l.dw, l.dw_b, l.bn_s, l.bn_b, o, a->offs, n_clips, R, AD, 9, st));
+        } else {
+            for (int c = 0; c < n_clips; c++) {
+                const int s = a->host_offs[c], t = a->host_offs[c + 1] - s;
+                L++;
+                CK(d1_conformer_dw(big + (size_t)s * 2 * AD, l.pw1_b, l.dw, l.dw_b, l.bn_s, l.bn_b,
+                                   o + (size_t)s * AD, t, AD, 9, st));
+            }
         }
         CK(gemm_add(AD, AD, o, l.pw2, x, 1.f));
         // FF2 half step

@@ -248,7 +248,7 @@ int d1_sgemm(int M, int N, int K, const float* X, int ldx, const float* W, int l
              const float* bias, int act, cudaStream_t stream);
 
 /* extension — the FastConformer rel-pos self-attention of packed clips in one kernel. Replaces the three
- * Blas::gemm_batched calls (src/cuda.rs:507-527, cuBLAS from Rust) and d1_relpos_softmax of src/audio.rs:567-570.
+ * Blas::gemm_batched calls (src/cuda.rs:507-527, cuBLAS from Rust) and d1_relpos_softmax of src/audio.rs:559-562.
  * Clip c holds rows offs[c] .. offs[c+1]-1 (offs: device int [n_clips + 1], every clip <= max_len <= 384 rows);
  * for head h (64 columns at h*64 of each operand), query i and key j of the clip:
  *   P[i][j] = fp16(softmax_j((qu_i . k_j + qv_i . pp[pp_center + j - i]) * scale)),  O_i = fp16(sum_j P[i][j] v_j)
@@ -266,6 +266,28 @@ int d1_relpos_attn(const d1_half* qu, const d1_half* qv, const d1_half* k, const
  * with the same fp32 operation order. */
 int d1_vision_pos(const float* grid, const float* patch_b, const int* spans, const float* w, int taps, int ph, int pw,
                   int C, float* out, cudaStream_t stream);
+
+/* extension — d1_layernorm (pending bias folded into x as there) with only the fp16 output, whose row r goes to
+ * row y_rows[r] of y (device int [rows]). With y_rows the 2x2 unshuffle permutation of a crop (row p = y*pw + x of
+ * the crop to row 4*((y/2)*(pw/2) + x/2) + 2*(y%2) + x%2 of y viewed as [rows][D]), the vision tower's
+ * post-LayerNorm writes the projector's input directly: src/vision.rs:369-377 (post_layernorm, then d1_unshuffle
+ * per crop) in one pass. */
+int d1_layernorm_rows(float* x, const float* pend_bias, float pend_scale, const float* w, const float* b, d1_half* y,
+                      const int* y_rows, int rows, int D, float eps, cudaStream_t stream);
+
+/* extension — the first two subsampling convs of the audio encoder in one kernel: d1_sub_conv0 (F mel bins ->
+ * F1 = (F-1)/2+1 bins x 256 channels, l1 rows) followed by d1_sub_dwconv (-> F2 = (F1-1)/2+1 bins, l2 rows), the
+ * intermediate kept in shared memory (src/audio.rs:514-515). out fp32 [l2][F2][256], bit-identical to the two calls.
+ * F <= 128. */
+int d1_sub_conv01(const float* mel, int tin_valid, int F, const float* w0, const float* b0, const float* w1,
+                  const float* b1, float* out, int l1, int l2, cudaStream_t stream);
+
+/* extension — d1_conformer_dw over the packed rows of several clips in one call: clip c holds rows offs[c] ..
+ * offs[c+1]-1 (offs: device int [n_clips + 1], offs[0] = 0, offs[n_clips] = rows), each zero-padded at its own
+ * edges, as src/audio.rs:567 does with one call per clip (the reference encodes one clip at a time). ksize <= 31. */
+int d1_conformer_dw_clips(const d1_half* a, const float* b1, const float* dw, const float* dwb, const float* bn_s,
+                          const float* bn_b, d1_half* out, const int* offs, int n_clips, int rows, int C, int ksize,
+                          cudaStream_t stream);
 
 /* extension — the audio front end on the GPU: normalised log-mel features of n (>= 1) samples at 16 kHz, device x
  * -> device mel fp32 [1 + n/160][128], of which the first n/160 frames are valid (the rest zero). Replaces

@@ -313,8 +313,9 @@ def test_audio_kernels(gpu_lib, ref_lib):
         r["cdw"] = np_(o)
         res[name] = r
     d, f = res["d1"], res["ref"]
-    assert np.allclose(d["conv0"], f["conv0"], rtol=1e-6, atol=1e-6)
-    assert np.allclose(d["dw"], f["dw"], rtol=1e-6, atol=1e-6)
+    # the reference's per-element arithmetic (bias, then fused multiply-adds over the taps in order): bit-identical
+    assert np.array_equal(d["conv0"], f["conv0"])
+    assert np.array_equal(d["dw"], f["dw"])
     assert all(np.array_equal(x, y) for x, y in zip(d["prep"], f["prep"]))
     assert half_ulp_close(d["softmax"], f["softmax"], 2.0 ** -10, 1e-6).all()
     assert np.array_equal(d["cdw"], f["cdw"])
@@ -324,3 +325,124 @@ def test_audio_kernels(gpu_lib, ref_lib):
     s = (ac + bd[:, i, j + T - 1 - i]) * 0.125
     s = np.exp(s - s.max(-1, keepdims=True))
     assert np.allclose(d["softmax"], s / s.sum(-1, keepdims=True), atol=2e-3)
+
+
+@pytest.mark.parametrize("tin", [1, 2, 5, 301, 3000])
+def test_subsampling_fused(gpu_lib, ref_lib, tin):
+    """d1_sub_conv01 (conv0 + the first depthwise conv, the conv0 rows in shared memory) equals d1_sub_conv0 +
+    d1_sub_dwconv bit for bit, and both equal the reference's two kernels; ragged lengths down to one frame and
+    a 30 s clip; the second depthwise conv (16 bins) against the reference's too."""
+    rng = np.random.default_rng(tin)
+    Fm = 128
+    l1 = (tin - 1) // 2 + 1
+    l2 = (l1 - 1) // 2 + 1
+    l3 = (l2 - 1) // 2 + 1
+    mel = rng.standard_normal((tin + 3, Fm)).astype(np.float32)  # rows past tin_valid must be ignored
+    w0, w2, w5 = [rng.standard_normal((256, 9)).astype(np.float32) * 0.3 for _ in range(3)]
+    b0, b2, b5 = [rng.standard_normal(256).astype(np.float32) * 0.1 for _ in range(3)]
+    s2s = {}
+    for name, lib in libs(gpu_lib, ref_lib):
+        s1 = torch.empty(l1, 64, 256, device="cuda")
+        s2 = torch.empty(l2, 32, 256, device="cuda")
+        s3 = torch.empty(l3, 16, 256, device="cuda")
+        assert lib.d1_sub_conv0(P(cu(mel)), tin, Fm, P(cu(w0)), P(cu(b0)), P(s1), l1, 64, ST()) == 0
+        assert lib.d1_sub_dwconv(P(s1), l1, 64, P(cu(w2)), P(cu(b2)), P(s2), l2, 32, ST()) == 0
+        assert lib.d1_sub_dwconv(P(s2), l2, 32, P(cu(w5)), P(cu(b5)), P(s3), l3, 16, ST()) == 0
+        s2s[name] = (np_(s2), np_(s3))
+    assert np.array_equal(s2s["d1"][0], s2s["ref"][0]) and np.array_equal(s2s["d1"][1], s2s["ref"][1])
+    fused = torch.full((l2, 32, 256), float("nan"), device="cuda")
+    assert gpu_lib.d1_sub_conv01(P(cu(mel)), tin, Fm, P(cu(w0)), P(cu(b0)), P(cu(w2)), P(cu(b2)), P(fused), l1, l2,
+                                 ST()) == 0
+    assert np.array_equal(np_(fused), s2s["ref"][0])
+    assert gpu_lib.d1_sub_conv01(P(cu(mel)), tin, 129, P(cu(w0)), P(cu(b0)), P(cu(w2)), P(cu(b2)), P(fused), l1, l2,
+                                 ST()) == -1  # more bins than the fused kernel stages
+
+
+@pytest.mark.parametrize("lens", [[38], [1, 9, 4, 200], [375, 375, 17]])
+def test_conformer_dw_clips(gpu_lib, ref_lib, lens):
+    """The packed form (every clip in one launch, zero padding at each clip's edges) equals the reference's kernel
+    run once per clip, bit for bit."""
+    rng = np.random.default_rng(sum(lens))
+    Dm, R = 512, sum(lens)
+    a = rng.standard_normal((R, 2 * Dm)).astype(np.float16)
+    b1 = rng.standard_normal(2 * Dm).astype(np.float32) * 0.1
+    dw = rng.standard_normal((Dm, 9)).astype(np.float32) * 0.3
+    dwb, s, sh = [rng.standard_normal(Dm).astype(np.float32) * 0.2 for _ in range(3)]
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ad = cu(a)
+    got = torch.full((R, Dm), float("nan"), dtype=torch.float16, device="cuda")
+    assert gpu_lib.d1_conformer_dw_clips(P(ad), P(cu(b1)), P(cu(dw)), P(cu(dwb)), P(cu(s)), P(cu(sh)), P(got),
+                                         P(cu(offs)), len(lens), R, Dm, 9, ST()) == 0
+    want = torch.empty(R, Dm, dtype=torch.float16, device="cuda")
+    for c in range(len(lens)):
+        o, t = int(offs[c]), lens[c]
+        assert ref_lib.d1_conformer_dw(C.c_void_p(ad.data_ptr() + o * 2 * Dm * 2), P(cu(b1)), P(cu(dw)), P(cu(dwb)),
+                                       P(cu(s)), P(cu(sh)), C.c_void_p(want.data_ptr() + o * Dm * 2), t, Dm, 9,
+                                       ST()) == 0
+    assert np.array_equal(np_(got), np_(want))
+
+
+@pytest.mark.parametrize("T", [38, 200, 400, 600])
+def test_relpos_softmax_lengths(gpu_lib, ref_lib, T):
+    """Every register-window width of the warp-per-row softmax (rows up to 128, 256, 512 columns, and longer)."""
+    rng = np.random.default_rng(T)
+    H = 8
+    ac = rng.standard_normal((H, T, T)).astype(np.float32)
+    bd = rng.standard_normal((H, T, 2 * T - 1)).astype(np.float32)
+    out = {}
+    for name, lib in libs(gpu_lib, ref_lib):
+        p = torch.empty(H, T, T, dtype=torch.float16, device="cuda")
+        assert lib.d1_relpos_softmax(P(cu(ac)), P(cu(bd)), P(p), T, H, 0.125, ST()) == 0
+        out[name] = np_(p)
+    assert half_ulp_close(out["d1"], out["ref"], 2.0 ** -10, 1e-6).all()
+
+
+@pytest.mark.parametrize("Dm", [512, 100])
+def test_relpos_prep_widths(gpu_lib, ref_lib, Dm):
+    """16-byte vectors (Dm a multiple of 8) and the one-column form, bit-exact against the reference."""
+    rng = np.random.default_rng(Dm)
+    T = 77
+    qkv = rng.standard_normal((T, 3 * Dm)).astype(np.float16)
+    vecs = [rng.standard_normal(Dm).astype(np.float32) * 0.1 for _ in range(5)]
+    res = {}
+    for name, lib in libs(gpu_lib, ref_lib):
+        outs = [torch.empty(T, Dm, dtype=torch.float16, device="cuda") for _ in range(4)]
+        assert lib.d1_relpos_prep(P(cu(qkv)), *[P(cu(v)) for v in vecs], *[P(o) for o in outs], T, Dm, ST()) == 0
+        res[name] = [np_(o) for o in outs]
+    assert all(np.array_equal(x, y) for x, y in zip(res["d1"], res["ref"]))
+
+
+def test_layernorm_rows_unshuffle(gpu_lib, ref_lib):
+    """d1_layernorm_rows with the unshuffle permutation as output rows equals d1_layernorm then d1_unshuffle per
+    crop (the vision tower's post-LayerNorm and projector input), pending bias included."""
+    rng = np.random.default_rng(12)
+    crops = [(4, 6), (2, 2), (8, 10)]
+    D = 768
+    rows = sum(h * w for h, w in crops)
+    x = rng.standard_normal((rows, D)).astype(np.float32) * 2
+    pend = rng.standard_normal(D).astype(np.float32) * 0.1
+    wn = rng.standard_normal(D).astype(np.float32)
+    bn = rng.standard_normal(D).astype(np.float32) * 0.1
+    yr, src, dst = [], 0, 0
+    for ph, pw in crops:
+        for y in range(ph):
+            for xx in range(pw):
+                yr.append(4 * (dst + (y // 2) * (pw // 2) + xx // 2) + 2 * (y % 2) + xx % 2)
+        dst += ph * pw // 4
+    got = torch.full((rows // 4, 4 * D), float("nan"), dtype=torch.float16, device="cuda")
+    xd = cu(x)
+    assert gpu_lib.d1_layernorm_rows(P(xd), P(cu(pend)), 1.0, P(cu(wn)), P(cu(bn)), P(got), P(cu(np.array(yr, np.int32))),
+                                     rows, D, 1e-6, ST()) == 0
+    x_after = np_(xd)
+    xr = cu(x)
+    xn = torch.empty(rows, D, dtype=torch.float16, device="cuda")
+    assert ref_lib.d1_layernorm(P(xr), P(cu(pend)), 1.0, P(cu(wn)), P(cu(bn)), P(xn), None, rows, D, 1e-6, ST()) == 0
+    want = torch.empty(rows // 4, 4 * D, dtype=torch.float16, device="cuda")
+    src = dst = 0
+    for ph, pw in crops:
+        assert ref_lib.d1_unshuffle(C.c_void_p(xn.data_ptr() + src * D * 2), C.c_void_p(want.data_ptr() + dst * 4 * D * 2),
+                                    ph, pw, D, ST()) == 0
+        src += ph * pw
+        dst += ph * pw // 4
+    assert np.array_equal(x_after, np_(xr))  # the pending bias folded into x as d1_layernorm does
+    assert half_ulp_close(np_(got), np_(want), 2.0 ** -10, 1e-6).all()
