@@ -470,6 +470,55 @@ def gemm_sweep(pkg, dev, stream, reps=20):
     return out
 
 
+def hbm_kernels(pkg, dev, reps=40, warm=5):
+    """The trunk's HBM-bound kernels at the metric's shape (8192 rows, D = 1024), each launched alone: RMSNorm (fp32
+    [T, D] -> fp16, 6,144 B/token), LayerNorm (same bytes), the double-gated short conv (fp16 [T, 3D] -> fp16 [T, D],
+    8,192 B/token). Inputs rotate over enough buffer sets to exceed the 126 MB L2, so every launch reads from DRAM.
+    CUDA-event average per launch; achieved GB/s = algorithmic bytes / time, against the measured HBM copy peak."""
+    import ctypes as C
+    import torch
+    lib = pkg.lib()
+    hbm, _, kind = peaks()
+    T, D = TOKENS, 1024
+    st = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    g = torch.Generator(device=dev).manual_seed(5)
+    arr = (pkg.abi.SeqInfo * N_SEQS)()
+    for i in range(N_SEQS):
+        arr[i].start, arr[i].len = i * SEQ_LEN, SEQ_LEN
+    seqs = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
+    tok = torch.arange(T, device=dev, dtype=torch.int32) // SEQ_LEN
+    w = torch.ones(D, device=dev)
+    b = torch.zeros(D, device=dev)
+    convw = torch.randn(D, 3, device=dev, generator=g) * 0.3
+    sets = 4  # 4 x (32 + 16) MB for the norms, 4 x (48 + 16) MB for the conv: each above L2
+    hs = [torch.randn(T, D, device=dev, generator=g) for _ in range(sets)]
+    ys = [torch.empty(T, D, device=dev, dtype=torch.float16) for _ in range(sets)]
+    bcus = [torch.randn(T, 3 * D, device=dev, generator=g).half() for _ in range(sets)]
+    cases = {
+        "k_rmsnorm": (6144, lambda i: lib.d1_rmsnorm(P(hs[i]), P(w), P(ys[i]), T, D, 1e-5, st)),
+        "k_layernorm": (6144, lambda i: lib.d1_layernorm(P(hs[i]), None, 1.0, P(w), P(b), P(ys[i]), None, T, D, 1e-5,
+                                                         st)),
+        "k_shortconv": (8192, lambda i: lib.d1_shortconv(P(bcus[i]), P(convw), P(tok), P(seqs), P(ys[i]), T, D, 0, st)),
+    }
+    out = {}
+    for name, (bpt, fn) in cases.items():
+        for i in range(warm):
+            assert fn(i % sets) == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i % sets)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / reps * 1e3
+        gbs = bpt * T / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 2), "bytes_per_launch": bpt * T, "gbs": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / hbm, 3)}
+    rec = {"sweep": "hbm_kernels", "rows": T, "D": D, "kernels": out, "peak": f"{hbm} GB/s ({kind} HBM copy)"}
+    print(json.dumps(rec), flush=True)
+
+
 def attn_config2(pkg, dev, reps=20, warm=3):
     """packed varlen bidirectional GQA attention (16 query heads, 8 KV heads, head dim 64,
     Q/K/V N(0,1) fp16, seed 2), lengths log-normal (median 384, sigma 1) clipped to 32..16384, at 2048, 8192 and
@@ -671,6 +720,8 @@ def main():
                     help="run only the runners' attention kernel on 8192/L sequences of L tokens (an ncu case)")
     ap.add_argument("--only-roofline", action="store_true",
                     help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
+    ap.add_argument("--hbm-kernels", action="store_true",
+                    help="time RMSNorm, LayerNorm and the short conv alone at 8192 x 1024 (an ncu case as well)")
     ap.add_argument("--attn-config2", action="store_true",
                     help="BASELINE config 2: attention at 2048/8192/16384 packed tokens, this library and the reference")
     ap.add_argument("--ref-engine-child", type=int, default=-1, metavar="EFFORT", help=argparse.SUPPRESS)
@@ -711,6 +762,10 @@ def main():
     if args.gemm_sweep:
         if rank == 0:
             gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
+        return
+    if args.hbm_kernels:
+        if rank == 0:
+            hbm_kernels(pkg, dev, reps=max(args.steps, 10), warm=args.warmup)
         return
     if args.attn_config2:
         if rank == 0:

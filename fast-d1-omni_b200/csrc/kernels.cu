@@ -263,11 +263,12 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint4* __restrict__ s
 
 // ------------------------------------------------------------------------------------------------ short conv
 // bcu [T][3D] = [b | c | u]. Each CTA covers kConvRows consecutive rows; a thread owns 8 channels. All of the
-// thread's loads (b and u of rows t0-1 .. t0+kConvRows, c of its rows: 28 independent 16-byte loads) are issued
-// before any arithmetic, so the kernel runs at HBM bandwidth instead of one dependent row at a time; each row is
-// read once per CTA plus a one-row halo on each side (an L2 hit). Sequence boundaries, the prefix's left state
+// thread's loads (b and u of rows t0-1 .. t0+kConvRows, c of its rows: 10 independent 16-byte loads) are issued
+// before any arithmetic. Two rows per CTA keep the thread's registers few (many CTAs resident per SM) and the CTAs
+// short, so the last partial wave of CTAs costs little; the one-row halo each side is an L2 hit (the neighbouring
+// CTAs read those rows at the same time), so DRAM sees each row once. Sequence boundaries, the prefix's left state
 // (ext_bx) and the saved last state (save_bx) follow cuda/kernels.cu:224-259.
-constexpr int kConvRows = 8;
+constexpr int kConvRows = 2;
 
 __device__ __forceinline__ void mul8(const uint4& b, const uint4& u, float* bx) {
     float fb[8], fu[8];
@@ -300,11 +301,23 @@ __global__ void __launch_bounds__(128) k_shortconv(const __half* __restrict__ bc
         sq[j] = __ldg(tok_seq + t);
     }
     float w0[8], w1[8], w2[8];
+    {
+        const float4* w4 = reinterpret_cast<const float4*>(convw + (size_t)c * 3);  // 24 consecutive floats
+        float wf[24];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        w0[i] = __ldg(convw + (c + i) * 3);
-        w1[i] = __ldg(convw + (c + i) * 3 + 1);
-        w2[i] = __ldg(convw + (c + i) * 3 + 2);
+        for (int i = 0; i < 6; i++) {
+            const float4 q = __ldg(w4 + i);
+            wf[4 * i] = q.x;
+            wf[4 * i + 1] = q.y;
+            wf[4 * i + 2] = q.z;
+            wf[4 * i + 3] = q.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            w0[i] = wf[3 * i];
+            w1[i] = wf[3 * i + 1];
+            w2[i] = wf[3 * i + 2];
+        }
     }
 #pragma unroll
     for (int j = 0; j < kConvRows; j++) {
@@ -965,7 +978,7 @@ int d1_gather_rows(const void* src, void* dst, const int* idx, int n, int row_by
 int d1_shortconv(const d1_half* bcu, const float* convw, const int* tok_seq, const SeqInfo* seqs, d1_half* out,
                  int rows, int D, int conv_idx, cudaStream_t st) {
     if (rows <= 0) return rows == 0 ? 0 : -1;
-    if (D % 8 || !al16(bcu) || !al16(out)) return -1;
+    if (D % 8 || !al16(bcu) || !al16(out) || !al16(convw)) return -1;
     const int threads = D / 8 < 128 ? D / 8 : 128;
     dim3 grid(nblk(rows, kConvRows), nblk(D / 8, threads));
     launch_pdl(k_shortconv, grid, threads, 0, st, bcu, convw, tok_seq, seqs, out, rows, D, conv_idx);
