@@ -254,31 +254,35 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // (it must cover every tile) and the runners pass one item per 256-row block. A unit is two 128-row query tiles
 // that share each K/V tile, one per softmax warpgroup.
 //
-// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM and
-// two P buffers in shared memory, so S(j+2) is issued as soon as P(j) is written and the softmax never waits for
-// the tensor core; its only other wait is for the P.V that last read the P buffer it is about to refill (two tiles
-// back). Every handoff has its own barrier per buffer, so no wait can confuse two phases of one barrier.
-// TMEM (512 columns): S[w][b] at (2w + b) * 64, O[w] at 256 + 64w.
+// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM, so
+// S(j+2) is issued as soon as P(j) is written. P never leaves TMEM: the softmax writes P(j) as fp16 pairs over the
+// first 32 columns of S(j)'s buffer, and P(j).V_j reads its A operand from there (tcgen05.mma with A in tensor
+// memory). The tensor core runs one thread's MMAs in issue order, so S(j+2), issued after P(j).V_j into the same
+// buffer, overwrites P(j) only after that MMA has read it, and the softmax's wait for S(j) also covers P(j-2).V_{j-2}.
+// The issuer serves each warpgroup as soon as its P is written, so the two drift apart and their exponentials
+// interleave on the SFU instead of running in lockstep. Every handoff has its own barrier per buffer.
+// TMEM (512 columns): S/P[w][b] at (2w + b) * 64, O[w] at 256 + 64w.
 // Warps:
 //   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
-//        reads its S row (one TMEM round trip), takes the row max in the exp2 domain, writes P = 2^(s - m) as fp16
-//        (128-byte swizzle: the A operand of P.V) and accumulates the row sum. O is rescaled in TMEM only when the
-//        row max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well
-//        inside fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory.
+//        reads its S row (one TMEM round trip), takes the row max in the exp2 domain (3-input max), writes
+//        P = 2^(s - m) as fp16 back to TMEM and accumulates the row sum. O is rescaled in TMEM only when the row
+//        max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well inside
+//        fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory: a whole
+//        128-row tile through its own shared-memory staging buffer and one bulk tensor store.
 //   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring and K/V tiles of 64 keys ([ext prefix keys |
-//        local keys]) into a 6-stage ring, in the swizzled layouts (V is the MN-major B operand of P.V: same bytes):
+//        local keys]) into an 8-stage ring, in the swizzled layouts (V is the MN-major B operand of P.V: same bytes):
 //        Q and whole local K/V tiles by TMA from one thread, prefix and partial tiles by cp.async from all three
 //        warps (each lane's copies complete the slot's barrier when they land); the next unit's loads overlap the
 //        current unit's math.
-//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64) and
-//        O_w += P_w(j).V_j (M=128, N=64, K=64).
+//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64, both operands in
+//        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=64, A in TMEM).
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
-constexpr int T_QSLOTS = 2, T_KVSTAGES = 6;
+constexpr int T_QSLOTS = 2, T_KVSTAGES = 8;
 constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
-constexpr int T_P_BYTES = TQ * 128;       // P of one query tile and K/V tile (64 keys: one swizzle block)
+constexpr int T_O_BYTES = TQ * 128;       // one warpgroup's O staging tile
 constexpr uint32_t T_TMEM_COLS = 512;
 constexpr float kLazyRescale = 8.f;
 enum : int {
@@ -288,14 +292,14 @@ enum : int {
     B_KVEMPTY = B_KVFULL + T_KVSTAGES,
     B_SFULL = B_KVEMPTY + T_KVSTAGES,  // [w][b]
     B_PFULL = B_SFULL + 4,             // [w][b]
-    B_ODONE = B_PFULL + 4,             // [w][b]: the P.V that read P[w][b]
+    B_ODONE = B_PFULL + 4,             // [w][b]: P.V of the tile whose P is in buffer b
     B_OFREE = B_ODONE + 4,             // [w]
     B_DRAIN = B_OFREE + 2,
     B_OSTAGED = B_DRAIN + 1,           // [w]: the warpgroup's O tile is in shared memory (4 warp arrivals)
-    B_OREAD = B_OSTAGED + 2,           // [w]: its bulk store has read it (the issuing thread)
+    B_OREAD = B_OSTAGED + 2,           // [w]: its previous bulk store has read the staging buffer
     T_NBARS = B_OREAD + 2
 };
-constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 4 * T_P_BYTES + T_NBARS * 8 + 16;
+constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_O_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
@@ -350,6 +354,25 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// D[tmem] (+)= A[tmem] . B[smem]: A (M=128 rows = TMEM lanes, K fp16 values packed two per 32-bit column) in
+// tensor memory, B through a shared-memory descriptor, fp32 accumulate; shape from the instruction descriptor.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
 // A unit: work item w (its 64-row query tile must start at a multiple of 256) and head h.
 struct Unit {
     AttnSeq s;
@@ -384,8 +407,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sQ = smem_raw;                                    // slot q: Q0 at q * 2 * T_QT_BYTES, Q1 after it
     uint8_t* sKV = sQ + T_QSLOTS * 2 * T_QT_BYTES;             // stage s: K at s * 2 * T_KV_BYTES, V after it
-    uint8_t* sP = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // P[w][b] at (2w + b) * T_P_BYTES
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * T_P_BYTES);
+    uint8_t* sO = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // O staging of warpgroup w at w * T_O_BYTES
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * T_O_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + T_NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     auto bar = [&](int i) { return smem_u32(bars + i); };
@@ -531,67 +554,46 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 const int qs = qi % T_QSLOTS;
                 if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
                 const uint32_t q_addr = smem_u32(sQ + qs * 2 * T_QT_BYTES);
-                // One step's MMAs are issued k-slice by k-slice across the independent accumulators (both
-                // warpgroups' P.V and S), so the tensor pipe overlaps their dependent chains.
                 auto k_addr = [&](int j) { return smem_u32(sKV + ((ki + j) % T_KVSTAGES) * 2 * T_KV_BYTES); };
                 auto kv_ready = [&](int j) {
                     return mbar_wait(bar(B_KVFULL + (ki + j) % T_KVSTAGES), ((ki + j) / T_KVSTAGES) & 1, abort_flag);
                 };
-                // S_w(j) goes to buffer (cnt[w] + j) % 2, which P(cnt[w] + j - 2) has released (its softmax read it)
-                auto s_buffer_free = [&](int w, int j) {
-                    const int c = cnt[w] + j;
-                    return c < 2 || mbar_wait(bar(B_PFULL + 2 * w + (c & 1)), ((c - 2) >> 1) & 1, abort_flag);
-                };
-                auto issue_s_pair = [&](int j) {  // S_w(j) for every active warpgroup, interleaved
+                // S_w(j) into buffer (cnt[w] + j) % 2. That buffer last held P(cnt[w] + j - 2), whose P.V this
+                // thread issued earlier: the tensor core reads it before this S overwrites it (issue order).
+                auto issue_s = [&](int w, int j) {
                     const uint32_t ka = k_addr(j);
+                    const int b = (cnt[w] + j) & 1;
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        for (int w = 0; w < nw; w++)
-                            tc_mma_f16(tmem + (2 * w + ((cnt[w] + j) & 1)) * TKV,
-                                       smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32), smem_desc_k128(ka + k * 32),
-                                       IDESC_S, k != 0);
-                    for (int w = 0; w < nw; w++) tc_commit(bar(B_SFULL + 2 * w + ((cnt[w] + j) & 1)));
+                        tc_mma_f16(tmem + (2 * w + b) * TKV, smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32),
+                                   smem_desc_k128(ka + k * 32), IDESC_S, k != 0);
+                    tc_commit(bar(B_SFULL + 2 * w + b));
                 };
                 for (int j = 0; j < 2 && j < un.nt && ok; j++) {  // prologue: S for tiles 0 and 1
                     if (!(ok = kv_ready(j))) break;
-                    for (int w = 0; w < nw && ok; w++) ok = s_buffer_free(w, j);
-                    if (!ok) break;
                     tc_fence_after();
-                    issue_s_pair(j);
+                    for (int w = 0; w < nw; w++) issue_s(w, j);
                 }
                 for (int j = 0; j < un.nt && ok; j++) {
-                    // P_w(j) written for every active warpgroup (so S_w(j) has been read and its buffer is free)
+                    const bool ahead = j + 2 < un.nt;
+                    if (ahead && !(ok = kv_ready(j + 2))) break;
+                    const uint32_t v_addr = k_addr(j) + T_KV_BYTES;
+                    // each warpgroup as soon as its P(j) is in TMEM: P(j).V_j, then S(j+2) into the same buffer
                     for (int w = 0; w < nw && ok; w++) {
-                        const int c = cnt[w] + j;
-                        ok = mbar_wait(bar(B_PFULL + 2 * w + (c & 1)), (c >> 1) & 1, abort_flag);
+                        const int c = cnt[w] + j, b = c & 1;
+                        ok = mbar_wait(bar(B_PFULL + 2 * w + b), (c >> 1) & 1, abort_flag);
                         // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
                         if (ok && j == 0 && units[w] > 0) ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag);
-                    }
-                    const bool ahead = j + 2 < un.nt;
-                    if (ok && ahead) ok = kv_ready(j + 2);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = k_addr(j) + T_KV_BYTES;
-                    const uint32_t ka2 = ahead ? k_addr(j + 2) : 0;
+                        if (!ok) break;
+                        tc_fence_after();
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        for (int w = 0; w < nw; w++) {
-                            const int c = cnt[w] + j;
-                            tc_mma_f16(tmem + 4 * TKV + w * 64,
-                                       smem_desc_k128(smem_u32(sP + (2 * w + (c & 1)) * T_P_BYTES) + k * 32),
-                                       smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                        }
-                        if (ahead)
-                            for (int w = 0; w < nw; w++)
-                                tc_mma_f16(tmem + (2 * w + ((cnt[w] + j) & 1)) * TKV,
-                                           smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32), smem_desc_k128(ka2 + k * 32),
-                                           IDESC_S, k != 0);
+                        for (int k = 0; k < 4; k++)
+                            tc_mma_f16_ts(tmem + 4 * TKV + w * 64, tmem + (2 * w + b) * TKV + k * 8,
+                                          smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
+                        tc_commit(bar(B_ODONE + 2 * w + b));
+                        if (ahead) issue_s(w, j + 2);
                     }
-                    for (int w = 0; w < nw; w++) {
-                        const int c = cnt[w] + j;
-                        tc_commit(bar(B_ODONE + 2 * w + (c & 1)));
-                        if (ahead) tc_commit(bar(B_SFULL + 2 * w + (c & 1)));  // S(j+2) shares buffer c % 2
-                    }
+                    if (!ok) break;
                     tc_commit(bar(B_KVEMPTY + (ki + j) % T_KVSTAGES));
                 }
                 if (!ok) break;
@@ -613,10 +615,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         const int w = warp >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
+        uint8_t* stile = sO + w * T_O_BYTES;
         int cnt = 0;
-        unsigned pend = 0;  // P buffers (bit b) holding an O tile whose bulk store may still be reading it
-        int nst = 0;        // O tiles this warpgroup has staged
-        int nread = 0;      // times it has waited for its stores to finish reading
+        int nst = 0;  // O tiles this warpgroup has staged
         bool ok = true;
         Unit un;
         for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
@@ -634,26 +635,22 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                 tc_wait_ld();
                 const int kbase = j * TKV;
-                // eight independent partial maxima (short dependency chains); keys past the sequence only in its
-                // last tile
-                float mx8[8];
+                if (kbase + TKV > total) {  // keys past the sequence: only in its last tile
 #pragma unroll
-                for (int i = 0; i < 8; i++) mx8[i] = -INFINITY;
-                // the max of the raw scores (the scale is positive), scaled once; the exponent below folds the
-                // scale in: P = 2^(s * scale - m)
-                if (kbase + TKV <= total) {
-#pragma unroll
-                    for (int i = 0; i < TKV; i++) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < TKV; i++) {
+                    for (int i = 0; i < TKV; i++)
                         if (kbase + i >= total) sr[i] = __float_as_uint(-INFINITY);
-                        mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
-                    }
                 }
-                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
-                                 a.scale_log2;
+                // the max of the raw scores (the scale is positive) in four independent 3-input chains, scaled
+                // once; the exponent below folds the scale in: P = 2^(s * scale - m)
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int i = 0; i < TKV; i += 8) {
+                    mx4[0] = fmax3(mx4[0], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+                    mx4[1] = fmax3(mx4[1], __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+                    mx4[2] = fmax3(mx4[2], __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+                    mx4[3] = fmax3(mx4[3], __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+                }
+                const float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]) * a.scale_log2;
                 float m_use = m, alpha = 1.f;
                 if (j == 0) {
                     m_use = mx;
@@ -661,10 +658,6 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     m_use = mx;
                     alpha = ex2(m - mx);
                 }
-                // the P.V that last read this P buffer (tile c - 2) is done
-                if (c >= 2 &&
-                    !(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + b), ((c - 2) >> 1) & 1, abort_flag))))
-                    break;
                 if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {  // rare: O must hold P.V up to tile c - 1
                     if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + (b ^ 1)), ((c - 1) >> 1) & 1,
                                                                   abort_flag))))
@@ -679,21 +672,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         for (int i = 0; i < 8; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                         tmem_st8(tO + q * 8, o);
                     }
-                    tc_wait_st();
-                }
-                if ((pend >> b) & 1) {  // an earlier O tile was staged here: wait until every store has read its tile
-                    if (row == 0) {
-                        o_store_read_done();
-                        mbar_arrive(bar(B_OREAD + w));
-                    }
-                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_OREAD + w), nread & 1, abort_flag)))) break;
-                    nread++;
-                    pend = 0;
                 }
                 float rs8[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) rs8[e] = 0.f;
-                uint8_t* prow = sP + (2 * w + b) * T_P_BYTES + row * 128;
+                uint32_t pr[TKV / 2];
 #pragma unroll
                 for (int ch = 0; ch < TKV / 8; ch++) {
                     float p[8];
@@ -702,10 +685,12 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         p[e] = ex2(fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use));
                         rs8[e] += p[e];
                     }
-                    *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
-                        make_uint4(pack_h2(p[0], p[1]), pack_h2(p[2], p[3]), pack_h2(p[4], p[5]), pack_h2(p[6], p[7]));
+#pragma unroll
+                    for (int e = 0; e < 4; e++) pr[ch * 4 + e] = pack_h2(p[2 * e], p[2 * e + 1]);
                 }
-                fence_async_smem_cta();
+                // P(j) over the first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
+                tmem_st32(tS, pr);
+                tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(B_PFULL + 2 * w + b));
@@ -730,10 +715,16 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             if (lane == 0) mbar_arrive(bar(B_OFREE + w));  // O is read: the next unit's first P.V may overwrite it
             const int q0w = un.q0 + w * TQ, q = q0w + row;
             if (q0w + TQ <= un.s.q_len) {
-                // a whole 128-row tile: staged in the P buffer the next unit writes second (both are free: every
-                // P.V of this unit is done), then one bulk tensor store of 16 KB
-                const int sb = (cnt + 1) & 1;
-                uint8_t* stile = sP + (2 * w + sb) * T_P_BYTES;
+                // a whole 128-row tile: staged in this warpgroup's buffer, then one bulk tensor store of 16 KB. The
+                // previous store from the buffer must have read it first (long done by now: a unit ago).
+                if (nst > 0) {
+                    if (row == 0) {
+                        o_store_read_done();
+                        mbar_arrive(bar(B_OREAD + w));
+                    }
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_OREAD + w), (nst - 1) & 1, abort_flag))))
+                        break;
+                }
 #pragma unroll
                 for (int ch = 0; ch < 8; ch++)
                     *reinterpret_cast<uint4*>(stile + row * 128 + ((ch ^ (row & 7)) << 4)) = make_uint4(
@@ -749,7 +740,6 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     staged_ok = mbar_wait(bar(B_OSTAGED + w), nst & 1, abort_flag);
                     if (staged_ok) o_tile_store(&tmO, smem_u32(stile), un.h * 64, un.s.q_start + q0w);
                 }
-                pend |= 1u << sb;
                 nst++;
                 if (!(ok = __all_sync(D1_FULL_MASK, staged_ok))) break;
             } else if (q < un.s.q_len) {  // a partial tile: this row's 128 bytes directly
