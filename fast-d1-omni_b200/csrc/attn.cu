@@ -354,6 +354,26 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, for part of the softmax's exponentials (the SFU is the attention's bottleneck at head dim
+// 64: one exponential per 256 FLOPs). Range reduction x = n + f with n = round(x), |f| <= 1/2, by adding and
+// subtracting 1.5 * 2^23 (round-to-nearest puts n in the low mantissa bits); 2^f by a cubic fitted here for minimal
+// relative error on [-1/2, 1/2] (Remez exchange: max relative error 7.5e-5, below half an fp16 ulp of P, so P
+// rounds to the same fp16 value as with the hardware approximation or differs by one ulp); n goes into the
+// exponent field by an integer add. x is clamped at -127 (keys masked with -inf and scores far below the row max
+// give 0 after the fp16 rounding of P); x <= 8 by the lazy rescale, so the result never overflows.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -127.f);
+    const float j = __fadd_rn(x, 12582912.f);
+    const float f = __fsub_rn(x, __fsub_rn(j, 12582912.f));
+    const float p = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261112511f), f, 0.69326096773f), f, 0.99992805719f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+#ifndef D1_POLY_PER8
+#define D1_POLY_PER8 2
+#endif
+constexpr int kPolyPer8 = D1_POLY_PER8;  // exponentials of each 8 computed by exp2_poly, the rest by the SFU
+static_assert(kPolyPer8 >= 0 && kPolyPer8 <= 8, "exp2_poly share");
+
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
@@ -682,7 +702,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     float p[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
-                        p[e] = ex2(fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use));
+                        const float x = fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use);
+                        p[e] = e < 8 - kPolyPer8 ? ex2(x) : exp2_poly(x);
                         rs8[e] += p[e];
                     }
 #pragma unroll
