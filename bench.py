@@ -350,6 +350,45 @@ def reference_gpu_engine(steps, warmup, effort):
         model.close()
 
 
+ONLY_GEMM = {"in_proj": (3072, 1024, 0), "qkv": (2048, 1024, 0), "out_proj": (1024, 1024, 1), "w2": (1024, 4608, 1)}
+
+
+def only_gemm(pkg, dev, stream, name, reps=20, warm=3):
+    """One trunk projection at M=8192 in its trunk form (fp16 store for in_proj / qkv, the fp32 residual reduce-add
+    for out_proj / w2) under the plan d1_lt_tune picks: the small case for an ncu capture of that GEMM."""
+    import ctypes as C
+    import torch
+    lib = pkg.lib()
+    ctx = lib.d1_lt_init(0)
+    N, K, res = ONLY_GEMM[name]
+    M = TOKENS
+    st = C.c_void_p(stream.cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(M, K, device=dev, generator=g).half()
+    wt = (torch.randn(N, K, device=dev, generator=g) * 0.02).half()
+    y = torch.zeros(M, N, device=dev) if res else torch.empty(M, N, device=dev, dtype=torch.float16)
+    lib.d1_lt_tune(ctx, M, N, K, K, K, 0, N, res, 0, 1, st)
+    fn = lambda: lib.d1_lt_gemm(ctx, M, N, K, P(x), K, P(wt), K, 0, P(y), N, res, 0, 1.0, float(res), st)  # noqa: E731
+    for _ in range(warm):
+        assert fn() == 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    err = lib.d1_lt_error(ctx)
+    lib.d1_lt_destroy(ctx)
+    if err:
+        raise RuntimeError(f"GEMM kernel reported error {err}")
+    us = e0.elapsed_time(e1) / reps * 1e3
+    _, tflops, _ = peaks()
+    tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+    return {"gemm": name, "M": M, "N": N, "K": K, "form": "residual f32" if res else "store f16", "us": round(us, 2),
+            "tflops": round(tf, 1), "frac_of_peak": round(tf / tflops, 3)}
+
+
 def swiglu_gemm_ms(pkg, dev, stream, reps=20):
     """Average CUDA-event time of one d1_gemm_swiglu launch at M=8192 (the trunk's w1|w3 projection)."""
     import ctypes as C
@@ -720,6 +759,8 @@ def main():
                     help="run only the runners' attention kernel on 8192/L sequences of L tokens (an ncu case)")
     ap.add_argument("--only-roofline", action="store_true",
                     help="run only the dominant GEMM (fused SwiGLU, M=8192) launches: the small case for ncu")
+    ap.add_argument("--only-gemm", default="", choices=[""] + list(ONLY_GEMM),
+                    help="run only one trunk projection GEMM at M=8192 in its trunk form (an ncu case)")
     ap.add_argument("--hbm-kernels", action="store_true",
                     help="time RMSNorm, LayerNorm and the short conv alone at 8192 x 1024 (an ncu case as well)")
     ap.add_argument("--attn-config2", action="store_true",
@@ -762,6 +803,11 @@ def main():
     if args.gemm_sweep:
         if rank == 0:
             gemm_sweep(pkg, dev, torch.cuda.Stream(dev))
+        return
+    if args.only_gemm:
+        if rank == 0:
+            print(json.dumps(only_gemm(pkg, dev, torch.cuda.Stream(dev), args.only_gemm, reps=args.steps,
+                                       warm=args.warmup)), flush=True)
         return
     if args.hbm_kernels:
         if rank == 0:

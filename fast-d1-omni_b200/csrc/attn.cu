@@ -359,10 +359,11 @@ __device__ __forceinline__ float ex2(float x) {
 // subtracting 1.5 * 2^23 (round-to-nearest puts n in the low mantissa bits); 2^f by a cubic fitted here for minimal
 // relative error on [-1/2, 1/2] (Remez exchange: max relative error 7.5e-5, below half an fp16 ulp of P, so P
 // rounds to the same fp16 value as with the hardware approximation or differs by one ulp); n goes into the
-// exponent field by an integer add. x is clamped at -127 (keys masked with -inf and scores far below the row max
-// give 0 after the fp16 rounding of P); x <= 8 by the lazy rescale, so the result never overflows.
+// exponent field by an integer add. x is clamped at -126 so that field stays >= 0 (the cubic is below 1 for f <= 0:
+// exponent field 126 before the add), which makes keys masked with -inf and scores far below the row max a tiny
+// positive value that rounds to fp16 zero; x <= 8 by the lazy rescale, so the result never overflows.
 __device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -127.f);
+    x = fmaxf(x, -126.f);
     const float j = __fadd_rn(x, 12582912.f);
     const float f = __fsub_rn(x, __fsub_rn(j, 12582912.f));
     const float p = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261112511f), f, 0.69326096773f), f, 0.99992805719f);
