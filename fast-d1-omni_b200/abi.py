@@ -96,7 +96,8 @@ class Row(C.Structure):
 
 class Media(C.Structure):
     _fields_ = [("kind", i32), ("n_crops", i32), ("ph", C.POINTER(i32)), ("pw", C.POINTER(i32)), ("patches", p),
-                ("mel", C.POINTER(f32)), ("valid", i32), ("pcm", C.POINTER(f32)), ("n_samples", i32)]
+                ("mel", C.POINTER(f32)), ("valid", i32), ("pcm", C.POINTER(f32)), ("n_samples", i32),
+                ("sample_rate", i32)]
 
 
 class Job(C.Structure):
@@ -150,6 +151,8 @@ EXTENSIONS = {
     "d1_relpos_attn": (i32, [p, p, p, p, i32, p, i32, i32, i32, p, i32, p, i32, i32, i32, f32, p]),
     "d1_relpos_attn_error": (i32, []),
     "d1_log_mel": (i32, [p, i32, p, p]),
+    "d1_resample_len": (i32, [i32, i32, i32]),
+    "d1_resample": (i32, [p, i32, i32, i32, p, p]),
     "d1_vision_pos": (i32, [p, p, p, p, i32, i32, i32, i32, p, p]),
     "d1_layernorm_rows": (i32, [p, p, f32, p, p, p, p, i32, i32, f32, p]),
     "d1_sub_conv01": (i32, [p, i32, i32, p, p, p, p, p, i32, i32, p]),
@@ -182,6 +185,7 @@ RUNNER = {
     "d1h_audio_destroy": (None, [p]),
     "d1h_audio_encode": (i32, [p, i32, C.POINTER(i32), p, p, p]),
     "d1h_audio_encode_pcm": (i32, [p, i32, C.POINTER(i32), p, p, C.POINTER(i32), p]),
+    "d1h_audio_encode_pcm_rates": (i32, [p, i32, C.POINTER(i32), C.POINTER(i32), p, p, C.POINTER(i32), p]),
     "d1h_vision_capacity": (i32, [p]),
     "d1h_model_layers": (i32, [p, i32]),
     "d1h_gemm_ctx": (p, [p]),

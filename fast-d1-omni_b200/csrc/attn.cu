@@ -254,14 +254,14 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // (it must cover every tile) and the runners pass one item per 256-row block. A unit is two 128-row query tiles
 // that share each K/V tile, one per softmax warpgroup.
 //
-// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM, so
-// S(j+2) is issued as soon as P(j) is written. P never leaves TMEM: the softmax writes P(j) as fp16 pairs over the
-// first 32 columns of S(j)'s buffer, and P(j).V_j reads its A operand from there (tcgen05.mma with A in tensor
-// memory). The tensor core runs one thread's MMAs in issue order, so S(j+2), issued after P(j).V_j into the same
-// buffer, overwrites P(j) only after that MMA has read it, and the softmax's wait for S(j) also covers P(j-2).V_{j-2}.
-// The issuer serves each warpgroup as soon as its P is written, so the two drift apart and their exponentials
-// interleave on the SFU instead of running in lockstep. Every handoff has its own barrier per buffer.
-// TMEM (512 columns): S/P[w][b] at (2w + b) * 64, O[w] at 256 + 64w.
+// The MMA issuer runs the score tiles three steps ahead of the softmax: each warpgroup has three S buffers in TMEM,
+// so S(j+3) is issued as soon as P(j) is written and the softmax has two tiles of work while it is computed. P never
+// leaves TMEM: the softmax writes P(j) as fp16 pairs over the first 32 columns of S(j)'s buffer, and P(j).V_j reads
+// its A operand from there (tcgen05.mma with A in tensor memory). The tensor core runs one thread's MMAs in issue
+// order, so S(j+3), issued after P(j).V_j into the same buffer, overwrites P(j) only after that MMA has read it, and
+// the softmax's wait for S(j) also covers P(j-3).V_{j-3}. The issuer serves each warpgroup as soon as its P is
+// written, so the two drift apart instead of running in lockstep. Every handoff has its own barrier per buffer.
+// TMEM (512 columns): S/P[w][b] at 256w + 64b (b < 3), O[w] at 256w + 192.
 // Warps:
 //   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
 //        reads its S row (one TMEM round trip), takes the row max in the exp2 domain (3-input max), writes
@@ -276,6 +276,8 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 //        current unit's math.
 //   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64, both operands in
 //        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=64, A in TMEM).
+// (Tried: a share of the exponentials by a cubic on the FMA pipe. Slower at every share, 152 -> 178 us at 4 x 2048
+// from none to half: the softmax is bound by instruction issue and waits, not by the SFU.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
@@ -284,6 +286,8 @@ constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
 constexpr int T_O_BYTES = TQ * 128;       // one warpgroup's O staging tile
 constexpr uint32_t T_TMEM_COLS = 512;
+constexpr int T_SBUF = 3;                 // S/P buffers per warpgroup (S runs T_SBUF tiles ahead)
+constexpr uint32_t T_WG_COLS = 256;       // TMEM columns per warpgroup: T_SBUF S/P buffers, then O
 constexpr float kLazyRescale = 8.f;
 enum : int {
     B_QFULL = 0,
@@ -291,9 +295,9 @@ enum : int {
     B_KVFULL = B_QEMPTY + T_QSLOTS,
     B_KVEMPTY = B_KVFULL + T_KVSTAGES,
     B_SFULL = B_KVEMPTY + T_KVSTAGES,  // [w][b]
-    B_PFULL = B_SFULL + 4,             // [w][b]
-    B_ODONE = B_PFULL + 4,             // [w][b]: P.V of the tile whose P is in buffer b
-    B_OFREE = B_ODONE + 4,             // [w]
+    B_PFULL = B_SFULL + 2 * T_SBUF,    // [w][b]
+    B_ODONE = B_PFULL + 2 * T_SBUF,    // [w][b]: P.V of the tile whose P is in buffer b
+    B_OFREE = B_ODONE + 2 * T_SBUF,    // [w]
     B_DRAIN = B_OFREE + 2,
     B_OSTAGED = B_DRAIN + 1,           // [w]: the warpgroup's O tile is in shared memory (4 warp arrivals)
     B_OREAD = B_OSTAGED + 2,           // [w]: its previous bulk store has read the staging buffer
@@ -301,6 +305,7 @@ enum : int {
 };
 constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_O_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
+static_assert(T_SBUF * TKV + 64 <= (int)T_WG_COLS && 2 * T_WG_COLS <= T_TMEM_COLS, "TMEM of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
 __device__ int g_fa_err = 0;
@@ -353,27 +358,6 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-
-// 2^x on the FMA pipe, for part of the softmax's exponentials (the SFU is the attention's bottleneck at head dim
-// 64: one exponential per 256 FLOPs). Range reduction x = n + f with n = round(x), |f| <= 1/2, by adding and
-// subtracting 1.5 * 2^23 (round-to-nearest puts n in the low mantissa bits); 2^f by a cubic fitted here for minimal
-// relative error on [-1/2, 1/2] (Remez exchange: max relative error 7.5e-5, below half an fp16 ulp of P, so P
-// rounds to the same fp16 value as with the hardware approximation or differs by one ulp); n goes into the
-// exponent field by an integer add. x is clamped at -126 so that field stays >= 0 (the cubic is below 1 for f <= 0:
-// exponent field 126 before the add), which makes keys masked with -inf and scores far below the row max a tiny
-// positive value that rounds to fp16 zero; x <= 8 by the lazy rescale, so the result never overflows.
-__device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -126.f);
-    const float j = __fadd_rn(x, 12582912.f);
-    const float f = __fsub_rn(x, __fsub_rn(j, 12582912.f));
-    const float p = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261112511f), f, 0.69326096773f), f, 0.99992805719f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
-}
-#ifndef D1_POLY_PER8
-#define D1_POLY_PER8 2
-#endif
-constexpr int kPolyPer8 = D1_POLY_PER8;  // exponentials of each 8 computed by exp2_poly, the rest by the SFU
-static_assert(kPolyPer8 >= 0 && kPolyPer8 <= 8, "exp2_poly share");
 
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -449,7 +433,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             mbar_init(bar(B_KVFULL + i), 32 * T_LOADERS);
             mbar_init(bar(B_KVEMPTY + i), 1);
         }
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 2 * T_SBUF; i++) {
             mbar_init(bar(B_SFULL + i), 1);
             mbar_init(bar(B_PFULL + i), 4);
             mbar_init(bar(B_ODONE + i), 1);
@@ -579,40 +563,40 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 auto kv_ready = [&](int j) {
                     return mbar_wait(bar(B_KVFULL + (ki + j) % T_KVSTAGES), ((ki + j) / T_KVSTAGES) & 1, abort_flag);
                 };
-                // S_w(j) into buffer (cnt[w] + j) % 2. That buffer last held P(cnt[w] + j - 2), whose P.V this
-                // thread issued earlier: the tensor core reads it before this S overwrites it (issue order).
+                // S_w(j) into buffer (cnt[w] + j) % T_SBUF. That buffer last held P(cnt[w] + j - T_SBUF), whose P.V
+                // this thread issued earlier: the tensor core reads it before this S overwrites it (issue order).
                 auto issue_s = [&](int w, int j) {
                     const uint32_t ka = k_addr(j);
-                    const int b = (cnt[w] + j) & 1;
+                    const int b = (cnt[w] + j) % T_SBUF;
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        tc_mma_f16(tmem + (2 * w + b) * TKV, smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32),
+                        tc_mma_f16(tmem + w * T_WG_COLS + b * TKV, smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32),
                                    smem_desc_k128(ka + k * 32), IDESC_S, k != 0);
-                    tc_commit(bar(B_SFULL + 2 * w + b));
+                    tc_commit(bar(B_SFULL + T_SBUF * w + b));
                 };
-                for (int j = 0; j < 2 && j < un.nt && ok; j++) {  // prologue: S for tiles 0 and 1
+                for (int j = 0; j < T_SBUF && j < un.nt && ok; j++) {  // prologue: S for the first T_SBUF tiles
                     if (!(ok = kv_ready(j))) break;
                     tc_fence_after();
                     for (int w = 0; w < nw; w++) issue_s(w, j);
                 }
                 for (int j = 0; j < un.nt && ok; j++) {
-                    const bool ahead = j + 2 < un.nt;
-                    if (ahead && !(ok = kv_ready(j + 2))) break;
+                    const bool ahead = j + T_SBUF < un.nt;
+                    if (ahead && !(ok = kv_ready(j + T_SBUF))) break;
                     const uint32_t v_addr = k_addr(j) + T_KV_BYTES;
-                    // each warpgroup as soon as its P(j) is in TMEM: P(j).V_j, then S(j+2) into the same buffer
+                    // each warpgroup as soon as its P(j) is in TMEM: P(j).V_j, then S(j+T_SBUF) into the same buffer
                     for (int w = 0; w < nw && ok; w++) {
-                        const int c = cnt[w] + j, b = c & 1;
-                        ok = mbar_wait(bar(B_PFULL + 2 * w + b), (c >> 1) & 1, abort_flag);
+                        const int c = cnt[w] + j, b = c % T_SBUF;
+                        ok = mbar_wait(bar(B_PFULL + T_SBUF * w + b), (c / T_SBUF) & 1, abort_flag);
                         // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
                         if (ok && j == 0 && units[w] > 0) ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
 #pragma unroll
                         for (int k = 0; k < 4; k++)
-                            tc_mma_f16_ts(tmem + 4 * TKV + w * 64, tmem + (2 * w + b) * TKV + k * 8,
+                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_SBUF * TKV, tmem + w * T_WG_COLS + b * TKV + k * 8,
                                           smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                        tc_commit(bar(B_ODONE + 2 * w + b));
-                        if (ahead) issue_s(w, j + 2);
+                        tc_commit(bar(B_ODONE + T_SBUF * w + b));
+                        if (ahead) issue_s(w, j + T_SBUF);
                     }
                     if (!ok) break;
                     tc_commit(bar(B_KVEMPTY + (ki + j) % T_KVSTAGES));
@@ -635,7 +619,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         // ------------------------------------------------------------------ softmax (warpgroups 0 and 1)
         const int w = warp >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tO = tmem + 4 * TKV + w * 64 + lane_off;
+        const uint32_t tO = tmem + w * T_WG_COLS + T_SBUF * TKV + lane_off;
         uint8_t* stile = sO + w * T_O_BYTES;
         int cnt = 0;
         int nst = 0;  // O tiles this warpgroup has staged
@@ -646,12 +630,13 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
-                const int c = cnt + j, b = c & 1;
-                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + 2 * w + b), (c >> 1) & 1, abort_flag))))
+                const int c = cnt + j, b = c % T_SBUF;
+                if (!(ok = __all_sync(D1_FULL_MASK,
+                                      mbar_wait(bar(B_SFULL + T_SBUF * w + b), (c / T_SBUF) & 1, abort_flag))))
                     break;
                 tc_fence_after();
                 uint32_t sr[TKV];
-                const uint32_t tS = tmem + (2 * w + b) * TKV + lane_off;
+                const uint32_t tS = tmem + w * T_WG_COLS + b * TKV + lane_off;
                 tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
                 tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
                 tc_wait_ld();
@@ -680,8 +665,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     alpha = ex2(m - mx);
                 }
                 if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {  // rare: O must hold P.V up to tile c - 1
-                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + (b ^ 1)), ((c - 1) >> 1) & 1,
-                                                                  abort_flag))))
+                    const int cp = c - 1;
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + T_SBUF * w + cp % T_SBUF),
+                                                                  (cp / T_SBUF) & 1, abort_flag))))
                         break;
                     tc_fence_after();
 #pragma unroll 1
@@ -703,8 +689,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     float p[8];
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
-                        const float x = fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use);
-                        p[e] = e < 8 - kPolyPer8 ? ex2(x) : exp2_poly(x);
+                        p[e] = ex2(fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use));
                         rs8[e] += p[e];
                     }
 #pragma unroll
@@ -715,7 +700,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(B_PFULL + 2 * w + b));
+                if (lane == 0) mbar_arrive(bar(B_PFULL + T_SBUF * w + b));
                 const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
                 l = l * alpha + rs;
                 m = m_use;
@@ -724,7 +709,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             cnt += un.nt;
             // the unit's last P.V (the earlier ones completed before it)
             const int cl = cnt - 1;
-            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + 2 * w + (cl & 1)), (cl >> 1) & 1, abort_flag))))
+            if (!(ok = __all_sync(D1_FULL_MASK,
+                                  mbar_wait(bar(B_ODONE + T_SBUF * w + cl % T_SBUF), (cl / T_SBUF) & 1, abort_flag))))
                 break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;

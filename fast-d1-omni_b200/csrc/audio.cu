@@ -23,6 +23,13 @@
 //   (src/audio.rs:401 MAX_T) — the reference's limit.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
 #include "common.cuh"
 #include "warp_mma.cuh"
 
@@ -661,4 +668,140 @@ extern "C" int d1_log_mel(const float* x, int n, float* mel, cudaStream_t st) {
     k_mel_frames<<<frames, 256, 0, st>>>(x, n, mel);
     k_mel_norm<<<MEL_N / MEL_CH, 256, 0, st>>>(mel, frames, valid);
     return (int)cudaGetLastError();
+}
+
+// ================================================================================================ resampler
+// d1_resample — the WAV front end's sample-rate conversion to 16 kHz (src/audio.rs:108-148, host code in the
+// reference) on the GPU. A polyphase Kaiser-windowed sinc filter: output n reads input position n * down / up
+// (up / down = dst / src reduced by their gcd), phase p = (n * down) % up, taps at inputs base - half .. base + half
+// with base = n * down / up; cutoff = min(up / down, 1) * 0.97, half = ceil(32 / cutoff), Kaiser beta 8.6.
+// The filter table [up][2*half+1] is evaluated on the host in f64 exactly as the reference's tap() does (its
+// zeroth-order Bessel series, its operation order) and rounded to fp32, once per (device, rate pair), then kept on
+// the device. The sum per output runs over the taps in order, skipping inputs outside the clip, as fp32 products
+// added to an fp32 accumulator (the reference's Rust does not fuse them), so the result is bit-identical.
+// A CTA computes 256 consecutive outputs from the input window they share, staged in shared memory.
+namespace {
+
+struct RsTable {
+    int up = 0, down = 0, half = 0;
+    float* d_table = nullptr;
+};
+
+bool rs_plan(int from, int to, int& up, int& down, int& half, double& cutoff) {
+    if (from <= 0 || to <= 0) return false;
+    int a = from, b = to;
+    while (b) {
+        const int t = a % b;
+        a = b;
+        b = t;
+    }
+    up = to / a;
+    down = from / a;
+    cutoff = std::min((double)up / (double)down, 1.0) * 0.97;
+    half = (int)std::ceil(32.0 / cutoff);
+    return true;
+}
+
+double rs_bessel_i0(double x) {  // src/audio.rs:97-104
+    double s = 1.0, t = 1.0;
+    for (int k = 1; k < 50; k++) {
+        const double y = x / (2.0 * (double)k);
+        t *= y * y;
+        s += t;
+    }
+    return s;
+}
+
+// The device table for (from, to) on the current device, built on first use (host f64 evaluation + one upload).
+const RsTable* rs_table(int from, int to) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int>, RsTable> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_tuple(dev, from, to);
+    auto it = cache.find(key);
+    if (it != cache.end()) return &it->second;
+    RsTable t;
+    double cutoff = 0.0;
+    if (!rs_plan(from, to, t.up, t.down, t.half, cutoff)) return nullptr;
+    const int taps = 2 * t.half + 1;
+    if ((long long)t.up * taps > (64ll << 20)) return nullptr;  // rates with no small common divisor
+    const double beta = 8.6, i0b = rs_bessel_i0(beta), pi = 3.14159265358979323846;
+    std::vector<float> h((size_t)t.up * taps);
+    for (int p = 0; p < t.up; p++) {
+        const double frac = (double)p / (double)t.up;
+        for (int j = 0; j < taps; j++) {
+            const double tt = (double)(j - t.half) - frac;
+            const double r = tt / (double)t.half;
+            double v = 0.0;
+            if (std::fabs(r) < 1.0) {
+                const double sinc = tt == 0.0 ? 1.0 : std::sin(pi * tt * cutoff) / (pi * tt * cutoff);
+                v = cutoff * sinc * rs_bessel_i0(beta * std::sqrt(1.0 - r * r)) / i0b;
+            }
+            h[(size_t)p * taps + j] = (float)v;
+        }
+    }
+    if (cudaMalloc(&t.d_table, h.size() * sizeof(float)) != cudaSuccess) return nullptr;
+    if (cudaMemcpy(t.d_table, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(t.d_table);
+        return nullptr;
+    }
+    return &(cache[key] = t);
+}
+
+constexpr int kRsOut = 256;  // outputs per CTA
+
+__global__ void __launch_bounds__(kRsOut) k_resample(const float* __restrict__ x, int n,
+                                                     const float* __restrict__ table, int up, int down, int half,
+                                                     float* __restrict__ y, int n_out, int win_cap) {
+    extern __shared__ float win[];
+    const int o0 = blockIdx.x * kRsOut;
+    const long long first = (long long)o0 * down / up - half;  // first input the CTA's outputs read
+    const int o_last = min(o0 + kRsOut, n_out) - 1;
+    const long long last = (long long)o_last * down / up + half;
+    const int len = (int)(last - first + 1);
+    for (int i = threadIdx.x; i < len && i < win_cap; i += blockDim.x) {
+        const long long g = first + i;
+        win[i] = (g >= 0 && g < n) ? x[g] : 0.f;
+    }
+    __syncthreads();
+    const int o = o0 + threadIdx.x;
+    if (o >= n_out) return;
+    const long long pos = (long long)o * down;
+    const long long base = pos / up;
+    const int ph = (int)(pos - base * up), taps = 2 * half + 1;
+    const float* w = table + (size_t)ph * taps;
+    // inputs base - half + j inside [0, n): the taps the reference does not skip
+    const int j0 = (int)max(0ll, (long long)half - base), j1 = (int)min((long long)taps, (long long)n - base + half);
+    const int off = (int)(base - half - first);
+    float acc = 0.f;
+    for (int j = j0; j < j1; j++) acc = __fadd_rn(acc, __fmul_rn(__ldg(w + j), win[off + j]));
+    y[o] = acc;
+}
+
+}  // namespace
+
+extern "C" int d1_resample_len(int n, int from, int to) {
+    int up, down, half;
+    double cutoff;
+    if (n < 0 || !rs_plan(from, to, up, down, half, cutoff)) return -1;
+    if (from == to) return n;
+    return (int)((long long)n * up / down);
+}
+
+extern "C" int d1_resample(const float* x, int n, int from, int to, float* y, cudaStream_t st) {
+    const int n_out = d1_resample_len(n, from, to);
+    if (n_out < 0 || (n > 0 && (!x || !y))) return -1;
+    if (n_out == 0) return 0;
+    if (from == to) return cudaMemcpyAsync(y, x, (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice, st) ? -1 : 0;
+    const RsTable* t = rs_table(from, to);
+    if (!t) return -1;
+    // shared-memory window: the inputs of 256 consecutive outputs plus the taps on both sides
+    const int win_cap = (int)((long long)kRsOut * t->down / t->up + 2 * t->half + 2);
+    if ((size_t)win_cap * sizeof(float) > 48 * 1024) return -1;
+    const int grid = (n_out + kRsOut - 1) / kRsOut;
+    k_resample<<<grid, kRsOut, (size_t)win_cap * sizeof(float), st>>>(x, n, t->d_table, t->up, t->down, t->half, y,
+                                                                       n_out, win_cap);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

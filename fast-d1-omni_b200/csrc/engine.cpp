@@ -56,7 +56,8 @@ struct JobState {
     std::vector<int> ph, pw;             // image crops
     std::vector<uint16_t> patches;       // fp16 bits [sum ph*pw][768]
     std::vector<float> mel;              // audio [valid][128] log-mel frames, or
-    std::vector<float> pcm;              // audio as a 16 kHz waveform
+    std::vector<float> pcm;              // audio as a waveform at `rate` Hz
+    int rate = 16000;
     int valid = 0;
     bool has_prefix = false;
     D1PrefixCache prefix{};
@@ -238,7 +239,7 @@ struct D1Engine {
         };
         // audio clips of the group go through one packed encoder call per input form (log-mel frames, waveforms),
         // then each clip's rows move to its offset
-        std::vector<int> avalid, pvalid, pns;
+        std::vector<int> avalid, pvalid, pns, prate;
         std::vector<float> amel, apcm;
         std::vector<size_t> aoff, poff;
         for (const auto& [id, off, len] : ok) {
@@ -271,6 +272,7 @@ struct D1Engine {
                 if (!js.pcm.empty()) {
                     pvalid.push_back(js.valid);
                     pns.push_back((int)js.pcm.size());
+                    prate.push_back(js.rate);
                     apcm.insert(apcm.end(), js.pcm.begin(), js.pcm.end());
                     poff.push_back(off);
                 } else {
@@ -289,7 +291,8 @@ struct D1Engine {
             for (int v : vv) arows += audio_rows(v);
             float* tmp = nullptr;
             if (cudaMallocAsync((void**)&tmp, arows * ED * 4, st) != cudaSuccess) return efail("audio buffer allocation");
-            const int r = form ? d1h_audio_encode_pcm(audio, (int)vv.size(), pns.data(), apcm.data(), tmp, nullptr, st)
+            const int r = form ? d1h_audio_encode_pcm_rates(audio, (int)vv.size(), pns.data(), prate.data(), apcm.data(),
+                                                            tmp, nullptr, st)
                                : d1h_audio_encode(audio, (int)vv.size(), vv.data(), amel.data(), tmp, st);
             if (r < 0) return efail(std::string("audio encode failed: ") + d1h_last_error());
             size_t src = 0;
@@ -521,10 +524,17 @@ long long d1e_submit(D1Engine* e, const D1Job* job) {
         js.patches.assign(p, p + np * 768);
     } else if (md.kind == D1_MEDIA_AUDIO) {
         if (md.pcm) {
-            if (md.n_samples < 0) return efail("bad audio media");
-            const int n = std::min(md.n_samples, 30 * 16000);  // src/audio.rs:241-247
+            const int rate = md.sample_rate ? md.sample_rate : 16000;
+            if (md.n_samples < 0 || rate <= 0) return efail("bad audio media");
+            // 16 kHz: cut to 30 s (src/audio.rs:241-247); another rate: what the WAV decoder keeps (30 s + 1 s,
+            // :59), resampled on the device, then cut to 30 s
+            const int n = rate == 16000 ? std::min(md.n_samples, 30 * 16000)
+                                        : (int)std::min<long long>(md.n_samples, 31ll * rate);
+            const int n16 = rate == 16000 ? n : d1_resample_len(n, rate, 16000);
+            if (n16 < 0) return efail("bad audio sample rate");
             js.pcm.assign(md.pcm, md.pcm + n);
-            js.valid = std::max(n, 8000) / 160;
+            js.rate = rate;
+            js.valid = std::max(std::min(n16, 30 * 16000), 8000) / 160;
         } else {
             if (md.valid < 1 || md.valid > 3000 || !md.mel) return efail("bad audio media");
             js.valid = md.valid;

@@ -1177,6 +1177,10 @@ struct D1Audio {
     int* host_offs = nullptr;          // pinned: clip offsets
     float* host_mel = nullptr;         // pinned staging of log-mel frames [mel_rows][128]
     float* host_pcm = nullptr;         // pinned staging of waveforms [pcm_cap]
+    float* src = nullptr;              // waveforms at other sample rates, before d1_resample [src_cap]
+    float* host_src = nullptr;         // their pinned staging
+    float* rs = nullptr;               // one clip resampled to 16 kHz [rs_cap]
+    size_t src_cap = 0, rs_cap = 0;    // grown on demand
     cudaEvent_t done = nullptr;        // the previous call's last kernel
     cudaEvent_t staged = nullptr;      // the previous call's host->device copies
     bool busy = false;
@@ -1250,7 +1254,9 @@ void d1h_audio_destroy(D1Audio* a) {
                     (void*)a->big, (void*)a->qu, (void*)a->qv, (void*)a->kk, (void*)a->vv, (void*)a->o,
                     (void*)a->offs})
         if (p) cudaFree(p);
-    for (void* p : {(void*)a->host_offs, (void*)a->host_mel, (void*)a->host_pcm})
+    for (void* p : {(void*)a->src, (void*)a->rs})
+        if (p) cudaFree(p);
+    for (void* p : {(void*)a->host_offs, (void*)a->host_mel, (void*)a->host_pcm, (void*)a->host_src})
         if (p) cudaFreeHost(p);
     if (a->done) cudaEventDestroy(a->done);
     if (a->staged) cudaEventDestroy(a->staged);
@@ -1316,13 +1322,30 @@ int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel
 
 int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const float* pcm, float* out, int* valid_out,
                          cudaStream_t st) {
+    return d1h_audio_encode_pcm_rates(a, n_clips, n_samples, nullptr, pcm, out, valid_out, st);
+}
+
+int d1h_audio_encode_pcm_rates(D1Audio* a, int n_clips, const int* n_samples, const int* rates, const float* pcm,
+                               float* out, int* valid_out, cudaStream_t st) {
     if (!a || n_clips <= 0 || n_clips > 4095 || !n_samples || !pcm || !out) return fail("bad arguments");
-    // src/audio.rs:238-247: at most 30 s, zero-padded to at least 0.5 s; valid = n / 160 frames
-    std::vector<int> valid(n_clips), used(n_clips);
-    size_t total = 0, frames = 0;
+    // a clip at another rate: the WAV decoder keeps at most 30 s + 1 s of it (src/audio.rs:59), resample() takes it
+    // to 16 kHz (:108-148); then, as for 16 kHz input, src/audio.rs:238-247: at most 30 s, zero-padded to at least
+    // 0.5 s; valid = n / 160 frames
+    std::vector<int> valid(n_clips), used(n_clips), rate(n_clips), src_n(n_clips, 0);
+    size_t total = 0, frames = 0, src_total = 0, rs_max = 0;
     for (int c = 0; c < n_clips; c++) {
         if (n_samples[c] < 0) return fail("negative sample count");
-        used[c] = std::min(n_samples[c], A_MAX_SAMPLES);
+        rate[c] = rates && rates[c] ? rates[c] : 16000;
+        if (rate[c] <= 0) return fail("sample rate must be positive");
+        int len16 = n_samples[c];
+        if (rate[c] != 16000) {
+            src_n[c] = (int)std::min<long long>(n_samples[c], 31ll * rate[c]);
+            len16 = d1_resample_len(src_n[c], rate[c], 16000);
+            if (len16 < 0) return fail("unsupported sample rate");
+            src_total += (size_t)src_n[c];
+            rs_max = std::max(rs_max, (size_t)len16);
+        }
+        used[c] = std::min(len16, A_MAX_SAMPLES);
         const int n = std::max(used[c], A_MIN_SAMPLES);
         valid[c] = n / 160;
         total += (size_t)n;
@@ -1333,24 +1356,61 @@ int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const fl
     const int rows = audio_prepare(a, n_clips, valid.data(), max_t, st);
     if (rows < 0) return rows;
     if (total > a->pcm_cap) return fail("clips exceed the audio waveform staging capacity");
-    // stage every clip (cut, zero-padded) in pinned memory, one copy, then the front end per clip
-    const float* src = pcm;
-    size_t off = 0;
+    if (src_total > a->src_cap || rs_max > a->rs_cap) {  // grow the resampling buffers (rare): nothing may use them
+        if (cudaStreamSynchronize(st) != cudaSuccess) return fail("stream sync failed");
+        if (src_total > a->src_cap) {
+            if (a->src) cudaFree(a->src);
+            if (a->host_src) cudaFreeHost(a->host_src);
+            a->src = nullptr;
+            a->host_src = nullptr;
+            a->src_cap = 0;
+            if (dmalloc(&a->src, src_total * 4) ||
+                cudaMallocHost((void**)&a->host_src, src_total * 4) != cudaSuccess)
+                return fail("resampler staging allocation failed");
+            a->src_cap = src_total;
+        }
+        if (rs_max > a->rs_cap) {
+            if (a->rs) cudaFree(a->rs);
+            a->rs = nullptr;
+            a->rs_cap = 0;
+            if (dmalloc(&a->rs, rs_max * 4)) return fail("resampler buffer allocation failed");
+            a->rs_cap = rs_max;
+        }
+    }
+    // stage every 16 kHz clip (cut, zero-padded) in pinned memory, and the other clips at their own rates; one
+    // copy each, then per clip the resampler (other rates) and the front end
+    const float* sp = pcm;
+    size_t off = 0, soff = 0;
     for (int c = 0; c < n_clips; c++) {
         const int n = std::max(used[c], A_MIN_SAMPLES);
-        memcpy(a->host_pcm + off, src, (size_t)used[c] * 4);
-        if (n > used[c]) memset(a->host_pcm + off + used[c], 0, (size_t)(n - used[c]) * 4);
-        src += n_samples[c];
+        if (rate[c] == 16000) {
+            memcpy(a->host_pcm + off, sp, (size_t)used[c] * 4);
+            if (n > used[c]) memset(a->host_pcm + off + used[c], 0, (size_t)(n - used[c]) * 4);
+        } else {
+            memcpy(a->host_src + soff, sp, (size_t)src_n[c] * 4);
+            soff += (size_t)src_n[c];
+        }
+        sp += n_samples[c];
         off += (size_t)n;
     }
     if (cudaMemcpyAsync(a->pcm, a->host_pcm, total * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        (src_total && cudaMemcpyAsync(a->src, a->host_src, src_total * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) ||
         cudaEventRecord(a->staged, st) != cudaSuccess)
         return fail("audio upload failed");
     std::vector<const float*> mp(n_clips);
     off = 0;
+    soff = 0;
     size_t moff = 0;
     for (int c = 0; c < n_clips; c++) {
         const int n = std::max(used[c], A_MIN_SAMPLES);
+        if (rate[c] != 16000) {
+            a->launches++;
+            if (d1_resample(a->src + soff, src_n[c], rate[c], 16000, a->rs, st) ||
+                (used[c] && cudaMemcpyAsync(a->pcm + off, a->rs, (size_t)used[c] * 4, cudaMemcpyDeviceToDevice, st)) ||
+                (n > used[c] && cudaMemsetAsync(a->pcm + off + used[c], 0, (size_t)(n - used[c]) * 4, st)))
+                return fail("resampling failed");
+            soff += (size_t)src_n[c];
+        }
         a->launches += 2;
         if (d1_log_mel(a->pcm + off, n, a->mel + moff * N_MELS, st)) return fail("log-mel front end failed");
         mp[c] = a->mel + moff * N_MELS;

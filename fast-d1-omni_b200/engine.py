@@ -14,6 +14,7 @@ The 600M model fits every GPU and requests are independent, so multi-GPU serving
 from __future__ import annotations
 
 import ctypes as C
+import math
 import threading
 import time
 
@@ -31,6 +32,15 @@ def audio_rows(valid: int) -> int:
     return valid
 
 
+def pcm_len_16k(n: int, rate: int) -> int:
+    """16 kHz samples of a waveform of n samples at `rate` Hz: the WAV decoder keeps at most 30 s + 1 s
+    (src/audio.rs:59), resample() writes n * up / down samples (up / down = 16000 / rate reduced, :108-113)."""
+    if rate == 16000:
+        return n
+    g = math.gcd(rate, 16000)
+    return min(n, 31 * rate) * (16000 // g) // (rate // g)
+
+
 def prefix_len(req) -> int:
     m = req.get("media")
     if not m:
@@ -38,7 +48,7 @@ def prefix_len(req) -> int:
     if m["kind"] == "images":
         return sum(ph * pw // 4 for ph, pw, _ in m["crops"])
     if m.get("pcm") is not None:  # src/audio.rs:241-247: cut to 30 s, padded to 0.5 s, hop 160
-        return audio_rows(max(min(len(m["pcm"]), 30 * 16000), 8000) // 160)
+        return audio_rows(max(min(pcm_len_16k(len(m["pcm"]), int(m.get("rate") or 16000)), 30 * 16000), 8000) // 160)
     return audio_rows(int(m["valid"]))
 
 
@@ -104,6 +114,7 @@ class Engine:
             job.media.kind = MEDIA_AUDIO
             job.media.pcm = pcm.ctypes.data_as(C.POINTER(C.c_float))
             job.media.n_samples = len(pcm)
+            job.media.sample_rate = int(m.get("rate") or 16000)
         elif m and m["kind"] == "audio":
             v = int(m["valid"])
             mel = np.ascontiguousarray(np.asarray(m["mel"], np.float32)[:v])

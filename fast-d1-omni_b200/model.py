@@ -320,21 +320,24 @@ class AudioModel:
         assert r == rows
         return out
 
-    def encode_pcm(self, waves, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-        """waves: [fp32 16 kHz samples] -> fp32 [sum T, 1024] on the device; log-mel features computed on the GPU
-        (each clip cut to 30 s and padded to 0.5 s first)."""
+    def encode_pcm(self, waves, out: torch.Tensor | None = None, stream=None, rates=None) -> torch.Tensor:
+        """waves: [fp32 samples] (16 kHz, or rates[i] Hz: resampled to 16 kHz on the GPU first) -> fp32 [sum T, 1024]
+        on the device; log-mel features computed on the GPU (each clip cut to 30 s and padded to 0.5 s first)."""
+        from .engine import pcm_len_16k
         n = len(waves)
+        rates = [int(r or 16000) for r in rates] if rates is not None else [16000] * n
         ns = (C.c_int * n)(*[len(w) for w in waves])
+        rt = (C.c_int * n)(*rates)
         pcm = np.ascontiguousarray(np.concatenate([np.asarray(w, np.float32) for w in waves]), np.float32)
-        valid = [max(min(len(w), 30 * 16000), 8000) // 160 for w in waves]
+        valid = [max(min(pcm_len_16k(len(w), r), 30 * 16000), 8000) // 160 for w, r in zip(waves, rates)]
         rows = sum(self.out_len(v) for v in valid)
         if out is None:
             out = torch.empty(rows, 1024, device=self.device, dtype=torch.float32)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         vo = (C.c_int * n)()
         with torch.cuda.device(self.device):
-            r = self.L.d1h_audio_encode_pcm(self.a, n, ns, C.c_void_p(pcm.ctypes.data), _ptr(out), vo,
-                                            C.c_void_p(s.cuda_stream))
+            r = self.L.d1h_audio_encode_pcm_rates(self.a, n, ns, rt, C.c_void_p(pcm.ctypes.data), _ptr(out), vo,
+                                                  C.c_void_p(s.cuda_stream))
         if r < 0:
             raise RuntimeError(f"d1h_audio_encode_pcm failed: {self.L.d1h_last_error().decode()}")
         assert r == rows and list(vo) == valid

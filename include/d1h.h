@@ -275,6 +275,12 @@ int d1h_audio_encode(D1Audio* a, int n_clips, const int* valid, const float* mel
  * computed on the device (d1_log_mel). valid_out (optional, [n_clips]) receives each clip's mel frame count. */
 int d1h_audio_encode_pcm(D1Audio* a, int n_clips, const int* n_samples, const float* pcm, float* out, int* valid_out,
                          cudaStream_t stream);
+/* d1h_audio_encode_pcm with a sample rate per clip (rates NULL, or an entry 0 or 16000: 16 kHz). A clip at another
+ * rate is what the reference's WAV decoder hands on (src/audio.rs:24-80: mono fp32, at most 30 s + 1 s of input):
+ * it is converted to 16 kHz on the device by d1_resample (src/audio.rs:108-148) before the front end. n_samples
+ * counts samples at the clip's own rate. */
+int d1h_audio_encode_pcm_rates(D1Audio* a, int n_clips, const int* n_samples, const int* rates, const float* pcm,
+                               float* out, int* valid_out, cudaStream_t stream);
 
 /* Vision batch capacity in patches (max_patches of d1h_vision_create). */
 int d1h_vision_capacity(const D1Vision* v);
@@ -319,8 +325,9 @@ typedef struct D1Media {         /* src/engine.rs:27-31 */
     const d1_half* patches;      /* host fp16 [sum ph*pw][768] */
     const float* mel;            /* audio: host fp32 [valid][128] normalised log-mel frames, or NULL with pcm */
     int valid;                   /* 1 .. 3000 */
-    const float* pcm;            /* audio as a 16 kHz waveform (features computed on the device), or NULL */
-    int n_samples;
+    const float* pcm;            /* audio as a waveform (features computed on the device), or NULL */
+    int n_samples;               /* at sample_rate */
+    int sample_rate;             /* of pcm in Hz; 0 means 16000 (other rates are resampled on the device) */
 } D1Media;
 
 typedef struct D1Job {           /* src/engine.rs:49-53 */

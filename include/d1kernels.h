@@ -298,6 +298,17 @@ int d1_conformer_dw_clips(const d1_half* a, const float* b1, const float* dw, co
  * statistics are f64 sums in 8 interleaved parts (the reference sums sequentially). */
 int d1_log_mel(const float* x, int n, float* mel, cudaStream_t stream);
 
+/* extension — the number of 16 kHz samples d1_resample writes for n input samples at `from` Hz (to = 16000 in the
+ * reference): n * up / down with up / down = to / from reduced (src/audio.rs:108-113); -1 for a rate <= 0. */
+int d1_resample_len(int n, int from, int to);
+
+/* extension — sample-rate conversion of n samples (device x) to `to` Hz (device y, d1_resample_len(n, from, to)
+ * samples): the reference's polyphase Kaiser-windowed sinc resampler (src/audio.rs:108-148, host code in the
+ * reference, run after WAV decoding) with the same fp32 filter table (evaluated in f64 on the host, once per rate
+ * pair and device, then kept on the device) and the same fp32 accumulation order: bit-identical results. from == to
+ * copies. Returns 0, or -1 for bad arguments or a rate pair whose filter table would exceed 64 Mi taps. */
+int d1_resample(const float* x, int n, int from, int to, float* y, cudaStream_t stream);
+
 /* extension — reads and clears d1_relpos_attn's device error word (nonzero: a clip longer than max_len was
  * skipped). */
 int d1_relpos_attn_error(void);

@@ -593,6 +593,64 @@ def slaney_filterbank(n_fft=512, sr=16000, n_mels=N_MELS):
     return w
 
 
+def resample_taps(src_rate, dst_rate):
+    """src/audio.rs:113-140: the polyphase Kaiser-windowed sinc filter of resample(): (up, down, half, table) with
+    table fp32 [up, 2*half + 1]; entry [p][j] = tap((j - half) - p/up), evaluated in f64 in the reference's order
+    (cutoff * sinc * I0(beta * sqrt(1 - r^2)) / I0(beta), beta 8.6, I0 by its 49-term series) and rounded to fp32.
+    The reference builds this table when up <= 4096 and evaluates the same tap() per sample otherwise (same
+    values)."""
+    g = math.gcd(src_rate, dst_rate)
+    up, down = dst_rate // g, src_rate // g
+    cutoff = min(up / down, 1.0) * 0.97
+    half = int(math.ceil(32.0 / cutoff))
+
+    def i0(x):
+        s = t = 1.0
+        for k in range(1, 50):
+            y = x / (2.0 * k)
+            t *= y * y
+            s += t
+        return s
+
+    beta = 8.6
+    i0b = i0(beta)
+    taps = 2 * half + 1
+
+    def tap(t):
+        r = t / half
+        if abs(r) >= 1.0:
+            return 0.0
+        sinc = 1.0 if t == 0.0 else math.sin(math.pi * t * cutoff) / (math.pi * t * cutoff)
+        return cutoff * sinc * i0(beta * math.sqrt(1.0 - r * r)) / i0b
+
+    table = np.empty((up, taps), np.float32)
+    for ph in range(up):
+        frac = ph / up
+        for j in range(taps):
+            table[ph, j] = np.float32(tap(float(j - half) - frac))
+    return up, down, half, table
+
+
+def resample(x, src_rate, dst_rate=16000):
+    """src/audio.rs:108-148: output n reads input position n * down / up (phase (n * down) % up); the sum runs over
+    the 2*half + 1 taps in order, skipping inputs outside the clip, as fp32 products added to an fp32 accumulator
+    (no fused multiply-add, as the reference's Rust compiles it)."""
+    x = np.asarray(x, np.float32)
+    if src_rate == dst_rate or x.shape[0] == 0:
+        return x.copy()
+    up, down, half, table = resample_taps(src_rate, dst_rate)
+    n_out = x.shape[0] * up // down
+    pos = np.arange(n_out, dtype=np.int64) * down
+    base, ph = pos // up, pos % up
+    acc = np.zeros(n_out, np.float32)
+    for j in range(2 * half + 1):
+        idx = base - half + j
+        ok = (idx >= 0) & (idx < x.shape[0])
+        prod = (table[ph[ok], j] * x[idx[ok]]).astype(np.float32)
+        acc[ok] = (acc[ok] + prod).astype(np.float32)
+    return acc
+
+
 def log_mel(samples):
     """src/audio.rs:238-299: pre-emphasis 0.97, centred 512-point frames (hop 160, 400-sample periodic-free Hann
     window centred in the frame), power spectrum, Slaney mel, ln(x + 2^-24), per-channel normalisation over the

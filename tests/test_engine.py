@@ -186,3 +186,26 @@ def test_audio_pcm_equals_mel(amodel):
     a = amodel.encode_pcm(waves).cpu().numpy()
     b = amodel.encode([O.log_mel(w) for w in waves]).cpu().numpy()
     assert np.sqrt(((a - b) ** 2).mean() / (b ** 2).mean()) <= 1e-3
+
+
+@pytest.mark.parametrize("rate,seconds", [(8000, 1.3), (22050, 2.0), (44100, 1.7), (48000, 3.1), (11025, 0.9),
+                                          (16000, 0.5)])
+def test_resample_vs_oracle(gpu_lib, rate, seconds):
+    """d1_resample (the WAV front end's conversion to 16 kHz, src/audio.rs:108-148) bit for bit against the oracle's
+    restatement: the same fp32 filter table and the same fp32 accumulation order."""
+    rng = np.random.default_rng(rate)
+    x = (rng.standard_normal(int(rate * seconds)) * 0.1).astype(np.float32)
+    want = O.resample(x, rate, 16000)
+    n_out = gpu_lib.d1_resample_len(len(x), rate, 16000)
+    assert n_out == len(want)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.full((n_out,), float("nan"), device="cuda")
+    assert gpu_lib.d1_resample(C.c_void_p(xd.data_ptr()), len(x), rate, 16000, C.c_void_p(y.data_ptr()),
+                               C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    assert np.array_equal(y.cpu().numpy(), want)
+
+
+def test_resample_rejects_bad_rates(gpu_lib):
+    assert gpu_lib.d1_resample_len(100, 0, 16000) == -1
+    assert gpu_lib.d1_resample(None, 100, 44100, 0, None, None) == -1
+    assert gpu_lib.d1_resample_len(0, 44100, 16000) == 0
