@@ -254,14 +254,14 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // (it must cover every tile) and the runners pass one item per 256-row block. A unit is two 128-row query tiles
 // that share each K/V tile, one per softmax warpgroup.
 //
-// The MMA issuer runs the score tiles three steps ahead of the softmax: each warpgroup has three S buffers in TMEM,
-// so S(j+3) is issued as soon as P(j) is written and the softmax has two tiles of work while it is computed. P never
-// leaves TMEM: the softmax writes P(j) as fp16 pairs over the first 32 columns of S(j)'s buffer, and P(j).V_j reads
-// its A operand from there (tcgen05.mma with A in tensor memory). The tensor core runs one thread's MMAs in issue
-// order, so S(j+3), issued after P(j).V_j into the same buffer, overwrites P(j) only after that MMA has read it, and
-// the softmax's wait for S(j) also covers P(j-3).V_{j-3}. The issuer serves each warpgroup as soon as its P is
-// written, so the two drift apart instead of running in lockstep. Every handoff has its own barrier per buffer.
-// TMEM (512 columns): S/P[w][b] at 256w + 64b (b < 3), O[w] at 256w + 192.
+// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM, so
+// S(j+2) is issued as soon as P(j) is written. P never leaves TMEM: the softmax writes P(j) as fp16 pairs over the
+// first 32 columns of S(j)'s buffer, and P(j).V_j reads its A operand from there (tcgen05.mma with A in tensor
+// memory). The tensor core runs one thread's MMAs in issue order, so S(j+2), issued after P(j).V_j into the same
+// buffer, overwrites P(j) only after that MMA has read it, and the softmax's wait for S(j) also covers
+// P(j-2).V_{j-2}. The issuer serves each warpgroup as soon as its P is written, so the two drift apart instead of
+// running in lockstep. Every handoff has its own barrier per buffer.
+// TMEM (512 columns): S/P[w][b] at 256w + 64b, O[w] at 256w + 64 T_SBUF.
 // Warps:
 //   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
 //        reads its S row (one TMEM round trip), takes the row max in the exp2 domain (3-input max), writes
@@ -276,8 +276,9 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 //        current unit's math.
 //   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64, both operands in
 //        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=64, A in TMEM).
-// (Tried: a share of the exponentials by a cubic on the FMA pipe. Slower at every share, 152 -> 178 us at 4 x 2048
-// from none to half: the softmax is bound by instruction issue and waits, not by the SFU.)
+// The softmax is bound by instruction issue and its waits, not by the SFU: it scales scores and sums P two at a time
+// with the packed fp32 instructions (fma / add .f32x2). (Tried and slower: a share of the exponentials by a cubic
+// on the FMA pipe, 152 -> 178 us at 4 x 2048 from none to half of them; S three tiles ahead, 152 -> 163 us.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
@@ -286,7 +287,7 @@ constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
 constexpr int T_O_BYTES = TQ * 128;       // one warpgroup's O staging tile
 constexpr uint32_t T_TMEM_COLS = 512;
-constexpr int T_SBUF = 3;                 // S/P buffers per warpgroup (S runs T_SBUF tiles ahead)
+constexpr int T_SBUF = 2;                 // S/P buffers per warpgroup (S runs T_SBUF tiles ahead)
 constexpr uint32_t T_WG_COLS = 256;       // TMEM columns per warpgroup: T_SBUF S/P buffers, then O
 constexpr float kLazyRescale = 8.f;
 enum : int {
@@ -357,6 +358,26 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Two fp32 lanes in one 64-bit register for the packed sm_100 instructions: d = a * b + c and d = a + b, per lane.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
 // max(a, b, c) in one instruction (sm_100).
@@ -680,21 +701,24 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         tmem_st8(tO + q * 8, o);
                     }
                 }
-                float rs8[8];
+                // x = s * scale - m two scores at a time; P = 2^x; the row sum in four packed pairs of partial sums
+                const uint64_t sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(-m_use, -m_use);
+                uint64_t rs2[4];
 #pragma unroll
-                for (int e = 0; e < 8; e++) rs8[e] = 0.f;
+                for (int e = 0; e < 4; e++) rs2[e] = f2_pack(0.f, 0.f);
                 uint32_t pr[TKV / 2];
 #pragma unroll
-                for (int ch = 0; ch < TKV / 8; ch++) {
-                    float p[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        p[e] = ex2(fmaf(__uint_as_float(sr[ch * 8 + e]), a.scale_log2, -m_use));
-                        rs8[e] += p[e];
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; e++) pr[ch * 4 + e] = pack_h2(p[2 * e], p[2 * e + 1]);
+                for (int i = 0; i < TKV / 2; i++) {
+                    float x0, x1;
+                    f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2),
+                              x0, x1);
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    rs2[i & 3] = f2_add(rs2[i & 3], f2_pack(p0, p1));
+                    pr[i] = pack_h2(p0, p1);
                 }
+                float rs8[8];
+#pragma unroll
+                for (int e = 0; e < 4; e++) f2_unpack(rs2[e], rs8[2 * e], rs8[2 * e + 1]);
                 // P(j) over the first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
                 tmem_st32(tS, pr);
                 tc_wait_st();

@@ -209,3 +209,40 @@ def test_resample_rejects_bad_rates(gpu_lib):
     assert gpu_lib.d1_resample_len(100, 0, 16000) == -1
     assert gpu_lib.d1_resample(None, 100, 44100, 0, None, None) == -1
     assert gpu_lib.d1_resample_len(0, 44100, 16000) == 0
+
+
+def test_audio_pcm_rates_equals_resampled(amodel):
+    """Clips at 44.1, 22.05 and 8 kHz through d1h_audio_encode_pcm_rates (resampled on the device) equal the same
+    clips resampled by the oracle and encoded as 16 kHz waveforms: the resampler is bit-exact, so the features and
+    the encoder's outputs are the same computation."""
+    rng = np.random.default_rng(47)
+    rates = [44100, 22050, 8000, 16000]
+    waves = [(rng.standard_normal(int(r * s)) * 0.1).astype(np.float32) for r, s in zip(rates, (2.3, 1.1, 4.0, 0.7))]
+    got = amodel.encode_pcm(waves, rates=rates).cpu().numpy()
+    want = amodel.encode_pcm([O.resample(w, r) for w, r in zip(waves, rates)]).cpu().numpy()
+    assert got.shape == want.shape
+    assert np.sqrt(((got - want) ** 2).mean() / (want ** 2).mean()) <= 1e-6
+
+
+def test_engine_resampled_audio_vs_oracle(tmodel, amodel, tw, aw):
+    """A request whose waveform is at 44.1 kHz: the engine resamples it on the device, computes the log-mel
+    features, encodes it and runs the prefix; against the oracle chain resample -> log_mel -> audio_encode ->
+    launch_prefix -> launch_text."""
+    from fast_d1_omni_b200.engine import Engine, prefix_len
+    rng = np.random.default_rng(48)
+    wave = (rng.standard_normal(int(44100 * 1.6)) * np.float32(0.1)).astype(np.float32)
+    req = dict(text_requests(49, 1, lo=30, hi=150)[0], media={"kind": "audio", "pcm": wave, "rate": 44100})
+    eng = Engine(tmodel, None, amodel, max_batch_tokens=8192)
+    try:
+        (logits, err), = eng.run([req])
+        st = eng.stats()
+    finally:
+        eng.close()
+    assert err == ""
+    mel, valid = O.log_mel(O.resample(wave, 44100))
+    emb = O.audio_encode(aw, mel, valid, "f32")
+    assert st["media_tokens"] == emb.shape[0] == prefix_len(req)
+    cache = O.launch_prefix(tw, [emb], "f32")[0]
+    rows = [dict(r, prefix=cache) for r in req["rows"]]
+    ref = O.launch_text(tw, rows, "f32")
+    assert_bar(ref, logits, [len(r["markers"]) for r in req["rows"]])
