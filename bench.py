@@ -679,7 +679,10 @@ def run_mixed(args, rank, world, local, dev):
     tokens = (s1["tokens"] - s0["tokens"]) + (s1["media_tokens"] - s0["media_tokens"])
     assert tokens == passes * sum(request_tokens(r) for r in mine) and all(e == "" for _, e in res)
     t = torch.tensor([dev_s, wall, float(tokens), float(len(mine) * passes)], dtype=torch.float64, device=dev)
+    per_rank = [t.clone()]
     if world > 1:
+        per_rank = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(per_rank, t)
         mx = t[:2].clone()
         sm = t[2:].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -700,6 +703,8 @@ def run_mixed(args, rank, world, local, dev):
                 "requests": int(nreq), "requests_per_s": nreq / dev_max,
                 "e2e": {"value": tok_all / wall_max, "unit": "tokens/s", "note": "wall clock, host request buffers"},
                 "engine": {k: s1[k] - s0[k] for k in s1}, "gpu_launches_text_runner": text.launches - l0,
+                "per_rank": [{"rank": i, "device_s": round(float(r[0]), 4), "wall_s": round(float(r[1]), 4),
+                              "tokens": int(r[2]), "requests": int(r[3])} for i, r in enumerate(per_rank)],
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     eng.close()

@@ -213,15 +213,16 @@ def test_resample_rejects_bad_rates(gpu_lib):
 
 def test_audio_pcm_rates_equals_resampled(amodel):
     """Clips at 44.1, 22.05 and 8 kHz through d1h_audio_encode_pcm_rates (resampled on the device) equal the same
-    clips resampled by the oracle and encoded as 16 kHz waveforms: the resampler is bit-exact, so the features and
-    the encoder's outputs are the same computation."""
+    clips resampled by the oracle and encoded as 16 kHz waveforms. The resampler is bit-exact, so the features are
+    the same; the encoder's split-K GEMMs sum partial tiles in arrival order, so two calls agree to the run-to-run
+    bound of test_audio_pcm_equals_mel (relative RMS 1e-3), not bit for bit."""
     rng = np.random.default_rng(47)
     rates = [44100, 22050, 8000, 16000]
     waves = [(rng.standard_normal(int(r * s)) * 0.1).astype(np.float32) for r, s in zip(rates, (2.3, 1.1, 4.0, 0.7))]
     got = amodel.encode_pcm(waves, rates=rates).cpu().numpy()
     want = amodel.encode_pcm([O.resample(w, r) for w, r in zip(waves, rates)]).cpu().numpy()
     assert got.shape == want.shape
-    assert np.sqrt(((got - want) ** 2).mean() / (want ** 2).mean()) <= 1e-6
+    assert np.sqrt(((got - want) ** 2).mean() / (want ** 2).mean()) <= 1e-3
 
 
 def test_engine_resampled_audio_vs_oracle(tmodel, amodel, tw, aw):
