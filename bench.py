@@ -638,7 +638,17 @@ def run_mixed(args, rank, world, local, dev):
     from fast_d1_omni_b200.model import AudioModel, TextModel, VisionModel
     from fast_d1_omni_b200.weights import audio_weights, mixed_requests, text_weights, vision_weights
     text = TextModel(text_weights(0), device=local, cap_tokens=TOKENS)
-    n_tuned = text.tune(TOKENS)
+    # GEMM plans: loaded from --plans when a previous run of this build saved them there, else tuned (and saved)
+    n_tuned = 0
+    if args.plans and Path(args.plans).exists():
+        try:
+            n_tuned = text.load_plans(args.plans)
+        except RuntimeError:
+            n_tuned = 0
+    if n_tuned == 0:
+        n_tuned = text.tune(TOKENS)
+        if args.plans and rank == 0:
+            text.save_plans(args.plans)
     vision = VisionModel(vision_weights(3), device=local, max_patches=16384)
     audio = AudioModel(audio_weights(4), device=local, max_rows=1536)
     eng = Engine(text, vision, audio, max_batch_tokens=TOKENS)
@@ -771,6 +781,8 @@ def main():
     ap.add_argument("--attn-config2", action="store_true",
                     help="BASELINE config 2: attention at 2048/8192/16384 packed tokens, this library and the reference")
     ap.add_argument("--ref-engine-child", type=int, default=-1, metavar="EFFORT", help=argparse.SUPPRESS)
+    ap.add_argument("--plans", default="", metavar="PATH",
+                    help="--workload mixed: GEMM plan file to load (or to write after tuning when it is missing)")
     ap.add_argument("--sustained-steps", type=int, default=SUSTAINED_STEPS,
                     help="steps of the second (>= 2 s) timed region; 0 skips it")
     args = ap.parse_args()
