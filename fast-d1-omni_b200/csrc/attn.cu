@@ -261,9 +261,7 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // buffer, overwrites P(j) only after that MMA has read it, and the softmax's wait for S(j) also covers
 // P(j-2).V_{j-2}. The issuer serves each warpgroup as soon as its P is written, so the two drift apart instead of
 // running in lockstep. Every handoff has its own barrier per buffer.
-// The row sums of P come from the tensor core too: one more MMA per tile (N = 16) multiplies P by a constant tile
-// whose first column is ones, accumulating sum_j P into TMEM beside O; it is rescaled with O and read once per unit.
-// TMEM (512 columns): S/P[w][b] at 256w + 64b, O[w] at 256w + 64 T_SBUF, the row sums L[w] at 64 columns after O.
+// TMEM (512 columns): S/P[w][b] at 256w + 64b, O[w] at 256w + 64 T_SBUF.
 // Warps:
 //   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
 //        reads its S row (one TMEM round trip), takes the row max in the exp2 domain (3-input max), writes
@@ -278,9 +276,10 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 //        current unit's math.
 //   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64, both operands in
 //        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=64, A in TMEM).
-// The softmax is bound by instruction issue and its waits, not by the SFU: it scales scores two at a time with the
-// packed fp32 fma.f32x2 and leaves the row sums to the tensor core. (Tried and slower: a share of the exponentials by a cubic
-// on the FMA pipe, 152 -> 178 us at 4 x 2048 from none to half of them; S three tiles ahead, 152 -> 163 us.)
+// The softmax is bound by instruction issue and its waits, not by the SFU: it scales scores and sums P two at a time
+// with the packed fp32 instructions (fma / add .f32x2). (Tried and slower: a share of the exponentials by a cubic
+// on the FMA pipe, 152 -> 178 us at 4 x 2048 from none to half of them; S three tiles ahead, 152 -> 163 us; the row
+// sums by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
@@ -288,7 +287,6 @@ constexpr int T_QSLOTS = 2, T_KVSTAGES = 8;
 constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
 constexpr int T_O_BYTES = TQ * 128;       // one warpgroup's O staging tile
-constexpr int T_ONES_BYTES = 16 * 128;    // B operand of the row-sum MMA: 16 rows (N) x 64 keys, row 0 ones
 constexpr uint32_t T_TMEM_COLS = 512;
 constexpr int T_SBUF = 2;                 // S/P buffers per warpgroup (S runs T_SBUF tiles ahead)
 constexpr uint32_t T_WG_COLS = 256;       // TMEM columns per warpgroup: T_SBUF S/P buffers, then O
@@ -307,11 +305,9 @@ enum : int {
     B_OREAD = B_OSTAGED + 2,           // [w]: its previous bulk store has read the staging buffer
     T_NBARS = B_OREAD + 2
 };
-constexpr int T_SMEM =
-    T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_O_BYTES + T_ONES_BYTES + T_NBARS * 8 + 16;
+constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_O_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
-static_assert(T_SBUF * TKV + 64 + 16 <= (int)T_WG_COLS && 2 * T_WG_COLS <= T_TMEM_COLS,
-              "TMEM of the tcgen05 attention");
+static_assert(T_SBUF * TKV + 64 <= (int)T_WG_COLS && 2 * T_WG_COLS <= T_TMEM_COLS, "TMEM of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
 __device__ int g_fa_err = 0;
@@ -365,7 +361,7 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// Two fp32 lanes in one 64-bit register for the packed sm_100 instruction d = a * b + c, per lane.
+// Two fp32 lanes in one 64-bit register for the packed sm_100 instructions: d = a * b + c and d = a + b, per lane.
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
     uint64_t r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -377,6 +373,11 @@ __device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
     uint64_t d;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
 
@@ -430,13 +431,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     const FaTcArgs a) {
     constexpr uint32_t IDESC_S = idesc_f16_f32(TQ, TKV);
     constexpr uint32_t IDESC_O = idesc_f16_f32(TQ, 64) | (1u << 16);  // B (= V) MN-major
-    constexpr uint32_t IDESC_L = idesc_f16_f32(TQ, 16);                // B = the ones tile, K-major
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sQ = smem_raw;                                    // slot q: Q0 at q * 2 * T_QT_BYTES, Q1 after it
     uint8_t* sKV = sQ + T_QSLOTS * 2 * T_QT_BYTES;             // stage s: K at s * 2 * T_KV_BYTES, V after it
     uint8_t* sO = sKV + T_KVSTAGES * 2 * T_KV_BYTES;           // O staging of warpgroup w at w * T_O_BYTES
-    uint8_t* sOnes = sO + 2 * T_O_BYTES;                       // the row-sum MMA's B operand
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + T_ONES_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * T_O_BYTES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + T_NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     auto bar = [&](int i) { return smem_u32(bars + i); };
@@ -481,12 +480,6 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         tmem_alloc(smem_u32(tmem_slot), T_TMEM_COLS);
         tmem_relinquish();
     }
-    // the ones tile: N row 0 = 64 fp16 ones (any 128-byte swizzle of one row of equal values is the same bytes),
-    // rows 1-15 zero; written by the generic proxy, read by the tensor core (async proxy)
-    for (int i = threadIdx.x; i < T_ONES_BYTES / 16; i += blockDim.x)
-        reinterpret_cast<uint4*>(sOnes)[i] = i < 8 ? make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u)
-                                                   : make_uint4(0u, 0u, 0u, 0u);
-    fence_async_smem_cta();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -621,13 +614,9 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         if (!ok) break;
                         tc_fence_after();
 #pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const uint32_t pa = tmem + w * T_WG_COLS + b * TKV + k * 8;
-                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_SBUF * TKV, pa, smem_desc_k128(v_addr + k * 2048),
-                                          IDESC_O, (j | k) != 0);
-                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_SBUF * TKV + 64, pa,
-                                          smem_desc_k128(smem_u32(sOnes) + k * 32), IDESC_L, (j | k) != 0);
-                        }
+                        for (int k = 0; k < 4; k++)
+                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_SBUF * TKV, tmem + w * T_WG_COLS + b * TKV + k * 8,
+                                          smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
                         tc_commit(bar(B_ODONE + T_SBUF * w + b));
                         if (ahead) issue_s(w, j + T_SBUF);
                     }
@@ -661,7 +650,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
             if (w == 1 && !un.two) continue;
             const int total = un.s.ext_len + un.s.kv_len;
-            float m = -INFINITY;
+            float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
                 const int c = cnt + j, b = c % T_SBUF;
                 if (!(ok = __all_sync(D1_FULL_MASK,
@@ -704,7 +693,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         break;
                     tc_fence_after();
 #pragma unroll 1
-                    for (int q = 0; q < 9; q++) {  // O's 64 columns and the row-sum block after them
+                    for (int q = 0; q < 8; q++) {
                         uint32_t o[8];
                         tmem_ld8(tO + q * 8, o);
                         tc_wait_ld();
@@ -713,22 +702,32 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                         tmem_st8(tO + q * 8, o);
                     }
                 }
-                // x = s * scale - m two scores at a time (packed f32x2); P = 2^x (the tensor core sums P)
+                // x = s * scale - m two scores at a time; P = 2^x; the row sum in four packed pairs of partial sums
                 const uint64_t sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(-m_use, -m_use);
+                uint64_t rs2[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) rs2[e] = f2_pack(0.f, 0.f);
                 uint32_t pr[TKV / 2];
 #pragma unroll
                 for (int i = 0; i < TKV / 2; i++) {
                     float x0, x1;
                     f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2),
                               x0, x1);
-                    pr[i] = pack_h2(ex2(x0), ex2(x1));
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    rs2[i & 3] = f2_add(rs2[i & 3], f2_pack(p0, p1));
+                    pr[i] = pack_h2(p0, p1);
                 }
+                float rs8[8];
+#pragma unroll
+                for (int e = 0; e < 4; e++) f2_unpack(rs2[e], rs8[2 * e], rs8[2 * e + 1]);
                 // P(j) over the first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
                 tmem_st32(tS, pr);
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(B_PFULL + T_SBUF * w + b));
+                const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+                l = l * alpha + rs;
                 m = m_use;
             }
             if (!ok) break;
@@ -739,13 +738,11 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                                   mbar_wait(bar(B_ODONE + T_SBUF * w + cl % T_SBUF), (cl / T_SBUF) & 1, abort_flag))))
                 break;
             tc_fence_after();
-            uint32_t o[64], lsum[8];
+            const float il = l > 0.f ? 1.f / l : 0.f;
+            uint32_t o[64];
             tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
             tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
-            tmem_ld8(tO + 64, lsum);  // column 0 of the row-sum block: sum_j P (fp16 P, as P.V used it)
             tc_wait_ld();
-            const float l = __uint_as_float(lsum[0]);
-            const float il = l > 0.f ? 1.f / l : 0.f;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_OFREE + w));  // O is read: the next unit's first P.V may overwrite it
