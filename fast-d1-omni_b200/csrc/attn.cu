@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // The softmax is bound by instruction issue and its waits, not by the SFU: it scales scores and sums P two at a time
 // with the packed fp32 instructions (fma / add .f32x2). (Tried and slower: a share of the exponentials by a cubic
 // on the FMA pipe, 152 -> 178 us at 4 x 2048 from none to half of them; S three tiles ahead, 152 -> 163 us; the row
-// sums by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us.)
+// sums by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us; the next
+// tile's S loaded from TMEM while the current P is stored, 146 -> 148 us with 154 registers instead of 128.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 64;                   // keys per K/V tile
@@ -651,22 +652,17 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             if (w == 1 && !un.two) continue;
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
-            // S(c) of the unit's first tile; every later tile's S is loaded while the previous P is stored
-            uint32_t sr[TKV];
-            auto load_s = [&](int cc) {
-                const uint32_t tSc = tmem + w * T_WG_COLS + (cc % T_SBUF) * TKV + lane_off;
-                tmem_ld32(tSc, *reinterpret_cast<uint32_t(*)[32]>(sr));
-                tmem_ld32(tSc + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-            };
-            if (!(ok = __all_sync(D1_FULL_MASK,
-                                  mbar_wait(bar(B_SFULL + T_SBUF * w + cnt % T_SBUF), (cnt / T_SBUF) & 1, abort_flag))))
-                break;
-            tc_fence_after();
-            load_s(cnt);
-            tc_wait_ld();
             for (int j = 0; j < un.nt; j++) {
                 const int c = cnt + j, b = c % T_SBUF;
+                if (!(ok = __all_sync(D1_FULL_MASK,
+                                      mbar_wait(bar(B_SFULL + T_SBUF * w + b), (c / T_SBUF) & 1, abort_flag))))
+                    break;
+                tc_fence_after();
+                uint32_t sr[TKV];
                 const uint32_t tS = tmem + w * T_WG_COLS + b * TKV + lane_off;
+                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
+                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                tc_wait_ld();
                 const int kbase = j * TKV;
                 if (kbase + TKV > total) {  // keys past the sequence: only in its last tile
 #pragma unroll
@@ -725,16 +721,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 float rs8[8];
 #pragma unroll
                 for (int e = 0; e < 4; e++) f2_unpack(rs2[e], rs8[2 * e], rs8[2 * e + 1]);
-                // S(j+1) (issued two steps ahead, so normally complete) comes in while P(j) goes out: P(j) over the
-                // first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
-                const bool more = j + 1 < un.nt;
-                if (more) {
-                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + T_SBUF * w + (c + 1) % T_SBUF),
-                                                                  ((c + 1) / T_SBUF) & 1, abort_flag))))
-                        break;
-                    tc_fence_after();
-                    load_s(c + 1);
-                }
+                // P(j) over the first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
                 tmem_st32(tS, pr);
                 tc_wait_st();
                 tc_fence_before();
@@ -743,7 +730,6 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
                 l = l * alpha + rs;
                 m = m_use;
-                if (more) tc_wait_ld();
             }
             if (!ok) break;
             cnt += un.nt;
