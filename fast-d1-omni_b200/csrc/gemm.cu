@@ -574,6 +574,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     constexpr int SUBTILES = OUT32 ? 1 : 2;  // 32x32 output blocks per 4 KB staging buffer
     constexpr int SUB_BYTES = EPI_BUF / SUBTILES;
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "pair MMA: M=256 needs N % 16 == 0, 16..256");
+    static_assert(S::BYTES <= 232448, "shared memory of the pair GEMM");
     static_assert(EPI != EPI_DIRECT && EPI != EPI_QKROPE, "the pair kernel takes the TMA epilogues but QK-rope");
 
     extern __shared__ uint8_t smem_raw[];
@@ -1030,13 +1031,21 @@ double wave_eff(long tiles, int sms) {
 
 // Kernel configurations a plan can name: the single-SM kernel with 128- or 256-column tiles, or the CTA-pair
 // kernel with 256 x 256 or 256 x 128 tiles.
-enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3, CFG_1SM_64 = 4 };
+// The pair's 256 x 192 tile is for N where 256-column tiles leave much of the last wave idle (N = 3072: 384 tiles
+// on 74 pairs = 5.19 waves, against 512 tiles = 6.92 waves).
+enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3, CFG_1SM_64 = 4, CFG_PAIR_192 = 5 };
+constexpr int CFG_LAST = CFG_PAIR_192;
+
+inline bool cfg_pair(int cfg) { return cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128 || cfg == CFG_PAIR_192; }
+inline int cfg_bn(int cfg) {
+    return cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : cfg == CFG_PAIR_192 ? 192 : 256;
+}
 
 // Fraction of the SM-time the tiles keep busy (wave quantisation x column padding), per configuration.
 double cfg_eff(Ctx* c, int cfg, int M, int N) {
-    const bool pair = cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128;
+    const bool pair = cfg_pair(cfg);
     const int bm = pair ? 2 * BM : BM;
-    const int bn = cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
+    const int bn = cfg_bn(cfg);
     const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const int slots = pair ? c->pair_slots : c->num_sms;
     const double pad = (double)M * N / ((double)((M + bm - 1) / bm) * bm * ((N + bn - 1) / bn) * bn);
@@ -1062,9 +1071,9 @@ int default_cfg(Ctx* c, int M, int N) {
 // Split-K for the reduce-add epilogue (partial sums land in Y through TMA reduce-add): enough work units to
 // cover the SMs when the tiles alone leave most of them idle, keeping >= 4 K blocks per unit.
 int default_split(Ctx* c, int cfg, int M, int N, int K) {
-    const bool pair = cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128;
+    const bool pair = cfg_pair(cfg);
     const int bm = pair ? 2 * BM : BM;
-    const int bn = cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256;
+    const int bn = cfg_bn(cfg);
     const long tiles = (long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const int slots = pair ? c->pair_slots : c->num_sms;
     const int kb = (K + BK - 1) / BK;
@@ -1102,6 +1111,11 @@ int run_store(Ctx* c, int cfg, int split, int M, int N, int K, const void* X, in
         if (add) return launch_tc2<128, 8, EPI_ADD, true>(c, 14, X, ldx, W, ldw, N, a, st);
         if (y_f32) return launch_tc2<128, 8, EPI_STORE, true>(c, 15, X, ldx, W, ldw, N, a, st);
         return launch_tc2<128, 8, EPI_STORE, false>(c, 16, X, ldx, W, ldw, N, a, st);
+    }
+    if (cfg == CFG_PAIR_192 && (store || add)) {
+        if (add) return launch_tc2<192, 6, EPI_ADD, true>(c, 27, X, ldx, W, ldw, N, a, st);
+        if (y_f32) return launch_tc2<192, 6, EPI_STORE, true>(c, 28, X, ldx, W, ldw, N, a, st);
+        return launch_tc2<192, 6, EPI_STORE, false>(c, 29, X, ldx, W, ldw, N, a, st);
     }
     const bool b128 = cfg == CFG_1SM_128 || cfg == CFG_1SM_64;
     if (store) {
@@ -1313,7 +1327,7 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
     float best = 1e30f;
     int best_cfg = CFG_1SM_256, best_split = 1;
     const bool tc = tc_ok(c->sx, ldx, c->sw, ldw, w_kn, K);
-    for (int cfg : {CFG_1SM_64, CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128}) {
+    for (int cfg : {CFG_1SM_64, CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128, CFG_PAIR_192}) {
         for (int split : {1, 2, 4}) {
             if (split > 1 && !y_f32) break;  // split-K only through the reduce-add epilogue
             if ((K + BK - 1) / BK < 4 * split) break;
@@ -1381,7 +1395,7 @@ int d1_lt_load(void* ctx, const char* path) {
         if (fscanf(f, "%d %d %d %d %d %d %d %d %d %d %d %f", &N, &K, &ldx, &ldw, &ldy, &w_kn, &y_f32, &epi, &b, &cfg,
                    &split, &us) != 12)
             break;
-        if (cfg < CFG_1SM_128 || cfg > CFG_1SM_64 || split < 1 || split > 64) continue;
+        if (cfg < CFG_1SM_128 || cfg > CFG_LAST || split < 1 || split > 64) continue;
         c->plans[PlanKey(N, K, ldx, ldw, ldy, w_kn, y_f32, epi, b)] = Plan{cfg, split, us};
         n++;
     }

@@ -17,16 +17,32 @@ def _free_port():
 
 def test_assign_is_balanced_and_whole():
     load_package()
-    from fast_d1_omni_b200.engine import assign, request_tokens
+    from fast_d1_omni_b200.engine import assign, request_cost, request_tokens
     from fast_d1_omni_b200.weights import mixed_requests
     reqs = mixed_requests(4, 40)
     for world in (1, 2, 3, 8):
         a = assign(reqs, world)
         assert len(a) == len(reqs) and set(a) <= set(range(world))
         assert a == assign(reqs, world)  # every rank computes the same split
-        loads = [sum(request_tokens(r) for r, d in zip(reqs, a) if d == i) for i in range(world)]
-        biggest = max(request_tokens(r) for r in reqs)
+        loads = [sum(request_cost(r) for r, d in zip(reqs, a) if d == i) for i in range(world)]
+        biggest = max(request_cost(r) for r in reqs)
         assert max(loads) - min(loads) <= biggest  # greedy least-loaded: within one request of balance
+
+
+def test_request_cost_weights_media():
+    """Media requests cost their encoder work on top of their trunk positions; text requests cost their tokens."""
+    load_package()
+    from fast_d1_omni_b200.engine import FRAME_COST, PATCH_COST, request_cost, request_tokens
+    from fast_d1_omni_b200.weights import mixed_requests
+    for r in mixed_requests(4, 40):
+        m = r["media"]
+        extra = request_cost(r) - request_tokens(r)
+        if m is None:
+            assert extra == 0
+        elif m["kind"] == "images":
+            assert np.isclose(extra, PATCH_COST * sum(ph * pw for ph, pw, _ in m["crops"]))
+        else:
+            assert np.isclose(extra, FRAME_COST * (max(min(len(m["pcm"]), 480000), 8000) // 160))
 
 
 def _fake_result(req):
