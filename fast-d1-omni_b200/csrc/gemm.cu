@@ -1031,15 +1031,14 @@ double wave_eff(long tiles, int sms) {
 
 // Kernel configurations a plan can name: the single-SM kernel with 128- or 256-column tiles, or the CTA-pair
 // kernel with 256 x 256 or 256 x 128 tiles.
-// The pair's 256 x 192 tile is for N where 256-column tiles leave much of the last wave idle (N = 3072: 384 tiles
-// on 74 pairs = 5.19 waves, against 512 tiles = 6.92 waves).
-enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3, CFG_1SM_64 = 4, CFG_PAIR_192 = 5 };
-constexpr int CFG_LAST = CFG_PAIR_192;
+// (A 256 x 192 pair tile, which would cut the idle part of the last wave for N = 3072 from 5.19 to 6.92 waves, was
+// slower than 256 x 256 on every trunk shape at M = 8192: in_proj 44.3 against 40.9 us, QKV 32.0 against 28.3 us.
+// Narrower tiles cost more per FLOP here, so the last wave is not what limits these GEMMs.)
+enum Cfg : int { CFG_1SM_128 = 0, CFG_1SM_256 = 1, CFG_PAIR_256 = 2, CFG_PAIR_128 = 3, CFG_1SM_64 = 4 };
+constexpr int CFG_LAST = CFG_1SM_64;
 
-inline bool cfg_pair(int cfg) { return cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128 || cfg == CFG_PAIR_192; }
-inline int cfg_bn(int cfg) {
-    return cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : cfg == CFG_PAIR_192 ? 192 : 256;
-}
+inline bool cfg_pair(int cfg) { return cfg == CFG_PAIR_256 || cfg == CFG_PAIR_128; }
+inline int cfg_bn(int cfg) { return cfg == CFG_1SM_64 ? 64 : (cfg == CFG_1SM_128 || cfg == CFG_PAIR_128) ? 128 : 256; }
 
 // Fraction of the SM-time the tiles keep busy (wave quantisation x column padding), per configuration.
 double cfg_eff(Ctx* c, int cfg, int M, int N) {
@@ -1111,11 +1110,6 @@ int run_store(Ctx* c, int cfg, int split, int M, int N, int K, const void* X, in
         if (add) return launch_tc2<128, 8, EPI_ADD, true>(c, 14, X, ldx, W, ldw, N, a, st);
         if (y_f32) return launch_tc2<128, 8, EPI_STORE, true>(c, 15, X, ldx, W, ldw, N, a, st);
         return launch_tc2<128, 8, EPI_STORE, false>(c, 16, X, ldx, W, ldw, N, a, st);
-    }
-    if (cfg == CFG_PAIR_192 && (store || add)) {
-        if (add) return launch_tc2<192, 6, EPI_ADD, true>(c, 27, X, ldx, W, ldw, N, a, st);
-        if (y_f32) return launch_tc2<192, 6, EPI_STORE, true>(c, 28, X, ldx, W, ldw, N, a, st);
-        return launch_tc2<192, 6, EPI_STORE, false>(c, 29, X, ldx, W, ldw, N, a, st);
     }
     const bool b128 = cfg == CFG_1SM_128 || cfg == CFG_1SM_64;
     if (store) {
@@ -1327,7 +1321,7 @@ float d1_lt_tune(void* ctx, int M, int N, int K, int ldx, int ldw, int w_kn, int
     float best = 1e30f;
     int best_cfg = CFG_1SM_256, best_split = 1;
     const bool tc = tc_ok(c->sx, ldx, c->sw, ldw, w_kn, K);
-    for (int cfg : {CFG_1SM_64, CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128, CFG_PAIR_192}) {
+    for (int cfg : {CFG_1SM_64, CFG_1SM_128, CFG_1SM_256, CFG_PAIR_256, CFG_PAIR_128}) {
         for (int split : {1, 2, 4}) {
             if (split > 1 && !y_f32) break;  // split-K only through the reduce-add epilogue
             if ((K + BK - 1) / BK < 4 * split) break;
