@@ -14,10 +14,10 @@
 // takes any work list, as the reference's kernel does, and adds biases on load.
 //
 // d1_flash_attn_tc (extension) is the same computation for the bias-free forms on tcgen05 (k_flash_attn_tc below:
-// S and O in TMEM, the score tiles issued two steps ahead of a ping-pong pair of softmax warpgroups, TMA loads and
-// stores). Measured on B200 (CUDA events, 16 heads, GQA 2): 29.5-31 us at 32 x 256 tokens (44 us for the mma.sync
-// kernel) and 165 us at 4 x 2048 tokens (417 TF/s; 263 us). The runners use it whenever the attention has no biases
-// to add on load (their work lists cover every 256-row block).
+// S, P and O in TMEM, 128-key tiles, the next score tile computed while two softmax warpgroups run the exponentials,
+// TMA loads and stores). Measured on B200 (CUDA events, 16 heads, GQA 2): ~24.3 us at 32 x 256 tokens (44 us for the
+// mma.sync kernel) and ~120 us at 4 x 2048 tokens (572 TF/s; 263 us). The runners use it whenever the attention has
+// no biases to add on load (their work lists cover every 256-row block).
 #include "common.cuh"
 #include "warp_mma.cuh"
 
@@ -254,61 +254,64 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // (it must cover every tile) and the runners pass one item per 256-row block. A unit is two 128-row query tiles
 // that share each K/V tile, one per softmax warpgroup.
 //
-// The MMA issuer runs the score tiles two steps ahead of the softmax: each warpgroup has two S buffers in TMEM, so
-// S(j+2) is issued as soon as P(j) is written. P never leaves TMEM: the softmax writes P(j) as fp16 pairs over the
-// first 32 columns of S(j)'s buffer, and P(j).V_j reads its A operand from there (tcgen05.mma with A in tensor
-// memory). The tensor core runs one thread's MMAs in issue order, so S(j+2), issued after P(j).V_j into the same
-// buffer, overwrites P(j) only after that MMA has read it, and the softmax's wait for S(j) also covers
-// P(j-2).V_{j-2}. The issuer serves each warpgroup as soon as its P is written, so the two drift apart instead of
-// running in lockstep. Every handoff has its own barrier per buffer.
-// TMEM (512 columns): S/P[w][b] at 256w + 64b, O[w] at 256w + 64 T_SBUF.
+// Each softmax warpgroup has its own S, P and O columns in TMEM. The softmax copies S(j) into registers and releases
+// it at once (SFREE), so the MMA issuer computes S(j+1) = Q.K_{j+1}^T while the exponentials of tile j run; P(j) goes
+// to the P columns as fp16 pairs once P(j-1).V_{j-1} has read them (ODONE), and P(j).V_j reads its A operand from
+// there (tcgen05.mma with A in tensor memory). The softmax therefore almost never waits for its scores: the
+// critical resource is the SFU (ex2), shared by the two warpgroups.
+// TMEM (512 columns): warpgroup w at 256w: S in 128 columns, P in 64, O in 64.
 // Warps:
-//   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 64-key tile it
+//   0-3, 4-7  softmax warpgroups 0 and 1: thread t owns query row t of its tile (TMEM lane t). Per 128-key tile it
 //        reads its S row (one TMEM round trip), takes the row max in the exp2 domain (3-input max), writes
-//        P = 2^(s - m) as fp16 back to TMEM and accumulates the row sum. O is rescaled in TMEM only when the row
-//        max grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well inside
-//        fp16) and the final O / l is unchanged. At the end of a unit it writes O / l to global memory: a whole
-//        128-row tile through its own shared-memory staging buffer and one bulk tensor store.
-//   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring and K/V tiles of 64 keys ([ext prefix keys |
-//        local keys]) into an 8-stage ring, in the swizzled layouts (V is the MN-major B operand of P.V: same bytes):
-//        Q and whole local K/V tiles by TMA from one thread, prefix and partial tiles by cp.async from all three
-//        warps (each lane's copies complete the slot's barrier when they land); the next unit's loads overlap the
-//        current unit's math.
-//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=64, K=64, both operands in
-//        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=64, A in TMEM).
-// The softmax is bound by instruction issue and its waits, not by the SFU: it scales scores and sums P two at a time
-// with the packed fp32 instructions (fma / add .f32x2). (Tried and slower: a share of the exponentials by a cubic
-// on the FMA pipe, 152 -> 178 us at 4 x 2048 from none to half of them; S three tiles ahead, 152 -> 163 us; the row
-// sums by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us; the next
-// tile's S loaded from TMEM while the current P is stored, 146 -> 148 us with 154 registers instead of 128.)
+//        P = 2^(s - m) as fp16 to TMEM and accumulates the row sum. O is rescaled in TMEM only when the row max
+//        grows by more than 8 (log2 units); otherwise P is taken against the old max (P <= 2^8, well inside fp16)
+//        and the final O / l is unchanged. At the end of a unit it writes O / l to global memory: a whole 128-row
+//        tile through its own shared-memory staging buffer and one bulk tensor store.
+//   8, 10, 11  loaders: the unit's two Q tiles into a 2-slot ring and K/V tiles of 128 keys ([ext prefix keys |
+//        local keys]) into a 4-stage ring, in the swizzled layouts (V is the MN-major B operand of P.V: same
+//        bytes): Q and whole local K/V tiles by TMA from one thread, prefix and partial tiles by cp.async from all
+//        three warps (each lane's copies complete the slot's barrier when they land); the next unit's loads overlap
+//        the current unit's math.
+//   9    TMEM allocation and the MMA issuer (one thread): S_w(j) = Q_w.K_j^T (M=128, N=128, K=64, both operands in
+//        shared memory) and O_w += P_w(j).V_j (M=128, N=64, K=128, A in TMEM).
+// Measured on B200 (per-tile clock64 stamps and a tcgen05 microbenchmark): an exponential phase of 128 keys takes
+// ~1500 clocks for one warp alone and ~2400 when both warpgroups run it at once (the SFU does 16 lanes per clock
+// per SM); loads, max and the P store add ~1100 per tile. One in eight exponential pairs is therefore computed on
+// the FMA pipe (ex2_poly2). The A-in-TMEM P.V runs at ~67 clocks per N=64 instruction (half the dense rate) but
+// overlaps the shared-memory S MMAs. (Tried and slower or equal: 64-key tiles with S two tiles ahead, 145 us at
+// 4 x 2048 against 120; 96-key tiles with two S buffers, 123 us; the two warpgroups taking turns on the
+// exponentials, 128 us; a quarter of the exponentials on the FMA pipe, 122 us; the row sums by one more MMA per
+// tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us with P through shared memory.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
-constexpr int TKV = 64;                   // keys per K/V tile
-constexpr int T_QSLOTS = 2, T_KVSTAGES = 8;
+constexpr int TKV = 128;                  // keys per K/V tile
+constexpr int T_QSLOTS = 2, T_KVSTAGES = 4;
 constexpr int T_QT_BYTES = TQ * 128;      // one 128-row x 64-dim fp16 tile
 constexpr int T_KV_BYTES = TKV * 128;     // K or V of one tile
 constexpr int T_O_BYTES = TQ * 128;       // one warpgroup's O staging tile
 constexpr uint32_t T_TMEM_COLS = 512;
-constexpr int T_SBUF = 2;                 // S/P buffers per warpgroup (S runs T_SBUF tiles ahead)
-constexpr uint32_t T_WG_COLS = 256;       // TMEM columns per warpgroup: T_SBUF S/P buffers, then O
+constexpr uint32_t T_WG_COLS = 256;       // TMEM columns per warpgroup: S, P, O
+constexpr uint32_t T_P_COL = TKV;         // P: TKV fp16 keys, two per column
+constexpr uint32_t T_O_COL = TKV + TKV / 2;
 constexpr float kLazyRescale = 8.f;
 enum : int {
     B_QFULL = 0,
     B_QEMPTY = B_QFULL + T_QSLOTS,
     B_KVFULL = B_QEMPTY + T_QSLOTS,
     B_KVEMPTY = B_KVFULL + T_KVSTAGES,
-    B_SFULL = B_KVEMPTY + T_KVSTAGES,  // [w][b]
-    B_PFULL = B_SFULL + 2 * T_SBUF,    // [w][b]
-    B_ODONE = B_PFULL + 2 * T_SBUF,    // [w][b]: P.V of the tile whose P is in buffer b
-    B_OFREE = B_ODONE + 2 * T_SBUF,    // [w]
+    B_SFULL = B_KVEMPTY + T_KVSTAGES,  // [w]: S of the warpgroup's next tile is in TMEM
+    B_PFULL = B_SFULL + 2,             // [w]: its P is in TMEM (4 warp arrivals)
+    B_ODONE = B_PFULL + 2,             // [w]: P.V of its last P has completed
+    B_OFREE = B_ODONE + 2,             // [w]: its O has been read (4 warp arrivals)
     B_DRAIN = B_OFREE + 2,
     B_OSTAGED = B_DRAIN + 1,           // [w]: the warpgroup's O tile is in shared memory (4 warp arrivals)
     B_OREAD = B_OSTAGED + 2,           // [w]: its previous bulk store has read the staging buffer
-    T_NBARS = B_OREAD + 2
+    B_SFREE = B_OREAD + 2,             // [w]: the warpgroup has read its S tile (4 warp arrivals)
+    T_NBARS = B_SFREE + 2
 };
 constexpr int T_SMEM = T_QSLOTS * 2 * T_QT_BYTES + T_KVSTAGES * 2 * T_KV_BYTES + 2 * T_O_BYTES + T_NBARS * 8 + 16;
 static_assert(T_SMEM <= 232448, "shared memory of the tcgen05 attention");
-static_assert(T_SBUF * TKV + 64 <= (int)T_WG_COLS && 2 * T_WG_COLS <= T_TMEM_COLS, "TMEM of the tcgen05 attention");
+static_assert(T_O_COL + 64 <= T_WG_COLS && 2 * T_WG_COLS <= T_TMEM_COLS, "TMEM of the tcgen05 attention");
 
 // Error word of the attention kernels (a wait that gave up); read and cleared by d1_flash_attn_error().
 __device__ int g_fa_err = 0;
@@ -380,6 +383,24 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
+}
+
+// 2^x of two lanes on the FMA pipe (Cody-Waite style): n = round(x) by the 1.5 * 2^23 shifter, f = x - n in
+// [-0.5, 0.5], 2^f by a cubic fitted for relative error on that interval (7.5e-5 max, below the fp16 rounding of
+// P), 2^n added into the exponent field. x is clamped to -126 first (masked keys give ~1e-38, zero in fp16).
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& p0, float& p1) {
+    const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const uint64_t t = f2_add(x, f2_pack(12582912.f, 12582912.f));
+    const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+    const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
+    uint64_t q = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.24261114f, 0.24261114f));
+    q = f2_fma(q, f, f2_pack(0.69326097f, 0.69326097f));
+    q = f2_fma(q, f, f2_pack(0.99992806f, 0.99992806f));
+    float q0, q1, t0, t1;
+    f2_unpack(q, q0, q1);
+    f2_unpack(t, t0, t1);
+    p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+    p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
 // max(a, b, c) in one instruction (sm_100).
@@ -456,7 +477,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             mbar_init(bar(B_KVFULL + i), 32 * T_LOADERS);
             mbar_init(bar(B_KVEMPTY + i), 1);
         }
-        for (int i = 0; i < 2 * T_SBUF; i++) {
+        for (int i = 0; i < 2; i++) {
             mbar_init(bar(B_SFULL + i), 1);
             mbar_init(bar(B_PFULL + i), 4);
             mbar_init(bar(B_ODONE + i), 1);
@@ -467,6 +488,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(B_OSTAGED + i), 4);
             mbar_init(bar(B_OREAD + i), 1);
+            mbar_init(bar(B_SFREE + i), 4);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -586,40 +608,40 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 auto kv_ready = [&](int j) {
                     return mbar_wait(bar(B_KVFULL + (ki + j) % T_KVSTAGES), ((ki + j) / T_KVSTAGES) & 1, abort_flag);
                 };
-                // S_w(j) into buffer (cnt[w] + j) % T_SBUF. That buffer last held P(cnt[w] + j - T_SBUF), whose P.V
-                // this thread issued earlier: the tensor core reads it before this S overwrites it (issue order).
-                auto issue_s = [&](int w, int j) {
+                // S_w(j) into the warpgroup's S columns once its softmax has read S_w(j - 1) (its tile cnt[w] + j - 1)
+                auto issue_s = [&](int w, int j) -> bool {
+                    const int c = cnt[w] + j;
+                    if (c > 0 && !mbar_wait(bar(B_SFREE + w), (c - 1) & 1, abort_flag)) return false;
+                    tc_fence_after();
                     const uint32_t ka = k_addr(j);
-                    const int b = (cnt[w] + j) % T_SBUF;
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        tc_mma_f16(tmem + w * T_WG_COLS + b * TKV, smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32),
+                        tc_mma_f16(tmem + w * T_WG_COLS, smem_desc_k128(q_addr + w * T_QT_BYTES + k * 32),
                                    smem_desc_k128(ka + k * 32), IDESC_S, k != 0);
-                    tc_commit(bar(B_SFULL + T_SBUF * w + b));
+                    tc_commit(bar(B_SFULL + w));
+                    return true;
                 };
-                for (int j = 0; j < T_SBUF && j < un.nt && ok; j++) {  // prologue: S for the first T_SBUF tiles
-                    if (!(ok = kv_ready(j))) break;
-                    tc_fence_after();
-                    for (int w = 0; w < nw; w++) issue_s(w, j);
-                }
+                if (!(ok = kv_ready(0))) break;
+                for (int w = 0; w < nw && ok; w++) ok = issue_s(w, 0);
                 for (int j = 0; j < un.nt && ok; j++) {
-                    const bool ahead = j + T_SBUF < un.nt;
-                    if (ahead && !(ok = kv_ready(j + T_SBUF))) break;
+                    if (j + 1 < un.nt) {  // S(j+1) computes while the softmax works on tile j
+                        if (!(ok = kv_ready(j + 1))) break;
+                        for (int w = 0; w < nw && ok; w++) ok = issue_s(w, j + 1);
+                        if (!ok) break;
+                    }
                     const uint32_t v_addr = k_addr(j) + T_KV_BYTES;
-                    // each warpgroup as soon as its P(j) is in TMEM: P(j).V_j, then S(j+T_SBUF) into the same buffer
                     for (int w = 0; w < nw && ok; w++) {
-                        const int c = cnt[w] + j, b = c % T_SBUF;
-                        ok = mbar_wait(bar(B_PFULL + T_SBUF * w + b), (c / T_SBUF) & 1, abort_flag);
+                        const int c = cnt[w] + j;
+                        ok = mbar_wait(bar(B_PFULL + w), c & 1, abort_flag);
                         // the first P.V of a unit overwrites O_w: its previous unit's O must have been read
                         if (ok && j == 0 && units[w] > 0) ok = mbar_wait(bar(B_OFREE + w), (units[w] - 1) & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
 #pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_SBUF * TKV, tmem + w * T_WG_COLS + b * TKV + k * 8,
+                        for (int k = 0; k < TKV / 16; k++)
+                            tc_mma_f16_ts(tmem + w * T_WG_COLS + T_O_COL, tmem + w * T_WG_COLS + T_P_COL + k * 8,
                                           smem_desc_k128(v_addr + k * 2048), IDESC_O, (j | k) != 0);
-                        tc_commit(bar(B_ODONE + T_SBUF * w + b));
-                        if (ahead) issue_s(w, j + T_SBUF);
+                        tc_commit(bar(B_ODONE + w));
                     }
                     if (!ok) break;
                     tc_commit(bar(B_KVEMPTY + (ki + j) % T_KVSTAGES));
@@ -642,7 +664,8 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         // ------------------------------------------------------------------ softmax (warpgroups 0 and 1)
         const int w = warp >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tO = tmem + w * T_WG_COLS + T_SBUF * TKV + lane_off;
+        const uint32_t tO = tmem + w * T_WG_COLS + T_O_COL + lane_off;
+        const uint32_t tP = tmem + w * T_WG_COLS + T_P_COL + lane_off;
         uint8_t* stile = sO + w * T_O_BYTES;
         int cnt = 0;
         int nst = 0;  // O tiles this warpgroup has staged
@@ -653,16 +676,18 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < un.nt; j++) {
-                const int c = cnt + j, b = c % T_SBUF;
-                if (!(ok = __all_sync(D1_FULL_MASK,
-                                      mbar_wait(bar(B_SFULL + T_SBUF * w + b), (c / T_SBUF) & 1, abort_flag))))
-                    break;
+                const int c = cnt + j;
+                if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_SFULL + w), c & 1, abort_flag)))) break;
                 tc_fence_after();
                 uint32_t sr[TKV];
-                const uint32_t tS = tmem + w * T_WG_COLS + b * TKV + lane_off;
-                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(sr));
-                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+                const uint32_t tS = tmem + w * T_WG_COLS + lane_off;
+#pragma unroll
+                for (int c32 = 0; c32 < TKV / 32; c32++)
+                    tmem_ld32(tS + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c32 * 32));
                 tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_SFREE + w));  // S is in registers: S(j+1) may overwrite it
                 const int kbase = j * TKV;
                 if (kbase + TKV > total) {  // keys past the sequence: only in its last tile
 #pragma unroll
@@ -689,9 +714,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 }
                 if (j > 0 && __any_sync(D1_FULL_MASK, alpha < 1.f)) {  // rare: O must hold P.V up to tile c - 1
                     const int cp = c - 1;
-                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + T_SBUF * w + cp % T_SBUF),
-                                                                  (cp / T_SBUF) & 1, abort_flag))))
-                        break;
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), cp & 1, abort_flag)))) break;
                     tc_fence_after();
 #pragma unroll 1
                     for (int q = 0; q < 8; q++) {
@@ -714,19 +737,32 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     float x0, x1;
                     f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2),
                               x0, x1);
-                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    float p0, p1;
+                    if (i % 8 == 7) {
+                        ex2_poly2(x0, x1, p0, p1);
+                    } else {
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
+                    }
                     rs2[i & 3] = f2_add(rs2[i & 3], f2_pack(p0, p1));
                     pr[i] = pack_h2(p0, p1);
                 }
                 float rs8[8];
 #pragma unroll
                 for (int e = 0; e < 4; e++) f2_unpack(rs2[e], rs8[2 * e], rs8[2 * e + 1]);
-                // P(j) over the first 32 columns of S(j)'s buffer (two fp16 keys per column), the A operand of P.V
-                tmem_st32(tS, pr);
+                // P(j) into the P columns (two fp16 keys per column), the A operand of P.V, once P.V(j-1) has read
+                // them
+                if (c > 0) {
+                    if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), (c - 1) & 1, abort_flag)))) break;
+                    tc_fence_after();
+                }
+#pragma unroll
+                for (int c32 = 0; c32 < TKV / 64; c32++)
+                    tmem_st32(tP + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(pr + c32 * 32));
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(B_PFULL + T_SBUF * w + b));
+                if (lane == 0) mbar_arrive(bar(B_PFULL + w));
                 const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
                 l = l * alpha + rs;
                 m = m_use;
@@ -735,9 +771,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             cnt += un.nt;
             // the unit's last P.V (the earlier ones completed before it)
             const int cl = cnt - 1;
-            if (!(ok = __all_sync(D1_FULL_MASK,
-                                  mbar_wait(bar(B_ODONE + T_SBUF * w + cl % T_SBUF), (cl / T_SBUF) & 1, abort_flag))))
-                break;
+            if (!(ok = __all_sync(D1_FULL_MASK, mbar_wait(bar(B_ODONE + w), cl & 1, abort_flag)))) break;
             tc_fence_after();
             const float il = l > 0.f ? 1.f / l : 0.f;
             uint32_t o[64];
