@@ -16,7 +16,7 @@
 // d1_flash_attn_tc (extension) is the same computation for the bias-free forms on tcgen05 (k_flash_attn_tc below:
 // S, P and O in TMEM, 128-key tiles, the next score tile computed while two softmax warpgroups run the exponentials,
 // TMA loads and stores). Measured on B200 (CUDA events, 16 heads, GQA 2): ~24.3 us at 32 x 256 tokens (44 us for the
-// mma.sync kernel) and ~120 us at 4 x 2048 tokens (572 TF/s; 263 us). The runners use it whenever the attention has
+// mma.sync kernel) and ~117 us at 4 x 2048 tokens (587 TF/s; 263 us). The runners use it whenever the attention has
 // no biases to add on load (their work lists cover every 256-row block).
 #include "common.cuh"
 #include "warp_mma.cuh"
@@ -279,9 +279,11 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // per SM); loads, max and the P store add ~1100 per tile. One in eight exponential pairs is therefore computed on
 // the FMA pipe (ex2_poly2). The A-in-TMEM P.V runs at ~67 clocks per N=64 instruction (half the dense rate) but
 // overlaps the shared-memory S MMAs. (Tried and slower or equal: 64-key tiles with S two tiles ahead, 145 us at
-// 4 x 2048 against 120; 96-key tiles with two S buffers, 123 us; the two warpgroups taking turns on the
-// exponentials, 128 us; a quarter of the exponentials on the FMA pipe, 122 us; the row sums by one more MMA per
-// tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us with P through shared memory.)
+// 4 x 2048 against 117; 96-key tiles with two S buffers, 123 us; the two warpgroups taking turns on the
+// exponentials, 128 us; four softmax warpgroups, two per query tile each taking 64 of the 128 keys and exchanging
+// the row max through shared memory, 127 us; a quarter of the exponentials on the FMA pipe, 122 us; the row sums
+// by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us with P through
+// shared memory.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
 constexpr int TQU = 2 * TQ;               // query rows per unit
 constexpr int TKV = 128;                  // keys per K/V tile
@@ -694,17 +696,19 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                     for (int i = 0; i < TKV; i++)
                         if (kbase + i >= total) sr[i] = __float_as_uint(-INFINITY);
                 }
-                // the max of the raw scores (the scale is positive) in four independent 3-input chains, scaled
+                // the max of the raw scores (the scale is positive) in eight independent 3-input chains, scaled
                 // once; the exponent below folds the scale in: P = 2^(s * scale - m)
-                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                float mx8[8];
 #pragma unroll
-                for (int i = 0; i < TKV; i += 8) {
-                    mx4[0] = fmax3(mx4[0], __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-                    mx4[1] = fmax3(mx4[1], __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
-                    mx4[2] = fmax3(mx4[2], __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
-                    mx4[3] = fmax3(mx4[3], __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+                for (int e = 0; e < 8; e++) mx8[e] = fmaxf(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1]));
+#pragma unroll
+                for (int i = 16; i < TKV; i += 16) {
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        mx8[e] = fmax3(mx8[e], __uint_as_float(sr[i + 2 * e]), __uint_as_float(sr[i + 2 * e + 1]));
                 }
-                const float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]) * a.scale_log2;
+                const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7]))) *
+                                 a.scale_log2;
                 float m_use = m, alpha = 1.f;
                 if (j == 0) {
                     m_use = mx;
