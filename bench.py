@@ -561,9 +561,11 @@ def hbm_kernels(pkg, dev, reps=40, warm=5):
 def attn_config2(pkg, dev, reps=20, warm=3):
     """packed varlen bidirectional GQA attention (16 query heads, 8 KV heads, head dim 64,
     Q/K/V N(0,1) fp16, seed 2), lengths log-normal (median 384, sigma 1) clipped to 32..16384, at 2048, 8192 and
-    16384 packed tokens. Times this library's tcgen05 kernel (d1_flash_attn_tc, 256-row work items), its mma.sync
-    kernel (d1_flash_attn, 64-row items as the reference builds them) and the reference's own k_flash_attn
-    (d1_flash_attn of oracle/_ref/libd1ref.so) on the same inputs; FLOPs = sum over sequences of 4 L^2 64 x 16."""
+    16384 packed tokens. Times this library's tcgen05 kernel (d1_flash_attn_tc, 256-row work items), its reference
+    ABI entry d1_flash_attn with 64-row items as the reference builds them ("abi": the list split onto the tcgen05
+    kernel), the same entry with that list shuffled ("mma_sync": no whole block left, so every item runs on the
+    mma.sync kernel) and the reference's own k_flash_attn (d1_flash_attn of oracle/_ref/libd1ref.so) on the same
+    inputs; FLOPs = sum over sequences of 4 L^2 64 x 16."""
     import ctypes as C
     import torch
     from fast_d1_omni_b200.weights import lognormal_lengths
@@ -589,14 +591,17 @@ def attn_config2(pkg, dev, reps=20, warm=3):
             return torch.tensor(np.asarray(w, np.int32).reshape(-1), device=dev), len(w)
         w64, n64 = work(64)
         w256, n256 = work(256)
+        wsh = w64.view(-1, 2)[torch.randperm(n64, generator=torch.Generator().manual_seed(5)).to(dev)].reshape(-1)
         g = torch.Generator(device=dev).manual_seed(2)
         qkv = torch.randn(total, 2048, device=dev, generator=g).half()
         out = torch.empty(total, 1024, device=dev, dtype=torch.float16)
         Q, K, V = qkv, qkv[:, 1024:], qkv[:, 1536:]
         runs = {"tcgen05": lambda: lib.d1_flash_attn_tc(P(Q), 2048, P(K), P(V), 2048, 512, P(out), 1024, P(meta),
                                                         P(w256), n256, 16, 2, 0.125, total, total, st),
+                "abi": lambda: lib.d1_flash_attn(P(Q), 2048, P(K), P(V), 2048, 512, None, None, None, P(out), 1024,
+                                                 P(meta), P(w64), n64, 16, 2, 0.125, st),
                 "mma_sync": lambda: lib.d1_flash_attn(P(Q), 2048, P(K), P(V), 2048, 512, None, None, None, P(out),
-                                                      1024, P(meta), P(w64), n64, 16, 2, 0.125, st)}
+                                                      1024, P(meta), P(wsh), n64, 16, 2, 0.125, st)}
         if ref is not None:
             runs["reference"] = lambda: ref.d1_flash_attn(P(Q), 2048, P(K), P(V), 2048, 512, None, None, None,
                                                           P(out), 1024, P(meta), P(w64), n64, 16, 2, 0.125, st)
@@ -618,6 +623,7 @@ def attn_config2(pkg, dev, reps=20, warm=3):
             raise RuntimeError("attention kernel reported a wait that gave up")
         if "reference" in rec:
             rec["tcgen05_speedup_vs_reference"] = round(rec["reference"]["us"] / rec["tcgen05"]["us"], 3)
+            rec["abi_speedup_vs_reference"] = round(rec["reference"]["us"] / rec["abi"]["us"], 3)
         rec["peak"] = f"{tflops} TFLOP/s ({kind}, bf16 cuBLAS burst)"
         print(json.dumps(rec), flush=True)
 

@@ -5,19 +5,24 @@
 //   [ext prefix keys | local keys] of that sequence, kv head g = h / group, fp32 softmax, optional fp32 biases
 //   added to q/k/v as they are loaded.
 //
-// d1_flash_attn runs an mma.sync kernel: one CTA per (64-query tile, kv head) runs all the query heads that share
-// that kv head (GQA group 2: 8 warps, two heads), so each K/V tile is fetched once for the group. Each warp owns 16
-// query rows of one head. K/V tiles of 64 keys are double-buffered in shared memory with cp.async (bias-free case)
-// so the next tile's loads overlap this tile's math; QK^T and PV run on m16n8k16 fp16 tensor-core MMAs with fp32
-// accumulation, S stays in registers and is re-packed as the A operand of PV; the online softmax works in the
-// exp2 domain. The output tile is staged through shared memory for 16-byte coalesced stores; 2 CTAs per SM. It
-// takes any work list, as the reference's kernel does, and adds biases on load.
+// d1_flash_attn takes any work list, as the reference's kernel does. Without biases it runs the tcgen05 kernel below
+// on the 256-row blocks the list names whole (all of the reference's own lists) and an mma.sync kernel on any other
+// item (see "reference ABI" below); with biases, the mma.sync kernel alone. The mma.sync kernel: one CTA per
+// (64-query tile, kv head) runs all the query heads that share that kv head (GQA group 2: 8 warps, two heads), so
+// each K/V tile is fetched once for the group. Each warp owns 16 query rows of one head. K/V tiles of 64 keys are
+// double-buffered in shared memory with cp.async (bias-free case) so the next tile's loads overlap this tile's math;
+// QK^T and PV run on m16n8k16 fp16 tensor-core MMAs with fp32 accumulation, S stays in registers and is re-packed as
+// the A operand of PV; the online softmax works in the exp2 domain. The output tile is staged through shared memory
+// for 16-byte coalesced stores; 2 CTAs per SM. It adds biases on load.
 //
 // d1_flash_attn_tc (extension) is the same computation for the bias-free forms on tcgen05 (k_flash_attn_tc below:
 // S, P and O in TMEM, 128-key tiles, the next score tile computed while two softmax warpgroups run the exponentials,
 // TMA loads and stores). Measured on B200 (CUDA events, 16 heads, GQA 2): ~24.3 us at 32 x 256 tokens (44 us for the
 // mma.sync kernel) and ~117 us at 4 x 2048 tokens (587 TF/s; 263 us). The runners use it whenever the attention has
 // no biases to add on load (their work lists cover every 256-row block).
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "warp_mma.cuh"
 
@@ -48,6 +53,8 @@ struct FaArgs {
     __half* O;
     const AttnSeq* seqs;
     const int2* work;
+    const int* n_items;  // when set: a pool of *n_items work items that the CTAs of each kv head (blockIdx.y) take
+    int* next_item;      // in turn through next_item[blockIdx.y]
     int ldq, ldkv, ext_ld, ldo, group;
     float scale_log2;
 };
@@ -61,190 +68,205 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
     __half* sV = sK + 2 * FA_B * FA_LD;                             // [2][64][FA_LD]
 
     pdl_entry();
-    const int2 wi = p.work[blockIdx.x];
-    const AttnSeq s = p.seqs[wi.x];
-    const int q0 = wi.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int hl = warp >> 2;                          // head of this warp within the CTA
-    const int g = blockIdx.y;                          // kv head
-    const int h0 = HPC > 1 ? g * p.group : blockIdx.y;  // first query head of the CTA
-    const int kvh = HPC > 1 ? g : blockIdx.y / p.group;
-    const int total = s.ext_len + s.kv_len;
-    constexpr int NT = 128 * HPC;
-
-    // ---- Q tiles (all heads of the CTA)
-    for (int i = tid; i < HPC * FA_B * 8; i += NT) {
-        const int hh = i / (FA_B * 8), r = (i / 8) % FA_B, c = (i % 8) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (q0 + r < s.q_len) {
-            v = *reinterpret_cast<const uint4*>(p.Q + (size_t)(s.q_start + q0 + r) * p.ldq + (h0 + hh) * 64 + c);
-            if (BIAS && p.bq) v = add_bias8(v, p.bq + (h0 + hh) * 64 + c);
+    // one item per CTA, or (the leftovers of the ABI split) items taken from a pool in turn until it is empty
+    __shared__ int s_item;
+    const int n_items = p.n_items ? *p.n_items : 0;
+    for (int iter = 0;; iter++) {
+        int item = blockIdx.x;
+        if (p.n_items) {
+            __syncthreads();  // the previous item's shared-memory reads are done, and s_item is free
+            if (threadIdx.x == 0) s_item = atomicAdd(p.next_item + blockIdx.y, 1);
+            __syncthreads();
+            item = s_item;
+            if (item >= n_items) break;
+        } else if (iter > 0) {
+            break;
         }
-        *reinterpret_cast<uint4*>(sQ + (hh * FA_B + r) * FA_LD + c) = v;
-    }
+        const int2 wi = p.work[item];
+        const AttnSeq s = p.seqs[wi.x];
+        const int q0 = wi.y;
+        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+        const int hl = warp >> 2;                          // head of this warp within the CTA
+        const int g = blockIdx.y;                          // kv head
+        const int h0 = HPC > 1 ? g * p.group : blockIdx.y;  // first query head of the CTA
+        const int kvh = HPC > 1 ? g : blockIdx.y / p.group;
+        const int total = s.ext_len + s.kv_len;
+        constexpr int NT = 128 * HPC;
 
-    // ---- K/V tile loader (64 keys x 64 dims each)
-    auto load_kv = [&](int j0, int buf) {
-        __half* dK = sK + buf * FA_B * FA_LD;
-        __half* dV = sV + buf * FA_B * FA_LD;
-        for (int i = tid; i < FA_B * 8; i += NT) {
-            const int r = i / 8, c = (i % 8) * 8;
-            const int j = j0 + r;
-            const __half* srck;
-            const __half* srcv;
-            bool valid = j < total;
-            bool ext = j < s.ext_len;
-            if (ext) {
-                srck = s.ext_k + (size_t)j * p.ext_ld + kvh * 64 + c;
-                srcv = s.ext_v + (size_t)j * p.ext_ld + kvh * 64 + c;
-            } else {
-                const size_t row = (size_t)(s.kv_start + (valid ? j - s.ext_len : 0)) * p.ldkv + kvh * 64 + c;
-                srck = p.K + row;
-                srcv = p.V + row;
+        // ---- Q tiles (all heads of the CTA)
+        for (int i = tid; i < HPC * FA_B * 8; i += NT) {
+            const int hh = i / (FA_B * 8), r = (i / 8) % FA_B, c = (i % 8) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (q0 + r < s.q_len) {
+                v = *reinterpret_cast<const uint4*>(p.Q + (size_t)(s.q_start + q0 + r) * p.ldq + (h0 + hh) * 64 + c);
+                if (BIAS && p.bq) v = add_bias8(v, p.bq + (h0 + hh) * 64 + c);
             }
-            if (BIAS) {
-                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-                if (valid) {
-                    kv = *reinterpret_cast<const uint4*>(srck);
-                    vv = *reinterpret_cast<const uint4*>(srcv);
-                    if (!ext && p.bk) kv = add_bias8(kv, p.bk + kvh * 64 + c);
-                    if (!ext && p.bv) vv = add_bias8(vv, p.bv + kvh * 64 + c);
+            *reinterpret_cast<uint4*>(sQ + (hh * FA_B + r) * FA_LD + c) = v;
+        }
+
+        // ---- K/V tile loader (64 keys x 64 dims each)
+        auto load_kv = [&](int j0, int buf) {
+            __half* dK = sK + buf * FA_B * FA_LD;
+            __half* dV = sV + buf * FA_B * FA_LD;
+            for (int i = tid; i < FA_B * 8; i += NT) {
+                const int r = i / 8, c = (i % 8) * 8;
+                const int j = j0 + r;
+                const __half* srck;
+                const __half* srcv;
+                bool valid = j < total;
+                bool ext = j < s.ext_len;
+                if (ext) {
+                    srck = s.ext_k + (size_t)j * p.ext_ld + kvh * 64 + c;
+                    srcv = s.ext_v + (size_t)j * p.ext_ld + kvh * 64 + c;
+                } else {
+                    const size_t row = (size_t)(s.kv_start + (valid ? j - s.ext_len : 0)) * p.ldkv + kvh * 64 + c;
+                    srck = p.K + row;
+                    srcv = p.V + row;
                 }
-                *reinterpret_cast<uint4*>(dK + r * FA_LD + c) = kv;
-                *reinterpret_cast<uint4*>(dV + r * FA_LD + c) = vv;
-            } else {
-                cp_async16(smem_u32(dK + r * FA_LD + c), valid ? srck : p.K, valid);
-                cp_async16(smem_u32(dV + r * FA_LD + c), valid ? srcv : p.V, valid);
+                if (BIAS) {
+                    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+                    if (valid) {
+                        kv = *reinterpret_cast<const uint4*>(srck);
+                        vv = *reinterpret_cast<const uint4*>(srcv);
+                        if (!ext && p.bk) kv = add_bias8(kv, p.bk + kvh * 64 + c);
+                        if (!ext && p.bv) vv = add_bias8(vv, p.bv + kvh * 64 + c);
+                    }
+                    *reinterpret_cast<uint4*>(dK + r * FA_LD + c) = kv;
+                    *reinterpret_cast<uint4*>(dV + r * FA_LD + c) = vv;
+                } else {
+                    cp_async16(smem_u32(dK + r * FA_LD + c), valid ? srck : p.K, valid);
+                    cp_async16(smem_u32(dV + r * FA_LD + c), valid ? srcv : p.V, valid);
+                }
             }
-        }
-        if (!BIAS) cp_async_commit();
-    };
+            if (!BIAS) cp_async_commit();
+        };
 
-    const int n_tiles = (total + FA_B - 1) / FA_B;
-    if (n_tiles > 0) load_kv(0, 0);
-    __syncthreads();
-
-    // ---- Q fragments of this warp's 16 rows (4 k-steps of 16 dims)
-    uint32_t qa[4][4];
-    {
-        const __half* base = sQ + (hl * FA_B + (warp & 3) * 16) * FA_LD;
-        const int r = (lane & 7) + ((lane >> 3) & 1) * 8, c = (lane >> 4) * 8;
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++)
-            ldsm_x4(qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], smem_u32(base + r * FA_LD + kk * 16 + c));
-    }
-
-    float o[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    const int gid = lane >> 2, tig = lane & 3;
-
-    for (int t = 0; t < n_tiles; t++) {
-        const int buf = t & 1;
-        if (t + 1 < n_tiles) {
-            __syncthreads();  // everyone is done reading buffer buf^1 (tile t-1)
-            load_kv((t + 1) * FA_B, buf ^ 1);
-            if (!BIAS) cp_async_wait<1>();
-        } else if (!BIAS) {
-            cp_async_wait<0>();
-        }
+        const int n_tiles = (total + FA_B - 1) / FA_B;
+        if (n_tiles > 0) load_kv(0, 0);
         __syncthreads();
-        const __half* cK = sK + buf * FA_B * FA_LD;
-        const __half* cV = sV + buf * FA_B * FA_LD;
 
-        // S = Q K^T: 16 rows x 64 keys per warp
-        float sc[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < 4; kk += 2) {
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(b0, b1, b2, b3, smem_u32(cK + (nt * 8 + (lane & 7)) * FA_LD + kk * 16 + (lane >> 3) * 8));
-                mma16816(sc[nt], qa[kk], b0, b1);
-                mma16816(sc[nt], qa[kk + 1], b2, b3);
+        // ---- Q fragments of this warp's 16 rows (4 k-steps of 16 dims)
+        uint32_t qa[4][4];
+        {
+            const __half* base = sQ + (hl * FA_B + (warp & 3) * 16) * FA_LD;
+            const int r = (lane & 7) + ((lane >> 3) & 1) * 8, c = (lane >> 4) * 8;
+    #pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+                ldsm_x4(qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], smem_u32(base + r * FA_LD + kk * 16 + c));
+        }
+
+        float o[8][4];
+    #pragma unroll
+        for (int i = 0; i < 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        const int gid = lane >> 2, tig = lane & 3;
+
+        for (int t = 0; t < n_tiles; t++) {
+            const int buf = t & 1;
+            if (t + 1 < n_tiles) {
+                __syncthreads();  // everyone is done reading buffer buf^1 (tile t-1)
+                load_kv((t + 1) * FA_B, buf ^ 1);
+                if (!BIAS) cp_async_wait<1>();
+            } else if (!BIAS) {
+                cp_async_wait<0>();
+            }
+            __syncthreads();
+            const __half* cK = sK + buf * FA_B * FA_LD;
+            const __half* cV = sV + buf * FA_B * FA_LD;
+
+            // S = Q K^T: 16 rows x 64 keys per warp
+            float sc[8][4];
+    #pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    #pragma unroll
+                for (int kk = 0; kk < 4; kk += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(b0, b1, b2, b3, smem_u32(cK + (nt * 8 + (lane & 7)) * FA_LD + kk * 16 + (lane >> 3) * 8));
+                    mma16816(sc[nt], qa[kk], b0, b1);
+                    mma16816(sc[nt], qa[kk + 1], b2, b3);
+                }
+            }
+            // mask keys beyond the sequence, scale into the exp2 domain, running max
+            const int j0 = t * FA_B;
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+    #pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const int key = j0 + nt * 8 + 2 * tig;
+    #pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const bool ok = key + e < total;
+                    sc[nt][e] = ok ? sc[nt][e] * p.scale_log2 : -INFINITY;
+                    sc[nt][2 + e] = ok ? sc[nt][2 + e] * p.scale_log2 : -INFINITY;
+                    mx0 = fmaxf(mx0, sc[nt][e]);
+                    mx1 = fmaxf(mx1, sc[nt][2 + e]);
+                }
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(D1_FULL_MASK, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(D1_FULL_MASK, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(D1_FULL_MASK, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(D1_FULL_MASK, mx1, 2));
+            const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+            const float a0 = exp2f(m0 - nm0), a1 = exp2f(m1 - nm1);
+            m0 = nm0;
+            m1 = nm1;
+            float rs0 = 0.f, rs1 = 0.f;
+            uint32_t pa[4][4];  // P as A fragments: k-step kk covers key n-tiles 2kk, 2kk+1
+    #pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const float p0 = exp2f(sc[nt][0] - nm0), p1 = exp2f(sc[nt][1] - nm0);
+                const float p2 = exp2f(sc[nt][2] - nm1), p3 = exp2f(sc[nt][3] - nm1);
+                rs0 += p0 + p1;
+                rs1 += p2 + p3;
+                pa[nt >> 1][(nt & 1) * 2] = pack_h2(p0, p1);
+                pa[nt >> 1][(nt & 1) * 2 + 1] = pack_h2(p2, p3);
+            }
+            l0 = l0 * a0 + rs0;
+            l1 = l1 * a1 + rs1;
+    #pragma unroll
+            for (int dt = 0; dt < 8; dt++) {
+                o[dt][0] *= a0;
+                o[dt][1] *= a0;
+                o[dt][2] *= a1;
+                o[dt][3] *= a1;
+            }
+            // O += P V
+    #pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+    #pragma unroll
+                for (int dt = 0; dt < 8; dt += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(b0, b1, b2, b3,
+                              smem_u32(cV + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * FA_LD + dt * 8 + (lane >> 4) * 8));
+                    mma16816(o[dt], pa[kk], b0, b1);
+                    mma16816(o[dt + 1], pa[kk], b2, b3);
+                }
             }
         }
-        // mask keys beyond the sequence, scale into the exp2 domain, running max
-        const int j0 = t * FA_B;
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const int key = j0 + nt * 8 + 2 * tig;
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const bool ok = key + e < total;
-                sc[nt][e] = ok ? sc[nt][e] * p.scale_log2 : -INFINITY;
-                sc[nt][2 + e] = ok ? sc[nt][2 + e] * p.scale_log2 : -INFINITY;
-                mx0 = fmaxf(mx0, sc[nt][e]);
-                mx1 = fmaxf(mx1, sc[nt][2 + e]);
-            }
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(D1_FULL_MASK, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(D1_FULL_MASK, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(D1_FULL_MASK, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(D1_FULL_MASK, mx1, 2));
-        const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
-        const float a0 = exp2f(m0 - nm0), a1 = exp2f(m1 - nm1);
-        m0 = nm0;
-        m1 = nm1;
-        float rs0 = 0.f, rs1 = 0.f;
-        uint32_t pa[4][4];  // P as A fragments: k-step kk covers key n-tiles 2kk, 2kk+1
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const float p0 = exp2f(sc[nt][0] - nm0), p1 = exp2f(sc[nt][1] - nm0);
-            const float p2 = exp2f(sc[nt][2] - nm1), p3 = exp2f(sc[nt][3] - nm1);
-            rs0 += p0 + p1;
-            rs1 += p2 + p3;
-            pa[nt >> 1][(nt & 1) * 2] = pack_h2(p0, p1);
-            pa[nt >> 1][(nt & 1) * 2 + 1] = pack_h2(p2, p3);
-        }
-        l0 = l0 * a0 + rs0;
-        l1 = l1 * a1 + rs1;
-#pragma unroll
+
+        // ---- normalise, stage through this warp's Q rows in shared memory, 16-byte coalesced stores
+        l0 += __shfl_xor_sync(D1_FULL_MASK, l0, 1);
+        l0 += __shfl_xor_sync(D1_FULL_MASK, l0, 2);
+        l1 += __shfl_xor_sync(D1_FULL_MASK, l1, 1);
+        l1 += __shfl_xor_sync(D1_FULL_MASK, l1, 2);
+        const float il0 = l0 > 0.f ? 1.f / l0 : 0.f, il1 = l1 > 0.f ? 1.f / l1 : 0.f;
+        __half* stage = sQ + (hl * FA_B + (warp & 3) * 16) * FA_LD;
+    #pragma unroll
         for (int dt = 0; dt < 8; dt++) {
-            o[dt][0] *= a0;
-            o[dt][1] *= a0;
-            o[dt][2] *= a1;
-            o[dt][3] *= a1;
+            *reinterpret_cast<uint32_t*>(stage + gid * FA_LD + dt * 8 + 2 * tig) = pack_h2(o[dt][0] * il0, o[dt][1] * il0);
+            *reinterpret_cast<uint32_t*>(stage + (gid + 8) * FA_LD + dt * 8 + 2 * tig) =
+                pack_h2(o[dt][2] * il1, o[dt][3] * il1);
         }
-        // O += P V
-#pragma unroll
-        for (int kk = 0; kk < 4; kk++) {
-#pragma unroll
-            for (int dt = 0; dt < 8; dt += 2) {
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(b0, b1, b2, b3,
-                          smem_u32(cV + (kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * FA_LD + dt * 8 + (lane >> 4) * 8));
-                mma16816(o[dt], pa[kk], b0, b1);
-                mma16816(o[dt + 1], pa[kk], b2, b3);
-            }
+        __syncwarp();
+        const int h = h0 + hl;
+    #pragma unroll
+        for (int i = lane; i < 16 * 8; i += 32) {
+            const int r = i / 8, c = (i % 8) * 8;
+            const int q = q0 + (warp & 3) * 16 + r;
+            if (q < s.q_len)
+                *reinterpret_cast<uint4*>(p.O + (size_t)(s.q_start + q) * p.ldo + h * 64 + c) =
+                    *reinterpret_cast<const uint4*>(stage + r * FA_LD + c);
         }
-    }
-
-    // ---- normalise, stage through this warp's Q rows in shared memory, 16-byte coalesced stores
-    l0 += __shfl_xor_sync(D1_FULL_MASK, l0, 1);
-    l0 += __shfl_xor_sync(D1_FULL_MASK, l0, 2);
-    l1 += __shfl_xor_sync(D1_FULL_MASK, l1, 1);
-    l1 += __shfl_xor_sync(D1_FULL_MASK, l1, 2);
-    const float il0 = l0 > 0.f ? 1.f / l0 : 0.f, il1 = l1 > 0.f ? 1.f / l1 : 0.f;
-    __half* stage = sQ + (hl * FA_B + (warp & 3) * 16) * FA_LD;
-#pragma unroll
-    for (int dt = 0; dt < 8; dt++) {
-        *reinterpret_cast<uint32_t*>(stage + gid * FA_LD + dt * 8 + 2 * tig) = pack_h2(o[dt][0] * il0, o[dt][1] * il0);
-        *reinterpret_cast<uint32_t*>(stage + (gid + 8) * FA_LD + dt * 8 + 2 * tig) =
-            pack_h2(o[dt][2] * il1, o[dt][3] * il1);
-    }
-    __syncwarp();
-    const int h = h0 + hl;
-#pragma unroll
-    for (int i = lane; i < 16 * 8; i += 32) {
-        const int r = i / 8, c = (i % 8) * 8;
-        const int q = q0 + (warp & 3) * 16 + r;
-        if (q < s.q_len)
-            *reinterpret_cast<uint4*>(p.O + (size_t)(s.q_start + q) * p.ldo + h * 64 + c) =
-                *reinterpret_cast<const uint4*>(stage + r * FA_LD + c);
     }
 }
 
@@ -325,6 +347,7 @@ struct FaTcArgs {
     __half* O;
     const AttnSeq* seqs;
     const int2* work;
+    const int* n_blocks;  // when set, the number of work items is read from here (device count)
     int n_units;  // work items x heads
     int heads;
     int ldq, ldkv, ext_ld, ldo, group;
@@ -432,8 +455,8 @@ struct Unit {
 };
 // This CTA's next unit at or after candidate u (its candidates are u, u + gridDim.x, ...); false when none is left.
 // Every role walks the same sequence.
-__device__ __forceinline__ bool next_unit(const FaTcArgs& a, int& u, Unit& out) {
-    for (; u < a.n_units; u += gridDim.x) {
+__device__ __forceinline__ bool next_unit(const FaTcArgs& a, int n_units, int& u, Unit& out) {
+    for (; u < n_units; u += gridDim.x) {
         const int2 wi = a.work[u / a.heads];
         if (wi.y % TQU) continue;
         out.s = a.seqs[wi.x];
@@ -510,6 +533,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_entry();  // barriers and TMEM are set up; global memory is touched only after this
+    const int n_units = a.n_blocks ? *a.n_blocks * a.heads : a.n_units;
 
     if (warp == 8 || warp >= 10) {
         // ------------------------------------------------------------------ loaders (warps 8, 10, 11)
@@ -527,7 +551,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         int qi = 0, ki = 0;
         bool ok = true;
         Unit un;
-        for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
+        for (int u = blockIdx.x; ok && next_unit(a, n_units, u, un); u += gridDim.x) {
             const int g = un.h / a.group, total = un.s.ext_len + un.s.kv_len;
             const int qs = qi % T_QSLOTS;
             if (warp == 8) {
@@ -601,7 +625,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
             int qi = 0, ki = 0;
             bool ok = true;
             Unit un;
-            for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
+            for (int u = blockIdx.x; ok && next_unit(a, n_units, u, un); u += gridDim.x) {
                 const int nw = un.two ? 2 : 1;
                 const int qs = qi % T_QSLOTS;
                 if (!(ok = mbar_wait(bar(B_QFULL + qs), (qi / T_QSLOTS) & 1, abort_flag))) break;
@@ -673,7 +697,7 @@ __global__ void __launch_bounds__(T_THREADS, 1)
         int nst = 0;  // O tiles this warpgroup has staged
         bool ok = true;
         Unit un;
-        for (int u = blockIdx.x; ok && next_unit(a, u, un); u += gridDim.x) {
+        for (int u = blockIdx.x; ok && next_unit(a, n_units, u, un); u += gridDim.x) {
             if (w == 1 && !un.two) continue;
             const int total = un.s.ext_len + un.s.kv_len;
             float m = -INFINITY, l = 0.f;
@@ -850,7 +874,7 @@ bool attn_tmap(CUtensorMap* m, const void* base, int cols, int rows, int ld, uin
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int launch_fa_tc(FaTcArgs& a, int n_work, int heads, int q_rows, int kv_rows, cudaStream_t st) {
+int launch_fa_tc(FaTcArgs& a, int n_work, int heads, int q_rows, int kv_rows, int o_rows, cudaStream_t st) {
     static unsigned long long attr_done = 0;
     static int sms[64] = {};
     int dev = 0;
@@ -867,7 +891,7 @@ int launch_fa_tc(FaTcArgs& a, int n_work, int heads, int q_rows, int kv_rows, cu
     CUtensorMap tq, tk, tv, to;
     const int kv_cols = heads / a.group * 64;
     if (!attn_tmap(&tq, a.Q, heads * 64, q_rows, a.ldq, TQ) || !attn_tmap(&tk, a.K, kv_cols, kv_rows, a.ldkv, TKV) ||
-        !attn_tmap(&tv, a.V, kv_cols, kv_rows, a.ldkv, TKV) || !attn_tmap(&to, a.O, heads * 64, q_rows, a.ldo, TQ))
+        !attn_tmap(&tv, a.V, kv_cols, kv_rows, a.ldkv, TKV) || !attn_tmap(&to, a.O, heads * 64, o_rows, a.ldo, TQ))
         return -1;
     const int grid = a.n_units < sms[dev & 63] ? a.n_units : sms[dev & 63];
     launch_pdl(k_flash_attn_tc, grid, T_THREADS, T_SMEM, st, tq, tk, tv, to, a);
@@ -893,6 +917,167 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
     return (int)cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------------------------- reference ABI
+// d1_flash_attn takes any list of 64-row work items and no buffer bounds. Its bias-free calls run on the tcgen05
+// kernel as far as the list allows: a one-CTA pass splits the list into the 256-row blocks whose tiles (those
+// inside the sequence) are listed consecutively from a multiple of 256 (the reference's own lists,
+// src/model.rs:328-339, consist of such blocks only) and every other item, which the mma.sync kernel computes
+// after it. Each row is computed as often as the list names it, as before. The tensor maps are bounded by the
+// allocations holding Q, K, V and O (cuMemGetAddressRange): whole K/V tiles lie inside their sequence, partial
+// ones are copied with zero fill, and the rows a Q tile reads past its sequence stay inside the allocation and are
+// never stored.
+constexpr int kAbiMaxItems = 1 << 16;
+constexpr int kAbiMaxGy = 128;  // leftover pool counters, one per grid row of the mma.sync kernel
+
+__global__ void __launch_bounds__(1024) k_split_work(const int2* __restrict__ work, int n_work,
+                                                     const AttnSeq* __restrict__ seqs, int2* blocks, int2* left,
+                                                     int* counts) {
+    __shared__ int nb, nl;
+    pdl_entry();
+    if (threadIdx.x == 0) {
+        nb = 0;
+        nl = 0;
+    }
+    if (threadIdx.x < kAbiMaxGy) counts[4 + threadIdx.x] = 0;  // the leftover pools' next items
+    __syncthreads();
+    for (int j = threadIdx.x; j < n_work; j += blockDim.x) {
+        const int2 it = work[j];
+        const int q_len = seqs[it.x].q_len;
+        const int r = (it.y & (TQU - 1)) / 64;  // the item's tile within its 256-row block
+        const int base = it.y - 64 * r;
+        bool whole = it.y >= 0 && it.y % 64 == 0 && it.y < q_len && j >= r;
+        if (whole) {
+            const int n = min(TQU / 64, (q_len - base + 63) / 64);  // the block's tiles inside the sequence
+            whole = j - r + n <= n_work;
+            for (int k = 0; k < n && whole; k++) {
+                const int2 o = work[j - r + k];
+                whole = o.x == it.x && o.y == base + 64 * k;
+            }
+        }
+        if (!whole)
+            left[atomicAdd(&nl, 1)] = it;
+        else if (r == 0)
+            blocks[atomicAdd(&nb, 1)] = make_int2(it.x, base);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        counts[0] = nb;
+        counts[1] = nl;
+    }
+}
+
+// Device lists of the split and the leftover pools' counters, one set per (device, stream) so that calls on
+// different streams do not share them; 1 MB each, allocated on a stream's first call (not while it is being
+// captured) and kept until exit.
+struct AbiScratch {
+    int2* blocks;
+    int2* left;
+    int* counts;
+};
+std::mutex g_abi_mu;
+std::map<std::pair<int, cudaStream_t>, AbiScratch> g_abi_scratch;
+
+AbiScratch* abi_scratch(int dev, cudaStream_t st) {
+    std::lock_guard<std::mutex> lock(g_abi_mu);
+    auto it = g_abi_scratch.find({dev, st});
+    if (it != g_abi_scratch.end()) return &it->second;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    void* mem = nullptr;
+    if (cudaMalloc(&mem, (size_t)2 * kAbiMaxItems * sizeof(int2) + (4 + kAbiMaxGy) * sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    AbiScratch s;
+    s.blocks = static_cast<int2*>(mem);
+    s.left = s.blocks + kAbiMaxItems;
+    s.counts = reinterpret_cast<int*>(s.left + kAbiMaxItems);
+    return &(g_abi_scratch[{dev, st}] = s);
+}
+
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+    static AddrRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddrRangeFn>(p);
+    });
+    return fn;
+}
+
+// Rows of pitch ld (fp16) from p to the end of the allocation holding p, at most 2^30; 0 if unknown.
+int alloc_rows(const void* p, int ld) {
+    AddrRangeFn f = addr_range_fn();
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!f || f(&base, &size, (CUdeviceptr)(uintptr_t)p) != CUDA_SUCCESS) return 0;
+    const unsigned long long rows = (base + size - (uintptr_t)p) / ((unsigned long long)ld * 2);
+    return rows > (1ull << 30) ? (1 << 30) : (int)rows;
+}
+
+int* fa_err_addr() {
+    static int* addr[64] = {};  // device address of g_fa_err, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&addr[dev & 63]), g_fa_err) != cudaSuccess)
+        return nullptr;
+    return addr[dev & 63];
+}
+
+// The bias-free d1_flash_attn call on the tcgen05 kernel plus the mma.sync kernel for the rest of the list:
+// 0 when launched, 1 when this path cannot take the call (the caller runs the mma.sync kernel alone), or a launch
+// error.
+int abi_flash_attn_tc(const FaArgs& fa, int n_work, int heads, cudaStream_t st) {
+    if (n_work > kAbiMaxItems || heads > kAbiMaxGy || fa.ldq < heads * 64 || fa.ldo < heads * 64 ||
+        fa.ldkv < heads / fa.group * 64)
+        return 1;
+    int dev = 0, major = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10) return 1;
+    const int q_rows = alloc_rows(fa.Q, fa.ldq), k_rows = alloc_rows(fa.K, fa.ldkv), v_rows = alloc_rows(fa.V, fa.ldkv),
+              o_rows = alloc_rows(fa.O, fa.ldo);
+    int* err = fa_err_addr();
+    AbiScratch* sc = abi_scratch(dev, st);
+    if (q_rows <= 0 || k_rows <= 0 || v_rows <= 0 || o_rows <= 0 || !err || !sc) return 1;
+    launch_pdl(k_split_work, 1, 1024, 0, st, fa.work, n_work, fa.seqs, sc->blocks, sc->left, sc->counts);
+    if (cudaError_t e = cudaGetLastError()) return (int)e;
+    FaTcArgs t;
+    t.Q = fa.Q;
+    t.K = fa.K;
+    t.V = fa.V;
+    t.O = fa.O;
+    t.seqs = fa.seqs;
+    t.work = sc->blocks;
+    t.n_blocks = sc->counts;
+    t.ldq = fa.ldq;
+    t.ldkv = fa.ldkv;
+    t.ext_ld = fa.ext_ld;
+    t.ldo = fa.ldo;
+    t.group = fa.group;
+    t.scale_log2 = fa.scale_log2;
+    t.err = err;
+    if (int r = launch_fa_tc(t, n_work, heads, q_rows, k_rows < v_rows ? k_rows : v_rows, o_rows, st)) return r;
+    // the leftover items (none for the reference's own lists) on one resident wave of CTAs taking them in turn
+    FaArgs rest = fa;
+    rest.work = sc->left;
+    rest.n_items = sc->counts + 1;
+    rest.next_item = sc->counts + 4;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int gy = fa.group == 2 ? heads / 2 : heads;
+    int gx = 2 * sms / gy;
+    gx = gx < 1 ? 1 : gx > n_work ? n_work : gx;
+    return fa.group == 2 ? launch_fa<2, false>(rest, gx, gy, st) : launch_fa<1, false>(rest, gx, gy, st);
+}
+
 }  // namespace
 
 extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld,
@@ -909,19 +1094,16 @@ extern "C" int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, con
     t.O = O;
     t.seqs = seqs;
     t.work = reinterpret_cast<const int2*>(work);
+    t.n_blocks = nullptr;
     t.ldq = ldq;
     t.ldkv = ldkv;
     t.ext_ld = ext_ld;
     t.ldo = ldo;
     t.group = group;
     t.scale_log2 = scale * 1.4426950408889634f;
-    static int* err_addr[64] = {};  // device address of g_fa_err, per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!err_addr[dev & 63] && cudaGetSymbolAddress(reinterpret_cast<void**>(&err_addr[dev & 63]), g_fa_err) != cudaSuccess)
-        return -1;
-    t.err = err_addr[dev & 63];
-    return launch_fa_tc(t, n_work, heads, q_rows, kv_rows, st);
+    t.err = fa_err_addr();
+    if (!t.err) return -1;
+    return launch_fa_tc(t, n_work, heads, q_rows, kv_rows, q_rows, st);
 }
 
 extern "C" int d1_flash_attn_error(void) {
@@ -951,6 +1133,8 @@ extern "C" int d1_flash_attn(const d1_half* Q, int ldq, const d1_half* K, const 
     a.O = O;
     a.seqs = seqs;
     a.work = reinterpret_cast<const int2*>(work);
+    a.n_items = nullptr;
+    a.next_item = nullptr;
     a.ldq = ldq;
     a.ldkv = ldkv;
     a.ext_ld = ext_ld;
@@ -958,6 +1142,10 @@ extern "C" int d1_flash_attn(const d1_half* Q, int ldq, const d1_half* K, const 
     a.group = group;
     a.scale_log2 = scale * 1.4426950408889634f;
     const bool bias = bq || bk || bv;
+    if (!bias) {  // the tcgen05 kernel for the list's whole 256-row blocks, the mma.sync kernel for the rest
+        const int r = abi_flash_attn_tc(a, n_work, heads, st);
+        if (r != 1) return r;
+    }
     if (group == 2) {
         const int gy = heads / 2;
         return bias ? launch_fa<2, true>(a, n_work, gy, st) : launch_fa<2, false>(a, n_work, gy, st);

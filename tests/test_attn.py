@@ -202,3 +202,49 @@ def test_prefix_keys(pkg, gpu_lib, ref_lib, lens):
     assert np.abs(got - want).max() <= 4e-3
     assert np.abs(got_tc - want).max() <= 4e-3
     assert np.abs(got - ref_k).max() <= 4e-3
+
+
+@pytest.mark.parametrize("case", ["shuffled", "holes", "mixed"])
+def test_abi_any_work_list(pkg, gpu_lib, case):
+    """d1_flash_attn takes any list of (seq, first row) items, each covering 64 query rows (cuda/kernels.cu:351-500):
+    the bias-free call runs the tcgen05 kernel on the 256-row blocks listed whole and in order, and the mma.sync
+    kernel on every other item. Rows named by the list match the oracle; rows it does not name are left as they
+    were."""
+    rng = np.random.default_rng({"shuffled": 21, "holes": 22, "mixed": 23}[case])
+    lens = [300, 513, 70, 256]
+    T = sum(lens)
+    qkv = rng.standard_normal((T, 2048)).astype(np.float16)
+    spans, s = [], 0
+    for n in lens:
+        spans.append((s, n, s, n))
+        s += n
+    canon = [(i, q) for i, n in enumerate(lens) for q in range(0, n, 64)]
+    if case == "shuffled":
+        work = [canon[i] for i in rng.permutation(len(canon))]
+    elif case == "holes":
+        work = [it for k, it in enumerate(canon) if k % 3 != 1]
+    else:  # whole blocks, a block missing a tile, duplicates, out-of-order items, rows not on a 64-row boundary
+        work = [(0, 0), (0, 64), (0, 128), (0, 192), (0, 256), (1, 0), (1, 64), (1, 192), (1, 256), (1, 320),
+                (1, 384), (1, 448), (1, 512), (1, 256), (2, 30), (3, 192), (3, 128), (3, 64), (3, 0), (3, 0), (3, 64),
+                (3, 128), (3, 192)]
+    arr = (pkg.abi.AttnSeq * len(spans))()
+    for i, (qs, ql, ks, kl) in enumerate(spans):
+        arr[i].q_start, arr[i].q_len, arr[i].kv_start, arr[i].kv_len = qs, ql, ks, kl
+    meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    wk = torch.tensor(np.asarray(work, np.int32).reshape(-1), device="cuda")
+    d = torch.from_numpy(qkv).cuda()
+    out = torch.full((T, 1024), 7.0, dtype=torch.float16, device="cuda")
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert gpu_lib.d1_flash_attn(P(d), 2048, P(d[:, 1024:]), P(d[:, 1536:]), 2048, 0, None, None, None, P(out), 1024,
+                                 P(meta), P(wk), len(work), 16, 2, 0.125, st) == 0
+    torch.cuda.synchronize()
+    assert gpu_lib.d1_flash_attn_error() == 0
+    got = out.float().cpu().numpy()
+    covered = np.zeros(T, bool)
+    for i, q0 in work:
+        qs, ql = spans[i][0], spans[i][1]
+        covered[qs + q0: qs + min(q0 + 64, ql)] = True
+    q = qkv.astype(np.float32)
+    want = O.attention(q[:, :1024], q[:, 1024:1536], q[:, 1536:], spans, 16, 2, 0.125)
+    assert np.abs(got[covered] - want[covered]).max() <= 4e-3
+    assert np.all(got[~covered] == 7.0)
