@@ -561,7 +561,8 @@ def hbm_kernels(pkg, dev, reps=40, warm=5):
 def attn_config2(pkg, dev, reps=20, warm=3):
     """packed varlen bidirectional GQA attention (16 query heads, 8 KV heads, head dim 64,
     Q/K/V N(0,1) fp16, seed 2), lengths log-normal (median 384, sigma 1) clipped to 32..16384, at 2048, 8192 and
-    16384 packed tokens. Times this library's tcgen05 kernel (d1_flash_attn_tc, 256-row work items), its reference
+    16384 packed tokens. Times this library's tcgen05 kernel (d1_flash_attn_tc, 256-row work items longest sequence
+    first, as the runners build them), its reference
     ABI entry d1_flash_attn with 64-row items as the reference builds them ("abi": the list split onto the tcgen05
     kernel), the same entry with that list shuffled ("mma_sync": no whole block left, so every item runs on the
     mma.sync kernel) and the reference's own k_flash_attn (d1_flash_attn of oracle/_ref/libd1ref.so) on the same
@@ -586,11 +587,12 @@ def attn_config2(pkg, dev, reps=20, warm=3):
             s += n
         meta = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dev)
 
-        def work(step):
-            w = [(i, q) for i, n in enumerate(lens) for q in range(0, n, step)]
+        def work(step, order):
+            w = [(i, q) for i in order for q in range(0, lens[i], step)]
             return torch.tensor(np.asarray(w, np.int32).reshape(-1), device=dev), len(w)
-        w64, n64 = work(64)
-        w256, n256 = work(256)
+        w64, n64 = work(64, range(len(lens)))  # the reference's list: every 64-row tile, in sequence order
+        # the runners' list: one item per 256-row block, longest sequence first (runner.cpp work_items)
+        w256, n256 = work(256, sorted(range(len(lens)), key=lambda i: -lens[i]))
         wsh = w64.view(-1, 2)[torch.randperm(n64, generator=torch.Generator().manual_seed(5)).to(dev)].reshape(-1)
         g = torch.Generator(device=dev).manual_seed(2)
         qkv = torch.randn(total, 2048, device=dev, generator=g).half()

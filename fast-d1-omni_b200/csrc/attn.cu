@@ -930,41 +930,85 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
 constexpr int kAbiMaxItems = 1 << 16;
 constexpr int kAbiMaxGy = 128;  // leftover pool counters, one per grid row of the mma.sync kernel
 
+// Is work[j] part of a 256-row block the list names whole (its tiles inside the sequence listed consecutively from a
+// multiple of 256)? head: work[j] is the block's first tile.
+__device__ __forceinline__ bool whole_block(const int2* __restrict__ work, int n_work, const AttnSeq* __restrict__ seqs,
+                                            int j, int2 it, bool& head) {
+    const int q_len = seqs[it.x].q_len;
+    const int r = (it.y & (TQU - 1)) / 64;  // the item's tile within its 256-row block
+    const int base = it.y - 64 * r;
+    head = r == 0;
+    if (it.y < 0 || it.y % 64 != 0 || it.y >= q_len || j < r) return false;
+    const int n = min(TQU / 64, (q_len - base + 63) / 64);  // the block's tiles inside the sequence
+    if (j - r + n > n_work) return false;
+    for (int k = 0; k < n; k++) {
+        const int2 o = work[j - r + k];
+        if (o.x != it.x || o.y != base + 64 * k) return false;
+    }
+    return true;
+}
+
+constexpr int kSplitBins = 1024;  // block cost classes: key tiles of 128 (ext + local keys), capped
+
+// The split, one CTA. Whole blocks are written longest sequence first (a counting sort on their key tiles), so the
+// tcgen05 kernel's round-robin assignment of units to CTAs starts the long ones in its first wave; leftovers in any
+// order (the mma.sync kernel takes them from a pool).
 __global__ void __launch_bounds__(1024) k_split_work(const int2* __restrict__ work, int n_work,
                                                      const AttnSeq* __restrict__ seqs, int2* blocks, int2* left,
                                                      int* counts) {
-    __shared__ int nb, nl;
+    __shared__ int start[kSplitBins];  // blocks per cost class, then each class's next output slot
+    __shared__ int warp_sum[32];
+    __shared__ int nl;
     pdl_entry();
-    if (threadIdx.x == 0) {
-        nb = 0;
-        nl = 0;
-    }
-    if (threadIdx.x < kAbiMaxGy) counts[4 + threadIdx.x] = 0;  // the leftover pools' next items
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    start[tid] = 0;
+    if (tid == 0) nl = 0;
+    if (tid < kAbiMaxGy) counts[4 + tid] = 0;  // the leftover pools' next items
     __syncthreads();
-    for (int j = threadIdx.x; j < n_work; j += blockDim.x) {
+    auto cost = [&](int2 it) {
+        const AttnSeq& q = seqs[it.x];
+        return min((q.ext_len + q.kv_len + TKV - 1) / TKV, kSplitBins - 1);
+    };
+    for (int j = tid; j < n_work; j += blockDim.x) {
         const int2 it = work[j];
-        const int q_len = seqs[it.x].q_len;
-        const int r = (it.y & (TQU - 1)) / 64;  // the item's tile within its 256-row block
-        const int base = it.y - 64 * r;
-        bool whole = it.y >= 0 && it.y % 64 == 0 && it.y < q_len && j >= r;
-        if (whole) {
-            const int n = min(TQU / 64, (q_len - base + 63) / 64);  // the block's tiles inside the sequence
-            whole = j - r + n <= n_work;
-            for (int k = 0; k < n && whole; k++) {
-                const int2 o = work[j - r + k];
-                whole = o.x == it.x && o.y == base + 64 * k;
-            }
-        }
-        if (!whole)
+        bool head;
+        if (!whole_block(work, n_work, seqs, j, it, head))
             left[atomicAdd(&nl, 1)] = it;
-        else if (r == 0)
-            blocks[atomicAdd(&nb, 1)] = make_int2(it.x, base);
+        else if (head)
+            atomicAdd(&start[cost(it)], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        counts[0] = nb;
-        counts[1] = nl;
+    // exclusive scan from the costliest class down: thread t holds class kSplitBins - 1 - t
+    const int c = start[kSplitBins - 1 - tid];
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(D1_FULL_MASK, incl, o);
+        if (lane >= o) incl += v;
     }
+    if (lane == 31) warp_sum[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        int w = warp_sum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(D1_FULL_MASK, w, o);
+            if (lane >= o) w += v;
+        }
+        warp_sum[lane] = w - warp_sum[lane];  // exclusive over warps
+    }
+    __syncthreads();
+    start[kSplitBins - 1 - tid] = warp_sum[wid] + incl - c;
+    if (tid == blockDim.x - 1) counts[0] = warp_sum[wid] + incl;  // whole blocks in all
+    __syncthreads();
+    for (int j = tid; j < n_work; j += blockDim.x) {
+        const int2 it = work[j];
+        bool head;
+        if (whole_block(work, n_work, seqs, j, it, head) && head)
+            blocks[atomicAdd(&start[cost(it)], 1)] = make_int2(it.x, it.y);
+    }
+    __syncthreads();
+    if (tid == 0) counts[1] = nl;
 }
 
 // Device lists of the split and the leftover pools' counters, one set per (device, stream) so that calls on
