@@ -81,14 +81,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// Suspend-time hint of every mbarrier wait (ns): a waiting warp is descheduled until the phase completes or this
+// time passes, instead of re-polling and taking issue slots from the warps doing the work on its SM sub-partition
+// (measured on B200: the whole forward step 5.15-5.24 -> 4.94-4.96 ms against the default, 5.09-5.16 ms at 20 us).
+// The bounded waits below still check their abort flag and time limit between tries.
+constexpr uint32_t kWaitSuspendNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kWaitSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -219,10 +225,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kWaitSuspendNs)
         : "memory");
     return ok != 0;
 }
