@@ -83,9 +83,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 
 // Suspend-time hint of every mbarrier wait (ns): a waiting warp is descheduled until the phase completes or this
 // time passes, instead of re-polling and taking issue slots from the warps doing the work on its SM sub-partition
-// (measured on B200: the whole forward step 5.15-5.24 -> 4.94-4.96 ms against the default, 5.09-5.16 ms at 20 us).
-// The bounded waits below still check their abort flag and time limit between tries.
-constexpr uint32_t kWaitSuspendNs = 1000000;
+// (measured on B200: the whole forward step 5.15-5.24 -> 4.94-4.96 ms against the default, 5.09-5.16 ms at 20 us;
+// 100 us, 1 ms and 10 ms within the run-to-run spread, 4.78-4.83 ms). The bounded waits below still check their abort
+// flag and time limit between tries.
+constexpr uint32_t kWaitSuspendNs = 100000;
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
