@@ -558,11 +558,37 @@ __global__ void __launch_bounds__(T_THREADS, 1)
                 if (!(ok = __all_sync(D1_FULL_MASK,
                                       mbar_wait(bar(B_QEMPTY + qs), ((qi / T_QSLOTS) & 1) ^ 1, abort_flag))))
                     break;
+                // A Q tile inside the sequence comes by TMA; one that the sequence ends in is copied row by row with
+                // the rows past its end as zeros, so no load reads a row outside a sequence. The copies are complete
+                // and visible to the tensor core before the slot's one arrival.
+                const uint32_t dq = smem_u32(sQ + qs * 2 * T_QT_BYTES);
+                const int nq = un.two ? 2 : 1;
+                bool partial = false;
+                for (int t = 0; t < nq; t++) {
+                    const int rows = un.s.q_len - (un.q0 + t * TQ);
+                    if (rows >= TQ) continue;
+                    partial = true;
+                    for (int c = lane; c < TQ * 8; c += 32) {
+                        const int r = c >> 3, ch = c & 7;
+                        const __half* src =
+                            r < rows ? a.Q + (size_t)(un.s.q_start + un.q0 + t * TQ + r) * a.ldq + un.h * 64 + ch * 8 : a.Q;
+                        cp_async16z(dq + t * T_QT_BYTES + r * 128 + ((ch ^ (r & 7)) << 4), src, r < rows ? 16 : 0);
+                    }
+                }
+                if (partial) {
+                    asm volatile("cp.async.wait_all;" ::: "memory");
+                    fence_async_smem_cta();
+                    __syncwarp();
+                }
                 if (issuer) {
-                    const uint32_t dq = smem_u32(sQ + qs * 2 * T_QT_BYTES);
-                    mbar_arrive_expect_tx(bar(B_QFULL + qs), (un.two ? 2 : 1) * T_QT_BYTES);
-                    tma_load_2d(dq, &tmQ, un.h * 64, un.s.q_start + un.q0, bar(B_QFULL + qs));
-                    if (un.two) tma_load_2d(dq + T_QT_BYTES, &tmQ, un.h * 64, un.s.q_start + un.q0 + TQ, bar(B_QFULL + qs));
+                    uint32_t bytes = 0;
+                    for (int t = 0; t < nq; t++)
+                        if (un.s.q_len - (un.q0 + t * TQ) >= TQ) bytes += T_QT_BYTES;
+                    mbar_arrive_expect_tx(bar(B_QFULL + qs), bytes);
+                    for (int t = 0; t < nq; t++)
+                        if (un.s.q_len - (un.q0 + t * TQ) >= TQ)
+                            tma_load_2d(dq + t * T_QT_BYTES, &tmQ, un.h * 64, un.s.q_start + un.q0 + t * TQ,
+                                        bar(B_QFULL + qs));
                 }
             }
             qi++;
@@ -923,11 +949,12 @@ int launch_fa(const FaArgs& a, int n_work, int gy, cudaStream_t st) {
 // kernel as far as the list allows: a one-CTA pass splits the list into the 256-row blocks whose tiles (those
 // inside the sequence) are listed consecutively from a multiple of 256 (the reference's own lists,
 // src/model.rs:328-339, consist of such blocks only) and every other item, which the mma.sync kernel computes
-// after it. Each row is computed as often as the list names it, as before. The tensor maps are bounded by the
-// allocations holding Q, K, V and O (cuMemGetAddressRange): whole K/V tiles lie inside their sequence, partial
-// ones are copied with zero fill, and the rows a Q tile reads past its sequence stay inside the allocation and are
-// never stored.
+// after it. Each row is computed as often as the list names it, as before. The caller gives no buffer sizes, and
+// the tcgen05 kernel needs none: its TMA loads and stores move only whole tiles inside a sequence (partial Q and K/V
+// tiles are copied row by row with zero fill, partial O tiles stored row by row), so its tensor maps carry a
+// nominal row count (kAbiRows) that no access reaches.
 constexpr int kAbiMaxItems = 1 << 16;
+constexpr int kAbiRows = 1 << 30;
 constexpr int kAbiMaxGy = 128;  // leftover pool counters, one per grid row of the mma.sync kernel
 
 // Is work[j] part of a 256-row block the list names whole (its tiles inside the sequence listed consecutively from a
@@ -1043,30 +1070,6 @@ AbiScratch* abi_scratch(int dev, cudaStream_t st) {
     return &(g_abi_scratch[{dev, st}] = s);
 }
 
-typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
-AddrRangeFn addr_range_fn() {
-    static AddrRangeFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<AddrRangeFn>(p);
-    });
-    return fn;
-}
-
-// Rows of pitch ld (fp16) from p to the end of the allocation holding p, at most 2^30; 0 if unknown.
-int alloc_rows(const void* p, int ld) {
-    AddrRangeFn f = addr_range_fn();
-    CUdeviceptr base = 0;
-    size_t size = 0;
-    if (!f || f(&base, &size, (CUdeviceptr)(uintptr_t)p) != CUDA_SUCCESS) return 0;
-    const unsigned long long rows = (base + size - (uintptr_t)p) / ((unsigned long long)ld * 2);
-    return rows > (1ull << 30) ? (1 << 30) : (int)rows;
-}
-
 int* fa_err_addr() {
     static int* addr[64] = {};  // device address of g_fa_err, per device
     int dev = 0;
@@ -1086,11 +1089,9 @@ int abi_flash_attn_tc(const FaArgs& fa, int n_work, int heads, cudaStream_t st) 
     int dev = 0, major = 0;
     cudaGetDevice(&dev);
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10) return 1;
-    const int q_rows = alloc_rows(fa.Q, fa.ldq), k_rows = alloc_rows(fa.K, fa.ldkv), v_rows = alloc_rows(fa.V, fa.ldkv),
-              o_rows = alloc_rows(fa.O, fa.ldo);
     int* err = fa_err_addr();
     AbiScratch* sc = abi_scratch(dev, st);
-    if (q_rows <= 0 || k_rows <= 0 || v_rows <= 0 || o_rows <= 0 || !err || !sc) return 1;
+    if (!err || !sc) return 1;
     launch_pdl(k_split_work, 1, 1024, 0, st, fa.work, n_work, fa.seqs, sc->blocks, sc->left, sc->counts);
     if (cudaError_t e = cudaGetLastError()) return (int)e;
     FaTcArgs t;
@@ -1108,7 +1109,7 @@ int abi_flash_attn_tc(const FaArgs& fa, int n_work, int heads, cudaStream_t st) 
     t.group = fa.group;
     t.scale_log2 = fa.scale_log2;
     t.err = err;
-    if (int r = launch_fa_tc(t, n_work, heads, q_rows, k_rows < v_rows ? k_rows : v_rows, o_rows, st)) return r;
+    if (int r = launch_fa_tc(t, n_work, heads, kAbiRows, kAbiRows, kAbiRows, st)) return r;
     // the leftover items (none for the reference's own lists) on one resident wave of CTAs taking them in turn
     FaArgs rest = fa;
     rest.work = sc->left;
