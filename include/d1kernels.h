@@ -227,10 +227,10 @@ int d1_lt_error(void* ctx);
  * q0 is a multiple of 256 (other items are ignored): the work list must hold such an item for every 256-row block
  * of every sequence — a list of every 64-row tile (as src/model.rs builds it) does, and a list of only the
  * 256-row block starts is the cheaper form. Pointers 16-byte aligned, leading dimensions multiples of 8.
- * q_rows / kv_rows: rows of Q and O / of K and V that may be accessed (every sequence's q_start + q_len <= q_rows,
- * kv_start + kv_len <= kv_rows); query and local key tiles are fetched by TMA, which reads whole 128-row / 64-row
- * tiles within those bounds (rows of other sequences are read but never used; rows of K and V inside the bounds
- * must hold finite values). */
+ * q_rows / kv_rows: rows of Q and O / of K and V (every sequence's q_start + q_len <= q_rows, kv_start + kv_len <=
+ * kv_rows), the row counts of the kernel's TMA tensor maps. Its bulk copies move only whole 128-row tiles that lie
+ * inside a sequence; a tile a sequence ends in is copied (Q, K, V) or stored (O) row by row, so no row outside the
+ * sequences is read or written. */
 int d1_flash_attn_tc(const d1_half* Q, int ldq, const d1_half* K, const d1_half* V, int ldkv, int ext_ld, d1_half* O,
                      int ldo, const AttnSeq* seqs, const int* work, int n_work, int heads, int group, float scale,
                      int q_rows, int kv_rows, cudaStream_t stream);
