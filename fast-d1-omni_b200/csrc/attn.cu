@@ -303,7 +303,9 @@ __global__ void __launch_bounds__(128 * HPC, 2) k_flash_attn(const FaArgs p) {
 // overlaps the shared-memory S MMAs. (Tried and slower or equal: 64-key tiles with S two tiles ahead, 145 us at
 // 4 x 2048 against 117; 96-key tiles with two S buffers, 123 us; the two warpgroups taking turns on the
 // exponentials, 128 us; four softmax warpgroups, two per query tile each taking 64 of the 128 keys and exchanging
-// the row max through shared memory, 127 us; a quarter of the exponentials on the FMA pipe, 122 us; the row sums
+// the row max through shared memory, 127 us; a fourth warpgroup that reads, normalises and stores O so the softmax
+// warpgroups go straight on to the next unit (512 threads, registers split 184 / 72 by setmaxnreg), 126 against 121 us
+// and 28.3 against 25.7 us at 32 x 256; a quarter of the exponentials on the FMA pipe, 122 us; the row sums
 // by one more MMA per tile, P times a shared-memory tile whose first column is ones, 144 -> 189 us with P through
 // shared memory.)
 constexpr int TQ = 128;                   // query rows per tile (TMEM lanes)
