@@ -233,10 +233,12 @@ class Dispatcher:
 
 # Media work in trunk-position equivalents, for the static split: a least-squares fit of the per-rank device times of
 # the config-4 stream on B200 at 1, 2, 4 and 8 GPUs against each rank's trunk positions, image patches and audio
-# frames gave 0.725 us per trunk position, 1.305 us per 16x16 image patch (vision tower and projector) and 0.858 us
-# per 10 ms audio frame (front end, subsampling, FastConformer and adapter at a few hundred rows per clip).
-PATCH_COST = 1.8
-FRAME_COST = 1.18
+# frames gave 0.7245 us per trunk position, 0.80 us per 16x16 image patch (vision tower and projector) and 1.05 us
+# per 10 ms audio frame (front end, subsampling, FastConformer and adapter at a few hundred rows per clip); residual
+# 1.5 ms of ~84 ms per pass. (A first fit, on a split that balanced positions only and an older build, gave 1.8 and
+# 1.18.)
+PATCH_COST = 1.10
+FRAME_COST = 1.45
 
 
 def request_cost(req) -> float:
